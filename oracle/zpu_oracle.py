@@ -1,0 +1,307 @@
+"""ctypes front end of the CPU oracle (liboracle.so, built from zpu_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline.  Only
+tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm
+import this module.  The product library (zpu_b200 / libzpucuda.so) never
+does, and has no CPU fallback.
+
+Also restates the shape logic of zpu's `ops.matmul` (src/zpu/ops.zig:1062-1205)
+in Python, so a batched/broadcast/vmapped matmul can be checked end to end.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+# src/zpu/prims.zig:9-109 element-wise codes (the first 32 unary, then binary)
+PRIM = {
+    "neg": 0, "abs": 1, "exp": 2, "expm1": 3, "log": 4, "log1p": 5, "sqrt": 6, "rsqrt": 7,
+    "square": 8, "recip": 9, "cbrt": 10, "sin": 11, "cos": 12, "tan": 13, "asin": 14,
+    "acos": 15, "atan": 16, "sinh": 17, "cosh": 18, "tanh": 19, "asinh": 20, "acosh": 21,
+    "atanh": 22, "erf": 23, "sigmoid": 24, "softplus": 25, "relu": 26, "floor": 27,
+    "ceil": 28, "round": 29, "trunc": 30, "sign": 31,
+    "add": 35, "sub": 36, "mul": 37, "div": 38, "pow": 39, "maximum": 40, "minimum": 41,
+}
+
+_lib = None
+
+
+def build():
+    """Compiles liboracle.so with the committed Makefile (gcc)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    src = os.path.join(HERE, "zpu_oracle.c")
+    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        build()
+    L = C.CDLL(LIB_PATH)
+    P, S, D, F, I64 = C.c_void_p, C.c_size_t, C.c_double, C.c_float, C.c_int64
+    sig = {
+        "zo_rng_next": (C.c_uint64, [P]),
+        "zo_rng_next_f64": (D, [P]),
+        "zo_uniform_range_f64": (None, [C.c_uint64, P, S, D, D]),
+        "zo_uniform_range_f32": (None, [C.c_uint64, P, S, D, D]),
+        "zo_normal_f64": (None, [C.c_uint64, P, S]),
+        "zo_normal_f32": (None, [C.c_uint64, P, S]),
+        "zo_randint_i64": (C.c_int, [C.c_uint64, P, S, I64, I64]),
+        "zo_gemm_f32": (None, [P, P, P, S, S, S]),
+        "zo_gemm_f64": (None, [P, P, P, S, S, S]),
+        "zo_gemm_batched_f32": (None, [P, P, P, S, S, S, C.c_int, P, P, P]),
+        "zo_gemm_batched_f64": (None, [P, P, P, S, S, S, C.c_int, P, P, P]),
+        "zo_reduce_sum_f32": (F, [P, S]),
+        "zo_reduce_sum_f64": (D, [P, S]),
+        "zo_reduce_maxmin_f32": (F, [P, S, C.c_int]),
+        "zo_sum_f64_of_f32": (D, [P, S]),
+        "zo_abssum_f64_of_f32": (D, [P, S]),
+        "zo_unary_f32": (F, [C.c_int, F]),
+        "zo_unary_f64": (D, [C.c_int, D]),
+        "zo_binary_f32": (F, [C.c_int, F, F]),
+        "zo_binary_f64": (D, [C.c_int, D, D]),
+        "zo_set_cores": (None, [S]),
+        "zo_worker_count": (S, [S]),
+        "zo_jit_chain_tanh_sq_affine_sum": (F, [P, S, F, F, P, P]),
+        "zo_pow": (D, [D, D]),
+        "zo_adam_step_f32": (None, [P, P, P, P, S, C.c_long, D, D, D, D]),
+        "zo_adam_step_f64": (None, [P, P, P, P, S, C.c_long, D, D, D, D]),
+        "zo_mlp_loss_grad": (F, [P, P, S, S, S, S, S] + [P] * 12),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+# --------------------------------------------------------------------------- rng
+def uniform_range(seed, n, lo, hi, dtype=np.float32):
+    out = np.empty(n, dtype=dtype)
+    f = lib().zo_uniform_range_f32 if dtype == np.float32 else lib().zo_uniform_range_f64
+    f(seed, _p(out), n, lo, hi)
+    return out
+
+
+def normal(seed, n, dtype=np.float32):
+    out = np.empty(n, dtype=dtype)
+    f = lib().zo_normal_f32 if dtype == np.float32 else lib().zo_normal_f64
+    f(seed, _p(out), n)
+    return out
+
+
+def randint(seed, n, lo, hi):
+    out = np.empty(n, dtype=np.int64)
+    if lib().zo_randint_i64(seed, _p(out), n, lo, hi) != 0:
+        raise ValueError("randint: high <= low")
+    return out
+
+
+# -------------------------------------------------------------------------- gemm
+def gemm(a, b):
+    """kernels.gemm on contiguous row-major 2-D arrays (bit-exact with zpu)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2 and a.dtype == b.dtype
+    d = np.empty((m, n), dtype=a.dtype)
+    f = lib().zo_gemm_f32 if a.dtype == np.float32 else lib().zo_gemm_f64
+    f(_p(a), _p(b), _p(d), m, k, n)
+    return d
+
+
+def gemm_batched(a, b, m, k, n, dims, acs, bcs):
+    """ops.gemmBatched: flat contiguous buffers, batch axes `dims` with element
+    strides `acs`/`bcs` (0 = broadcast)."""
+    total = int(np.prod(dims)) if len(dims) else 1
+    d = np.empty(total * m * n, dtype=a.dtype)
+    dims_ = np.asarray(dims, dtype=np.int64)
+    acs_ = np.asarray(acs, dtype=np.int64)
+    bcs_ = np.asarray(bcs, dtype=np.int64)
+    f = lib().zo_gemm_batched_f32 if a.dtype == np.float32 else lib().zo_gemm_batched_f64
+    f(_p(a), _p(b), _p(d), m, k, n, len(dims), _p(dims_), _p(acs_), _p(bcs_))
+    return d
+
+
+def matmul(a, b, a_depth=0, b_depth=0):
+    """ops.matmul (ops.zig:1062-1205) with NumPy semantics and vmap depth:
+    leading `depth` axes are vmap axes; 1-D operands are promoted and the
+    added axis squeezed; payload batch axes broadcast right-aligned."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    depth = max(a_depth, b_depth)
+    # withVmapDepth (ops.zig:1211-1224): lead with size-1 stride-0 axes
+    if a_depth < depth:
+        a = a.reshape((1,) * (depth - a_depth) + a.shape)
+    if b_depth < depth:
+        b = b.reshape((1,) * (depth - b_depth) + b.shape)
+    prep_a = a.ndim - depth == 1
+    prep_b = b.ndim - depth == 1
+    if prep_a:
+        a = np.expand_dims(a, depth)
+    if prep_b:
+        b = np.expand_dims(b, b.ndim)
+    m, k = a.shape[-2:]
+    k2, n = b.shape[-2:]
+    if k != k2:
+        raise ValueError("ShapeMismatch")
+    a_nba, b_nba = a.ndim - 2 - depth, b.ndim - 2 - depth
+    nb = max(a_nba, b_nba)
+    adims = [1] * (nb - a_nba) + list(a.shape[depth:depth + a_nba])
+    bdims = [1] * (nb - b_nba) + list(b.shape[depth:depth + b_nba])
+    cdims = []
+    for x, y in zip(adims, bdims):
+        if x == y or y == 1:
+            cdims.append(x)
+        elif x == 1:
+            cdims.append(y)
+        else:
+            raise ValueError("ShapeMismatch")
+    lead = [max(a.shape[i], b.shape[i]) for i in range(depth)]
+    ast = [s // a.itemsize for s in a.strides]
+    bst = [s // b.itemsize for s in b.strides]
+    gdims, acs, bcs = [], [], []
+    for i in range(depth):
+        gdims.append(lead[i])
+        acs.append(ast[i] if a.shape[i] == lead[i] else 0)
+        bcs.append(bst[i] if b.shape[i] == lead[i] else 0)
+    for i in range(nb):
+        gdims.append(cdims[i])
+        aj, bj = i - (nb - a_nba), i - (nb - b_nba)
+        acs.append(ast[aj + depth] if aj >= 0 and adims[i] == cdims[i] else 0)
+        bcs.append(bst[bj + depth] if bj >= 0 and bdims[i] == cdims[i] else 0)
+    out = gemm_batched(a.ravel(), b.ravel(), m, k, n, gdims, acs, bcs)
+    out = out.reshape(tuple(lead) + tuple(cdims) + (m, n))
+    if prep_a:
+        out = np.squeeze(out, axis=out.ndim - 2)
+    if prep_b:
+        out = np.squeeze(out, axis=out.ndim - 1)
+    return out
+
+
+# --------------------------------------------------------------- elementwise/sum
+def unary(prim, x):
+    L = lib()
+    code = PRIM[prim]
+    x = np.asarray(x)
+    if x.dtype == np.float32:
+        return np.array([L.zo_unary_f32(code, float(v)) for v in x.ravel()], dtype=np.float32).reshape(x.shape)
+    return np.array([L.zo_unary_f64(code, float(v)) for v in x.ravel()], dtype=np.float64).reshape(x.shape)
+
+
+def binary(prim, a, b):
+    L = lib()
+    code = PRIM[prim]
+    a, b = np.broadcast_arrays(np.asarray(a), np.asarray(b))
+    if a.dtype == np.float32:
+        f, dt = L.zo_binary_f32, np.float32
+    else:
+        f, dt = L.zo_binary_f64, np.float64
+    return np.array([f(code, float(x), float(y)) for x, y in zip(a.ravel(), b.ravel())], dtype=dt).reshape(a.shape)
+
+
+def reduce_sum(x):
+    """kernels.reduceAll(.sum) in zpu's exact accumulation order."""
+    x = np.ascontiguousarray(x).ravel()
+    if x.dtype == np.float32:
+        return np.float32(lib().zo_reduce_sum_f32(_p(x), x.size))
+    return np.float64(lib().zo_reduce_sum_f64(_p(x), x.size))
+
+
+def reduce_max(x):
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    return np.float32(lib().zo_reduce_maxmin_f32(_p(x), x.size, 1))
+
+
+def sum_f64(x):
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    return lib().zo_sum_f64_of_f32(_p(x), x.size)
+
+
+def abssum_f64(x):
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    return lib().zo_abssum_f64_of_f32(_p(x), x.size)
+
+
+def set_cores(n):
+    lib().zo_set_cores(n)
+
+
+def worker_count(n):
+    return lib().zo_worker_count(n)
+
+
+def jit_chain_tanh_sq_affine_sum(x, a, b, want_vector=False):
+    """y = sumAll(tanh(x*x)*a + b) as jit.Plan.runAll runs it on the CPU.
+    Returns (zpu's f32 sum, f64 sum of the same vector, vector or None)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    t = np.empty_like(x) if want_vector else None
+    s64 = C.c_double(0.0)
+    s = lib().zo_jit_chain_tanh_sq_affine_sum(_p(x), x.size, a, b, _p(t) if t is not None else None,
+                                              C.byref(s64))
+    return np.float32(s), s64.value, t
+
+
+# -------------------------------------------------------------------------- adam
+def pow_(x, y):
+    return lib().zo_pow(x, y)
+
+
+class Adam:
+    """optim.Adam (optim.zig:149-259) with f32 moment state."""
+
+    def __init__(self, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8):
+        self.lr, self.beta1, self.beta2, self.eps = lr, beta1, beta2, eps
+        self.t = 0
+        self.m = None
+        self.v = None
+
+    def step(self, params, grads):
+        if self.m is None:
+            self.m = [np.zeros(p.size, dtype=np.float32) for p in params]
+            self.v = [np.zeros(p.size, dtype=np.float32) for p in params]
+        self.t += 1
+        for p, g, m, v in zip(params, grads, self.m, self.v):
+            assert p.flags.c_contiguous and g.flags.c_contiguous
+            f = lib().zo_adam_step_f32 if p.dtype == np.float32 else lib().zo_adam_step_f64
+            f(_p(p), _p(g), _p(m), _p(v), p.size, self.t, self.lr, self.beta1, self.beta2, self.eps)
+
+
+# --------------------------------------------------------------------------- mlp
+XAVIER_SEED0 = 0x5EED0010
+
+
+def mlp_init(dims, seed0=XAVIER_SEED0):
+    """Xavier-uniform W_l ~ U(-sqrt(6/(in+out)), +sqrt(6/(in+out))) seeded
+    seed0 + l (rng.zig:46 uniformRange), zero biases."""
+    params = []
+    for l in range(len(dims) - 1):
+        fin, fout = dims[l], dims[l + 1]
+        lim = (6.0 / (fin + fout)) ** 0.5
+        W = uniform_range(seed0 + l, fin * fout, -lim, lim).reshape(fin, fout)
+        params += [W, np.zeros(fout, dtype=np.float32)]
+    return params
+
+
+def mlp_loss_grad(X, labels, params):
+    """Loss and gradients of dense->tanh->dense->tanh->dense->sparseCrossEntropy."""
+    W1, b1, W2, b2, W3, b3 = params
+    B, d0 = X.shape
+    d1, d2, d3 = W1.shape[1], W2.shape[1], W3.shape[1]
+    grads = [np.empty_like(p) for p in params]
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    labels = np.ascontiguousarray(labels, dtype=np.int64)
+    loss = lib().zo_mlp_loss_grad(_p(X), _p(labels), B, d0, d1, d2, d3,
+                                  *[_p(p) for p in params], *[_p(g) for g in grads])
+    return np.float32(loss), grads

@@ -1,0 +1,137 @@
+"""Extracts the golden vectors for the hot path from the reference checkout.
+
+Run once, in a container that has the reference mounted:
+
+    python tests/golden/make_golden.py /root/reference
+
+It reads the reference's own snapshot files (snapshots/zpu/**.snap, written by
+`zig build test -Dupdate-snapshots`) and pairs each with the inputs that
+tests/snap/zpu.zig feeds it, plus the known answers of src/zpu/tests.zig and
+the kernel tests of src/zpu/kernels.zig.  The result, zpu_golden.json, is
+committed; the tests read only that file, never the reference.
+"""
+import json
+import math
+import os
+import sys
+
+CASES = {
+    # name -> (snapshot path, tolerance from tests/snap/zpu.zig)
+    "linalg/matmul-3x3": 1e-9,     # tests/snap/zpu.zig:118
+    "linalg/matvec": 1e-9,         # tests/snap/zpu.zig:119
+    "transforms/vmap": 1e-9,       # tests/snap/zpu.zig:279
+    "transforms/jit-replay": 1e-9, # tests/snap/zpu.zig:288
+    "reduce/sum-all": 1e-9,        # tests/snap/zpu.zig:85
+    "reduce/sum-axis0": 1e-9,      # tests/snap/zpu.zig:86
+    "ops/tanh": 1e-9,              # tests/snap/zpu.zig:62
+    "ops/exp": 1e-9,               # tests/snap/zpu.zig:60
+    "ops/sigmoid": 1e-9,           # tests/snap/zpu.zig:61
+    "ops/erf": 1e-9,               # tests/snap/zpu.zig:63
+    "ops/mul-scalar": 1e-9,        # tests/snap/zpu.zig:67
+    "ops/add-broadcast": 1e-9,     # tests/snap/zpu.zig:66
+    "ops/square-rsqrt": 1e-9,      # tests/snap/zpu.zig:65
+    "ops/sqrt-abs": 1e-9,          # tests/snap/zpu.zig:64
+    "ops/maximum": 1e-9,           # tests/snap/zpu.zig:68
+    "nn/log-softmax": 1e-9,        # tests/snap/zpu.zig:143
+    "nn/softmax": 1e-9,            # tests/snap/zpu.zig:142
+    "optim/adam-step1": 1e-9,      # tests/snap/zpu.zig:340
+    "optim/adam-step10": 1e-9,     # tests/snap/zpu.zig:342
+    "rng/normal-seed12345": 0.0,   # tests/snap/zpu.zig:355
+    "rng/uniform-seed12345": 0.0,  # tests/snap/zpu.zig:358
+}
+
+
+def parse_snap(path):
+    shape, dtype, values = None, None, []
+    with open(path) as f:
+        for line in f:
+            line = line.strip()
+            if not line:
+                continue
+            if line.startswith("#"):
+                parts = line[1:].split()
+                if parts and parts[0] == "shape":
+                    i = parts.index("dtype")
+                    dims = parts[1:i]
+                    shape = [] if dims == ["()"] else [int(d) for d in dims]
+                    dtype = parts[i + 1]
+                continue
+            values.extend(float(v) for v in line.split())
+    return {"shape": shape, "dtype": dtype, "values": values}
+
+
+def spread(n):
+    """tests/snap/zpu.zig:28-36: sin(0.7 i) * 1.5 + 0.01 i - 0.25."""
+    return [math.sin(i * 0.7) * 1.5 + i * 0.01 - 0.25 for i in range(n)]
+
+
+def main(ref):
+    snaps = {}
+    for name, tol in CASES.items():
+        snap = parse_snap(os.path.join(ref, "snapshots", "zpu", name + ".snap"))
+        snap["tol"] = tol
+        snaps["zpu/" + name] = snap
+    with open(os.path.join(ref, "snapshots", "zpu", "transforms", "jit-steps.snap")) as f:
+        jit_steps = int(f.read().split()[1])
+
+    inputs = {
+        # tests/snap/zpu.zig:111-119
+        "spd3": [4.0, 1.0, 0.5, 1.0, 3.0, 0.25, 0.5, 0.25, 2.0],
+        "rhs3": [1.0, 2.0, 3.0],
+        # tests/snap/zpu.zig:28-36 (x = spread(8) for ops, spread(12) as 3x4 for reductions)
+        "spread8": spread(8),
+        "spread12": spread(12),
+        # tests/snap/zpu.zig:137-141
+        "logits3x3": [1.0, 2.0, 3.0, -1.0, 0.0, 0.5, 2.5, -2.5, 0.0],
+        # tests/snap/zpu.zig:267-276 (shape [3,2,2] each); f = tanh(matmul(a, b))
+        "vmap_a": [1, 2, 3, 4, 0.5, -1, 2, 0.25, 2, 0, -1, 1],
+        "vmap_b": [1, 0, 0, 1, 2, -1, 0.5, 1, -1, 1, 1, 0],
+        # tests/snap/zpu.zig:333-342: Adam(lr=0.01) on f64 params
+        "adam_params": [1.0, -2.0, 0.5],
+        "adam_grads": [0.1, -0.25, 0.05],
+        "adam_lr": 0.01,
+        "rng_seed": 12345,
+    }
+
+    known = [
+        # src/zpu/tests.zig:145-171
+        {"name": "matmul 2x3 @ 3x2", "a": [1, 2, 3, 4, 5, 6], "a_shape": [2, 3],
+         "b": [7, 8, 9, 10, 11, 12], "b_shape": [3, 2], "want": [58, 64, 139, 154], "tol": 1e-12},
+        {"name": "matmul vector @ matrix", "a": [1, 1, 1], "a_shape": [3],
+         "b": [7, 8, 9, 10, 11, 12], "b_shape": [3, 2], "want": [27, 30], "tol": 1e-12},
+        {"name": "matmul matrix @ vector", "a": [1, 2, 3, 4, 5, 6], "a_shape": [2, 3],
+         "b": [1, 1, 1], "b_shape": [3], "want": [6, 15], "tol": 1e-12},
+        {"name": "matmul batched", "a": [1, 2, 3, 4, 1, 0, 0, 1], "a_shape": [2, 2, 2],
+         "b": [5, 6, 7, 8, 1, 2, 3, 4], "b_shape": [2, 2, 2], "want": [19, 22, 43, 50, 1, 2, 3, 4],
+         "tol": 1e-12},
+        {"name": "matmul batch broadcast", "a": [1, 2, 3, 4, 1, 0, 0, 1], "a_shape": [2, 2, 2],
+         "b": [1, 2, 3, 4], "b_shape": [2, 2], "want": [7, 10, 15, 22, 1, 2, 3, 4], "tol": 1e-12},
+    ]
+
+    # src/zpu/kernels.zig:512-543: gemm vs the naive triple loop at 1e-12 on
+    # these shapes, inputs a[i] = (i % 7) * 0.5 - 1, b[i] = (i % 5) * 0.25 - 0.5.
+    gemm_shapes = [[1, 1, 1], [3, 4, 5], [32, 7, 128], [35, 9, 133], [2, 33, 2]]
+    # src/zpu/kernels.zig:545-581: reduction edges (lengths 0, 1, L, L+1, 4L+3
+    # of 0..len-1 sum exactly) and data[i] = sin(0.37 i) * 3 for n = 1000.
+    reduce_lengths = [0, 1, 8, 9, 35]
+
+    out = {
+        "generated_by": "tests/golden/make_golden.py",
+        "reference_files": ["snapshots/zpu/**/*.snap", "tests/snap/zpu.zig",
+                            "src/zpu/tests.zig", "src/zpu/kernels.zig"],
+        "snapshot_tolerance_rule": "|w - g| <= tol * max(1, |w|, |g|)  (tests/snapshot.zig:239-244)",
+        "snapshots": snaps,
+        "jit_steps": jit_steps,
+        "inputs": inputs,
+        "known_answers": known,
+        "gemm_shapes": gemm_shapes,
+        "reduce_lengths": reduce_lengths,
+    }
+    dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "zpu_golden.json")
+    with open(dst, "w") as f:
+        json.dump(out, f, indent=1)
+    print("wrote", dst)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,247 @@
+"""The CPU oracle against the reference's own golden vectors (snapshots,
+known answers, kernel tests) — this pins the oracle before anything is
+checked against it."""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import zpu_oracle as zo
+
+
+def snap_close(want, got, tol):
+    """tests/snapshot.zig:239-244: |w - g| <= tol * max(1, |w|, |g|)."""
+    want = np.asarray(want, dtype=np.float64).ravel()
+    got = np.asarray(got, dtype=np.float64).ravel()
+    assert want.shape == got.shape
+    bound = tol * np.maximum(1.0, np.maximum(np.abs(want), np.abs(got)))
+    bad = np.abs(want - got) > bound
+    assert not bad.any(), (want[bad], got[bad])
+
+
+def snap(golden, name):
+    s = golden["snapshots"][name]
+    return np.asarray(s["values"]), s["tol"], s["shape"]
+
+
+def test_rng_normal_exact(golden):
+    want, tol, shape = snap(golden, "zpu/rng/normal-seed12345")
+    assert tol == 0.0
+    got = zo.normal(golden["inputs"]["rng_seed"], int(np.prod(shape)), np.float64)
+    assert np.array_equal(want, got), (want, got)
+
+
+def test_rng_uniform_exact(golden):
+    want, tol, shape = snap(golden, "zpu/rng/uniform-seed12345")
+    s = np.uint64(golden["inputs"]["rng_seed"])
+    got = zo.uniform_range(int(s), int(np.prod(shape)), 0.0, 1.0, np.float64)
+    assert np.array_equal(want, got)
+
+
+def test_matmul_snapshots(golden):
+    a = np.array(golden["inputs"]["spd3"]).reshape(3, 3)
+    want, tol, _ = snap(golden, "zpu/linalg/matmul-3x3")
+    snap_close(want, zo.matmul(a, a), tol)
+    want, tol, _ = snap(golden, "zpu/linalg/matvec")
+    got = zo.matmul(a, np.array(golden["inputs"]["rhs3"]))
+    assert got.shape == (3,)
+    snap_close(want, got, tol)
+
+
+def test_vmap_and_jit_replay_snapshots(golden):
+    a = np.array(golden["inputs"]["vmap_a"], dtype=np.float64).reshape(3, 2, 2)
+    b = np.array(golden["inputs"]["vmap_b"], dtype=np.float64).reshape(3, 2, 2)
+    got = zo.unary("tanh", zo.matmul(a, b, 1, 1))
+    for name in ("zpu/transforms/vmap", "zpu/transforms/jit-replay"):
+        want, tol, shape = snap(golden, name)
+        assert list(got.shape) == shape
+        snap_close(want, got, tol)
+    assert golden["jit_steps"] == 2
+
+
+@pytest.mark.parametrize("name,fn", [
+    ("zpu/ops/tanh", lambda x: zo.unary("tanh", x)),
+    ("zpu/ops/exp", lambda x: zo.unary("exp", x)),
+    ("zpu/ops/sigmoid", lambda x: zo.unary("sigmoid", x)),
+    ("zpu/ops/erf", lambda x: zo.unary("erf", x)),
+    ("zpu/ops/sqrt-abs", lambda x: zo.unary("sqrt", zo.unary("abs", x))),
+    ("zpu/ops/square-rsqrt", lambda x: zo.unary("rsqrt", zo.unary("square", x))),
+    ("zpu/ops/mul-scalar", lambda x: zo.binary("mul", x, 2.5)),
+    ("zpu/ops/add-broadcast", lambda x: zo.binary("add", x, np.array([1.0]))),
+    ("zpu/ops/maximum", lambda x: zo.binary("maximum", x, zo.unary("neg", x))),
+])
+def test_elementwise_snapshots(golden, name, fn):
+    x = np.array(golden["inputs"]["spread8"], dtype=np.float64)
+    want, tol, _ = snap(golden, name)
+    snap_close(want, fn(x), tol)
+
+
+def test_reduction_snapshots(golden):
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    want, tol, _ = snap(golden, "zpu/reduce/sum-all")
+    snap_close(want, [zo.reduce_sum(x)], tol)
+    # sum over axis 0 is the generic row-order walk (ops.zig:746-752)
+    col = np.zeros(4)
+    for r in range(3):
+        col = col + x[r]
+    want, tol, _ = snap(golden, "zpu/reduce/sum-axis0")
+    snap_close(want, col, tol)
+
+
+def _log_softmax_rows(x):
+    out = np.empty_like(x)
+    sm = np.empty_like(x)
+    for i, row in enumerate(x):
+        m = max(row)
+        s = row - m
+        e = zo.unary("exp", s)
+        z = zo.reduce_sum(e)
+        out[i] = s - math.log(z)
+        sm[i] = e / z
+    return out, sm
+
+
+def test_softmax_snapshots(golden):
+    x = np.array(golden["inputs"]["logits3x3"], dtype=np.float64).reshape(3, 3)
+    lsm, sm = _log_softmax_rows(x)
+    want, tol, _ = snap(golden, "zpu/nn/log-softmax")
+    snap_close(want, lsm, tol)
+    want, tol, _ = snap(golden, "zpu/nn/softmax")
+    snap_close(want, sm, tol)
+
+
+def test_adam_snapshots(golden):
+    inp = golden["inputs"]
+    p = np.array(inp["adam_params"], dtype=np.float64)
+    g = np.array(inp["adam_grads"], dtype=np.float64)
+    opt = zo.Adam(lr=inp["adam_lr"])
+    opt.step([p], [g])
+    want, tol, _ = snap(golden, "zpu/optim/adam-step1")
+    snap_close(want, p, tol)
+    for _ in range(9):
+        opt.step([p], [g])
+    want, tol, _ = snap(golden, "zpu/optim/adam-step10")
+    snap_close(want, p, tol)
+
+
+def test_known_answer_matmuls(golden):
+    for case in golden["known_answers"]:
+        a = np.array(case["a"], dtype=np.float64).reshape(case["a_shape"])
+        b = np.array(case["b"], dtype=np.float64).reshape(case["b_shape"])
+        got = zo.matmul(a, b)
+        assert np.allclose(got.ravel(), case["want"], rtol=case["tol"], atol=0), case["name"]
+
+
+def test_gemm_vs_naive_kernel_shapes(golden):
+    """kernels.zig:512-543."""
+    for m, k, n in golden["gemm_shapes"]:
+        a = (np.arange(m * k) % 7) * 0.5 - 1.0
+        b = (np.arange(k * n) % 5) * 0.25 - 0.5
+        a, b = a.reshape(m, k), b.reshape(k, n)
+        got = zo.gemm(a, b)
+        want = np.zeros((m, n))
+        for p in range(k):
+            want += np.outer(a[:, p], b[p])
+        assert np.allclose(got, want, rtol=1e-12, atol=1e-300)
+
+
+def test_gemm_is_the_fma_chain():
+    """Per element: c = 0; c = fma(a[i,p], b[p,j], c) for p ascending, with
+    the non-vector tail columns as mul+add (kernels.zig:369-398)."""
+    rng = np.random.default_rng(3)
+    m, k, n = 5, 37, 139  # n = 128 + 11: a second panel with an 8-wide part and a tail
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    got = zo.gemm(a, b)
+    want = np.zeros((m, n), dtype=np.float32)
+    for j in range(n):
+        pj = j % 128
+        nb = min(128, n - (j - pj))
+        vec = pj < (nb // 8) * 8
+        for i in range(m):
+            c = np.float32(0)
+            for p in range(k):
+                if vec:
+                    c = np.float32(np.float64(a[i, p]) * np.float64(b[p, j]) + np.float64(c))
+                else:
+                    c = np.float32(c + np.float32(a[i, p] * b[p, j]))
+            want[i, j] = c
+    # fma(a,b,c) for f32 == round_f32(a*b + c in f64) except in double-rounding
+    # corner cases; the products of two f32 are exact in f64, so only the final
+    # sum is rounded twice -- allow a 1-ulp difference there and none elsewhere.
+    assert np.max(np.abs(got.view(np.int32) - want.view(np.int32))) <= 1
+
+
+def test_reduce_edges(golden):
+    """kernels.zig:571-581: sums of 0..len-1 are exact at every edge length."""
+    for n in golden["reduce_lengths"]:
+        x = np.arange(n, dtype=np.float32)
+        assert zo.reduce_sum(x) == np.float32(n * (n - 1) // 2)
+    nan = np.full(8, np.nan, dtype=np.float32)
+    assert np.isnan(zo.reduce_max(nan))
+
+
+def test_reduce_matches_left_to_right_loosely():
+    """kernels.zig:545-569: n = 1000, data[i] = sin(0.37 i) * 3."""
+    data = np.sin(np.arange(1000) * 0.37) * 3.0
+    want = 0.0
+    for v in data:
+        want += v
+    assert abs(zo.reduce_sum(data) - want) <= 1e-12 * abs(want)
+
+
+def test_worker_count_matches_parallel_zig():
+    zo.set_cores(8)
+    assert zo.worker_count(63999) == 1
+    assert zo.worker_count(64000) == 4
+    assert zo.worker_count(1 << 26) == 8
+    zo.set_cores(0)
+
+
+def test_jit_chain_small():
+    x = zo.normal(0x5EED0003, 1000)
+    s, s64, t = zo.jit_chain_tanh_sq_affine_sum(x, 0.5, -0.25, want_vector=True)
+    ref = np.array([np.float32(np.float32(math.tanh(float(np.float32(v * v)))) * np.float32(0.5)) for v in x],
+                   dtype=np.float32) + np.float32(-0.25)
+    assert np.array_equal(t, ref)
+    assert s == zo.reduce_sum(ref)
+    assert abs(s64 - sum(float(v) for v in ref)) < 1e-9
+
+
+def test_pow_integer_powers():
+    for t in range(1, 30):
+        # repeated squaring (Go's algorithm) sits within a few ulp of libm pow
+        assert abs(zo.pow_(0.9, t) - 0.9 ** t) <= 1e-15 * 0.9 ** t
+
+
+def test_mlp_gradient_finite_difference():
+    """The oracle's analytic MLP gradient against central differences in f64
+    arithmetic on a tiny network (a check of the restated backward pass)."""
+    rng = np.random.default_rng(0)
+    B, dims = 4, (6, 5, 4, 3)
+    X = rng.uniform(0, 1, (B, dims[0])).astype(np.float32)
+    y = rng.integers(0, dims[3], B).astype(np.int64)
+    params = zo.mlp_init(list(dims))
+    params[1][:] = 0.1
+    loss, grads = zo.mlp_loss_grad(X, y, params)
+
+    def f64_loss(ps):
+        W1, b1, W2, b2, W3, b3 = [p.astype(np.float64) for p in ps]
+        h = np.tanh(X.astype(np.float64) @ W1 + b1)
+        h = np.tanh(h @ W2 + b2)
+        lg = h @ W3 + b3
+        lg = lg - lg.max(1, keepdims=True)
+        lp = lg - np.log(np.exp(lg).sum(1, keepdims=True))
+        return -lp[np.arange(B), y].mean()
+
+    assert abs(loss - f64_loss(params)) < 1e-5
+    for pi in range(6):
+        for idx in [0, params[pi].size - 1]:
+            ps = [p.astype(np.float64) for p in params]
+            h = 1e-6
+            ps[pi].ravel()[idx] += h
+            up = f64_loss(ps)
+            ps[pi].ravel()[idx] -= 2 * h
+            dn = f64_loss(ps)
+            fd = (up - dn) / (2 * h)
+            assert abs(grads[pi].ravel()[idx] - fd) < 1e-4, (pi, idx, grads[pi].ravel()[idx], fd)
