@@ -1,0 +1,223 @@
+/*
+ * zpucuda.h -- C ABI of libzpucuda.so, the B200 (sm_100a) execution layer for
+ * zpu's data-parallel hot path: ops.matmul (f32 / f64, batched / vmapped),
+ * the elementwise + reduction regions of a jit plan, and the MLP train step.
+ *
+ * Conventions
+ *  - Every entry point returns an int status (ZPUCUDA_OK == 0).  Codes 1..12
+ *    are the members of zpu's tensor.Error in declaration order
+ *    (src/zpu/tensor.zig:58-71); codes 13.. are device-side failures.
+ *  - Pointers named `d_*` or documented as device pointers are HBM addresses
+ *    (from zpucuda_buf_devptr, cudaMalloc, or any allocator on the same
+ *    device).  Sizes and strides are in ELEMENTS unless named *_bytes.
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the calling
+ *    thread's bound stream (zpucuda_thread_bind), mirroring zpu's threadlocal
+ *    context (src/zpu/context.zig:34-58).  To run on the legacy default
+ *    stream pass cudaStreamLegacy ((void*)0x1).  Calls are asynchronous with respect
+ *    to the host unless documented otherwise; zpucuda_sync waits, bounded.
+ *  - No entry point falls back to a CPU implementation: an unsupported case
+ *    returns ZPUCUDA_ERR_NOT_SUPPORTED and computes nothing.
+ */
+#ifndef ZPUCUDA_H
+#define ZPUCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+enum {
+    ZPUCUDA_OK = 0,
+    ZPUCUDA_ERR_OUT_OF_MEMORY = 1,       /* tensor.Error.OutOfMemory */
+    ZPUCUDA_ERR_SHAPE_MISMATCH = 2,      /* tensor.Error.ShapeMismatch */
+    ZPUCUDA_ERR_DTYPE_MISMATCH = 3,      /* tensor.Error.DTypeMismatch */
+    ZPUCUDA_ERR_RANK_TOO_LARGE = 4,      /* tensor.Error.RankTooLarge */
+    ZPUCUDA_ERR_INVALID_SHAPE = 5,       /* tensor.Error.InvalidShape */
+    ZPUCUDA_ERR_INVALID_AXIS = 6,        /* tensor.Error.InvalidAxis */
+    ZPUCUDA_ERR_NON_CONTIGUOUS = 7,      /* tensor.Error.NonContiguous */
+    ZPUCUDA_ERR_INDEX_OUT_OF_RANGE = 8,  /* tensor.Error.IndexOutOfRange */
+    ZPUCUDA_ERR_NOT_SUPPORTED = 9,       /* tensor.Error.NotSupported */
+    ZPUCUDA_ERR_NOT_DIFFERENTIABLE = 10, /* tensor.Error.NotDifferentiable */
+    ZPUCUDA_ERR_NOT_POSITIVE_DEFINITE = 11,
+    ZPUCUDA_ERR_DEVICE_MISMATCH = 12,    /* tensor.Error.DeviceMismatch */
+    ZPUCUDA_ERR_TIMEOUT = 13,            /* a bounded wait ran out */
+    ZPUCUDA_ERR_CUDA = 14,               /* a CUDA runtime/driver call failed */
+    ZPUCUDA_ERR_NO_DEVICE = 15,          /* no usable sm_100 device */
+    ZPUCUDA_ERR_INVALID_ARGUMENT = 16    /* NULL pointer, negative size, ... */
+};
+
+/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13). */
+enum { ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1 };
+
+/* prims.AXIS_NONE (src/zpu/prims.zig:169). */
+#define ZPUCUDA_AXIS_NONE (-2)
+/* shape.MAX_RANK (src/zpu/prims.zig:5). */
+#define ZPUCUDA_MAX_RANK 8
+
+const char *zpucuda_status_string(int status);
+/* Text of the last CUDA error seen by this thread (for ZPUCUDA_ERR_CUDA). */
+const char *zpucuda_last_error(void);
+/* Library version: major * 10000 + minor * 100 + patch. */
+int zpucuda_version(void);
+
+/* ------------------------------------------------------ device / context */
+/* Replaces zpu.init's per-thread context set-up (src/zpu/context.zig:74-78):
+ * selects `device` for the calling thread and creates its stream. */
+int zpucuda_device_count(int *count);
+int zpucuda_init(int device);
+int zpucuda_thread_bind(int device);
+/* The calling thread's stream (cudaStream_t). */
+int zpucuda_get_stream(void **stream);
+/* Make `stream` (a caller-owned cudaStream_t) the thread's stream; NULL
+ * restores the library-created one. */
+int zpucuda_set_stream(void *stream);
+/* Waits for the thread's stream for at most timeout_ms (<0: the library's
+ * default of 60 s); ZPUCUDA_ERR_TIMEOUT when it does not drain in time. */
+int zpucuda_sync(int64_t timeout_ms);
+/* Number of kernels this library has launched from the calling process. */
+uint64_t zpucuda_launch_count(void);
+
+/* --------------------------------------------------------------- buffers */
+/* Refcounted HBM storage: the device counterpart of zpu's Buffer
+ * (src/zpu/buffer.zig:14-102): create / retain / release with an atomic
+ * count, 256-byte aligned, freed when the count reaches zero. */
+typedef struct zpucuda_buf zpucuda_buf;
+int zpucuda_buf_alloc(size_t nbytes, zpucuda_buf **out);         /* Buffer.create */
+int zpucuda_buf_alloc_zeroed(size_t nbytes, zpucuda_buf **out);  /* Buffer.createZeroed */
+/* Non-owning wrapper of caller memory (Buffer.wrapConst): release never frees it. */
+int zpucuda_buf_wrap(void *d_ptr, size_t nbytes, zpucuda_buf **out);
+zpucuda_buf *zpucuda_buf_retain(zpucuda_buf *b);                 /* Buffer.retain */
+void zpucuda_buf_release(zpucuda_buf *b);                        /* Buffer.release */
+uint32_t zpucuda_buf_refcount(const zpucuda_buf *b);
+void *zpucuda_buf_devptr(const zpucuda_buf *b);
+size_t zpucuda_buf_bytes(const zpucuda_buf *b);                  /* Buffer.byteLen */
+/* Host <-> HBM copies on the thread's stream; both wait for completion. */
+int zpucuda_buf_upload(zpucuda_buf *b, size_t off_bytes, const void *host, size_t nbytes);
+int zpucuda_buf_download(const zpucuda_buf *b, size_t off_bytes, void *host, size_t nbytes);
+
+/* ------------------------------------------------------------------ GEMM */
+/* C[b] = op(A[b]) @ op(B[b]) for b in 0..batch, row-major, written (not
+ * accumulated) -- kernels.gemm / kernels.gemmBatch (src/zpu/kernels.zig:339,
+ * :417) and ops.gemmTyped / ops.gemmBatched (src/zpu/ops.zig:1016, :1226).
+ *   op(A) is [m,k]: transA == 0 reads A as [m,k] (lda >= k), transA != 0
+ *   reads A as [k,m] (lda >= m) -- the swapLastTwo view the matmul VJP passes
+ *   (src/zpu/autodiff.zig:480-487), consumed without a toContiguous copy.
+ *   op(B) is [k,n]: transB == 0 reads [k,n] (ldb >= n), else [n,k] (ldb >= k).
+ *   stride_a / stride_b: elements between consecutive batch matrices, 0 to
+ *   broadcast one matrix over the batch (ops.zig:1143-1171); stride_c >= m*ldc.
+ * f32 runs on tcgen05 tensor cores with a 3xTF32 split (relative Frobenius
+ * error <= 1e-5 against zpu's f32 FMA chain); f64 on the FP64 DMMA path. */
+int zpucuda_gemm_f32(const float *d_a, const float *d_b, float *d_c,
+                     int64_t m, int64_t n, int64_t k,
+                     int64_t lda, int64_t ldb, int64_t ldc,
+                     int trans_a, int trans_b,
+                     int64_t batch, int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                     void *stream);
+int zpucuda_gemm_f64(const double *d_a, const double *d_b, double *d_c,
+                     int64_t m, int64_t n, int64_t k,
+                     int64_t lda, int64_t ldb, int64_t ldc,
+                     int trans_a, int trans_b,
+                     int64_t batch, int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                     void *stream);
+
+/* A strided tensor view as zpu's Tensor holds it (src/zpu/tensor.zig:79-89),
+ * with the data pointer already advanced by `offset` elements. */
+typedef struct zpucuda_tensor {
+    void *data;
+    int32_t dtype;
+    int32_t rank;
+    int64_t dims[ZPUCUDA_MAX_RANK];
+    int64_t strides[ZPUCUDA_MAX_RANK]; /* elements; 0 = broadcast */
+    int32_t batch_depth;               /* vmap axes leading the shape */
+} zpucuda_tensor;
+
+/* ops.matmul (src/zpu/ops.zig:1062-1205): NumPy semantics on the last two
+ * axes, right-aligned broadcast of payload batch axes, leading vmap axes
+ * (batch_depth) carried through, 1-D promotion and squeeze.
+ * zpucuda_matmul_shape fills `out` (dims, rank, batch_depth, contiguous
+ * strides; data untouched).  zpucuda_matmul computes into out->data, which
+ * must be a contiguous buffer of that shape.  Each operand's last two axes
+ * must be row-major or transposed (unit stride on one of them); anything else
+ * returns ZPUCUDA_ERR_NON_CONTIGUOUS and the caller materialises it. */
+int zpucuda_matmul_shape(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out);
+int zpucuda_matmul(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out,
+                   void *stream);
+
+/* --------------------------------------------------------------- jit plan */
+/* A value of a jit trace: an argument, a folded constant or a step output,
+ * identified as in zpu (Tensor.id, src/zpu/tensor.zig:88). */
+typedef struct zpucuda_value {
+    uint64_t id;
+    int32_t dtype;
+    int32_t rank;
+    int64_t dims[ZPUCUDA_MAX_RANK];
+    int32_t batch_depth;
+} zpucuda_value;
+
+/* jit.Step (src/zpu/jit.zig:30-36) with the Attrs fields reductions use. */
+typedef struct zpucuda_step {
+    int32_t prim;     /* prims.Prim code (src/zpu/prims.zig:9-109) */
+    int32_t n_inputs;
+    uint64_t ins[3];
+    uint64_t out;
+    int32_t axis;     /* Attrs.axis, ZPUCUDA_AXIS_NONE for a full reduction */
+    int32_t keepdims; /* Attrs.withKeepDims */
+} zpucuda_step;
+
+/* jit.Blob (src/zpu/jit.zig:39-42): a constant folded at build time; its
+ * host data is copied into HBM when the plan is created. */
+typedef struct zpucuda_blob {
+    zpucuda_value value;
+    const void *host_data;
+} zpucuda_blob;
+
+typedef struct zpucuda_plan zpucuda_plan;
+
+/* Lowers a built jit plan (the output of jit.build, src/zpu/jit.zig:130-256):
+ * maximal runs of element-wise steps (prims.isElementwise,
+ * src/zpu/prims.zig:198) that end in at most one sum / prod / max / min over
+ * all axes or the last axis become ONE fused kernel each (no intermediate
+ * HBM traffic); matmul steps become GEMM launches.  Region kernels come from
+ * a catalogue generated at build time, with a one-pass bytecode kernel for
+ * regions outside it.  Steps outside that set make creation fail with
+ * ZPUCUDA_ERR_NOT_SUPPORTED. */
+int zpucuda_plan_create(const zpucuda_value *args, int n_args,
+                        const zpucuda_blob *blobs, int n_blobs,
+                        const zpucuda_step *steps, int n_steps,
+                        const uint64_t *out_ids, int n_outs,
+                        zpucuda_plan **out);
+/* jit.Plan.runAll (src/zpu/jit.zig:99-126): `args[i]` are device pointers
+ * to contiguous argument data, `outs[i]` device pointers to contiguous
+ * output buffers (shapes from zpucuda_plan_output). */
+int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *outs, void *stream);
+/* The same call for HOST-resident tensors, i.e. Jit.call on zpu tensors
+ * whose Buffer lives in host memory (src/zpu/transforms.zig:408-411): copies
+ * each argument to HBM staging owned by the plan, runs, copies the outputs
+ * back and waits (bounded) for the stream.  Pinned host memory gives full
+ * copy bandwidth; pageable memory works at the driver's staging speed. */
+int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs,
+                          void *stream);
+int zpucuda_plan_output(const zpucuda_plan *plan, int i, zpucuda_value *value);
+int zpucuda_plan_num_steps(const zpucuda_plan *plan);   /* jit.Plan.numSteps */
+int zpucuda_plan_num_kernels(const zpucuda_plan *plan); /* launches per run */
+/* Plan.describe (src/zpu/jit.zig:71-83) plus the lowering: one line per
+ * kernel.  Writes at most `len` bytes including the terminating NUL. */
+int zpucuda_plan_describe(const zpucuda_plan *plan, char *buf, size_t len);
+void zpucuda_plan_destroy(zpucuda_plan *plan);
+
+/* ------------------------------------------------------------------- rng */
+/* rng.Rng (src/zpu/rng.zig:15-102) on the device: the same splitmix64 stream
+ * as Rng.init(seed) drawn sequentially (state after i draws = seed + i*gamma,
+ * so every element is generated independently).  uniform: Rng.uniformRange;
+ * normal: Rng.normal (Box-Muller pairs); randint: Rng.randint (int64). */
+int zpucuda_rng_uniform(uint64_t seed, int dtype, void *d_out, int64_t n, double lo, double hi, void *stream);
+int zpucuda_rng_normal(uint64_t seed, int dtype, void *d_out, int64_t n, void *stream);
+int zpucuda_rng_randint(uint64_t seed, int64_t *d_out, int64_t n, int64_t lo, int64_t hi, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZPUCUDA_H */

@@ -271,7 +271,7 @@ enum {
     P_CBRT, P_SIN, P_COS, P_TAN, P_ASIN, P_ACOS, P_ATAN, P_SINH, P_COSH, P_TANH, P_ASINH,
     P_ACOSH, P_ATANH, P_ERF, P_SIGMOID, P_SOFTPLUS, P_RELU, P_FLOOR, P_CEIL, P_ROUND,
     P_TRUNC, P_SIGN,
-    P_ADD = 35, P_SUB, P_MUL, P_DIV, P_POW, P_MAXIMUM, P_MINIMUM
+    P_ADD = 35, P_SUB, P_MUL, P_DIV, P_POW, P_MAXIMUM, P_MINIMUM, P_ATAN2, P_HYPOT, P_MOD
 };
 
 /* scalar.zig:74-134: zpu's own erf (Maclaurin series below 1, Lentz
@@ -412,6 +412,14 @@ static double binary_f64(int p, double a, double b) {
     case P_POW: return go_pow(a, b); /* scalar.zig:152-154 -> std.math.pow */
     case P_MAXIMUM: return (a != a) ? a : ((b != b) ? b : (a > b ? a : b));
     case P_MINIMUM: return (a != a) ? a : ((b != b) ? b : (a < b ? a : b));
+    case P_ATAN2: return atan2(a, b);
+    case P_HYPOT: return hypot(a, b);
+    case P_MOD: { /* scalar.zig:155-160: truncated remainder, sign of b */
+        if (b == 0) return NAN;
+        double r = fmod(a, b);
+        if (r != 0 && ((r < 0) != (b < 0))) r += b;
+        return r;
+    }
     default: return NAN;
     }
 }

@@ -25,6 +25,7 @@ PRIM = {
     "atanh": 22, "erf": 23, "sigmoid": 24, "softplus": 25, "relu": 26, "floor": 27,
     "ceil": 28, "round": 29, "trunc": 30, "sign": 31,
     "add": 35, "sub": 36, "mul": 37, "div": 38, "pow": 39, "maximum": 40, "minimum": 41,
+    "atan2": 42, "hypot": 43, "mod_op": 44,
 }
 
 _lib = None

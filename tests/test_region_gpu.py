@@ -1,0 +1,239 @@
+"""Fused jit regions on the B200 against the oracle (zpu's CPU jit path).
+
+Tolerances (stated, per the north star):
+  * element-wise: <= 4 ulp per primitive against the oracle's f32 result;
+  * the full chain tanh(x*x)*a + b: the tanh step within 4 ulp, and every
+    element within |a| * 4 ulp(tanh) + 1 ulp(y) of the oracle;
+  * sums: |gpu - f64 reference| <= 1e-6 * sum(|t_i|) (the GPU accumulates in
+    f64; zpu's own f32 order is reported, not required).
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import zpu_oracle as zo
+from tests.helpers import ulp_diff_f32
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+SEED_X = 0x5EED0003  # the chain workload's input seed
+N_FULL = 1 << 26
+
+
+@pytest.fixture(scope="module")
+def zc():
+    import zpu_b200
+    zpu_b200.check(zpu_b200.lib().zpucuda_init(0))
+    return zpu_b200
+
+
+def chain_plan(zc, n, reduce, a_as_blob=True):
+    steps = [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0), ("mul", [11, 2], 12, -2, 0),
+             ("add", [12, 3], 13, -2, 0)]
+    out = 13
+    if reduce:
+        steps.append(("sum", [13], 14, -2, 0))
+        out = 14
+    if a_as_blob:
+        return zc.Plan([(1, zc.F32, (n,))], [(2, np.float32(0.5)), (3, np.float32(-0.25))], steps, [out])
+    return zc.Plan([(1, zc.F32, (n,)), (2, zc.F32, ()), (3, zc.F32, ())], [], steps, [out])
+
+
+def test_device_rng_is_zpus_stream(zc):
+    n = 4097
+    for seed in (12345, SEED_X):
+        u = zc.rng_uniform(seed, n, -1.0, 1.0).cpu().numpy()
+        assert np.array_equal(u, zo.uniform_range(seed, n, -1.0, 1.0))
+        g = zc.rng_normal(seed, n).cpu().numpy()
+        assert ulp_diff_f32(g, zo.normal(seed, n)).max() <= 1
+        g64 = zc.rng_normal(seed, n, dtype=torch.float64).cpu().numpy()
+        # CUDA's f64 log/sin/cos are within an ulp or two of glibc's: compare
+        # against the radius r (|r cos|, |r sin| <= r) rather than the value
+        want64 = zo.normal(seed, n, np.float64)
+        assert np.max(np.abs(g64 - want64)) <= 1e-14
+        r = zc.rng_randint(seed, n, 0, 10).cpu().numpy()
+        assert np.array_equal(r, zo.randint(seed, n, 0, 10))
+
+
+def test_chain_lowers_to_one_catalogued_kernel(zc):
+    p = chain_plan(zc, 1 << 20, True)
+    assert p.num_kernels() == 1
+    assert "catalogue tanh_sq_affine+sum" in p.describe()
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 5, 33, 1000, (1 << 20) + 3])
+def test_chain_elementwise_within_tolerance(zc, n):
+    x = zo.normal(SEED_X, n)
+    _, _, want = zo.jit_chain_tanh_sq_affine_sum(x, 0.5, -0.25, want_vector=True)
+    p = chain_plan(zc, n, False)
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    got = got.cpu().numpy()
+    tanh_want = np.array([zo.lib().zo_unary_f32(19, float(np.float32(v * v))) for v in x[:2000]], np.float32)
+    tanh_plan = zc.Plan([(1, zc.F32, (n,))], [], [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0)], [11])
+    (tg,) = tanh_plan.run([torch.from_numpy(x).cuda()])
+    tg = tg.cpu().numpy()
+    assert ulp_diff_f32(tg[:2000], tanh_want).max() <= 4
+    ulp_t = np.spacing(np.abs(tg).astype(np.float32)).astype(np.float64)
+    ulp_y = np.spacing(np.abs(want).astype(np.float32)).astype(np.float64)
+    bound = 0.5 * 4 * ulp_t + ulp_y
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert (err <= bound).all(), (err.max(), n)
+
+
+def test_chain_tanh_ulp_full_size(zc):
+    """tanh(x*x) over the whole 2^26-element workload: max ulp vs the oracle."""
+    x_d = zc.rng_normal(SEED_X, N_FULL)
+    p = zc.Plan([(1, zc.F32, (N_FULL,))], [], [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0)], [11])
+    (t,) = p.run([x_d])
+    x = x_d.cpu().numpy()
+    sq = (x * x).astype(np.float32)
+    want = np.tanh(sq.astype(np.float64)).astype(np.float32)  # (f32)tanh((f64)v): scalar.zig:262-266
+    d = ulp_diff_f32(t.cpu().numpy(), want)
+    assert d.max() <= 4, d.max()
+
+
+@pytest.mark.parametrize("n", [0, 1, 7, 1000, (1 << 20) + 3, N_FULL])
+def test_chain_fused_sum(zc, n):
+    x_d = zc.rng_normal(SEED_X, n) if n else torch.empty(0, device="cuda")
+    x = x_d.cpu().numpy()
+    s32, s64, t = zo.jit_chain_tanh_sq_affine_sum(x, 0.5, -0.25, want_vector=True)
+    p = chain_plan(zc, n, True)
+    (got,) = p.run([x_d])
+    g = float(got.cpu().numpy())
+    scale = zo.abssum_f64(t) if n else 0.0
+    assert abs(g - s64) <= 1e-6 * scale + 1e-30, (g, s64, s32)
+    # determinism: a second run gives the same bits
+    (again,) = p.run([x_d])
+    assert float(again.cpu().numpy()) == g
+
+
+def test_chain_scalars_as_arguments(zc):
+    n = 100003
+    x = zo.normal(SEED_X, n)
+    s32, s64, t = zo.jit_chain_tanh_sq_affine_sum(x, 0.5, -0.25, want_vector=True)
+    p = chain_plan(zc, n, True, a_as_blob=False)
+    a = torch.tensor(0.5, dtype=torch.float32, device="cuda")
+    b = torch.tensor(-0.25, dtype=torch.float32, device="cuda")
+    (got,) = p.run([torch.from_numpy(x).cuda(), a, b])
+    assert abs(float(got.cpu()) - s64) <= 1e-6 * zo.abssum_f64(t)
+
+
+def test_misaligned_input_takes_the_bytecode_path(zc):
+    n = 4099
+    x = zo.normal(SEED_X, n + 1)
+    s32, s64, t = zo.jit_chain_tanh_sq_affine_sum(x[1:], 0.5, -0.25, want_vector=True)
+    base = torch.from_numpy(x).cuda()
+    p = chain_plan(zc, n, True)
+    (got,) = p.run([base[1:]])  # 4-byte offset: not 16-byte aligned
+    assert abs(float(got.cpu()) - s64) <= 1e-6 * zo.abssum_f64(t)
+
+
+UNARY = [("neg", -3, 3), ("abs", -3, 3), ("exp", -10, 10), ("expm1", -3, 3), ("log", 0.01, 100),
+         ("log1p", -0.9, 10), ("sqrt", 0, 100), ("rsqrt", 0.01, 100), ("square", -10, 10),
+         ("recip", 0.1, 10), ("cbrt", -8, 8), ("sin", -6, 6), ("cos", -6, 6), ("tan", -1.4, 1.4),
+         ("asin", -1, 1), ("acos", -1, 1), ("atan", -10, 10), ("sinh", -5, 5), ("cosh", -5, 5),
+         ("tanh", -5, 5), ("asinh", -10, 10), ("acosh", 1, 10), ("atanh", -0.99, 0.99),
+         ("erf", -3, 3), ("sigmoid", -10, 10), ("softplus", -10, 10), ("relu", -3, 3),
+         ("floor", -3, 3), ("ceil", -3, 3), ("round", -3, 3), ("trunc", -3, 3), ("sign", -3, 3)]
+
+
+@pytest.mark.parametrize("prim,lo,hi", UNARY)
+def test_bytecode_unary_within_4ulp(zc, prim, lo, hi):
+    n = 3001
+    x = zo.uniform_range(77, n, lo, hi)
+    p = zc.Plan([(1, zc.F32, (n,))], [], [(prim, [1], 10, -2, 0), ("neg", [10], 11, -2, 0)], [11])
+    assert "bytecode" in p.describe()
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    want = -zo.unary(prim, x)
+    assert ulp_diff_f32(got.cpu().numpy(), want).max() <= 4, prim
+
+
+@pytest.mark.parametrize("prim", ["add", "sub", "mul", "div", "pow", "maximum", "minimum", "atan2",
+                                  "hypot", "mod_op"])
+def test_bytecode_binary_within_4ulp(zc, prim):
+    n = 2001
+    a = zo.uniform_range(5, n, 0.1, 4.0)
+    b = zo.uniform_range(6, n, -3.0, 3.0)
+    if prim in ("pow", "mod_op"):
+        b = zo.uniform_range(6, n, 0.5, 3.0)
+    p = zc.Plan([(1, zc.F32, (n,)), (2, zc.F32, (n,))], [], [(prim, [1, 2], 10, -2, 0), ("neg", [10], 11, -2, 0)],
+                [11])
+    (got,) = p.run([torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    want = -zo.binary(prim, a, b)
+    assert ulp_diff_f32(got.cpu().numpy(), want).max() <= 4, prim
+
+
+def test_row_broadcast_and_row_reductions(zc):
+    rows, cols = 37, 129
+    x = zo.uniform_range(9, rows * cols, -2, 2).reshape(rows, cols)
+    bias = zo.uniform_range(10, cols, -1, 1)
+    for prim, fn in (("sum", np.sum), ("max_reduce", np.max), ("min_reduce", np.min)):
+        p = zc.Plan([(1, zc.F32, (rows, cols)), (2, zc.F32, (cols,))], [],
+                    [("add", [1, 2], 10, -2, 0), ("exp", [10], 11, -2, 0), (prim, [11], 12, -1, 0)], [12, 11])
+        red, e = p.run([torch.from_numpy(x).cuda(), torch.from_numpy(bias).cuda()])
+        want_e = zo.unary("exp", zo.binary("add", x, bias))
+        assert ulp_diff_f32(e.cpu().numpy(), want_e).max() <= 4
+        want = fn(want_e.astype(np.float64), axis=1)
+        assert np.allclose(red.cpu().numpy(), want, rtol=2e-6), prim
+
+
+def test_general_broadcast_and_keepdims(zc):
+    x = zo.uniform_range(11, 6 * 5 * 4, -1, 1).reshape(6, 5, 4)
+    col = zo.uniform_range(12, 5, -1, 1).reshape(5, 1)
+    p = zc.Plan([(1, zc.F32, (6, 5, 4)), (2, zc.F32, (5, 1))], [],
+                [("mul", [1, 2], 10, -2, 0), ("sum", [10], 11, -1, 1)], [11, 10])
+    assert ";FG;" in p.describe()
+    red, prod = p.run([torch.from_numpy(x).cuda(), torch.from_numpy(col).cuda()])
+    want = (x * col).astype(np.float32)
+    assert np.array_equal(prod.cpu().numpy(), want)
+    assert red.shape == (6, 5, 1)
+    assert np.allclose(red.cpu().numpy()[..., 0], want.astype(np.float64).sum(-1), rtol=1e-6, atol=1e-7)
+
+
+def test_f64_region_and_prod_reduction(zc):
+    n = 999
+    x = zo.uniform_range(13, n, 0.99, 1.01, np.float64)
+    p = zc.Plan([(1, zc.F64, (n,))], [(2, np.float64(1.0))],
+                [("mul", [1, 2], 10, -2, 0), ("prod_op", [10], 11, -2, 0), ("sum", [1], 12, -2, 0)], [11, 12])
+    assert p.num_kernels() == 2
+    pr, sm = p.run([torch.from_numpy(x).cuda()])
+    assert abs(float(pr.cpu()) - np.prod(x)) <= 1e-12 * abs(np.prod(x))
+    assert abs(float(sm.cpu()) - zo.reduce_sum(x)) <= 1e-12 * n
+
+
+def test_multi_region_plan_with_intermediates(zc):
+    """softmax-like: m = max(x); e = exp(x - m); s = sum(e); y = e / s."""
+    n = 50001
+    x = zo.uniform_range(14, n, -5, 5)
+    steps = [("max_reduce", [1], 10, -2, 0), ("sub", [1, 10], 11, -2, 0), ("exp", [11], 12, -2, 0),
+             ("sum", [12], 13, -2, 0), ("div", [12, 13], 14, -2, 0)]
+    p = zc.Plan([(1, zc.F32, (n,))], [], steps, [14])
+    assert p.num_kernels() == 3, p.describe()
+    (y,) = p.run([torch.from_numpy(x).cuda()])
+    m = np.float32(x.max())
+    e = zo.unary("exp", (x - m).astype(np.float32))
+    want = (e / np.float32(e.astype(np.float64).sum())).astype(np.float32)
+    assert ulp_diff_f32(y.cpu().numpy(), want).max() <= 8
+
+
+def test_run_host_matches_device_run(zc):
+    n = (1 << 20) + 5
+    x_d = zc.rng_normal(SEED_X, n)
+    p = chain_plan(zc, n, True)
+    (dev,) = p.run([x_d])
+    host = x_d.cpu().pin_memory()
+    (h,) = p.run_host([host])
+    assert float(h) == float(dev.cpu())
+
+
+def test_launch_counter_counts_region_launches(zc):
+    p = chain_plan(zc, 4096, True)
+    x = zc.rng_normal(SEED_X, 4096)
+    before = zc.launch_count()
+    for _ in range(3):
+        p.run([x])
+    torch.cuda.synchronize()
+    assert zc.launch_count() - before == 3

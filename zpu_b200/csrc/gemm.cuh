@@ -1,0 +1,48 @@
+// Batched GEMM entry points shared by the matmul front end and the kernels.
+#pragma once
+#include "common.cuh"
+
+namespace zc {
+
+constexpr int kGemmMaxBatchAxes = 6;
+
+// The flattened batch of ops.gemmBatched (src/zpu/ops.zig:1226-1282): batch
+// index -> (a, b) element offsets through per-axis strides (0 = broadcast),
+// walked row-major; the output is contiguous with stride_c per matrix.
+struct GemmBatch {
+    int32_t nax;
+    int64_t dims[kGemmMaxBatchAxes];
+    int64_t sa[kGemmMaxBatchAxes];
+    int64_t sb[kGemmMaxBatchAxes];
+};
+
+__host__ __device__ inline int64_t batch_count(const GemmBatch &g) {
+    int64_t t = 1;
+    for (int i = 0; i < g.nax; i++) t *= g.dims[i];
+    return t;
+}
+
+// Element offsets of batch `bi` into A and B.
+__host__ __device__ inline void batch_offsets(const GemmBatch &g, int64_t bi, int64_t *oa, int64_t *ob) {
+    int64_t a = 0, b = 0;
+    for (int ax = g.nax - 1; ax >= 0; ax--) {
+        const int64_t d = g.dims[ax];
+        const int64_t i = d ? bi % d : 0;
+        bi = d ? bi / d : 0;
+        a += i * g.sa[ax];
+        b += i * g.sb[ax];
+    }
+    *oa = a;
+    *ob = b;
+}
+
+// op(A)[m,k] @ op(B)[k,n] -> C[m,n] (ldc), per batch; trans flags as in
+// zpucuda_gemm_f32.
+int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                    int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                    cudaStream_t s);
+int gemm_f64_device(const double *A, const double *B, double *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                    int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                    cudaStream_t s);
+
+}  // namespace zc

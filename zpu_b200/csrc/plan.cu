@@ -1,0 +1,609 @@
+// jit-plan lowering: turns the steps of a built jit.Plan (src/zpu/jit.zig:
+// 30-36, 130-256) into a short list of launches -- one fused kernel per
+// element-wise(+reduction) region, one GEMM per matmul step -- and replays
+// that list on every run (the device counterpart of Plan.runAll,
+// jit.zig:99-126, which interprets one ops.applyPrim per step and
+// materialises every intermediate).
+#include <stdio.h>
+#include <string.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "region.cuh"
+
+namespace zc {
+int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, cudaStream_t s);
+}
+
+using namespace zc;
+
+namespace {
+
+// prims.Prim codes the lowering knows (src/zpu/prims.zig:9-109).
+enum {
+    PRIM_SUM = 58,
+    PRIM_PROD = 59,
+    PRIM_MAX_REDUCE = 60,
+    PRIM_MIN_REDUCE = 61,
+    PRIM_MATMUL = 80,
+};
+
+const char *kPrimNames[] = {
+    "neg", "abs", "exp", "expm1", "log", "log1p", "sqrt", "rsqrt", "square", "recip", "cbrt",
+    "sin", "cos", "tan", "asin", "acos", "atan", "sinh", "cosh", "tanh", "asinh", "acosh",
+    "atanh", "erf", "sigmoid", "softplus", "relu", "floor", "ceil", "round", "trunc", "sign",
+    "isnan", "isinf", "isfinite", "add", "sub", "mul", "div", "pow", "maximum", "minimum",
+    "atan2", "hypot", "mod_op"};
+
+// The element-wise prims a region kernel evaluates (prims.isElementwise,
+// src/zpu/prims.zig:198, minus predicates and the selection ops).
+bool region_unary(int p) { return p >= 0 && p <= 31; }
+bool region_binary(int p) { return p >= 35 && p <= 44; }
+bool region_reduce(int p) { return p >= PRIM_SUM && p <= PRIM_MIN_REDUCE; }
+
+struct Shape {
+    int rank = 0;
+    int64_t dims[ZPUCUDA_MAX_RANK] = {0};
+    int64_t numel() const {
+        int64_t n = 1;
+        for (int i = 0; i < rank; i++) n *= dims[i];
+        return n;
+    }
+    bool operator==(const Shape &o) const {
+        if (rank != o.rank) return false;
+        for (int i = 0; i < rank; i++)
+            if (dims[i] != o.dims[i]) return false;
+        return true;
+    }
+};
+
+// NumPy broadcasting, right-aligned (shape.broadcastShapeRanked for
+// batch_depth 0, src/zpu/shape.zig:78).
+bool broadcast(const Shape &a, const Shape &b, Shape *out) {
+    Shape r;
+    r.rank = std::max(a.rank, b.rank);
+    for (int i = 0; i < r.rank; i++) {
+        const int ia = a.rank - r.rank + i, ib = b.rank - r.rank + i;
+        const int64_t da = ia >= 0 ? a.dims[ia] : 1, db = ib >= 0 ? b.dims[ib] : 1;
+        if (da == db || db == 1) r.dims[i] = da;
+        else if (da == 1) r.dims[i] = db;
+        else return false;
+    }
+    *out = r;
+    return true;
+}
+
+enum SlotKind { SLOT_ARG, SLOT_BLOB, SLOT_TEMP, SLOT_OUT };
+struct Slot {
+    SlotKind kind = SLOT_TEMP;
+    int index = -1;
+};
+
+struct Value {
+    int32_t dtype = ZPUCUDA_F32;
+    Shape shape;
+    int32_t depth = 0;
+    int producer = -1;  // step index, -1 for args / blobs
+    bool is_arg = false, is_blob = false;
+    int arg_index = -1, blob_index = -1;
+    bool materialised = false;  // has a Slot
+    Slot slot;
+};
+
+struct Launch {
+    enum { REGION, MATMUL } kind = REGION;
+    RegionProgram prog;
+    const CatalogueEntry *cat = nullptr;
+    std::string signature;
+    std::vector<Slot> ins, outs;
+    Slot red;
+    bool has_red = false;
+    void *workspace = nullptr;
+    // matmul
+    Slot ma, mb, mc;
+    zpucuda_tensor ta, tb, tc;
+    std::string text;
+};
+
+}  // namespace
+
+struct zpucuda_plan {
+    int n_args = 0;
+    int n_steps = 0;
+    std::vector<zpucuda_value> arg_values;
+    std::vector<void *> stage_in, stage_out;  // HBM staging of zpucuda_plan_run_host
+    std::vector<Launch> launches;
+    std::vector<zpucuda_value> outputs;
+    std::vector<void *> blobs;  // HBM copies of folded constants
+    std::vector<void *> temps;  // intermediates that cross launches
+    std::vector<void *> workspaces;
+    std::string text;
+    ~zpucuda_plan() {
+        for (void *p : blobs) cudaFree(p);
+        for (void *p : temps) cudaFree(p);
+        for (void *p : workspaces) cudaFree(p);
+        for (void *p : stage_in) cudaFree(p);
+        for (void *p : stage_out) cudaFree(p);
+    }
+};
+
+namespace {
+
+size_t itemsize(int dt) { return dt == ZPUCUDA_F64 ? 8 : 4; }
+
+int lower_fail(zpucuda_plan *p, int st, const std::string &why) {
+    delete p;
+    return set_error(st, "zpucuda_plan_create: " + why);
+}
+
+std::string prim_name(int p) {
+    if (p >= 0 && p < (int)(sizeof(kPrimNames) / sizeof(kPrimNames[0]))) return kPrimNames[p];
+    return "prim" + std::to_string(p);
+}
+
+}  // namespace
+
+extern "C" {
+
+int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blob *blobs, int n_blobs,
+                        const zpucuda_step *steps, int n_steps, const uint64_t *out_ids, int n_outs,
+                        zpucuda_plan **out) {
+    ZC_CHECK(out && (args || !n_args) && (blobs || !n_blobs) && (steps || !n_steps) && out_ids && n_outs > 0,
+             ZPUCUDA_ERR_INVALID_ARGUMENT);
+    *out = nullptr;
+    zpucuda_plan *plan = new zpucuda_plan;
+    plan->n_args = n_args;
+    plan->n_steps = n_steps;
+    plan->arg_values.assign(args, args + n_args);
+    std::map<uint64_t, Value> vals;
+
+    auto add_value = [&](const zpucuda_value &v) -> Value & {
+        Value &x = vals[v.id];
+        x.dtype = v.dtype;
+        x.shape.rank = v.rank;
+        for (int i = 0; i < v.rank; i++) x.shape.dims[i] = v.dims[i];
+        x.depth = v.batch_depth;
+        return x;
+    };
+    for (int i = 0; i < n_args; i++) {
+        if (args[i].rank < 0 || args[i].rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "arg rank");
+        if (args[i].dtype != ZPUCUDA_F32 && args[i].dtype != ZPUCUDA_F64) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "arg dtype");
+        Value &v = add_value(args[i]);
+        v.is_arg = true;
+        v.arg_index = i;
+        v.materialised = true;
+        v.slot = {SLOT_ARG, i};
+    }
+    for (int i = 0; i < n_blobs; i++) {
+        const zpucuda_value &bv = blobs[i].value;
+        if (bv.rank < 0 || bv.rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "blob rank");
+        if (bv.dtype != ZPUCUDA_F32 && bv.dtype != ZPUCUDA_F64) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "blob dtype");
+        Value &v = add_value(bv);
+        v.is_blob = true;
+        v.blob_index = i;
+        v.materialised = true;
+        v.slot = {SLOT_BLOB, i};
+        const size_t nb = (size_t)v.shape.numel() * itemsize(v.dtype);
+        void *d = nullptr;
+        if (cudaMalloc(&d, nb ? nb : 16) != cudaSuccess) {
+            cudaGetLastError();
+            return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "blob allocation");
+        }
+        plan->blobs.push_back(d);
+        if (nb && cudaMemcpy(d, blobs[i].host_data, nb, cudaMemcpyHostToDevice) != cudaSuccess) {
+            cudaGetLastError();
+            return lower_fail(plan, ZPUCUDA_ERR_CUDA, "blob upload");
+        }
+    }
+
+    // ---- shapes of every step output, and who uses what
+    std::map<uint64_t, std::vector<int>> users;
+    for (int s = 0; s < n_steps; s++) {
+        const zpucuda_step &st = steps[s];
+        if (st.n_inputs < 0 || st.n_inputs > 3) return lower_fail(plan, ZPUCUDA_ERR_INVALID_ARGUMENT, "step arity");
+        for (int k = 0; k < st.n_inputs; k++) {
+            if (!vals.count(st.ins[k])) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "step input not defined before use");
+            users[st.ins[k]].push_back(s);
+        }
+        Value o;
+        o.producer = s;
+        const Value &a = vals[st.ins[0]];
+        o.dtype = a.dtype;
+        o.depth = a.depth;
+        if (region_unary(st.prim) && st.n_inputs == 1) {
+            o.shape = a.shape;
+        } else if (region_binary(st.prim) && st.n_inputs == 2) {
+            const Value &b = vals[st.ins[1]];
+            if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
+            if (a.depth != b.depth && a.shape.rank && b.shape.rank)
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "vmap depth mismatch in an element-wise step");
+            o.depth = std::max(a.depth, b.depth);
+            if (!broadcast(a.shape, b.shape, &o.shape)) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
+        } else if (region_reduce(st.prim) && st.n_inputs == 1) {
+            if (st.axis == ZPUCUDA_AXIS_NONE) {
+                o.shape.rank = st.keepdims ? a.shape.rank : 0;
+                for (int i = 0; i < o.shape.rank; i++) o.shape.dims[i] = 1;
+            } else {
+                int ax = st.axis < 0 ? st.axis + a.shape.rank : st.axis;
+                if (ax != a.shape.rank - 1 || a.shape.rank == 0)
+                    return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "only full and last-axis reductions are fused");
+                o.shape = a.shape;
+                if (st.keepdims) o.shape.dims[ax] = 1;
+                else o.shape.rank -= 1;
+            }
+        } else if (st.prim == PRIM_MATMUL && st.n_inputs == 2) {
+            const Value &b = vals[st.ins[1]];
+            if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed-dtype matmul");
+            zpucuda_tensor ta = {}, tb = {}, tc = {};
+            ta.dtype = a.dtype;
+            ta.rank = a.shape.rank;
+            ta.batch_depth = a.depth;
+            tb.dtype = b.dtype;
+            tb.rank = b.shape.rank;
+            tb.batch_depth = b.depth;
+            for (int i = 0; i < a.shape.rank; i++) ta.dims[i] = a.shape.dims[i];
+            for (int i = 0; i < b.shape.rank; i++) tb.dims[i] = b.shape.dims[i];
+            int64_t st_ = 1;
+            for (int i = ta.rank - 1; i >= 0; i--) { ta.strides[i] = st_; st_ *= ta.dims[i]; }
+            st_ = 1;
+            for (int i = tb.rank - 1; i >= 0; i--) { tb.strides[i] = st_; st_ *= tb.dims[i]; }
+            int r = zpucuda_matmul_shape(&ta, &tb, &tc);
+            if (r) return lower_fail(plan, r, "matmul shape");
+            o.shape.rank = tc.rank;
+            for (int i = 0; i < tc.rank; i++) o.shape.dims[i] = tc.dims[i];
+            o.depth = tc.batch_depth;
+        } else {
+            return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " is not lowered to the device");
+        }
+        if (vals.count(st.out)) return lower_fail(plan, ZPUCUDA_ERR_INVALID_ARGUMENT, "step output id reused");
+        vals[st.out] = o;
+    }
+    std::map<uint64_t, int> out_index;
+    for (int i = 0; i < n_outs; i++) {
+        if (!vals.count(out_ids[i])) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "unknown output id");
+        if (!out_index.count(out_ids[i])) out_index[out_ids[i]] = i;
+        const Value &v = vals[out_ids[i]];
+        zpucuda_value ov = {};
+        ov.id = out_ids[i];
+        ov.dtype = v.dtype;
+        ov.rank = v.shape.rank;
+        for (int d = 0; d < v.shape.rank; d++) ov.dims[d] = v.shape.dims[d];
+        ov.batch_depth = v.depth;
+        plan->outputs.push_back(ov);
+    }
+
+    // Where a step output lives once a launch writes it.
+    auto materialise = [&](uint64_t id) -> Slot {
+        Value &v = vals[id];
+        if (v.materialised) return v.slot;
+        auto it = out_index.find(id);
+        if (it != out_index.end()) {
+            v.slot = {SLOT_OUT, it->second};
+        } else {
+            void *d = nullptr;
+            const size_t nb = (size_t)v.shape.numel() * itemsize(v.dtype);
+            if (cudaMalloc(&d, nb ? nb : 16) != cudaSuccess) {
+                cudaGetLastError();
+                v.slot = {SLOT_TEMP, -1};
+                return v.slot;
+            }
+            plan->temps.push_back(d);
+            v.slot = {SLOT_TEMP, (int)plan->temps.size() - 1};
+        }
+        v.materialised = true;
+        return v.slot;
+    };
+
+    // ---- cut regions
+    int s = 0;
+    while (s < n_steps) {
+        const zpucuda_step &st0 = steps[s];
+        if (st0.prim == PRIM_MATMUL) {
+            Launch L;
+            L.kind = Launch::MATMUL;
+            const Value &a = vals[st0.ins[0]], &b = vals[st0.ins[1]];
+            L.ma = a.slot;
+            L.mb = b.slot;
+            memset(&L.ta, 0, sizeof L.ta);
+            memset(&L.tb, 0, sizeof L.tb);
+            L.ta.dtype = a.dtype; L.ta.rank = a.shape.rank; L.ta.batch_depth = a.depth;
+            L.tb.dtype = b.dtype; L.tb.rank = b.shape.rank; L.tb.batch_depth = b.depth;
+            for (int i = 0; i < a.shape.rank; i++) L.ta.dims[i] = a.shape.dims[i];
+            for (int i = 0; i < b.shape.rank; i++) L.tb.dims[i] = b.shape.dims[i];
+            int64_t q = 1;
+            for (int i = L.ta.rank - 1; i >= 0; i--) { L.ta.strides[i] = q; q *= L.ta.dims[i]; }
+            q = 1;
+            for (int i = L.tb.rank - 1; i >= 0; i--) { L.tb.strides[i] = q; q *= L.tb.dims[i]; }
+            zpucuda_matmul_shape(&L.ta, &L.tb, &L.tc);
+            L.mc = materialise(st0.out);
+            if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            char buf[160];
+            snprintf(buf, sizeof buf, "  kernel %zu: gemm %s (%%%llu = matmul(%%%llu, %%%llu))\n", plan->launches.size(),
+                     a.dtype == ZPUCUDA_F64 ? "f64 dmma" : "f32 3xtf32", (unsigned long long)st0.out,
+                     (unsigned long long)st0.ins[0], (unsigned long long)st0.ins[1]);
+            L.text = buf;
+            plan->launches.push_back(L);
+            s++;
+            continue;
+        }
+        // a region: element-wise steps over one shape, at most one trailing reduction
+        Launch L;
+        RegionProgram &P = L.prog;
+        memset(&P, 0, sizeof P);
+        std::map<uint64_t, int> reg;  // value id -> register
+        std::vector<uint64_t> loads;  // external inputs in order of first use
+        std::vector<int> member;      // steps in this region
+        Shape rshape;
+        int32_t rdtype = -1;
+        bool have_shape = false;
+        int e = s;
+        // first pass: which steps join
+        for (; e < n_steps; e++) {
+            const zpucuda_step &st = steps[e];
+            const Value &ov = vals[st.out];
+            if (region_unary(st.prim) || region_binary(st.prim)) {
+                if (have_shape && (!(ov.shape == rshape) || ov.dtype != rdtype)) break;
+                if (!have_shape) { rshape = ov.shape; rdtype = ov.dtype; have_shape = true; }
+                member.push_back(e);
+                continue;
+            }
+            if (region_reduce(st.prim)) {
+                const Value &iv = vals[st.ins[0]];
+                bool inside = std::find(member.begin(), member.end(), iv.producer) != member.end();
+                if (member.empty() || inside) {
+                    if (!have_shape) { rshape = iv.shape; rdtype = iv.dtype; have_shape = true; }
+                    if (inside || member.empty()) { member.push_back(e); e++; }
+                }
+            }
+            break;
+        }
+        if (member.empty()) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "step " + std::to_string(s) + " cannot start a region");
+        P.dtype = rdtype;
+        P.rank = rshape.rank;
+        for (int i = 0; i < rshape.rank; i++) P.dims[i] = rshape.dims[i];
+        P.numel = rshape.numel();
+        std::vector<Insn> ops;
+        int next_reg_after_loads = 0;
+        // inputs: every operand not produced inside the region
+        auto in_region = [&](uint64_t id) {
+            const Value &v = vals[id];
+            return v.producer >= 0 && std::find(member.begin(), member.end(), v.producer) != member.end();
+        };
+        for (int m : member)
+            for (int k = 0; k < steps[m].n_inputs; k++) {
+                uint64_t id = steps[m].ins[k];
+                if (!in_region(id) && std::find(loads.begin(), loads.end(), id) == loads.end()) loads.push_back(id);
+            }
+        if ((int)loads.size() > RP_MAX_IN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region has too many inputs");
+        P.n_in = (int)loads.size();
+        std::string sig = std::string(rdtype == ZPUCUDA_F64 ? "f64" : "f32") + ";";
+        std::string kinds;
+        for (int k = 0; k < P.n_in; k++) {
+            Value &iv = vals[loads[k]];
+            if (!iv.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "region input not materialised");
+            if (iv.dtype != rdtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in a region");
+            reg[loads[k]] = k;
+            P.insn[k] = Insn{OPC_LOAD, (uint8_t)k, (uint8_t)k, 0};
+            L.ins.push_back(iv.slot);
+            const Shape &is = iv.shape;
+            P.in_numel[k] = is.numel();
+            if (is == rshape) {
+                P.in_kind[k] = IN_FULL;
+                kinds += "F";
+            } else if (is.numel() == 1) {
+                P.in_kind[k] = IN_SCALAR;
+                kinds += "S";
+            } else {
+                // right-aligned broadcast: strides over the region's axes
+                bool row = is.rank <= rshape.rank;
+                int64_t stride = 1;
+                for (int d = rshape.rank - 1; d >= 0; d--) {
+                    const int id = is.rank - rshape.rank + d;
+                    const int64_t dim = id >= 0 ? is.dims[id] : 1;
+                    if (dim != 1 && dim != rshape.dims[d]) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "region broadcast");
+                    P.in_strides[k][d] = dim == 1 ? 0 : stride;
+                    if (id < 0 || dim == 1) { if (id >= 0) row = false; }
+                    else if (dim != rshape.dims[d]) row = false;
+                    stride *= dim;
+                }
+                // a row: the input is exactly the region's trailing axes
+                int lead = rshape.rank - is.rank;
+                for (int d = 0; d < is.rank && row; d++)
+                    if (is.dims[d] != rshape.dims[lead + d]) row = false;
+                P.in_kind[k] = row ? IN_ROW : IN_GENERAL;
+                kinds += row ? "R" : "G";
+            }
+        }
+        sig += kinds;
+        next_reg_after_loads = P.n_in;
+        int nreg = P.n_in;
+        int n_insn = P.n_in;
+        bool has_red = false;
+        int red_prim = -1, red_axis = ZPUCUDA_AXIS_NONE;
+        uint64_t red_in = 0, red_out_id = 0;
+        for (int m : member) {
+            const zpucuda_step &st = steps[m];
+            if (region_reduce(st.prim)) {
+                has_red = true;
+                red_prim = st.prim;
+                red_axis = st.axis;
+                red_in = st.ins[0];
+                red_out_id = st.out;
+                continue;
+            }
+            if (nreg >= RP_MAX_REG || n_insn >= RP_MAX_INSN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
+            Insn in{(uint8_t)st.prim, (uint8_t)nreg, (uint8_t)reg[st.ins[0]], (uint8_t)(st.n_inputs > 1 ? reg[st.ins[1]] : 0)};
+            P.insn[n_insn++] = in;
+            char buf[64];
+            if (st.n_inputs > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b);
+            else snprintf(buf, sizeof buf, ";r%d=%s(r%d)", nreg, prim_name(st.prim).c_str(), in.a);
+            sig += buf;
+            reg[st.out] = nreg++;
+        }
+        (void)next_reg_after_loads;
+        P.n_insn = n_insn;
+        // element-wise values needed after this region
+        for (int m : member) {
+            const zpucuda_step &st = steps[m];
+            if (region_reduce(st.prim)) continue;
+            bool needed = out_index.count(st.out) > 0;
+            for (int u : users[st.out])
+                if (std::find(member.begin(), member.end(), u) == member.end()) needed = true;
+            if (needed) {
+                if (P.n_out >= RP_MAX_OUT) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region has too many outputs");
+                P.out_reg[P.n_out++] = reg[st.out];
+                Slot sl = materialise(st.out);
+                if (sl.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+                L.outs.push_back(sl);
+            }
+        }
+        if (has_red) {
+            P.reduce = red_prim == PRIM_SUM ? RED_SUM : red_prim == PRIM_PROD ? RED_PROD
+                     : red_prim == PRIM_MAX_REDUCE ? RED_MAX : RED_MIN;
+            P.reduce_all = red_axis == ZPUCUDA_AXIS_NONE;
+            P.reduce_reg = reg[red_in];
+            P.inner = P.reduce_all ? P.numel : (rshape.rank ? rshape.dims[rshape.rank - 1] : 1);
+            P.outer = P.reduce_all ? 1 : (P.inner ? P.numel / P.inner : 1);
+            if (!P.reduce_all && P.inner == 0) {
+                P.outer = 1;
+                for (int d = 0; d < rshape.rank - 1; d++) P.outer *= rshape.dims[d];
+            }
+            L.has_red = true;
+            L.red = materialise(red_out_id);
+            if (L.red.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            char buf[64];
+            snprintf(buf, sizeof buf, ";out=r%d;red=%s%s", P.reduce_reg,
+                     red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max" : "min",
+                     P.reduce_all ? "" : "_rows");
+            sig += buf;
+            if (P.reduce_all) {
+                void *w = nullptr;
+                if (cudaMalloc(&w, kRegionWorkspaceBytes) != cudaSuccess || cudaMemset(w, 0, kRegionWorkspaceBytes) != cudaSuccess) {
+                    cudaGetLastError();
+                    return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "region workspace");
+                }
+                plan->workspaces.push_back(w);
+                L.workspace = w;
+            }
+        } else {
+            char buf[64];
+            snprintf(buf, sizeof buf, ";out=r%d;red=none", P.n_out == 1 ? P.out_reg[0] : -1);
+            sig += buf;
+        }
+        L.signature = sig;
+        const bool catalogue_shape = ((!has_red && P.n_out == 1) || (has_red && P.reduce == RED_SUM && P.reduce_all && P.n_out == 0)) &&
+                                     kinds.find_first_of("RG") == std::string::npos;
+        L.cat = catalogue_shape ? catalogue_find(sig.c_str()) : nullptr;
+        L.text = "  kernel " + std::to_string(plan->launches.size()) + ": region " +
+                 (L.cat ? std::string("[catalogue ") + L.cat->name + "]" : std::string("[bytecode]")) + " " + sig + "\n";
+        plan->launches.push_back(L);
+        s = member.back() + 1;
+    }
+    char head[160];
+    snprintf(head, sizeof head, "plan: %d steps -> %zu kernels\n", n_steps, plan->launches.size());
+    plan->text = head;
+    for (auto &L : plan->launches) plan->text += L.text;
+    *out = plan;
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *outs, void *stream) {
+    ZC_CHECK(plan && (args || !plan->n_args) && outs, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    cudaStream_t s = resolve_stream(stream);
+    auto ptr = [&](const Slot &sl) -> void * {
+        switch (sl.kind) {
+        case SLOT_ARG: return (void *)args[sl.index];
+        case SLOT_BLOB: return plan->blobs[sl.index];
+        case SLOT_OUT: return outs[sl.index];
+        default: return plan->temps[sl.index];
+        }
+    };
+    for (auto &L : plan->launches) {
+        int st;
+        if (L.kind == Launch::MATMUL) {
+            zpucuda_tensor a = L.ta, b = L.tb, c = L.tc;
+            a.data = ptr(L.ma);
+            b.data = ptr(L.mb);
+            c.data = ptr(L.mc);
+            st = matmul_device(&a, &b, &c, s);
+        } else {
+            RegionIO io;
+            memset(&io, 0, sizeof io);
+            for (size_t k = 0; k < L.ins.size(); k++) io.in[k] = ptr(L.ins[k]);
+            for (size_t o = 0; o < L.outs.size(); o++) io.out[o] = ptr(L.outs[o]);
+            if (L.has_red) io.red_out = ptr(L.red);
+            if (L.workspace) {
+                io.ticket = (unsigned int *)L.workspace;
+                io.partials = (double *)((char *)L.workspace + 256);
+            }
+            st = region_launch(L.prog, L.cat, io, s);
+        }
+        if (st) return st;
+    }
+    return ZPUCUDA_OK;
+}
+
+static size_t value_bytes(const zpucuda_value &v) {
+    size_t n = 1;
+    for (int d = 0; d < v.rank; d++) n *= (size_t)v.dims[d];
+    return n * (v.dtype == ZPUCUDA_F64 ? 8 : 4);
+}
+
+int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs, void *stream) {
+    ZC_CHECK(plan && (host_args || !plan->n_args) && host_outs, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    cudaStream_t s = resolve_stream(stream);
+    if (plan->stage_in.size() != plan->arg_values.size() || plan->stage_out.size() != plan->outputs.size()) {
+        for (auto &v : plan->arg_values) {
+            void *d = nullptr;
+            ZC_CUDA(cudaMalloc(&d, value_bytes(v) ? value_bytes(v) : 16));
+            plan->stage_in.push_back(d);
+        }
+        for (auto &v : plan->outputs) {
+            void *d = nullptr;
+            ZC_CUDA(cudaMalloc(&d, value_bytes(v) ? value_bytes(v) : 16));
+            plan->stage_out.push_back(d);
+        }
+    }
+    for (size_t i = 0; i < plan->arg_values.size(); i++) {
+        const size_t nb = value_bytes(plan->arg_values[i]);
+        if (nb) ZC_CUDA(cudaMemcpyAsync(plan->stage_in[i], host_args[i], nb, cudaMemcpyHostToDevice, s));
+    }
+    int st = zpucuda_plan_run(plan, (const void *const *)plan->stage_in.data(), plan->stage_out.data(), s);
+    if (st) return st;
+    for (size_t i = 0; i < plan->outputs.size(); i++) {
+        const size_t nb = value_bytes(plan->outputs[i]);
+        if (nb) ZC_CUDA(cudaMemcpyAsync(host_outs[i], plan->stage_out[i], nb, cudaMemcpyDeviceToHost, s));
+    }
+    // bounded wait on this stream
+    for (int64_t spins = 0;; spins++) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return ZPUCUDA_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+        if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_plan_run_host: stream did not drain");
+        if (spins > 1000) usleep(10);
+    }
+}
+
+int zpucuda_plan_output(const zpucuda_plan *plan, int i, zpucuda_value *value) {
+    ZC_CHECK(plan && value, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    ZC_CHECK(i >= 0 && i < (int)plan->outputs.size(), ZPUCUDA_ERR_INDEX_OUT_OF_RANGE);
+    *value = plan->outputs[i];
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_plan_num_steps(const zpucuda_plan *plan) { return plan ? plan->n_steps : -1; }
+int zpucuda_plan_num_kernels(const zpucuda_plan *plan) { return plan ? (int)plan->launches.size() : -1; }
+
+int zpucuda_plan_describe(const zpucuda_plan *plan, char *buf, size_t len) {
+    ZC_CHECK(plan && buf && len, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    snprintf(buf, len, "%s", plan->text.c_str());
+    return ZPUCUDA_OK;
+}
+
+void zpucuda_plan_destroy(zpucuda_plan *plan) { delete plan; }
+
+}  // extern "C"

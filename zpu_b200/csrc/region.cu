@@ -1,0 +1,299 @@
+// Region kernels: the catalogue lookup, the grid sizing, and the generic
+// one-pass bytecode kernel that runs any lowered region the build-time
+// catalogue does not cover (still one read of each input, no intermediate
+// HBM traffic, same reduction scheme).
+#include <math.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "region.cuh"
+#include "regions_gen.cuh"
+
+namespace zc {
+
+const CatalogueEntry *catalogue_find(const char *sig) {
+    for (int i = 0; i < kCatalogueSize; i++)
+        if (strcmp(kCatalogue[i].signature, sig) == 0) return &kCatalogue[i];
+    return nullptr;
+}
+
+int fused_grid(const void *kernel, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, int> cache;
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(kernel);
+    if (it != cache.end()) return it->second * num_sms();
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    cache[kernel] = per_sm;
+    return per_sm * num_sms();
+}
+
+// ------------------------------------------------------------ per-op math
+//
+// f32 semantics follow zpu: + - * / are single IEEE f32 operations
+// (kernels.applyBinary, src/zpu/kernels.zig:141-150); transcendental steps
+// are evaluated in f64 and rounded once, which is what zpu's scalar path does
+// (scalar.zig:262-266) and within one rounding of its f32 vector forms.
+
+__device__ __forceinline__ double mod_f64(double a, double b) {
+    if (b == 0.0) return nan("");
+    double r = fmod(a, b);
+    if (r != 0.0 && ((r < 0.0) != (b < 0.0))) r += b;
+    return r;
+}
+
+__device__ double unary_f64(int op, double x) {
+    switch (op) {
+    case 0: return -x;
+    case 1: return fabs(x);
+    case 2: return exp(x);
+    case 3: return expm1(x);
+    case 4: return log(x);
+    case 5: return log1p(x);
+    case 6: return sqrt(x);
+    case 7: return 1.0 / sqrt(x);
+    case 8: return x * x;
+    case 9: return 1.0 / x;
+    case 10: return cbrt(x);
+    case 11: return sin(x);
+    case 12: return cos(x);
+    case 13: return tan(x);
+    case 14: return asin(x);
+    case 15: return acos(x);
+    case 16: return atan(x);
+    case 17: return sinh(x);
+    case 18: return cosh(x);
+    case 19: return tanh(x);
+    case 20: return asinh(x);
+    case 21: return acosh(x);
+    case 22: return atanh(x);
+    case 23: return erf(x);
+    case 24: return 1.0 / (1.0 + exp(-x));
+    case 25: return fmax(x, 0.0) + log1p(exp(-fabs(x)));
+    case 26: return x > 0.0 ? x : 0.0;
+    case 27: return floor(x);
+    case 28: return ceil(x);
+    case 29: return round(x);
+    case 30: return trunc(x);
+    case 31: return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0);
+    default: return nan("");
+    }
+}
+
+__device__ float unary_f32(int op, float x) {
+    switch (op) {
+    case 0: return -x;
+    case 1: return fabsf(x);
+    case 6: return __fsqrt_rn(x);
+    case 7: return __fdiv_rn(1.0f, __fsqrt_rn(x));
+    case 8: return __fmul_rn(x, x);
+    case 9: return __fdiv_rn(1.0f, x);
+    case 24: {  // the f32 vector form 1 / (1 + exp(-x)) (kernels.zig:96)
+        const float e = (float)exp(-(double)x);
+        return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    }
+    case 26: return x > 0.0f ? x : 0.0f;
+    case 27: return floorf(x);
+    case 28: return ceilf(x);
+    case 29: return roundf(x);
+    case 30: return truncf(x);
+    case 31: return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+    default: return (float)unary_f64(op, (double)x);
+    }
+}
+
+__device__ __forceinline__ double binary_f64(int op, double a, double b) {
+    switch (op) {
+    case 35: return a + b;
+    case 36: return a - b;
+    case 37: return a * b;
+    case 38: return a / b;
+    case 39: return pow(a, b);
+    case 40: return isnan(a) ? a : (isnan(b) ? b : (a > b ? a : b));
+    case 41: return isnan(a) ? a : (isnan(b) ? b : (a < b ? a : b));
+    case 42: return atan2(a, b);
+    case 43: return hypot(a, b);
+    case 44: return mod_f64(a, b);
+    default: return nan("");
+    }
+}
+
+__device__ __forceinline__ float binary_f32(int op, float a, float b) {
+    switch (op) {
+    case 35: return __fadd_rn(a, b);
+    case 36: return __fsub_rn(a, b);
+    case 37: return __fmul_rn(a, b);
+    case 38: return __fdiv_rn(a, b);
+    default: return (float)binary_f64(op, (double)a, (double)b);
+    }
+}
+
+template <class T> __device__ __forceinline__ T un(int op, T x);
+template <> __device__ __forceinline__ float un<float>(int op, float x) { return unary_f32(op, x); }
+template <> __device__ __forceinline__ double un<double>(int op, double x) { return unary_f64(op, x); }
+template <class T> __device__ __forceinline__ T bin(int op, T a, T b);
+template <> __device__ __forceinline__ float bin<float>(int op, float a, float b) { return binary_f32(op, a, b); }
+template <> __device__ __forceinline__ double bin<double>(int op, double a, double b) { return binary_f64(op, a, b); }
+
+// ------------------------------------------------------- bytecode kernel
+
+template <class T>
+__device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io, int k, int64_t i) {
+    const T *src = (const T *)io.in[k];
+    switch (p.in_kind[k]) {
+    case IN_FULL: return src[i];
+    case IN_SCALAR: return src[0];
+    case IN_ROW: return src[i % p.in_numel[k]];
+    default: {
+        int64_t rem = i, off = 0;
+        for (int d = p.rank - 1; d >= 0; d--) {
+            const int64_t idx = rem % p.dims[d];
+            rem /= p.dims[d];
+            off += idx * p.in_strides[k][d];
+        }
+        return src[off];
+    }
+    }
+}
+
+template <class T>
+__device__ __forceinline__ void eval(const RegionProgram &p, const RegionIO &io, int64_t i, T *r) {
+    for (int k = 0; k < p.n_insn; k++) {
+        const Insn in = p.insn[k];
+        if (in.op == OPC_LOAD) r[in.dst] = load_in<T>(p, io, in.a, i);
+        else if (in.op < 35) r[in.dst] = un<T>(in.op, r[in.a]);
+        else r[in.dst] = bin<T>(in.op, r[in.a], r[in.b]);
+    }
+}
+
+__device__ __forceinline__ double red_identity(int red) {
+    switch (red) {
+    case RED_PROD: return 1.0;
+    case RED_MAX: return -INFINITY;
+    case RED_MIN: return INFINITY;
+    default: return 0.0;
+    }
+}
+// NaN propagates through max/min, as reduceStep does (src/zpu/ops.zig:688-695).
+__device__ __forceinline__ double red_combine(int red, double acc, double v) {
+    switch (red) {
+    case RED_PROD: return acc * v;
+    case RED_MAX: return isnan(v) || isnan(acc) ? (isnan(acc) ? acc : v) : (v > acc ? v : acc);
+    case RED_MIN: return isnan(v) || isnan(acc) ? (isnan(acc) ? acc : v) : (v < acc ? v : acc);
+    default: return acc + v;
+    }
+}
+__device__ __forceinline__ double warp_reduce(int red, double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = red_combine(red, v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+constexpr int kInterpThreads = 256;
+
+template <class T>
+__device__ __forceinline__ void store_outputs(const RegionProgram &p, const RegionIO &io, int64_t i, const T *r) {
+    for (int o = 0; o < p.n_out; o++) ((T *)io.out[o])[i] = r[p.out_reg[o]];
+}
+
+// MODE 0: element-wise outputs only; 1: plus a full reduction; 2: plus a
+// reduction over the last axis (one warp per row).
+template <class T, int MODE>
+__global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_constant__ RegionProgram p,
+                                                                const __grid_constant__ RegionIO io) {
+    T r[RP_MAX_REG];
+    if (MODE == 0) {
+        for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
+             i += (int64_t)gridDim.x * kInterpThreads) {
+            eval<T>(p, io, i, r);
+            store_outputs<T>(p, io, i, r);
+        }
+    } else if (MODE == 1) {
+        double acc = red_identity(p.reduce);
+        for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
+             i += (int64_t)gridDim.x * kInterpThreads) {
+            eval<T>(p, io, i, r);
+            store_outputs<T>(p, io, i, r);
+            acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
+        }
+        __shared__ double part[kInterpThreads / 32];
+        __shared__ bool last;
+        acc = warp_reduce(p.reduce, acc);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double b = part[0];
+            for (int w = 1; w < kInterpThreads / 32; w++) b = red_combine(p.reduce, b, part[w]);
+            io.partials[blockIdx.x] = b;
+            __threadfence();
+            last = atomicAdd(io.ticket, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (!last || threadIdx.x != 0) return;
+        __threadfence();
+        double v = red_identity(p.reduce);
+        for (unsigned b = 0; b < gridDim.x; b++) v = red_combine(p.reduce, v, __ldcg(io.partials + b));
+        *(T *)io.red_out = (T)v;
+        *io.ticket = 0u;
+    } else {
+        const int lane = threadIdx.x & 31;
+        const int64_t warps = (int64_t)gridDim.x * (kInterpThreads / 32);
+        for (int64_t row = ((int64_t)blockIdx.x * kInterpThreads + threadIdx.x) >> 5; row < p.outer; row += warps) {
+            double acc = red_identity(p.reduce);
+            for (int64_t j = lane; j < p.inner; j += 32) {
+                const int64_t i = row * p.inner + j;
+                eval<T>(p, io, i, r);
+                store_outputs<T>(p, io, i, r);
+                acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
+            }
+            acc = warp_reduce(p.reduce, acc);
+            if (lane == 0) ((T *)io.red_out)[row] = (T)acc;
+        }
+    }
+}
+
+template <class T>
+int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
+    const int sms = num_sms();
+    if (p.reduce == RED_NONE) {
+        if (p.numel == 0) return ZPUCUDA_OK;
+        int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
+        if (g > sms * 8) g = sms * 8;
+        interp_kernel<T, 0><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+    } else if (p.reduce_all) {
+        int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
+        if (g > sms * 8) g = sms * 8;
+        if (g < 1) g = 1;
+        interp_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+    } else {
+        if (p.outer == 0) return ZPUCUDA_OK;
+        int64_t g = (p.outer + (kInterpThreads / 32) - 1) / (kInterpThreads / 32);
+        if (g > sms * 8) g = sms * 8;
+        interp_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+    }
+    ZC_LAUNCHED("region bytecode kernel");
+    return ZPUCUDA_OK;
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+int region_launch(const RegionProgram &p, const CatalogueEntry *cat, const RegionIO &io, cudaStream_t s) {
+    if (cat && p.dtype == ZPUCUDA_F32) {
+        bool ok = true;
+        for (int k = 0; k < p.n_in; k++)
+            if (p.in_kind[k] == IN_FULL && !aligned16(io.in[k])) ok = false;
+        for (int o = 0; o < p.n_out; o++)
+            if (!aligned16(io.out[o])) ok = false;
+        if (ok) return cat->launch(p, io, s);
+    }
+    if (p.dtype == ZPUCUDA_F32) return launch_interp<float>(p, io, s);
+    return launch_interp<double>(p, io, s);
+}
+
+}  // namespace zc
