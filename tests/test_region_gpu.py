@@ -95,6 +95,42 @@ def test_chain_tanh_ulp_full_size(zc):
     assert d.max() <= 4, d.max()
 
 
+def test_catalogue_tanh_every_float(zc):
+    """The catalogued kernels' own tanh over EVERY f32 in [FLT_MIN, 10] and
+    its negatives' sign rule: at most 1 ulp from (f32)tanh((f64)x) (the f64
+    reference is torch's device tanh, rounded once)."""
+    lo, hi = np.float32(np.finfo(np.float32).tiny).view(np.int32), np.float32(10.0).view(np.int32)
+    p = None
+    worst = 0
+    chunk = 1 << 27
+    for start in range(int(lo), int(hi), chunk):
+        bits = torch.arange(start, min(start + chunk, int(hi)), dtype=torch.int32, device="cuda")
+        x = bits.view(torch.float32)
+        if p is None or p.outputs[0][1][0] != x.numel():
+            p = zc.Plan([(1, zc.F32, (x.numel(),))], [], [("tanh", [1], 10, -2, 0)], [10])
+            assert "catalogue tanh]" in p.describe()
+        (t,) = p.run([x])
+        want = torch.tanh(x.double()).float()
+        d = (t.view(torch.int32).long() - want.view(torch.int32).long()).abs().max().item()
+        worst = max(worst, d)
+        (tn,) = p.run([-x])
+        assert torch.equal(tn, -t)
+    assert worst <= 1, worst
+
+
+def test_catalogue_tanh_special_values(zc):
+    x = np.array([0.0, -0.0, 1e-30, 1e-45, 0.89999, 0.9, 0.90001, 3.0, 9.0, 9.1, 9.2, 20.0, 1e30, np.inf,
+                  -np.inf, np.nan], dtype=np.float32)
+    p = zc.Plan([(1, zc.F32, (x.size,))], [], [("tanh", [1], 10, -2, 0)], [10])
+    (t,) = p.run([torch.from_numpy(x).cuda()])
+    t = t.cpu().numpy()
+    assert np.isnan(t[-1])
+    assert t[-3] == 1.0 and t[-2] == -1.0 and t[-4] == 1.0
+    assert np.signbit(t[1]) and t[1] == 0.0
+    want = np.tanh(x[:-1].astype(np.float64)).astype(np.float32)
+    assert ulp_diff_f32(t[:-1], want).max() <= 1
+
+
 @pytest.mark.parametrize("n", [0, 1, 7, 1000, (1 << 20) + 3, N_FULL])
 def test_chain_fused_sum(zc, n):
     x_d = zc.rng_normal(SEED_X, n) if n else torch.empty(0, device="cuda")

@@ -538,6 +538,7 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
             if (L.has_red) io.red_out = ptr(L.red);
             if (L.workspace) {
                 io.ticket = (unsigned int *)L.workspace;
+                io.error = (unsigned int *)L.workspace + 1;
                 io.partials = (double *)((char *)L.workspace + 256);
             }
             st = region_launch(L.prog, L.cat, io, s);

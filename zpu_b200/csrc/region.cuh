@@ -1,14 +1,14 @@
 // Fused element-wise + reduction regions: the program format shared by the
 // jit-plan lowering (plan.cu) and the kernels (region.cu), and the templated
-// straight-line kernel that gen_regions.py instantiates per catalogued region.
+// straight-line kernels that gen_regions.py instantiates per catalogued region.
 //
 // What a region computes is fixed by zpu's step semantics: every element-wise
 // step rounds to the element type on its own (src/zpu/ops.zig:297-345,
 // scalar.zig:262-302), a full `sum` reduces everything (ops.zig:820-869).
 // What changes is where it runs: one kernel per region, every element read
 // once from HBM with 128-bit loads, intermediates kept in registers, the sum
-// accumulated in f64 per thread and per block, and the blocks combined by the
-// last block to finish (no spin-waits, deterministic order).
+// accumulated per thread and per block in f64, and the blocks combined by the
+// last block to finish (no spin-waits between blocks, deterministic order).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -61,9 +61,11 @@ struct RegionIO {
     void *red_out;          // reduced output (numel/inner values, or 1)
     double *partials;       // one per block (full reductions)
     unsigned int *ticket;   // zero between launches
+    unsigned int *error;    // set (never cleared by a kernel) when a bounded wait runs out
 };
 
-// Scratch a full reduction needs: a ticket word plus one double per block.
+// Scratch a full reduction needs: a ticket word, an error word, one double
+// per block.
 constexpr int kMaxRegionBlocks = 148 * 16;
 constexpr size_t kRegionWorkspaceBytes = 256 + sizeof(double) * kMaxRegionBlocks;
 
@@ -74,10 +76,125 @@ struct CatalogueEntry {
     FusedLaunch launch;
 };
 
-// The f32 tanh the fused kernels use: CUDA's tanhf, whose documented error
-// bound (2 ulp) keeps a catalogued region within 2 ulp of zpu's
-// f64-then-round tanh plus the latter's half ulp.
-__device__ __forceinline__ float zc_tanhf(float x) { return tanhf(x); }
+// ------------------------------------------------------ packed f32 pairs
+//
+// sm_100 executes f32x2 add / sub / mul / fma as one instruction on a
+// 64-bit register pair, each lane an ordinary IEEE round-to-nearest f32
+// operation: the same bits as two scalar __fadd_rn / __fmul_rn / fmaf, at
+// half the issue slots.  Catalogued regions evaluate two elements at a time.
+typedef unsigned long long f2_t;
+__device__ __forceinline__ f2_t pk2(float a, float b) {
+    f2_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(f2_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ f2_t add2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2_t sub2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
+    f2_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
+    f2_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f2_t splat2(float a) { return pk2(a, a); }
+
+// ------------------------------------------------------------------ tanh
+//
+// The f32 tanh of the catalogued regions, written for this library (zpu
+// computes tanh in f64 and rounds, src/zpu/scalar.zig:199,262-266):
+//   |x| <  0.9:  tanh(x) = x + x z P(z), z = x^2, P a degree-5 minimax
+//                polynomial for (tanh(x)/x - 1)/z on [0, 0.9] (0.27 ulp;
+//                coefficients from fit_tanh.py: Lawson-weighted least squares
+//                on the relative error, f32-rounded coefficients);
+//   |x| >= 0.9:  tanh(x) = 1 - 2 / (1 + e^(2|x|)), e^(2|x|) = 2^(2 log2(e) |x|)
+//                and 1/(1 + e) from the SFU (ex2.approx, rcp.approx).  There
+//                the quotient is <= 0.29, so the SFU's ~2^-22 relative errors
+//                move the result by under one ulp; ex2 overflows to inf for
+//                huge |x| and the result is exactly 1.
+// Both branches run and a select picks one (no divergence); NaN fails the
+// `< 0.9` test and propagates through ex2.  Measured exhaustively on the B200
+// over every f32 in [FLT_MIN, 10] against (float)tanh((double)x): max 1 ulp.
+// This form keeps the FMA pipe light; its limit is the SFU (two ops per
+// element).  A polynomial exponential (one SFU op) or a polynomial for
+// 2/(1 + e^-2x) trades that for more issue slots than it saves: both measured
+// slower on the B200.
+#define ZC_TANH_P0 -3.333321214e-01f
+#define ZC_TANH_P1 1.333034933e-01f
+#define ZC_TANH_P2 -5.372043326e-02f
+#define ZC_TANH_P3 2.090060711e-02f
+#define ZC_TANH_P4 -6.855268497e-03f
+#define ZC_TANH_P5 1.301668934e-03f
+#define ZC_TANH_SPLIT 0.9f
+#define ZC_TWO_LOG2E 2.8853900817779268f
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// tanh of a value known to be >= 0 or NaN (e.g. a square).
+__device__ __forceinline__ float zc_tanh_nonneg(float ax) {
+    const float z = __fmul_rn(ax, ax);
+    float p = fmaf(ZC_TANH_P5, z, ZC_TANH_P4);
+    p = fmaf(p, z, ZC_TANH_P3);
+    p = fmaf(p, z, ZC_TANH_P2);
+    p = fmaf(p, z, ZC_TANH_P1);
+    p = fmaf(p, z, ZC_TANH_P0);
+    const float small = fmaf(__fmul_rn(ax, z), p, ax);
+    const float e = ex2_approx(__fmul_rn(ax, ZC_TWO_LOG2E));
+    const float large = fmaf(-2.0f, rcp_approx(__fadd_rn(e, 1.0f)), 1.0f);
+    return ax < ZC_TANH_SPLIT ? small : large;
+}
+__device__ __forceinline__ float zc_tanhf(float x) { return copysignf(zc_tanh_nonneg(fabsf(x)), x); }
+
+// The same computation on a pair; every lane gives the scalar version's bits.
+__device__ __forceinline__ f2_t zc_tanh_nonneg2(f2_t ax) {
+    const f2_t z = mul2(ax, ax);
+    f2_t p = fma2(splat2(ZC_TANH_P5), z, splat2(ZC_TANH_P4));
+    p = fma2(p, z, splat2(ZC_TANH_P3));
+    p = fma2(p, z, splat2(ZC_TANH_P2));
+    p = fma2(p, z, splat2(ZC_TANH_P1));
+    p = fma2(p, z, splat2(ZC_TANH_P0));
+    const f2_t small = fma2(mul2(ax, z), p, ax);
+    float g0, g1;
+    upk2(mul2(ax, splat2(ZC_TWO_LOG2E)), g0, g1);
+    float d0, d1;
+    upk2(add2(pk2(ex2_approx(g0), ex2_approx(g1)), splat2(1.0f)), d0, d1);
+    const f2_t large = fma2(splat2(-2.0f), pk2(rcp_approx(d0), rcp_approx(d1)), splat2(1.0f));
+    float a0, a1, s0, s1, l0, l1;
+    upk2(ax, a0, a1);
+    upk2(small, s0, s1);
+    upk2(large, l0, l1);
+    return pk2(a0 < ZC_TANH_SPLIT ? s0 : l0, a1 < ZC_TANH_SPLIT ? s1 : l1);
+}
+__device__ __forceinline__ f2_t zc_tanh2(f2_t x) {
+    float x0, x1;
+    upk2(x, x0, x1);
+    float t0, t1;
+    upk2(zc_tanh_nonneg2(pk2(fabsf(x0), fabsf(x1))), t0, t1);
+    return pk2(copysignf(t0, x0), copysignf(t1, x1));
+}
 
 // ---------------------------------------------------------------- reduction
 
@@ -129,62 +246,100 @@ __device__ __forceinline__ void finish_full_sum(double block_total, const Region
 
 // ------------------------------------------------- catalogued f32 regions
 //
-// F::call(v) is the region's straight-line code on one element; v holds the
-// region's inputs (full tensors element i, scalars their single value).
+// F::call(v) / F::call2(v) are the region's straight-line code on one element
+// / one pair of elements; v holds the region's inputs (full tensors: the
+// element(s); scalars: their single value).
 
 constexpr int kFusedThreads = 256;
-constexpr int kFusedUnroll = 4;  // 16-byte loads in flight per thread per input
+constexpr int kFusedUnroll = 8;  // 16-byte loads in flight per thread per input
 
+// Evaluates F on one float4 group: two packed lane pairs (f32x2).
+template <class F>
+__device__ __forceinline__ void eval_group(const float4 (&v)[F::NIN > 0 ? F::NIN : 1],
+                                           const f2_t (&sv2)[F::NIN > 0 ? F::NIN : 1], f2_t &y01, f2_t &y23) {
+    constexpr int NIN = F::NIN > 0 ? F::NIN : 1;
+    f2_t lo[NIN], hi[NIN];
+#pragma unroll
+    for (int k = 0; k < F::NIN; k++) {
+        if (F::SCALARS & (1u << k)) {
+            lo[k] = sv2[k];
+            hi[k] = sv2[k];
+        } else {
+            lo[k] = pk2(v[k].x, v[k].y);
+            hi[k] = pk2(v[k].z, v[k].w);
+        }
+    }
+    y01 = F::call2(lo);
+    y23 = F::call2(hi);
+}
+
+// Register-loop kernel: each thread keeps kFusedUnroll 16-byte loads per
+// input in flight, evaluates them, and stores (element-wise) or sums them (a
+// full sum: the 32 values of one iteration in f32 pairs, then one f64 add).
 template <class F, bool SUM>
 __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_constant__ RegionIO io, int64_t n) {
-    constexpr int NIN = F::NIN;
-    float sv[NIN > 0 ? NIN : 1];
+    constexpr int NIN = F::NIN > 0 ? F::NIN : 1;
+    float sv[NIN];
+    f2_t sv2[NIN];
+    const float4 *src[NIN];
 #pragma unroll
-    for (int k = 0; k < NIN; k++)
-        if (F::SCALARS & (1u << k)) sv[k] = __ldg((const float *)io.in[k]);
-
+    for (int k = 0; k < F::NIN; k++) {
+        src[k] = (const float4 *)io.in[k];
+        sv[k] = (F::SCALARS & (1u << k)) ? __ldg((const float *)io.in[k]) : 0.0f;
+        sv2[k] = splat2(sv[k]);
+    }
+    float4 *dst = (float4 *)io.out[0];
     const int64_t n4 = n >> 2;
     const int64_t G = (int64_t)gridDim.x * kFusedThreads;
     double acc = 0.0;
-    for (int64_t base = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x; base < n4; base += kFusedUnroll * G) {
-        float4 v[kFusedUnroll][NIN > 0 ? NIN : 1];
+    int64_t base = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
+    for (; base + (kFusedUnroll - 1) * G < n4; base += kFusedUnroll * G) {
+        float4 v[kFusedUnroll][NIN];
+#pragma unroll
+        for (int u = 0; u < kFusedUnroll; u++)
+#pragma unroll
+            for (int k = 0; k < F::NIN; k++)
+                if (!(F::SCALARS & (1u << k))) v[u][k] = __ldcs(src[k] + base + u * G);
+        f2_t s = 0ull;
 #pragma unroll
         for (int u = 0; u < kFusedUnroll; u++) {
-            const int64_t q = base + u * G;
-#pragma unroll
-            for (int k = 0; k < NIN; k++)
-                if (!(F::SCALARS & (1u << k)))
-                    v[u][k] = q < n4 ? __ldcs((const float4 *)io.in[k] + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < kFusedUnroll; u++) {
-            const int64_t q = base + u * G;
-            if (q >= n4) break;
-            float y[4];
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-                float e[NIN > 0 ? NIN : 1];
-#pragma unroll
-                for (int k = 0; k < NIN; k++) {
-                    if (F::SCALARS & (1u << k)) e[k] = sv[k];
-                    else e[k] = l == 0 ? v[u][k].x : l == 1 ? v[u][k].y : l == 2 ? v[u][k].z : v[u][k].w;
-                }
-                y[l] = F::call(e);
-            }
+            f2_t y01, y23;
+            eval_group<F>(v[u], sv2, y01, y23);
             if (SUM) {
-                acc += (double)((y[0] + y[1]) + (y[2] + y[3]));
+                s = u ? add2(s, add2(y01, y23)) : add2(y01, y23);
             } else {
-                __stcs((float4 *)io.out[0] + q, make_float4(y[0], y[1], y[2], y[3]));
+                float4 o;
+                upk2(y01, o.x, o.y);
+                upk2(y23, o.z, o.w);
+                __stcs(dst + base + u * G, o);
             }
         }
+        if (SUM) {
+            float s0, s1;
+            upk2(s, s0, s1);
+            acc += (double)(s0 + s1);
+        }
+    }
+    for (; base < n4; base += G) {
+        float4 v[NIN];
+#pragma unroll
+        for (int k = 0; k < F::NIN; k++)
+            if (!(F::SCALARS & (1u << k))) v[k] = __ldcs(src[k] + base);
+        f2_t y01, y23;
+        eval_group<F>(v, sv2, y01, y23);
+        float s0, s1, s2, s3;
+        upk2(y01, s0, s1);
+        upk2(y23, s2, s3);
+        if (SUM) acc += (double)((s0 + s1) + (s2 + s3));
+        else __stcs(dst + base, make_float4(s0, s1, s2, s3));
     }
     // the n % 4 leftover elements
     const int64_t t = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
     if (t < (n & 3)) {
         const int64_t i = (n4 << 2) + t;
-        float e[NIN > 0 ? NIN : 1];
+        float e[NIN];
 #pragma unroll
-        for (int k = 0; k < NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : ((const float *)io.in[k])[i];
+        for (int k = 0; k < F::NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : ((const float *)io.in[k])[i];
         const float y = F::call(e);
         if (SUM) acc += (double)y;
         else ((float *)io.out[0])[i] = y;
@@ -195,14 +350,194 @@ __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_c
     }
 }
 
-// Grid of the fused kernels: every SM full, one wave (grid-stride loop).
-int fused_grid(const void *kernel, int threads, size_t smem);
+// --------------------------------------- full reductions: bulk-copy pipeline
+//
+// For an HBM-bound full sum the memory side runs as a bulk-async-copy
+// pipeline: one thread per block streams tiles of every full input into
+// kBulkStages shared-memory stages with cp.async.bulk (completion counted on
+// an mbarrier per stage) while all threads evaluate the region out of shared
+// memory.  Tiles go to blocks round-robin, so the grid reads one contiguous
+// stretch of HBM at a time.  Every wait is bounded: a wait that runs out sets
+// the error word, turns the result into NaN and drains the copies still in
+// flight (again bounded) before the block leaves.
 
-template <class F, bool SUM>
+constexpr int kBulkTile = 4096;  // elements per tile per input (16 KiB)
+constexpr int kBulkStages = 4;
+constexpr int kBulkThreads = 256;
+constexpr int kBulkPer = kBulkTile / 4 / kBulkThreads;  // float4 per thread per tile
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on one phase of a stage barrier.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpinLimit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <class F>
+struct FullInputs {
+    static constexpr int count() {
+        int c = 0;
+        for (int k = 0; k < F::NIN; k++)
+            if (!(F::SCALARS & (1u << k))) c++;
+        return c;
+    }
+    static constexpr int N = count() > 0 ? count() : 1;
+};
+
+template <class F>
+__global__ void __launch_bounds__(kBulkThreads) fused_sum_bulk_kernel(const __grid_constant__ RegionIO io, int64_t n) {
+    constexpr int NIN = F::NIN > 0 ? F::NIN : 1;
+    constexpr int NF = FullInputs<F>::N;
+    extern __shared__ __align__(128) float tiles[];  // [kBulkStages][NF][kBulkTile]
+    __shared__ __align__(8) uint64_t full[kBulkStages];
+    __shared__ int failed;
+
+    float sv[NIN];
+    f2_t sv2[NIN];
+    const float *src[NF];
+    {
+        int j = 0;
+#pragma unroll
+        for (int k = 0; k < F::NIN; k++) {
+            sv[k] = 0.0f;
+            if (F::SCALARS & (1u << k)) sv[k] = __ldg((const float *)io.in[k]);
+            else src[j++] = (const float *)io.in[k];
+            sv2[k] = splat2(sv[k]);
+        }
+    }
+
+    const int64_t ntiles = n / kBulkTile;
+    const int64_t mine = ntiles > (int64_t)blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBulkStages; s++) mbar_init(&full[s], 1);
+        failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // thread 0: tile j of this block into stage j % kBulkStages
+    auto issue = [&](int64_t j) {
+        const int s = (int)(j % kBulkStages);
+        const int64_t tile = (int64_t)blockIdx.x + j * gridDim.x;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&full[s], (uint32_t)(NF * kBulkTile * sizeof(float)));
+#pragma unroll
+        for (int f = 0; f < NF; f++)
+            bulk_g2s(tiles + ((size_t)s * NF + f) * kBulkTile, src[f] + tile * kBulkTile,
+                     (uint32_t)(kBulkTile * sizeof(float)), &full[s]);
+    };
+    if (threadIdx.x == 0)
+        for (int64_t j = 0; j < mine && j < kBulkStages; j++) issue(j);
+
+    double acc = 0.0;
+    int64_t j = 0;
+    for (; j < mine; j++) {
+        const int s = (int)(j % kBulkStages);
+        const uint32_t parity = (uint32_t)((j / kBulkStages) & 1);
+        if (!mbar_wait(&full[s], parity)) failed = 1;
+        __syncthreads();
+        if (failed) break;
+        f2_t part[kBulkPer];
+#pragma unroll
+        for (int c = 0; c < kBulkPer; c++) {
+            const int e4 = c * kBulkThreads + threadIdx.x;  // float4 index within the tile
+            float4 v[NIN];
+            int fi = 0;
+#pragma unroll
+            for (int k = 0; k < F::NIN; k++)
+                if (!(F::SCALARS & (1u << k)))
+                    v[k] = reinterpret_cast<const float4 *>(tiles + ((size_t)s * NF + fi++) * kBulkTile)[e4];
+            f2_t y01, y23;
+            eval_group<F>(v, sv2, y01, y23);
+            part[c] = add2(y01, y23);
+        }
+#pragma unroll
+        for (int w = kBulkPer / 2; w >= 1; w >>= 1)
+#pragma unroll
+            for (int c = 0; c < w; c++) part[c] = add2(part[c], part[c + w]);
+        float s0, s1;
+        upk2(part[0], s0, s1);
+        acc += (double)(s0 + s1);
+        __syncthreads();  // stage s fully read: it may be refilled
+        if (threadIdx.x == 0 && j + kBulkStages < mine) issue(j + kBulkStages);
+    }
+    if (failed) {
+        // drain the copies this block still has in flight (bounded), then
+        // report: the error word, and NaN through this block's partial
+        if (threadIdx.x == 0) {
+            for (int64_t q = j + 1; q < mine && q < j + kBulkStages; q++)
+                mbar_wait(&full[q % kBulkStages], (uint32_t)((q / kBulkStages) & 1));
+            if (io.error) atomicOr(io.error, 1u);
+        }
+        acc = __int_as_float(0x7fc00000);
+    }
+    // the elements past the last full tile, grid-strided
+    for (int64_t i = ntiles * kBulkTile + (int64_t)blockIdx.x * kBulkThreads + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * kBulkThreads) {
+        float e[NIN];
+        int fi = 0;
+#pragma unroll
+        for (int k = 0; k < F::NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : src[fi++][i];
+        acc += (double)F::call(e);
+    }
+    const double b = block_sum<kBulkThreads>(acc);
+    finish_full_sum<kBulkThreads>(b, io, false);
+}
+
+// Grid of the fused kernels: a fixed number of blocks per SM (grid-stride
+// loop); ZPUCUDA_REGION_BPS / ZPUCUDA_REGION_BULK_BPS override the defaults
+// for tuning sweeps.
+int fused_blocks_per_sm();
+int bulk_blocks_per_sm();
+
+// SUM: the region ends in a full sum.  BULK (full sums only): stream through
+// the bulk-copy pipeline -- the generator picks it for regions with no
+// transcendental step, which are HBM-bound; regions with SFU work keep the
+// register loop, whose higher occupancy feeds the SFU better (measured).
+template <class F, bool SUM, bool BULK>
 int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
+    if (SUM && BULK) {
+        auto k = fused_sum_bulk_kernel<F>;
+        const size_t smem = (size_t)kBulkStages * FullInputs<F>::N * kBulkTile * sizeof(float);
+        static bool attr = false;
+        if (!attr) {
+            ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr = true;
+        }
+        int per_sm = bulk_blocks_per_sm();
+        const int fit = (int)((220u * 1024u) / (smem + 1024));
+        if (per_sm > fit) per_sm = fit < 1 ? 1 : fit;
+        int grid = num_sms() * per_sm;
+        if (grid > kMaxRegionBlocks) grid = kMaxRegionBlocks;
+        k<<<grid, kBulkThreads, smem, s>>>(io, p.numel);
+        ZC_LAUNCHED("fused region kernel (bulk pipeline)");
+        return ZPUCUDA_OK;
+    }
     auto k = fused_f32_kernel<F, SUM>;
-    int grid = fused_grid((const void *)k, kFusedThreads, 0);
-    if (SUM && grid > kMaxRegionBlocks) grid = kMaxRegionBlocks;
+    int grid = num_sms() * fused_blocks_per_sm();
+    if (grid > kMaxRegionBlocks) grid = kMaxRegionBlocks;
     k<<<grid, kFusedThreads, 0, s>>>(io, p.numel);
     ZC_LAUNCHED("fused region kernel");
     return ZPUCUDA_OK;
