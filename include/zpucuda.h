@@ -217,6 +217,28 @@ int zpucuda_rng_uniform(uint64_t seed, int dtype, void *d_out, int64_t n, double
 int zpucuda_rng_normal(uint64_t seed, int dtype, void *d_out, int64_t n, void *stream);
 int zpucuda_rng_randint(uint64_t seed, int64_t *d_out, int64_t n, int64_t lo, int64_t hi, void *stream);
 
+/* ------------------------------------------------- allocation-free variant */
+/* No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory -- an application embedding this library inside a
+ * framework whose caching allocator owns the device (a side cudaMalloc would
+ * escape its accounting and limits), or a latency-critical loop where
+ * cudaMalloc's implicit synchronisation is not allowed.
+ * *d_out = sumAll(tanh(x*x) * a + b) over the n f32 elements at d_x (16-byte
+ * aligned), a = *d_a, b = *d_b (device scalars): the same fused kernel and
+ * result as the plan of that jit chain, but its reduction scratch lives in a
+ * static 16.25 KiB device array inside the library (held by every GPU that
+ * loads it until exit), so the call allocates nothing.
+ *  - The first call on a device looks the array's address up
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - Every call shares the one array: calls that overlap on the GPU (other
+ *    streams, other threads) race and corrupt each other's result; order
+ *    them on one stream.  Each call zeroes the counters it needs.
+ *  - Launches whose grid needs more block partials than the array holds
+ *    (2048) are rejected with ZPUCUDA_ERR_NOT_SUPPORTED and a message. */
+int zpucuda_chain_tanh_sq_affine_sum_noalloc(const float *d_x, int64_t n, const float *d_a, const float *d_b,
+                                             float *d_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,6 +102,7 @@ SIGNATURES = {
     "zpucuda_rng_uniform": (I32, [U64, I32, P, I64, C.c_double, C.c_double, P]),
     "zpucuda_rng_normal": (I32, [U64, I32, P, I64, P]),
     "zpucuda_rng_randint": (I32, [U64, P, I64, I64, I64, P]),
+    "zpucuda_chain_tanh_sq_affine_sum_noalloc": (I32, [P, I64, P, P, P, P]),
 }
 
 
