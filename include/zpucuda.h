@@ -79,6 +79,10 @@ int zpucuda_set_stream(void *stream);
 int zpucuda_sync(int64_t timeout_ms);
 /* Number of kernels this library has launched from the calling process. */
 uint64_t zpucuda_launch_count(void);
+/* Reads the device error word the kernels' bounded waits set when they run
+ * out (synchronous): ZPUCUDA_ERR_TIMEOUT if any did, else ZPUCUDA_OK.  The
+ * word is sticky for the process. */
+int zpucuda_check_device(void);
 
 /* --------------------------------------------------------------- buffers */
 /* Refcounted HBM storage: the device counterpart of zpu's Buffer

@@ -1,0 +1,106 @@
+"""f32 GEMM (tcgen05 3xTF32) and ops.matmul on the B200 against the oracle.
+
+Tolerance: relative Frobenius error <= 1e-5 against zpu's f32 FMA-chain
+gemm (the north star's bound for f32).
+"""
+import numpy as np
+import pytest
+
+from oracle import zpu_oracle as zo
+from tests.helpers import rel_fro
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def zc():
+    import zpu_b200
+    zpu_b200.check(zpu_b200.lib().zpucuda_init(0))
+    return zpu_b200
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def check_no_device_error(zc):
+    torch.cuda.synchronize()
+    zc.check(zc.lib().zpucuda_check_device())
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("m,k,n", [(128, 32, 128), (256, 64, 256), (129, 100, 136), (300, 516, 260),
+                                   (1, 8, 4), (513, 33, 1000)])
+def test_layouts_and_edges(zc, ta, tb, m, k, n):
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    want = zo.gemm(a, b)
+    A = dev(a.T.copy()) if ta else dev(a)
+    B = dev(b.T.copy()) if tb else dev(b)
+    got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+    check_no_device_error(zc)
+    assert rel_fro(got, want) <= TOL, (m, k, n, ta, tb, rel_fro(got, want))
+
+
+def test_kernel_test_shapes_take_the_fma_path(zc, golden):
+    """kernels.zig:512-543 shapes (odd pitches run the FMA-chain kernel)."""
+    for m, k, n in golden["gemm_shapes"]:
+        a = ((np.arange(m * k) % 7) * 0.5 - 1.0).astype(np.float32).reshape(m, k)
+        b = ((np.arange(k * n) % 5) * 0.25 - 0.5).astype(np.float32).reshape(k, n)
+        got = zc.gemm(dev(a), dev(b)).cpu().numpy()
+        assert rel_fro(got, zo.gemm(a, b)) <= TOL
+
+
+def test_config1_1024_cubed(zc):
+    """zpu.matmul f32 1024^3, A, B ~ U[-1, 1] (seeds 0x5EED0001/2)."""
+    n = 1024
+    A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
+    B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
+    got = zc.matmul(A, B).cpu().numpy()
+    check_no_device_error(zc)
+    want = zo.gemm(A.cpu().numpy(), B.cpu().numpy())
+    assert rel_fro(got, want) <= TOL
+
+
+def test_config3_vmap_batched(zc):
+    """vmap-batched 512^3 products, N(0, 1/512) inputs, checked on 4 of them
+    (here 16 matrices in the batch; the full 256 runs in bench)."""
+    bsz, n = 16, 512
+    s = 1.0 / np.sqrt(512.0)
+    A = (zc.rng_normal(0x5EED0004, bsz * n * n) * s).view(bsz, n, n)
+    B = (zc.rng_normal(0x5EED0005, bsz * n * n) * s).view(bsz, n, n)
+    got = zc.matmul(A, B, a_depth=1, b_depth=1).cpu().numpy()
+    check_no_device_error(zc)
+    a, b = A.cpu().numpy(), B.cpu().numpy()
+    for i in (0, 5, 10, 15):
+        assert rel_fro(got[i], zo.gemm(a[i], b[i])) <= TOL
+
+
+def test_batch_broadcast_and_transposed_views(zc):
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((6, 64, 96)).astype(np.float32)
+    w = rng.standard_normal((96, 128)).astype(np.float32)
+    got = zc.matmul(dev(a), dev(w)).cpu().numpy()
+    assert rel_fro(got, zo.matmul(a, w)) <= TOL
+    # the matmul VJP's a^T g and g w^T, read in place
+    x = rng.standard_normal((256, 96)).astype(np.float32)
+    g = rng.standard_normal((256, 128)).astype(np.float32)
+    X, G, W = dev(x), dev(g), dev(w)
+    got = zc.matmul(X.transpose(0, 1), G).cpu().numpy()
+    assert rel_fro(got, zo.gemm(x.T.copy(), g)) <= TOL
+    got = zc.matmul(G, W.transpose(0, 1)).cpu().numpy()
+    assert rel_fro(got, zo.gemm(g, w.T.copy())) <= TOL
+    check_no_device_error(zc)
+
+
+def test_empty_contraction_writes_zeros(zc):
+    a = torch.zeros((4, 0), dtype=torch.float32, device="cuda")
+    b = torch.zeros((0, 3), dtype=torch.float32, device="cuda")
+    c = torch.full((4, 3), 7.0, dtype=torch.float32, device="cuda")
+    zc.gemm(a, b, out=c)
+    assert float(c.abs().sum()) == 0.0

@@ -76,6 +76,7 @@ SIGNATURES = {
     "zpucuda_set_stream": (I32, [P]),
     "zpucuda_sync": (I32, [I64]),
     "zpucuda_launch_count": (U64, []),
+    "zpucuda_check_device": (I32, []),
     "zpucuda_buf_alloc": (I32, [S, C.POINTER(P)]),
     "zpucuda_buf_alloc_zeroed": (I32, [S, C.POINTER(P)]),
     "zpucuda_buf_wrap": (I32, [P, S, C.POINTER(P)]),

@@ -1,7 +1,495 @@
+// f32 GEMM for sm_100a: tcgen05 tensor cores with a 3xTF32 split.
+//
+// Replaces kernels.gemm / ops.gemmTyped for f32 (src/zpu/kernels.zig:339-408,
+// src/zpu/ops.zig:1016-1049) and ops.gemmBatched (ops.zig:1226-1282).
+// zpu computes each element as an f32 FMA chain; TF32 keeps 10 mantissa
+// bits, so every operand is split x = hi + lo with hi, lo exact TF32 values
+// and C = A_hi B_hi + A_hi B_lo + A_lo B_hi (the lo*lo term is below f32
+// resolution): three tensor-core MMAs per K step.
+//
+// The tensor core's own f32 accumulation drifts with the number of MMAs it
+// chains (measured: relative error growing linearly with K, 3e-5 at
+// K = 4096), so the K loop is cut into chunks of KC_BLOCKS * 32: each chunk
+// accumulates in one of two TMEM buffers, and epilogue warps fold finished
+// chunks into registers with round-to-nearest f32 adds while the tensor core
+// fills the other buffer.
+//
+// One CTA computes a 128 x 128 tile with 16 warps in fixed roles:
+//   warp 0      TMA producer: 3-D tensor maps (inner, rows, matrix) stream
+//               32-wide K slices of A and B into STAGES shared-memory stages
+//               (out-of-range rows/columns read as zero);
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma (kind::tf32) and
+//               the tcgen05.commits;
+//   warps 2-7   split each landed stage: hi = x with the low 13 mantissa bits
+//               cleared (in place), lo = round-to-nearest TF32 of x - hi into
+//               the stage's lo buffer at the same (swizzled) position, so hi
+//               and lo tiles share their descriptors;
+//   warps 8-15  fold each finished chunk (tcgen05.ld 32x32b) into registers,
+//               then store the tile; warp w reads TMEM lanes 32 (w % 4) ..
+//               +31 and columns 64 ((w - 8) / 4) .. +63.
+// K-major operands use the 128-byte swizzle; MN-major ones (the matmul VJP's
+// swapLastTwo views, read in place) use the 128-byte swizzle with 32-byte
+// atoms, the only shared-memory layout tcgen05 takes for MN-major TF32.
+// Every mbarrier wait is bounded: a wait that runs out sets an error word
+// (zpucuda_check_device) and its warp stops; TMEM is freed before exit.
+//
+// Shapes the tensor maps cannot describe (row pitch not a multiple of 4
+// elements, base not 16-byte aligned, batch offsets that are not whole
+// matrices) run a plain FMA-chain kernel instead.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <string.h>
+
+#include <mutex>
+
 #include "gemm.cuh"
+
 namespace zc {
-int gemm_f32_device(const float *, const float *, float *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                    bool, bool, const GemmBatch &, int64_t, cudaStream_t) {
-    return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "f32 gemm kernel not built yet");
+
+static __device__ unsigned int g_gemm_error;
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, THREADS = 512;
+constexpr int KC_BLOCKS = 4;  // K-slices per accumulation chunk (K = 128)
+constexpr int NCONV = 192;    // converter threads (warps 2-7)
+constexpr int NEPI = 256;     // epilogue threads (warps 8-15)
+constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;  // 16 KiB each
+constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);          // hi + lo of A and B
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t kGemmSpin = 1u << 24;
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mb_init(uint64_t *b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
 }
+__device__ __forceinline__ void mb_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity) {
+    for (uint32_t i = 0; i < kGemmSpin; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(su32(b)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    atomicOr(&g_gemm_error, 1u);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100, version 1).  layout: 2 = 128-byte
+// swizzle, 1 = 128-byte swizzle with 32-byte atoms.
+__device__ __forceinline__ uint64_t sdesc(const void *p, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return (uint64_t)((su32(p) >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// Descriptor of the 8-element K step `kk` of a staged operand tile.
+//   K-major tile [rows][32] (128-byte swizzle): SBO = 1024 (8 rows),
+//   step = 32 bytes.
+//   MN-major tile of 32-wide chunks [chunk][32 k][32] (32-byte-atom swizzle):
+//   LBO = 4096 (next MN chunk), SBO = 512 (next 4 k-rows), step = 1024 bytes.
+template <bool KMAJOR>
+__device__ __forceinline__ uint64_t op_desc(const uint8_t *tile, int kk) {
+    return KMAJOR ? sdesc(tile + kk * 32, 16, 1024, 2) : sdesc(tile + kk * 1024, 4096, 512, 1);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// hi / lo split of one 16-byte chunk (hi in place).
+__device__ __forceinline__ void split4(uint4 &x, uint4 &lo) {
+    uint32_t *v = &x.x, *l = &lo.x;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t hi = v[i] & 0xFFFFE000u;
+        const float rest = __fsub_rn(__uint_as_float(v[i]), __uint_as_float(hi));
+        uint32_t r;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(rest));
+        v[i] = hi;
+        l[i] = r;
+    }
+}
+
+struct Maps {
+    CUtensorMap a, b;
+};
+
+struct Params {
+    int64_t M, N, K, ldc, stride_c;
+    int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
+    GemmBatch bt;
+};
+
+// instruction descriptor: f32 accumulate, tf32 A and B, majors, N, M
+template <bool TA, bool TB>
+constexpr uint32_t idesc() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((TA ? 1u : 0u) << 15) | ((TB ? 0u : 1u) << 16) |
+           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(THREADS, 1)
+    tf32x3_gemm_kernel(const __grid_constant__ Maps maps, float *__restrict__ C, const __grid_constant__ Params P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[STAGES], conv[STAGES], empty[STAGES], tfull[2], tfree[2];
+    __shared__ uint32_t tmem_base;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int64_t oa, ob;
+    batch_offsets(P.bt, blockIdx.z, &oa, &ob);
+    const int za = (int)(P.mat_a ? oa / P.mat_a : 0), zb = (int)(P.mat_b ? ob / P.mat_b : 0);
+    const int m0 = (int)blockIdx.y * BM, n0 = (int)blockIdx.x * BN;
+    const int KT = (int)((P.K + BK - 1) / BK);
+    const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mb_init(&full[s], 1);
+            mb_init(&conv[s], NCONV);
+            mb_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mb_init(&tfull[b], 1);
+            mb_init(&tfree[b], NEPI);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = tmem_base;
+
+    auto a_hi = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
+    auto a_lo = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
+    auto b_hi = [&](int s) { return smem + (size_t)s * STAGE_BYTES + 2 * A_BYTES; };
+    auto b_lo = [&](int s) { return smem + (size_t)s * STAGE_BYTES + 2 * A_BYTES + B_BYTES; };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int j = 0; j < KT; j++) {
+                const int s = j % STAGES;
+                if (j >= STAGES && !mb_wait(&empty[s], ((j / STAGES) - 1) & 1)) break;
+                mb_expect_tx(&full[s], A_BYTES + B_BYTES);
+                const int k0 = j * BK;
+                if (!TA) tma_load_3d(a_hi(s), &maps.a, k0, m0, za, &full[s]);
+                else
+                    for (int c = 0; c < BM / 32; c++) tma_load_3d(a_hi(s) + c * 4096, &maps.a, m0 + 32 * c, k0, za, &full[s]);
+                if (TB) tma_load_3d(b_hi(s), &maps.b, k0, n0, zb, &full[s]);
+                else
+                    for (int c = 0; c < BN / 32; c++) tma_load_3d(b_hi(s) + c * 4096, &maps.b, n0 + 32 * c, k0, zb, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t ID = idesc<TA, TB>();
+            bool ok = true;
+            for (int j = 0; j < KT && ok; j++) {
+                const int s = j % STAGES, q = j / KC_BLOCKS, buf = q & 1;
+                const bool first = (j % KC_BLOCKS) == 0;
+                const bool last = (j % KC_BLOCKS) == KC_BLOCKS - 1 || j == KT - 1;
+                if (first && q >= 2 && !mb_wait(&tfree[buf], ((q / 2) - 1) & 1)) break;
+                if (!mb_wait(&conv[s], (j / STAGES) & 1)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t d = tmem + (uint32_t)(buf * BN);
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; kk++) {
+                    const uint64_t ah = op_desc<!TA>(a_hi(s), kk), al = op_desc<!TA>(a_lo(s), kk);
+                    const uint64_t bh = op_desc<TB>(b_hi(s), kk), bl = op_desc<TB>(b_lo(s), kk);
+                    mma_tf32(d, ah, bh, ID, (first && kk == 0) ? 0u : 1u);
+                    mma_tf32(d, ah, bl, ID, 1u);
+                    mma_tf32(d, al, bh, ID, 1u);
+                }
+                mma_commit(&empty[s]);
+                if (last) mma_commit(&tfull[buf]);
+            }
+        }
+    } else if (warp < 8) {
+        // converters
+        const int ct = threadIdx.x - 64;
+        for (int j = 0; j < KT; j++) {
+            const int s = j % STAGES;
+            if (!mb_wait(&full[s], (j / STAGES) & 1)) break;
+            uint4 *ah = (uint4 *)a_hi(s), *al = (uint4 *)a_lo(s);
+            for (int i = ct; i < (int)(A_BYTES / 16); i += NCONV) {
+                uint4 x = ah[i], lo;
+                split4(x, lo);
+                ah[i] = x;
+                al[i] = lo;
+            }
+            uint4 *bh = (uint4 *)b_hi(s), *bl = (uint4 *)b_lo(s);
+            for (int i = ct; i < (int)(B_BYTES / 16); i += NCONV) {
+                uint4 x = bh[i], lo;
+                split4(x, lo);
+                bh[i] = x;
+                bl[i] = lo;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mb_arrive(&conv[s]);
+        }
+    } else {
+        // epilogue: fold finished chunks into registers, then store
+        const int q4 = warp & 3, half = (warp - 8) >> 2;
+        float acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+        bool ok = true;
+        for (int q = 0; q < NQ; q++) {
+            const int buf = q & 1;
+            if (!mb_wait(&tfull[buf], (q / 2) & 1)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * BN + half * 64);
+            float v[32];
+            tmem_ld32(taddr, v);
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[i] = __fadd_rn(acc[i], v[i]);
+            tmem_ld32(taddr + 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; i++) acc[32 + i] = __fadd_rn(acc[32 + i], v[i]);
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            mb_arrive(&tfree[buf]);
+        }
+        const int64_t row = (int64_t)m0 + q4 * 32 + lane;
+        if (ok && row < P.M) {
+            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
+            const int64_t col0 = (int64_t)n0 + half * 64;
+            if (col0 + 64 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
+#pragma unroll
+                for (int v = 0; v < 16; v++)
+                    *(float4 *)(crow + col0 + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            } else {
+#pragma unroll
+                for (int v = 0; v < 64; v++)
+                    if (col0 + v < P.N) crow[col0 + v] = acc[v];
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------ plain FMA-chain fallback
+//
+// For shapes the tensor maps cannot take: each output element is the FMA
+// chain of zpu's kernel (k ascending from 0), 16x16 tiles through shared
+// memory.  Correct for any strides; not the fast path.
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
+                                                       float *__restrict__ C, int64_t M, int64_t N, int64_t K,
+                                                       int64_t lda, int64_t ldb, int64_t ldc,
+                                                       const __grid_constant__ GemmBatch bt, int64_t stride_c) {
+    __shared__ float sa[16][17], sb[16][17];
+    int64_t oa, ob;
+    batch_offsets(bt, blockIdx.z, &oa, &ob);
+    A += oa;
+    B += ob;
+    C += (int64_t)blockIdx.z * stride_c;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int64_t row = (int64_t)blockIdx.y * 16 + ty, col = (int64_t)blockIdx.x * 16 + tx;
+    float acc = 0.0f;
+    for (int64_t k0 = 0; k0 < K; k0 += 16) {
+        const int64_t ka = k0 + tx, kb = k0 + ty;
+        const int64_t ar = (int64_t)blockIdx.y * 16 + ty, bc = (int64_t)blockIdx.x * 16 + tx;
+        sa[ty][tx] = (ar < M && ka < K) ? (TA ? A[ka * lda + ar] : A[ar * lda + ka]) : 0.0f;
+        sb[ty][tx] = (kb < K && bc < N) ? (TB ? B[bc * ldb + kb] : B[kb * ldb + bc]) : 0.0f;
+        __syncthreads();
+        const int kmax = (int)(K - k0 < 16 ? K - k0 : 16);
+        for (int kk = 0; kk < kmax; kk++) acc = fmaf(sa[ty][kk], sb[kk][tx], acc);
+        __syncthreads();
+    }
+    if (row < M && col < N) C[row * ldc + col] = acc;
+}
+
+// ------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int encode_fn() {
+    static std::once_flag once;
+    static int status = ZPUCUDA_OK;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn) {
+            cudaGetLastError();
+            status = ZPUCUDA_ERR_NO_DEVICE;
+            return;
+        }
+        g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    });
+    return status;
+}
+
+// 3-D f32 tensor map (inner, rows, matrices), box {32, box_rows, 1};
+// out-of-range elements read as zero.  K-major operands: 128-byte swizzle;
+// MN-major: 128-byte swizzle with 32-byte atoms.
+bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t rows, int64_t ld, int64_t nmats,
+              int64_t mat_stride, int box_rows, bool kmajor) {
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)nmats};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(nmats > 1 ? mat_stride : rows * ld) * 4};
+    cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          kmajor ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// The smallest positive batch stride of an operand, provided every batch
+// stride is a multiple of it (so batch offsets are whole matrices); 0 when
+// the operand does not move with the batch.
+bool matrix_stride(const int64_t *s, int nax, int64_t *out) {
+    int64_t m = 0;
+    for (int i = 0; i < nax; i++)
+        if (s[i] < 0) return false;
+        else if (s[i] > 0 && (m == 0 || s[i] < m)) m = s[i];
+    for (int i = 0; i < nax; i++)
+        if (m && s[i] % m) return false;
+    *out = m;
+    return true;
+}
+
+int64_t max_offset(const GemmBatch &bt, const int64_t *s) {
+    int64_t o = 0;
+    for (int i = 0; i < bt.nax; i++) o += (bt.dims[i] > 0 ? bt.dims[i] - 1 : 0) * s[i];
+    return o;
+}
+
+template <bool TA, bool TB>
+int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
+    auto k = tf32x3_gemm_kernel<TA, TB>;
+    static bool attr = false;
+    if (!attr) {
+        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
+        attr = true;
+    }
+    dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)batches);
+    k<<<grid, THREADS, SMEM_BYTES, s>>>(maps, C, P);
+    ZC_LAUNCHED("tf32x3_gemm_kernel");
+    return ZPUCUDA_OK;
+}
+
+}  // namespace
+
+int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                    int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                    cudaStream_t s) {
+    const int64_t batches = batch_count(bt);
+    if (m == 0 || n == 0 || batches == 0) return ZPUCUDA_OK;
+    if (!C || ldc < n) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if (k == 0) {  // kernels.zig:346-349: an empty contraction writes zeros
+        for (int64_t b = 0; b < batches; b++)
+            ZC_CUDA(cudaMemset2DAsync(C + b * stride_c, ldc * sizeof(float), 0, n * sizeof(float), m, s));
+        return ZPUCUDA_OK;
+    }
+    if (!A || !B) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if ((!ta && lda < k) || (ta && lda < m) || (!tb && ldb < n) || (tb && ldb < k)) return ZPUCUDA_ERR_INVALID_SHAPE;
+    if (batches > 65535 || (m + BM - 1) / BM > 65535) return ZPUCUDA_ERR_NOT_SUPPORTED;
+
+    // the tensor-core path needs what a TMA tensor map can describe
+    int64_t mat_a = 0, mat_b = 0;
+    bool tc = encode_fn() == ZPUCUDA_OK && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0) && lda % 4 == 0 &&
+              ldb % 4 == 0 && matrix_stride(bt.sa, bt.nax, &mat_a) && matrix_stride(bt.sb, bt.nax, &mat_b) &&
+              mat_a % 4 == 0 && mat_b % 4 == 0 && m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31);
+    if (tc) {
+        // inner extent / rows of each operand as stored
+        const int64_t a_inner = ta ? m : k, a_rows = ta ? k : m;
+        const int64_t b_inner = tb ? k : n, b_rows = tb ? n : k;
+        const int64_t na = mat_a ? max_offset(bt, bt.sa) / mat_a + 1 : 1;
+        const int64_t nb = mat_b ? max_offset(bt, bt.sb) / mat_b + 1 : 1;
+        Maps maps;
+        memset(&maps, 0, sizeof maps);
+        tc = make_map(&maps.a, A, a_inner, a_rows, lda, na, mat_a, ta ? 32 : BM, !ta) &&
+             make_map(&maps.b, B, b_inner, b_rows, ldb, nb, mat_b, tb ? BN : 32, tb);
+        if (tc) {
+            Params P;
+            memset(&P, 0, sizeof P);
+            P.M = m;
+            P.N = n;
+            P.K = k;
+            P.ldc = ldc;
+            P.stride_c = stride_c;
+            P.mat_a = mat_a;
+            P.mat_b = mat_b;
+            P.bt = bt;
+            if (!ta && !tb) return launch_tf32x3<false, false>(maps, C, P, batches, s);
+            if (!ta && tb) return launch_tf32x3<false, true>(maps, C, P, batches, s);
+            if (ta && !tb) return launch_tf32x3<true, false>(maps, C, P, batches, s);
+            return launch_tf32x3<true, true>(maps, C, P, batches, s);
+        }
+    }
+    dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16), (unsigned)batches);
+    if ((m + 15) / 16 > 65535) return ZPUCUDA_ERR_NOT_SUPPORTED;
+#define ZC_FG(TA_, TB_) fma_gemm_kernel<TA_, TB_><<<grid, 256, 0, s>>>(A, B, C, m, n, k, lda, ldb, ldc, bt, stride_c)
+    if (!ta && !tb) ZC_FG(false, false);
+    else if (!ta && tb) ZC_FG(false, true);
+    else if (ta && !tb) ZC_FG(true, false);
+    else ZC_FG(true, true);
+#undef ZC_FG
+    ZC_LAUNCHED("fma_gemm_kernel");
+    return ZPUCUDA_OK;
+}
+
 }  // namespace zc
+
+extern "C" int zpucuda_check_device(void) {
+    unsigned int e = 0;
+    cudaError_t r = cudaMemcpyFromSymbol(&e, zc::g_gemm_error, sizeof e);
+    if (r != cudaSuccess) return zc::cuda_fail(r, "cudaMemcpyFromSymbol(device error word)");
+    if (e) return zc::set_error(ZPUCUDA_ERR_TIMEOUT, "a device-side bounded wait ran out in a GEMM kernel");
+    return ZPUCUDA_OK;
+}
