@@ -177,6 +177,72 @@ def run_reference(args):
     return 0
 
 
+def _peak_tflops():
+    """TF32 and FP64 denominators: TF32 dense is half the measured bf16
+    rate (MEASURED_PEAKS.json), 3xTF32's algorithmic ceiling a third of
+    that; FP64 is the nominal 40 TFLOP/s (no measured FP64 peak exists)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+        src = "measured bf16 / 2"
+    except Exception:
+        bf16, src = 1590.0, "fallback bf16 / 2"
+    return bf16 / 2.0, 40.0, src
+
+
+def _time_events(fn, reps, warm=2):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gemm_configs():
+    """The GEMM workloads of the hot path, each timed with CUDA events on
+    device-resident inputs (zpu's RNG streams, seeds per config):
+    1: f32 1024^3 U[-1,1]; 3: vmap-batched 256 x 512^3, N(0, 1/512);
+    5: f64 8192^3 N(0,1)."""
+    import torch
+    import zpu_b200 as zc
+    tf32, fp64, src = _peak_tflops()
+    out = {}
+    n = 1024
+    A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
+    B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
+    C = torch.empty(n, n, device="cuda")
+    ms = _time_events(lambda: zc.matmul(A, B, out=C), 20)
+    t = 2 * n ** 3 / ms / 1e9
+    out["config1_f32_gemm_1024"] = {"tflops": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3),
+                                    "ceiling_tflops": tf32 / 3, "ceiling_source": src}
+    bsz, n = 256, 512
+    s = 1.0 / (512.0 ** 0.5)
+    A = (zc.rng_normal(0x5EED0004, bsz * n * n) * s).view(bsz, n, n)
+    B = (zc.rng_normal(0x5EED0005, bsz * n * n) * s).view(bsz, n, n)
+    C = torch.empty(bsz, n, n, device="cuda")
+    ms = _time_events(lambda: zc.matmul(A, B, a_depth=1, b_depth=1, out=C), 10)
+    t = bsz * 2 * n ** 3 / ms / 1e9
+    out["config3_vmap_batched_f32_256x512"] = {"tflops": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3)}
+    del A, B, C
+    n = 8192
+    A = zc.rng_normal(0x5EED0008, n * n, dtype=torch.float64).view(n, n)
+    B = zc.rng_normal(0x5EED0009, n * n, dtype=torch.float64).view(n, n)
+    C = torch.empty(n, n, dtype=torch.float64, device="cuda")
+    ms = _time_events(lambda: zc.matmul(A, B, out=C), 3, warm=1)
+    t = 2 * n ** 3 / ms / 1e9
+    out["config5_f64_gemm_8192"] = {"tflops": t, "ms": ms, "frac_of_fp64_nominal": t / fp64,
+                                    "fp64_peak_tflops": fp64, "fp64_peak_source": "nominal B200"}
+    del A, B, C
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import zpu_b200 as zc
@@ -286,6 +352,8 @@ def run_ours(args):
         "clocks": clk,
         "warmup_soak_steps": soak,
     }
+    if world == 1:
+        line["other_configs"] = gemm_configs()
     if rank == 0 and world == 1:
         gbs, cores, sample, per = cpu_chain_baseline()
         line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
