@@ -243,6 +243,90 @@ def gemm_configs():
     return out
 
 
+MLP_DIMS = (784, 4096, 4096, 10)
+MLP_BATCH = 8192
+# GEMM flops of one step: forward 2*B*(784*4096 + 4096^2 + 4096*10), backward
+# the weight gradients (the same again) plus the activation gradients of
+# layers 3 and 2, 2*B*(4096*10 + 4096^2)
+MLP_FLOPS = 2 * MLP_BATCH * (784 * 4096 + 4096 * 4096 + 4096 * 10) * 2 + 2 * MLP_BATCH * (4096 * 10 + 4096 * 4096)
+MLP_PARAMS = 784 * 4096 + 4096 + 4096 * 4096 + 4096 + 4096 * 10 + 10
+
+
+def mlp_config(rank, world, steps, warmup, dev):
+    """The data-parallel MLP train step (784->4096->4096->10, tanh, softmax
+    cross-entropy, global batch 8192, Adam lr 1e-3): each rank takes 8192/N
+    rows of X ~ U[0,1] (seed 0x5EED0006) and labels randint(0,10) (seed
+    0x5EED0007), Xavier-uniform init (seeds 0x5EED0010 + l), gradients summed
+    over NCCL in two buckets overlapping the backward pass.  Device-timed
+    steps (max over ranks) and an end-to-end run with X and labels copied
+    from pinned host memory and the loss copied back every step."""
+    import torch
+    import zpu_b200 as zc
+    from zpu_b200 import mlp as zm
+    tf32, _, src = _peak_tflops()
+    bl = MLP_BATCH // world
+    xs = zc.rng_uniform(0x5EED0006, MLP_BATCH * 784, 0.0, 1.0, device=dev).view(MLP_BATCH, 784)
+    ys = zc.rng_randint(0x5EED0007, MLP_BATCH, 0, 10, device=dev)
+    x = xs[rank * bl:(rank + 1) * bl].contiguous()
+    y = ys[rank * bl:(rank + 1) * bl].contiguous()
+    del xs, ys
+    if world > 1:
+        zm.init_process_group_nccl(rank, world)
+    m = zm.MLP(*MLP_DIMS, max_batch=bl)
+    m.init_xavier()
+    stream = torch.cuda.current_stream()
+    for _ in range(max(3, warmup)):
+        m.train_step(x, y, global_batch=MLP_BATCH)
+    loss0 = m.loss()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    l0 = zc.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        m.train_step(x, y, global_batch=MLP_BATCH)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = zc.launch_count() - l0
+    ms = e0.elapsed_time(e1) / steps
+    # end to end: pinned host X / labels -> HBM, the step, loss -> host
+    xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
+    lh = torch.empty(1, dtype=torch.float32).pin_memory()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(steps):
+        x.copy_(xh, non_blocking=True)
+        y.copy_(yh, non_blocking=True)
+        m.train_step(x, y, global_batch=MLP_BATCH)
+        m.loss_to(lh.data_ptr())
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e2.elapsed_time(e3) / steps
+    loss1 = float(lh[0])
+    if world > 1:
+        t = torch.tensor([ms, e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e_ms = float(t[0]), float(t[1])
+    m.close()
+    if world > 1:
+        zm.nccl_destroy()
+    del x, y
+    torch.cuda.empty_cache()
+    tflops = MLP_FLOPS / (ms / 1e3) / 1e12
+    return {"metric": "MLP train steps/s (global batch 8192)", "steps_per_s": 1e3 / ms, "ms_per_step": ms,
+            "n_gpus": world, "batch_per_gpu": bl, "gemm_tflops_whole_job": tflops,
+            "gemm_tflops_per_gpu": tflops / world, "frac_of_3xtf32_ceiling_per_gpu": tflops / world / (tf32 / 3),
+            "flops_per_step": MLP_FLOPS, "params": MLP_PARAMS, "allreduce_bytes_per_step": MLP_PARAMS * 4,
+            "kernel_launches_per_step": launches / steps, "loss_after_warmup": loss0, "loss_last": loss1,
+            "e2e": {"steps_per_s": 1e3 / e_ms, "ms_per_step": e_ms, "h2d_bytes_per_step": bl * (784 * 4 + 8),
+                    "d2h_bytes_per_step": 4},
+            "scaling": "strong (global batch fixed)", "dtype": "f32 (3xTF32 GEMMs)"}
+
+
 def run_ours(args):
     import torch
     import zpu_b200 as zc
@@ -352,8 +436,8 @@ def run_ours(args):
         "clocks": clk,
         "warmup_soak_steps": soak,
     }
-    if world == 1:
-        line["other_configs"] = gemm_configs()
+    line["other_configs"] = gemm_configs() if world == 1 else {}
+    line["other_configs"]["config4_mlp_train_step"] = mlp_config(rank, world, min(args.steps, 20), args.warmup, dev)
     if rank == 0 and world == 1:
         gbs, cores, sample, per = cpu_chain_baseline()
         line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",

@@ -221,6 +221,83 @@ int zpucuda_rng_uniform(uint64_t seed, int dtype, void *d_out, int64_t n, double
 int zpucuda_rng_normal(uint64_t seed, int dtype, void *d_out, int64_t n, void *stream);
 int zpucuda_rng_randint(uint64_t seed, int64_t *d_out, int64_t n, int64_t lo, int64_t hi, void *stream);
 
+/* ------------------------------------------------------------ collectives */
+/* No counterpart in the reference (it runs on one CPU): the gradient
+ * exchange of the data-parallel MLP step, one process (or thread) per GPU,
+ * NCCL over NVLink.  libnccl.so.2 is opened at run time on first use; without
+ * it these calls return ZPUCUDA_ERR_NOT_SUPPORTED.  The communicator belongs
+ * to the calling thread's bound device.
+ *  zpucuda_nccl_unique_id: rank 0 creates the id (ncclGetUniqueId) and hands
+ *    the 128 bytes to the other ranks by any host channel.
+ *  zpucuda_nccl_init: joins; returns ZPUCUDA_ERR_TIMEOUT (and tears the
+ *    half-made communicator down) when not every rank joined within
+ *    timeout_ms (< 0: no limit).
+ *  zpucuda_nccl_allreduce_f32: in-place sum of count floats on `stream`.
+ *  zpucuda_nccl_world: rank and world size (0 and 1 without a communicator).
+ *  zpucuda_nccl_destroy: finalizes (bounded by timeout_ms) and frees it. */
+#define ZPUCUDA_NCCL_ID_BYTES 128
+int zpucuda_nccl_unique_id(uint8_t *id);
+int zpucuda_nccl_init(int rank, int world, const uint8_t *id, int64_t timeout_ms);
+int zpucuda_nccl_allreduce_f32(float *d_buf, int64_t count, void *stream);
+int zpucuda_nccl_world(int *rank, int *world);
+int zpucuda_nccl_destroy(int64_t timeout_ms);
+
+/* ---------------------------------------------------------- MLP train step */
+/* The MLP step as a device-resident program: x -> tanh(x W1 + b1) ->
+ * tanh(. W2 + b2) -> . W3 + b3 = logits, loss = nn.sparseCrossEntropy(logits,
+ * labels) (src/zpu/nn.zig:123-134,190-194), its gradients as
+ * zpu.valueAndGrad computes them (src/zpu/transforms.zig:87-148,
+ * src/zpu/autodiff.zig:51,323-330,451-454,480-487), and Adam.step with f32
+ * moments (src/zpu/optim.zig:149-259), lowered to 13 kernels per step.
+ * Parameters are numbered in the reference's argument order: 0 W1 [d_in,d_h1],
+ * 1 b1 [d_h1], 2 W2 [d_h1,d_h2], 3 b2 [d_h2], 4 W3 [d_h2,d_out], 5 b3 [d_out],
+ * row-major as the reference stores them; the handle owns the parameters,
+ * gradients and Adam moments in HBM (all zero after create).
+ *  create: max_batch bounds the rows of one call; d_out <= 64.
+ *  write / read: copy parameter i of the array `what` (ZPUCUDA_MLP_*) from /
+ *    to any host or device pointer (numel = the parameter's element count),
+ *    asynchronously on `stream`.
+ *  array: the device address and length (floats, padding included) of a
+ *    whole array -- for callers that exchange it themselves.
+ *  adam_config: Adam's lr, beta1, beta2, eps (defaults 1e-3, 0.9, 0.999,
+ *    1e-8: optim.AdamConfig); weight decay is not supported.
+ *  value_and_grad: gradients of the loss over d_x [batch, d_in] f32 (16-byte
+ *    aligned) and d_labels [batch] int64, the loss averaged over
+ *    global_batch rows (= batch on one GPU; the sum over ranks of each
+ *    rank's slice otherwise).  Gradients land in the GRAD array, the loss in
+ *    a device word read by zpucuda_mlp_loss.
+ *  allreduce_grads: sums the GRAD array and the loss over the device's NCCL
+ *    communicator (no-op without one).
+ *  adam_step: one Adam.step with the GRAD array (step counter inside).
+ *  train_step: value_and_grad, the gradient sum across ranks when the device
+ *    has a communicator (two buckets on a side stream, overlapping the last
+ *    backward GEMMs), and adam_step.
+ *  loss: copies the last loss (f32) to dst (host or device) on `stream`.
+ *  check: synchronous; ZPUCUDA_ERR_INDEX_OUT_OF_RANGE when a label of an
+ *    earlier step was outside [0, d_out) (nn.oneHot's error; that row's
+ *    one-hot row was zero), and clears the flag.
+ *  steps: Adam steps taken. */
+typedef struct zpucuda_mlp zpucuda_mlp;
+enum { ZPUCUDA_MLP_PARAM = 0, ZPUCUDA_MLP_GRAD = 1, ZPUCUDA_MLP_ADAM_M = 2, ZPUCUDA_MLP_ADAM_V = 3 };
+int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int64_t d_out, int64_t max_batch,
+                       zpucuda_mlp **out);
+void zpucuda_mlp_destroy(zpucuda_mlp *h);
+int zpucuda_mlp_param_numel(const zpucuda_mlp *h, int i, int64_t *numel);
+int zpucuda_mlp_param_count(const zpucuda_mlp *h, int64_t *count);
+int zpucuda_mlp_write(zpucuda_mlp *h, int what, int i, const float *src, int64_t numel, void *stream);
+int zpucuda_mlp_read(const zpucuda_mlp *h, int what, int i, float *dst, int64_t numel, void *stream);
+int zpucuda_mlp_array(const zpucuda_mlp *h, int what, float **d_ptr, int64_t *n);
+int zpucuda_mlp_adam_config(zpucuda_mlp *h, double lr, double beta1, double beta2, double eps);
+int zpucuda_mlp_value_and_grad(zpucuda_mlp *h, const float *d_x, const int64_t *d_labels, int64_t batch,
+                               int64_t global_batch, void *stream);
+int zpucuda_mlp_allreduce_grads(zpucuda_mlp *h, void *stream);
+int zpucuda_mlp_adam_step(zpucuda_mlp *h, void *stream);
+int zpucuda_mlp_train_step(zpucuda_mlp *h, const float *d_x, const int64_t *d_labels, int64_t batch,
+                           int64_t global_batch, void *stream);
+int zpucuda_mlp_loss(const zpucuda_mlp *h, float *dst, void *stream);
+int zpucuda_mlp_check(zpucuda_mlp *h);
+int64_t zpucuda_mlp_steps(const zpucuda_mlp *h);
+
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot
  * allocate device memory -- an application embedding this library inside a

@@ -104,6 +104,26 @@ SIGNATURES = {
     "zpucuda_rng_normal": (I32, [U64, I32, P, I64, P]),
     "zpucuda_rng_randint": (I32, [U64, P, I64, I64, I64, P]),
     "zpucuda_chain_tanh_sq_affine_sum_noalloc": (I32, [P, I64, P, P, P, P]),
+    "zpucuda_nccl_unique_id": (I32, [P]),
+    "zpucuda_nccl_init": (I32, [I32, I32, P, I64]),
+    "zpucuda_nccl_allreduce_f32": (I32, [P, I64, P]),
+    "zpucuda_nccl_world": (I32, [C.POINTER(I32), C.POINTER(I32)]),
+    "zpucuda_nccl_destroy": (I32, [I64]),
+    "zpucuda_mlp_create": (I32, [I64, I64, I64, I64, I64, C.POINTER(P)]),
+    "zpucuda_mlp_destroy": (None, [P]),
+    "zpucuda_mlp_param_numel": (I32, [P, I32, C.POINTER(I64)]),
+    "zpucuda_mlp_param_count": (I32, [P, C.POINTER(I64)]),
+    "zpucuda_mlp_write": (I32, [P, I32, I32, P, I64, P]),
+    "zpucuda_mlp_read": (I32, [P, I32, I32, P, I64, P]),
+    "zpucuda_mlp_array": (I32, [P, I32, C.POINTER(P), C.POINTER(I64)]),
+    "zpucuda_mlp_adam_config": (I32, [P, C.c_double, C.c_double, C.c_double, C.c_double]),
+    "zpucuda_mlp_value_and_grad": (I32, [P, P, P, I64, I64, P]),
+    "zpucuda_mlp_allreduce_grads": (I32, [P, P]),
+    "zpucuda_mlp_adam_step": (I32, [P, P]),
+    "zpucuda_mlp_train_step": (I32, [P, P, P, I64, I64, P]),
+    "zpucuda_mlp_loss": (I32, [P, P, P]),
+    "zpucuda_mlp_check": (I32, [P]),
+    "zpucuda_mlp_steps": (I64, [P]),
 }
 
 

@@ -66,7 +66,7 @@ def build(force=False, verbose=False, jobs=None):
             for rep in ex.map(lambda so: _compile(so[0], so[1], verbose), todo):
                 reports.append(rep)
     if force or todo or _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lpthread"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (r.stdout, r.stderr))

@@ -36,8 +36,29 @@ __host__ __device__ inline void batch_offsets(const GemmBatch &g, int64_t bi, in
     *ob = b;
 }
 
+// What the f32 GEMM does with each result element before storing it: the
+// element-wise steps that follow a matmul in nn.dense + tanh and in the tanh
+// VJP (src/zpu/nn.zig:190, src/zpu/autodiff.zig:323-330), fused so the
+// product never makes an extra HBM round trip.  Each step rounds to f32 on
+// its own, as zpu's ops do.
+enum EpiMode : int32_t {
+    EPI_STORE = 0,      // c
+    EPI_BIAS_TANH = 1,  // tanh(c + bias[col])
+    EPI_TANH_GRAD = 2,  // c * (1 - y*y), y = aux[row, col] (a tanh output)
+    EPI_BIAS = 3,       // c + bias[col]
+};
+struct Epilogue {
+    int32_t mode = EPI_STORE;
+    const float *bias = nullptr;
+    const float *aux = nullptr;
+    int64_t ldaux = 0;
+};
+
 // op(A)[m,k] @ op(B)[k,n] -> C[m,n] (ldc), per batch; trans flags as in
 // zpucuda_gemm_f32.
+int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                        int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                        const Epilogue &epi, cudaStream_t s);
 int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                     int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                     cudaStream_t s);

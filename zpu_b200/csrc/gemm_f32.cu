@@ -43,6 +43,7 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "region.cuh"
 
 namespace zc {
 
@@ -157,14 +158,57 @@ struct Maps {
 struct Params {
     int64_t M, N, K, ldc, stride_c;
     int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
+    int32_t nmma;          // MMA width: N rounded up to 16, at most BN
+    uint32_t idesc;
+    Epilogue epi;
     GemmBatch bt;
 };
 
 // instruction descriptor: f32 accumulate, tf32 A and B, majors, N, M
-template <bool TA, bool TB>
-constexpr uint32_t idesc() {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((TA ? 1u : 0u) << 15) | ((TB ? 0u : 1u) << 16) |
-           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+uint32_t make_idesc(bool ta, bool tb, int nmma) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((ta ? 1u : 0u) << 15) | ((tb ? 0u : 1u) << 16) |
+           ((uint32_t)(nmma >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// One result element through the epilogue (the element is at row, col of C).
+__device__ __forceinline__ float epi_apply(const Epilogue &e, float c, int64_t row, int64_t col) {
+    if (e.mode == EPI_BIAS_TANH) return zc_tanhf(__fadd_rn(c, e.bias[col]));
+    if (e.mode == EPI_BIAS) return __fadd_rn(c, e.bias[col]);
+    if (e.mode == EPI_TANH_GRAD) {
+        const float y = e.aux[row * e.ldaux + col];
+        return __fmul_rn(c, __fsub_rn(1.0f, __fmul_rn(y, y)));
+    }
+    return c;
+}
+
+// The epilogue on 64 consecutive columns of one row, all inside C.
+__device__ __forceinline__ void epi_apply64(const Epilogue &e, float (&acc)[64], int64_t row, int64_t col0) {
+    if (e.mode == EPI_STORE) return;
+    if (e.mode == EPI_TANH_GRAD) {
+        const float *y = e.aux + row * e.ldaux + col0;
+        if ((((uintptr_t)y) & 15) == 0) {
+#pragma unroll
+            for (int v = 0; v < 16; v++) {
+                const float4 q = __ldg((const float4 *)y + v);
+                acc[4 * v] = __fmul_rn(acc[4 * v], __fsub_rn(1.0f, __fmul_rn(q.x, q.x)));
+                acc[4 * v + 1] = __fmul_rn(acc[4 * v + 1], __fsub_rn(1.0f, __fmul_rn(q.y, q.y)));
+                acc[4 * v + 2] = __fmul_rn(acc[4 * v + 2], __fsub_rn(1.0f, __fmul_rn(q.z, q.z)));
+                acc[4 * v + 3] = __fmul_rn(acc[4 * v + 3], __fsub_rn(1.0f, __fmul_rn(q.w, q.w)));
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < 64; v++) acc[v] = __fmul_rn(acc[v], __fsub_rn(1.0f, __fmul_rn(y[v], y[v])));
+        }
+        return;
+    }
+    const float *b = e.bias + col0;
+    if (e.mode == EPI_BIAS_TANH) {
+#pragma unroll
+        for (int v = 0; v < 64; v++) acc[v] = zc_tanhf(__fadd_rn(acc[v], __ldg(b + v)));
+    } else {
+#pragma unroll
+        for (int v = 0; v < 64; v++) acc[v] = __fadd_rn(acc[v], __ldg(b + v));
+    }
 }
 
 template <bool TA, bool TB>
@@ -227,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t ID = idesc<TA, TB>();
+            const uint32_t ID = P.idesc;
             bool ok = true;
             for (int j = 0; j < KT && ok; j++) {
                 const int s = j % STAGES, q = j / KC_BLOCKS, buf = q & 1;
@@ -288,12 +332,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * BN + half * 64);
             float v[32];
-            tmem_ld32(taddr, v);
+            if (half * 64 < P.nmma) {  // columns past the MMA width hold nothing
+                tmem_ld32(taddr, v);
 #pragma unroll
-            for (int i = 0; i < 32; i++) acc[i] = __fadd_rn(acc[i], v[i]);
-            tmem_ld32(taddr + 32, v);
+                for (int i = 0; i < 32; i++) acc[i] = __fadd_rn(acc[i], v[i]);
+            }
+            if (half * 64 + 32 < P.nmma) {
+                tmem_ld32(taddr + 32, v);
 #pragma unroll
-            for (int i = 0; i < 32; i++) acc[32 + i] = __fadd_rn(acc[32 + i], v[i]);
+                for (int i = 0; i < 32; i++) acc[32 + i] = __fadd_rn(acc[32 + i], v[i]);
+            }
             asm volatile("tcgen05.fence::before_thread_sync;");
             mb_arrive(&tfree[buf]);
         }
@@ -302,13 +350,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
             const int64_t col0 = (int64_t)n0 + half * 64;
             if (col0 + 64 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
+                epi_apply64(P.epi, acc, row, col0);
 #pragma unroll
                 for (int v = 0; v < 16; v++)
                     *(float4 *)(crow + col0 + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
             } else {
 #pragma unroll
                 for (int v = 0; v < 64; v++)
-                    if (col0 + v < P.N) crow[col0 + v] = acc[v];
+                    if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
             }
         }
     }
@@ -329,7 +378,8 @@ template <bool TA, bool TB>
 __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
                                                        float *__restrict__ C, int64_t M, int64_t N, int64_t K,
                                                        int64_t lda, int64_t ldb, int64_t ldc,
-                                                       const __grid_constant__ GemmBatch bt, int64_t stride_c) {
+                                                       const __grid_constant__ GemmBatch bt, int64_t stride_c,
+                                                       const __grid_constant__ Epilogue epi) {
     __shared__ float sa[16][17], sb[16][17];
     int64_t oa, ob;
     batch_offsets(bt, blockIdx.z, &oa, &ob);
@@ -349,7 +399,7 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
         for (int kk = 0; kk < kmax; kk++) acc = fmaf(sa[ty][kk], sb[kk][tx], acc);
         __syncthreads();
     }
-    if (row < M && col < N) C[row * ldc + col] = acc;
+    if (row < M && col < N) C[row * ldc + col] = epi_apply(epi, acc, row, col);
 }
 
 // ------------------------------------------------------------- host side
@@ -428,9 +478,20 @@ int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, 
 int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                     int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                     cudaStream_t s) {
+    return gemm_f32_device_epi(A, B, C, m, n, k, lda, ldb, ldc, ta, tb, bt, stride_c, Epilogue{}, s);
+}
+
+int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                        int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                        const Epilogue &epi, cudaStream_t s) {
     const int64_t batches = batch_count(bt);
     if (m == 0 || n == 0 || batches == 0) return ZPUCUDA_OK;
     if (!C || ldc < n) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if (epi.mode != EPI_STORE) {  // the epilogue inputs belong to one matrix
+        if (batches != 1 || epi.mode < 0 || epi.mode > EPI_BIAS) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        if ((epi.mode == EPI_TANH_GRAD) ? (!epi.aux || epi.ldaux < n) : !epi.bias) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        if (k == 0) return ZPUCUDA_ERR_NOT_SUPPORTED;
+    }
     if (k == 0) {  // kernels.zig:346-349: an empty contraction writes zeros
         for (int64_t b = 0; b < batches; b++)
             ZC_CUDA(cudaMemset2DAsync(C + b * stride_c, ldc * sizeof(float), 0, n * sizeof(float), m, s));
@@ -465,6 +526,9 @@ int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t
             P.stride_c = stride_c;
             P.mat_a = mat_a;
             P.mat_b = mat_b;
+            P.nmma = (int32_t)(n >= BN ? BN : (n + 15) / 16 * 16);
+            P.idesc = make_idesc(ta, tb, P.nmma);
+            P.epi = epi;
             P.bt = bt;
             if (!ta && !tb) return launch_tf32x3<false, false>(maps, C, P, batches, s);
             if (!ta && tb) return launch_tf32x3<false, true>(maps, C, P, batches, s);
@@ -474,7 +538,8 @@ int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t
     }
     dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16), (unsigned)batches);
     if ((m + 15) / 16 > 65535) return ZPUCUDA_ERR_NOT_SUPPORTED;
-#define ZC_FG(TA_, TB_) fma_gemm_kernel<TA_, TB_><<<grid, 256, 0, s>>>(A, B, C, m, n, k, lda, ldb, ldc, bt, stride_c)
+#define ZC_FG(TA_, TB_) \
+    fma_gemm_kernel<TA_, TB_><<<grid, 256, 0, s>>>(A, B, C, m, n, k, lda, ldb, ldc, bt, stride_c, epi)
     if (!ta && !tb) ZC_FG(false, false);
     else if (!ta && tb) ZC_FG(false, true);
     else if (ta && !tb) ZC_FG(true, false);
