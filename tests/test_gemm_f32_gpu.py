@@ -104,3 +104,20 @@ def test_empty_contraction_writes_zeros(zc):
     c = torch.full((4, 3), 7.0, dtype=torch.float32, device="cuda")
     zc.gemm(a, b, out=c)
     assert float(c.abs().sum()) == 0.0
+
+
+def test_nan_propagates_like_the_fma_chain(zc):
+    """A NaN in row i of A makes row i of C NaN (zpu's FMA chain); every
+    other element stays finite and within tolerance."""
+    rng = np.random.default_rng(7)
+    m, k, n = 256, 96, 200
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    a[5, 17] = np.nan
+    a[130, 0] = np.nan
+    want = zo.gemm(a, b)
+    got = zc.gemm(dev(a), dev(b)).cpu().numpy()
+    check_no_device_error(zc)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    fin = ~np.isnan(want)
+    assert rel_fro(got[fin], want[fin]) <= TOL

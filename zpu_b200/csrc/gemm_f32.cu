@@ -5,28 +5,42 @@
 // zpu computes each element as an f32 FMA chain; TF32 keeps 10 mantissa
 // bits, so every operand is split x = hi + lo with hi, lo exact TF32 values
 // and C = A_hi B_hi + A_hi B_lo + A_lo B_hi (the lo*lo term is below f32
-// resolution): three tensor-core MMAs per K step.
+// resolution): three tensor-core MMAs per K step.  hi is the f32 operand as
+// loaded: the tensor core reads f32 data as TF32 by ignoring the 13 low
+// mantissa bits (truncation), so only lo = x - trunc(x) is computed.
 //
 // The tensor core's own f32 accumulation drifts with the number of MMAs it
 // chains (measured: relative error growing linearly with K, 3e-5 at
 // K = 4096), so the K loop is cut into chunks of KC_BLOCKS * 32: each chunk
-// accumulates in one of two TMEM buffers, and epilogue warps fold finished
-// chunks into registers with round-to-nearest f32 adds while the tensor core
-// fills the other buffer.
+// accumulates in one of two TMEM buffers, and folding warps add finished
+// chunks into a running sum (a third TMEM region) with round-to-nearest f32
+// adds while the tensor core fills the other buffer.
 //
-// One CTA computes a 128 x 128 tile with 16 warps in fixed roles:
+// Shared-memory bandwidth is what limits this kernel: per 32-wide K slice
+// the TMA writes 32 KiB, making lo reads 32 and writes 32, and the three
+// MMAs read 96 (measured: the pipeline without making lo ran 1.7x faster;
+// ncu shows the LSU and tensor-core shared-memory pipes together near
+// saturation).  So every warp that is not the producer or the MMA issuer
+// converts, raw tiles have a deeper ring than lo tiles, and the hi tiles are
+// never rewritten.  (Feeding A from TMEM instead -- tcgen05.mma with a TMEM A
+// operand, hi and lo written by tcgen05.st -- cuts the traffic to 128 KiB but
+// measured slower: that pipeline peaked at 180 TFLOP/s even without
+// conversion, against 220 for this one.)
+//
+// One CTA computes a 128 x 128 tile with 16 warps:
 //   warp 0      TMA producer: 3-D tensor maps (inner, rows, matrix) stream
-//               32-wide K slices of A and B into STAGES shared-memory stages
+//               32-wide K slices of A and B into RAW shared-memory stages
 //               (out-of-range rows/columns read as zero);
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma (kind::tf32) and
 //               the tcgen05.commits;
-//   warps 2-7   split each landed stage: hi = x with the low 13 mantissa bits
-//               cleared (in place), lo = round-to-nearest TF32 of x - hi into
-//               the stage's lo buffer at the same (swizzled) position, so hi
-//               and lo tiles share their descriptors;
-//   warps 8-15  fold each finished chunk (tcgen05.ld 32x32b) into registers,
-//               then store the tile; warp w reads TMEM lanes 32 (w % 4) ..
-//               +31 and columns 64 ((w - 8) / 4) .. +63.
+//   warps 2-15  write lo of each landed stage into one of LO lo slots at the
+//               same (swizzled) position, so hi and lo tiles share their
+//               descriptor layout;
+//   warps 8-15  also fold each finished chunk (tcgen05.ld / tcgen05.st
+//               32x32b) whenever they wait, then store the tile; warp w owns
+//               TMEM lanes 32 (w % 4) .. +31 and columns 64 ((w - 8) / 4) ..
+//               +63.
+// TMEM columns: chunk accumulators 0-127 and 128-255, running sum 256-383.
 // K-major operands use the 128-byte swizzle; MN-major ones (the matmul VJP's
 // swapLastTwo views, read in place) use the 128-byte swizzle with 32-byte
 // atoms, the only shared-memory layout tcgen05 takes for MN-major TF32.
@@ -51,14 +65,18 @@ static __device__ unsigned int g_gemm_error;
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, THREADS = 512;
+constexpr int BM = 128, BN = 128, BK = 32, THREADS = 512;
+constexpr int RAW = 4;        // stages of raw A/B tiles (the hi operands)
+constexpr int LO = 2;         // slots of lo tiles
 constexpr int KC_BLOCKS = 4;  // K-slices per accumulation chunk (K = 128)
-constexpr int NCONV = 192;    // converter threads (warps 2-7)
-constexpr int NEPI = 256;     // epilogue threads (warps 8-15)
+constexpr int NWORK = 14;     // converter warps (2-15)
+constexpr int NFOLD = 256;    // folding / storing threads (warps 8-15)
 constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;  // 16 KiB each
-constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);          // hi + lo of A and B
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t RAW_BYTES = A_BYTES + B_BYTES;                   // one stage (and one lo slot)
+constexpr int CONV_ITERS = (RAW_BYTES / 16 + NWORK * 32 - 1) / (NWORK * 32);
+constexpr size_t SMEM_BYTES = (size_t)(RAW + LO) * RAW_BYTES + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 512;   // two chunk accumulators + the running sum
+constexpr uint32_t SUM_COL = 2 * BN;  // first column of the running sum
 constexpr uint32_t kGemmSpin = 1u << 24;
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -122,7 +140,7 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ void tmem_ld32p(uint32_t taddr, float *v) {
     uint32_t r[32];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -136,19 +154,85 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) { tmem_ld32p(taddr, v); }
 
-// hi / lo split of one 16-byte chunk (hi in place).
-__device__ __forceinline__ void split4(uint4 &x, uint4 &lo) {
-    uint32_t *v = &x.x, *l = &lo.x;
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mb_test(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// One try_wait with a short suspend hint (ns): true when the phase is done.
+__device__ __forceinline__ bool mb_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity), "r"(200u)
+        : "memory");
+    return ok != 0;
+}
+
+// The lo half of the TF32 split of four f32 values: x - trunc_tf32(x)
+// (exact in f32), rounded to nearest TF32.  The hi half is x itself: the
+// tensor core reads an f32 operand as TF32 by ignoring its 13 low mantissa
+// bits, i.e. it truncates.  Infinities get lo = 0 (so inf * b stays inf);
+// NaN gives lo = NaN.
+__device__ __forceinline__ uint4 lo4(const uint4 &x) {
+    uint4 out;
+    const uint32_t *v = &x.x;
+    uint32_t *l = &out.x;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const uint32_t hi = v[i] & 0xFFFFE000u;
         const float rest = __fsub_rn(__uint_as_float(v[i]), __uint_as_float(hi));
         uint32_t r;
         asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(rest));
-        v[i] = hi;
-        l[i] = r;
+        l[i] = ((v[i] & 0x7FFFFFFFu) == 0x7F800000u) ? 0u : r;
     }
+    return out;
+}
+
+// Folds accumulation chunk q (TMEM buffer q & 1) into the running sum at
+// SUM_COL with round-to-nearest f32 adds; this warp's 32 lanes, columns
+// half*64 .. +63 (those inside the MMA width).
+__device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q, int half, int nmma) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+        const int col = half * 64 + c * 32;
+        if (col >= nmma) continue;
+        float v[32];
+        tmem_ld32(tmem + lanes + (uint32_t)((q & 1) * BN + col), v);
+        if (q > 0) {
+            float sum[32];
+            tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)col, sum);
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = __fadd_rn(sum[i], v[i]);
+        }
+        tmem_st32(tmem + lanes + SUM_COL + (uint32_t)col, v);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
 }
 
 struct Maps {
@@ -216,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ Maps maps, float *__restrict__ C, const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[STAGES], conv[STAGES], empty[STAGES], tfull[2], tfree[2];
+    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[LO], lofree[LO], tfull[2], tfree[2];
     __shared__ uint32_t tmem_base;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -228,14 +312,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
+        for (int s = 0; s < RAW; s++) {
             mb_init(&full[s], 1);
-            mb_init(&conv[s], NCONV);
             mb_init(&empty[s], 1);
+        }
+        for (int l = 0; l < LO; l++) {
+            mb_init(&conv[l], NWORK);
+            mb_init(&lofree[l], 1);
         }
         for (int b = 0; b < 2; b++) {
             mb_init(&tfull[b], 1);
-            mb_init(&tfree[b], NEPI);
+            mb_init(&tfree[b], NFOLD);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -249,115 +336,131 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = tmem_base;
 
-    auto a_hi = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
-    auto a_lo = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
-    auto b_hi = [&](int s) { return smem + (size_t)s * STAGE_BYTES + 2 * A_BYTES; };
-    auto b_lo = [&](int s) { return smem + (size_t)s * STAGE_BYTES + 2 * A_BYTES + B_BYTES; };
+    // raw stage s: A then B (the hi operands as loaded); lo slot l: A then B
+    auto raw_a = [&](int s) { return smem + (size_t)s * RAW_BYTES; };
+    auto raw_b = [&](int s) { return smem + (size_t)s * RAW_BYTES + A_BYTES; };
+    auto lo_a = [&](int l) { return smem + (size_t)RAW * RAW_BYTES + (size_t)l * RAW_BYTES; };
+    auto lo_b = [&](int l) { return smem + (size_t)RAW * RAW_BYTES + (size_t)l * RAW_BYTES + A_BYTES; };
 
     if (warp == 0) {
         if (lane == 0) {
             for (int j = 0; j < KT; j++) {
-                const int s = j % STAGES;
-                if (j >= STAGES && !mb_wait(&empty[s], ((j / STAGES) - 1) & 1)) break;
+                const int s = j % RAW;
+                if (j >= RAW && !mb_wait(&empty[s], ((j / RAW) - 1) & 1)) break;
                 mb_expect_tx(&full[s], A_BYTES + B_BYTES);
                 const int k0 = j * BK;
-                if (!TA) tma_load_3d(a_hi(s), &maps.a, k0, m0, za, &full[s]);
+                if (!TA) tma_load_3d(raw_a(s), &maps.a, k0, m0, za, &full[s]);
                 else
-                    for (int c = 0; c < BM / 32; c++) tma_load_3d(a_hi(s) + c * 4096, &maps.a, m0 + 32 * c, k0, za, &full[s]);
-                if (TB) tma_load_3d(b_hi(s), &maps.b, k0, n0, zb, &full[s]);
+                    for (int c = 0; c < BM / 32; c++) tma_load_3d(raw_a(s) + c * 4096, &maps.a, m0 + 32 * c, k0, za, &full[s]);
+                if (TB) tma_load_3d(raw_b(s), &maps.b, k0, n0, zb, &full[s]);
                 else
-                    for (int c = 0; c < BN / 32; c++) tma_load_3d(b_hi(s) + c * 4096, &maps.b, n0 + 32 * c, k0, zb, &full[s]);
+                    for (int c = 0; c < BN / 32; c++) tma_load_3d(raw_b(s) + c * 4096, &maps.b, n0 + 32 * c, k0, zb, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t ID = P.idesc;
-            bool ok = true;
-            for (int j = 0; j < KT && ok; j++) {
-                const int s = j % STAGES, q = j / KC_BLOCKS, buf = q & 1;
+            for (int j = 0; j < KT; j++) {
+                const int s = j % RAW, l = j % LO, q = j / KC_BLOCKS, buf = q & 1;
                 const bool first = (j % KC_BLOCKS) == 0;
                 const bool last = (j % KC_BLOCKS) == KC_BLOCKS - 1 || j == KT - 1;
                 if (first && q >= 2 && !mb_wait(&tfree[buf], ((q / 2) - 1) & 1)) break;
-                if (!mb_wait(&conv[s], (j / STAGES) & 1)) break;
+                if (!mb_wait(&conv[l], (j / LO) & 1)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t d = tmem + (uint32_t)(buf * BN);
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; kk++) {
-                    const uint64_t ah = op_desc<!TA>(a_hi(s), kk), al = op_desc<!TA>(a_lo(s), kk);
-                    const uint64_t bh = op_desc<TB>(b_hi(s), kk), bl = op_desc<TB>(b_lo(s), kk);
+                    const uint64_t ah = op_desc<!TA>(raw_a(s), kk), al = op_desc<!TA>(lo_a(l), kk);
+                    const uint64_t bh = op_desc<TB>(raw_b(s), kk), bl = op_desc<TB>(lo_b(l), kk);
                     mma_tf32(d, ah, bh, ID, (first && kk == 0) ? 0u : 1u);
                     mma_tf32(d, ah, bl, ID, 1u);
                     mma_tf32(d, al, bh, ID, 1u);
                 }
                 mma_commit(&empty[s]);
+                mma_commit(&lofree[l]);
                 if (last) mma_commit(&tfull[buf]);
             }
         }
-    } else if (warp < 8) {
-        // converters
-        const int ct = threadIdx.x - 64;
-        for (int j = 0; j < KT; j++) {
-            const int s = j % STAGES;
-            if (!mb_wait(&full[s], (j / STAGES) & 1)) break;
-            uint4 *ah = (uint4 *)a_hi(s), *al = (uint4 *)a_lo(s);
-            for (int i = ct; i < (int)(A_BYTES / 16); i += NCONV) {
-                uint4 x = ah[i], lo;
-                split4(x, lo);
-                ah[i] = x;
-                al[i] = lo;
+    } else {
+        // workers: every landed stage -> its lo tiles; warps 8-15 also fold
+        // finished chunks into the running sum and store the tile
+        const int wt = threadIdx.x - 64;
+        const bool folder = warp >= 8;
+        const int q4 = warp & 3, half = (warp - 8) >> 2;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        int folded = 0;
+        bool ok = true;
+        // folds every chunk whose MMAs have completed (folder warps only)
+        auto try_folds = [&]() {
+            while (folded < NQ && __all_sync(0xffffffffu, mb_test(&tfull[folded & 1], (folded >> 1) & 1))) {
+                fold_chunk(tmem, lanes, folded, half, P.nmma);
+                mb_arrive(&tfree[folded & 1]);
+                folded++;
             }
-            uint4 *bh = (uint4 *)b_hi(s), *bl = (uint4 *)b_lo(s);
-            for (int i = ct; i < (int)(B_BYTES / 16); i += NCONV) {
-                uint4 x = bh[i], lo;
-                split4(x, lo);
-                bh[i] = x;
-                bl[i] = lo;
+        };
+        // a bounded wait that keeps folding while it waits
+        auto wait = [&](uint64_t *bar, uint32_t parity) {
+            if (!folder) return mb_wait(bar, parity);
+            for (uint32_t i = 0; i < kGemmSpin; i++) {
+                if (__all_sync(0xffffffffu, mb_try(bar, parity))) return true;
+                try_folds();
+            }
+            atomicOr(&g_gemm_error, 1u);
+            return false;
+        };
+        for (int j = 0; j < KT && ok; j++) {
+            const int s = j % RAW, l = j % LO;
+            if (!wait(&full[s], (j / RAW) & 1)) ok = false;
+            else if (j >= LO && !wait(&lofree[l], ((j / LO) - 1) & 1)) ok = false;
+            if (!ok) break;
+            const uint4 *src = (const uint4 *)raw_a(s);  // A then B, contiguous
+            uint4 *dst = (uint4 *)lo_a(l);
+            uint4 x[CONV_ITERS];
+#pragma unroll
+            for (int u = 0; u < CONV_ITERS; u++) {
+                const int i = wt + u * NWORK * 32;
+                if (i < (int)(RAW_BYTES / 16)) x[u] = src[i];
+            }
+#pragma unroll
+            for (int u = 0; u < CONV_ITERS; u++) {
+                const int i = wt + u * NWORK * 32;
+                if (i < (int)(RAW_BYTES / 16)) dst[i] = lo4(x[u]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mb_arrive(&conv[s]);
+            __syncwarp();
+            if (lane == 0) mb_arrive(&conv[l]);
+            if (folder) try_folds();
         }
-    } else {
-        // epilogue: fold finished chunks into registers, then store
-        const int q4 = warp & 3, half = (warp - 8) >> 2;
-        float acc[64];
-#pragma unroll
-        for (int i = 0; i < 64; i++) acc[i] = 0.0f;
-        bool ok = true;
-        for (int q = 0; q < NQ; q++) {
-            const int buf = q & 1;
-            if (!mb_wait(&tfull[buf], (q / 2) & 1)) {
-                ok = false;
-                break;
+        if (folder) {
+            while (ok && folded < NQ) {
+                if (!mb_wait(&tfull[folded & 1], (folded >> 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                __syncwarp();
+                fold_chunk(tmem, lanes, folded, half, P.nmma);
+                mb_arrive(&tfree[folded & 1]);
+                folded++;
             }
+            const int64_t row = (int64_t)m0 + q4 * 32 + lane;
+            float acc[64];
+            __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(buf * BN + half * 64);
-            float v[32];
-            if (half * 64 < P.nmma) {  // columns past the MMA width hold nothing
-                tmem_ld32(taddr, v);
+            if (ok && half * 64 < P.nmma) tmem_ld32p(tmem + lanes + SUM_COL + half * 64, acc);
+            if (ok && half * 64 + 32 < P.nmma) tmem_ld32p(tmem + lanes + SUM_COL + half * 64 + 32, acc + 32);
+            if (ok && row < P.M) {
+                float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
+                const int64_t col0 = (int64_t)n0 + half * 64;
+                if (col0 + 64 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
+                    epi_apply64(P.epi, acc, row, col0);
 #pragma unroll
-                for (int i = 0; i < 32; i++) acc[i] = __fadd_rn(acc[i], v[i]);
-            }
-            if (half * 64 + 32 < P.nmma) {
-                tmem_ld32(taddr + 32, v);
+                    for (int v = 0; v < 16; v++)
+                        *(float4 *)(crow + col0 + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 32; i++) acc[32 + i] = __fadd_rn(acc[32 + i], v[i]);
-            }
-            asm volatile("tcgen05.fence::before_thread_sync;");
-            mb_arrive(&tfree[buf]);
-        }
-        const int64_t row = (int64_t)m0 + q4 * 32 + lane;
-        if (ok && row < P.M) {
-            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
-            const int64_t col0 = (int64_t)n0 + half * 64;
-            if (col0 + 64 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
-                epi_apply64(P.epi, acc, row, col0);
-#pragma unroll
-                for (int v = 0; v < 16; v++)
-                    *(float4 *)(crow + col0 + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-            } else {
-#pragma unroll
-                for (int v = 0; v < 64; v++)
-                    if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                    for (int v = 0; v < 64; v++)
+                        if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                }
             }
         }
     }
