@@ -39,6 +39,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default=None, choices=sorted(ONLY_CASES),
+                    help="run one workload alone (for profiling) and print its timing")
     return ap.parse_args()
 
 
@@ -450,8 +452,67 @@ def run_ours(args):
     return 0
 
 
+def _only_gemm(kind, steps, warmup):
+    import torch
+    import zpu_b200 as zc
+    if kind == "f32_1024":
+        n, bsz = 1024, 0
+        A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
+        B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
+    elif kind == "f32_4096":
+        n, bsz = 4096, 0
+        A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
+        B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
+    elif kind == "f32_batched":
+        n, bsz = 512, 256
+        s = 1.0 / (512.0 ** 0.5)
+        A = (zc.rng_normal(0x5EED0004, bsz * n * n) * s).view(bsz, n, n)
+        B = (zc.rng_normal(0x5EED0005, bsz * n * n) * s).view(bsz, n, n)
+    else:
+        n, bsz = 4096, 0
+        A = zc.rng_normal(0x5EED0008, n * n, dtype=torch.float64).view(n, n)
+        B = zc.rng_normal(0x5EED0009, n * n, dtype=torch.float64).view(n, n)
+    C = torch.empty_like(A)
+    d = 1 if bsz else 0
+    ms = _time_events(lambda: zc.matmul(A, B, a_depth=d, b_depth=d, out=C), steps, warm=warmup)
+    return {"ms": ms, "tflops": max(1, bsz) * 2 * n ** 3 / ms / 1e9, "n": n, "batch": max(1, bsz)}
+
+
+ONLY_CASES = {
+    "chain": None, "mlp": None,
+    "gemm_f32_1024": "f32_1024", "gemm_f32_4096": "f32_4096", "gemm_f32_batched": "f32_batched",
+    "gemm_f64_4096": "f64_4096",
+}
+
+
+def run_only(args):
+    """One workload alone, for ncu captures: the same kernels and inputs as
+    the full run, none of the others."""
+    import torch
+    import numpy as np
+    import zpu_b200 as zc
+    torch.cuda.set_device(0)
+    zc.check(zc.lib().zpucuda_init(0))
+    if args.only == "mlp":
+        out = mlp_config(0, 1, args.steps, args.warmup, torch.device("cuda", 0))
+    elif args.only == "chain":
+        x = zc.rng_normal(SEED_X, N_ELEM)
+        steps_def = [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0), ("mul", [11, 2], 12, -2, 0),
+                     ("add", [12, 3], 13, -2, 0), ("sum", [13], 14, -2, 0)]
+        plan = zc.Plan([(1, zc.F32, (N_ELEM,))], [(2, np.float32(A)), (3, np.float32(B))], steps_def, [14])
+        y = torch.empty((), dtype=torch.float32, device="cuda")
+        ms = _time_events(lambda: plan.run([x], [y]), args.steps, warm=args.warmup)
+        out = {"ms": ms, "gbs": BYTES_PER_STEP / ms / 1e6}
+    else:
+        out = _only_gemm(ONLY_CASES[args.only], args.steps, args.warmup)
+    print(json.dumps({"only": args.only, **out}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.only:
+        return run_only(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -8,7 +8,8 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libzpucuda.so")
+# ZPUCUDA_LIB names another build of the library (same ABI) to load instead.
+LIB_PATH = os.environ.get("ZPUCUDA_LIB") or os.path.join(HERE, "libzpucuda.so")
 
 MAX_RANK = 8
 AXIS_NONE = -2

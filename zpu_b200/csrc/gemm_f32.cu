@@ -27,7 +27,9 @@
 // measured slower: that pipeline peaked at 180 TFLOP/s even without
 // conversion, against 220 for this one.)
 //
-// One CTA computes a 128 x 128 tile with 16 warps:
+// One CTA computes a 128 x BN tile (BN = 128 or 256, chosen per problem by
+// how the tiles fill the SMs; the Tile struct has the differences) with 16
+// warps:
 //   warp 0      TMA producer: 3-D tensor maps (inner, rows, matrix) stream
 //               32-wide K slices of A and B into RAW shared-memory stages
 //               (out-of-range rows/columns read as zero);
@@ -38,9 +40,9 @@
 //               descriptor layout;
 //   warps 8-15  also fold each finished chunk (tcgen05.ld / tcgen05.st
 //               32x32b) whenever they wait, then store the tile; warp w owns
-//               TMEM lanes 32 (w % 4) .. +31 and columns 64 ((w - 8) / 4) ..
-//               +63.
-// TMEM columns: chunk accumulators 0-127 and 128-255, running sum 256-383.
+//               TMEM lanes 32 (w % 4) .. +31 and columns BN/2 ((w - 8) / 4)
+//               .. + BN/2 - 1.
+// TMEM columns: chunk accumulators below 256, running sum from 256.
 // K-major operands use the 128-byte swizzle; MN-major ones (the matmul VJP's
 // swapLastTwo views, read in place) use the 128-byte swizzle with 32-byte
 // atoms, the only shared-memory layout tcgen05 takes for MN-major TF32.
@@ -65,18 +67,35 @@ static __device__ unsigned int g_gemm_error;
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, THREADS = 512;
-constexpr int RAW = 4;        // stages of raw A/B tiles (the hi operands)
-constexpr int LO = 2;         // slots of lo tiles
-constexpr int KC_BLOCKS = 4;  // K-slices per accumulation chunk (K = 128)
-constexpr int NWORK = 14;     // converter warps (2-15)
-constexpr int NFOLD = 256;    // folding / storing threads (warps 8-15)
-constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;  // 16 KiB each
-constexpr uint32_t RAW_BYTES = A_BYTES + B_BYTES;                   // one stage (and one lo slot)
-constexpr int CONV_ITERS = (RAW_BYTES / 16 + NWORK * 32 - 1) / (NWORK * 32);
-constexpr size_t SMEM_BYTES = (size_t)(RAW + LO) * RAW_BYTES + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 512;   // two chunk accumulators + the running sum
-constexpr uint32_t SUM_COL = 2 * BN;  // first column of the running sum
+constexpr int BM = 128, BK = 32, THREADS = 512;
+constexpr int NWORK = 14;   // converter warps (2-15)
+constexpr int NFOLD = 256;  // folding / storing threads (warps 8-15)
+constexpr uint32_t A_BYTES = BM * BK * 4;  // 16 KiB
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t SUM_COL = 256;  // the running sum starts at TMEM column 256
+
+// The two tile shapes, 128 x BN.
+//   BN = 128: two chunk accumulators (TMEM columns 0-127, 128-255), so the
+//             tensor core never waits for a fold; 4 raw stages.
+//   BN = 256: one chunk accumulator (columns 0-255) and 256-wide K chunks
+//             (the tensor core waits for each fold, ~4% of the time); 2 raw
+//             stages.  Half the shared-memory traffic per flop for A, hence
+//             ~14% faster where the tile count fills the SMs.
+template <int BN_>
+struct Tile {
+    static constexpr int BN = BN_;
+    static constexpr int NBUF = BN_ == 128 ? 2 : 1;
+    static constexpr int KC_BLOCKS = BN_ == 128 ? 4 : 8;  // K-slices per accumulation chunk
+    static constexpr int RAW = BN_ == 128 ? 4 : 2;        // stages of raw A/B tiles (the hi operands)
+    static constexpr int LO = 2;                          // slots of lo tiles
+    static constexpr uint32_t B_BYTES = BN_ * BK * 4;
+    static constexpr uint32_t RAW_BYTES = A_BYTES + B_BYTES;  // one stage (and one lo slot)
+    static constexpr int CONV_ITERS = (RAW_BYTES / 16 + NWORK * 32 - 1) / (NWORK * 32);
+    static constexpr size_t SMEM_BYTES = (size_t)(RAW + LO) * RAW_BYTES + 1024;  // + alignment slack
+    static constexpr int FOLD_COLS = BN_ / 2;  // columns per folding thread
+    static_assert(NBUF * BN_ <= (int)SUM_COL && SUM_COL + BN_ <= TMEM_COLS, "TMEM columns");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
 constexpr uint32_t kGemmSpin = 1u << 24;
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -213,17 +232,19 @@ __device__ __forceinline__ uint4 lo4(const uint4 &x) {
     return out;
 }
 
-// Folds accumulation chunk q (TMEM buffer q & 1) into the running sum at
+// Folds accumulation chunk q (TMEM buffer q % NBUF) into the running sum at
 // SUM_COL with round-to-nearest f32 adds; this warp's 32 lanes, columns
-// half*64 .. +63 (those inside the MMA width).
+// half * FOLD_COLS .. + FOLD_COLS - 1 (those inside the MMA width).
+template <int BN_>
 __device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q, int half, int nmma) {
+    using T = Tile<BN_>;
     asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-        const int col = half * 64 + c * 32;
+    for (int c = 0; c < T::FOLD_COLS / 32; c++) {
+        const int col = half * T::FOLD_COLS + c * 32;
         if (col >= nmma) continue;
         float v[32];
-        tmem_ld32(tmem + lanes + (uint32_t)((q & 1) * BN + col), v);
+        tmem_ld32(tmem + lanes + (uint32_t)((q % T::NBUF) * BN_ + col), v);
         if (q > 0) {
             float sum[32];
             tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)col, sum);
@@ -265,14 +286,14 @@ __device__ __forceinline__ float epi_apply(const Epilogue &e, float c, int64_t r
     return c;
 }
 
-// The epilogue on 64 consecutive columns of one row, all inside C.
-__device__ __forceinline__ void epi_apply64(const Epilogue &e, float (&acc)[64], int64_t row, int64_t col0) {
+// The epilogue on 32 consecutive columns of one row, all inside C.
+__device__ __forceinline__ void epi_apply32(const Epilogue &e, float (&acc)[32], int64_t row, int64_t col0) {
     if (e.mode == EPI_STORE) return;
     if (e.mode == EPI_TANH_GRAD) {
         const float *y = e.aux + row * e.ldaux + col0;
         if ((((uintptr_t)y) & 15) == 0) {
 #pragma unroll
-            for (int v = 0; v < 16; v++) {
+            for (int v = 0; v < 8; v++) {
                 const float4 q = __ldg((const float4 *)y + v);
                 acc[4 * v] = __fmul_rn(acc[4 * v], __fsub_rn(1.0f, __fmul_rn(q.x, q.x)));
                 acc[4 * v + 1] = __fmul_rn(acc[4 * v + 1], __fsub_rn(1.0f, __fmul_rn(q.y, q.y)));
@@ -281,26 +302,29 @@ __device__ __forceinline__ void epi_apply64(const Epilogue &e, float (&acc)[64],
             }
         } else {
 #pragma unroll
-            for (int v = 0; v < 64; v++) acc[v] = __fmul_rn(acc[v], __fsub_rn(1.0f, __fmul_rn(y[v], y[v])));
+            for (int v = 0; v < 32; v++) acc[v] = __fmul_rn(acc[v], __fsub_rn(1.0f, __fmul_rn(y[v], y[v])));
         }
         return;
     }
     const float *b = e.bias + col0;
     if (e.mode == EPI_BIAS_TANH) {
 #pragma unroll
-        for (int v = 0; v < 64; v++) acc[v] = zc_tanhf(__fadd_rn(acc[v], __ldg(b + v)));
+        for (int v = 0; v < 32; v++) acc[v] = zc_tanhf(__fadd_rn(acc[v], __ldg(b + v)));
     } else {
 #pragma unroll
-        for (int v = 0; v < 64; v++) acc[v] = __fadd_rn(acc[v], __ldg(b + v));
+        for (int v = 0; v < 32; v++) acc[v] = __fadd_rn(acc[v], __ldg(b + v));
     }
 }
 
-template <bool TA, bool TB>
+template <bool TA, bool TB, int BN_>
 __global__ void __launch_bounds__(THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ Maps maps, float *__restrict__ C, const __grid_constant__ Params P) {
+    using T = Tile<BN_>;
+    constexpr int BN = BN_, RAW = T::RAW, LO = T::LO, NBUF = T::NBUF, KC_BLOCKS = T::KC_BLOCKS;
+    constexpr uint32_t B_BYTES = T::B_BYTES, RAW_BYTES = T::RAW_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[LO], lofree[LO], tfull[2], tfree[2];
+    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[LO], lofree[LO], tfull[NBUF], tfree[NBUF];
     __shared__ uint32_t tmem_base;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -320,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mb_init(&conv[l], NWORK);
             mb_init(&lofree[l], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NBUF; b++) {
             mb_init(&tfull[b], 1);
             mb_init(&tfree[b], NFOLD);
         }
@@ -361,10 +385,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             const uint32_t ID = P.idesc;
             for (int j = 0; j < KT; j++) {
-                const int s = j % RAW, l = j % LO, q = j / KC_BLOCKS, buf = q & 1;
+                const int s = j % RAW, l = j % LO, q = j / KC_BLOCKS, buf = q % NBUF;
                 const bool first = (j % KC_BLOCKS) == 0;
                 const bool last = (j % KC_BLOCKS) == KC_BLOCKS - 1 || j == KT - 1;
-                if (first && q >= 2 && !mb_wait(&tfree[buf], ((q / 2) - 1) & 1)) break;
+                if (first && q >= NBUF && !mb_wait(&tfree[buf], ((q / NBUF) - 1) & 1)) break;
                 if (!mb_wait(&conv[l], (j / LO) & 1)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t d = tmem + (uint32_t)(buf * BN);
@@ -392,9 +416,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool ok = true;
         // folds every chunk whose MMAs have completed (folder warps only)
         auto try_folds = [&]() {
-            while (folded < NQ && __all_sync(0xffffffffu, mb_test(&tfull[folded & 1], (folded >> 1) & 1))) {
-                fold_chunk(tmem, lanes, folded, half, P.nmma);
-                mb_arrive(&tfree[folded & 1]);
+            while (folded < NQ &&
+                   __all_sync(0xffffffffu, mb_test(&tfull[folded % NBUF], (folded / NBUF) & 1))) {
+                fold_chunk<BN_>(tmem, lanes, folded, half, P.nmma);
+                mb_arrive(&tfree[folded % NBUF]);
                 folded++;
             }
         };
@@ -415,14 +440,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!ok) break;
             const uint4 *src = (const uint4 *)raw_a(s);  // A then B, contiguous
             uint4 *dst = (uint4 *)lo_a(l);
-            uint4 x[CONV_ITERS];
+            uint4 x[T::CONV_ITERS];
 #pragma unroll
-            for (int u = 0; u < CONV_ITERS; u++) {
+            for (int u = 0; u < T::CONV_ITERS; u++) {
                 const int i = wt + u * NWORK * 32;
                 if (i < (int)(RAW_BYTES / 16)) x[u] = src[i];
             }
 #pragma unroll
-            for (int u = 0; u < CONV_ITERS; u++) {
+            for (int u = 0; u < T::CONV_ITERS; u++) {
                 const int i = wt + u * NWORK * 32;
                 if (i < (int)(RAW_BYTES / 16)) dst[i] = lo4(x[u]);
             }
@@ -433,33 +458,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (folder) {
             while (ok && folded < NQ) {
-                if (!mb_wait(&tfull[folded & 1], (folded >> 1) & 1)) {
+                if (!mb_wait(&tfull[folded % NBUF], (folded / NBUF) & 1)) {
                     ok = false;
                     break;
                 }
                 __syncwarp();
-                fold_chunk(tmem, lanes, folded, half, P.nmma);
-                mb_arrive(&tfree[folded & 1]);
+                fold_chunk<BN_>(tmem, lanes, folded, half, P.nmma);
+                mb_arrive(&tfree[folded % NBUF]);
                 folded++;
             }
             const int64_t row = (int64_t)m0 + q4 * 32 + lane;
-            float acc[64];
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;");
-            if (ok && half * 64 < P.nmma) tmem_ld32p(tmem + lanes + SUM_COL + half * 64, acc);
-            if (ok && half * 64 + 32 < P.nmma) tmem_ld32p(tmem + lanes + SUM_COL + half * 64 + 32, acc + 32);
-            if (ok && row < P.M) {
-                float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
-                const int64_t col0 = (int64_t)n0 + half * 64;
-                if (col0 + 64 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
-                    epi_apply64(P.epi, acc, row, col0);
+            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
+#pragma unroll 1
+            for (int c = 0; c < T::FOLD_COLS / 32; c++) {
+                const int cl = half * T::FOLD_COLS + c * 32;
+                if (!ok || cl >= P.nmma) break;
+                float acc[32];
+                tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)cl, acc);
+                const int64_t col0 = (int64_t)n0 + cl;
+                if (row < P.M) {
+                    if (col0 + 32 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
+                        epi_apply32(P.epi, acc, row, col0);
 #pragma unroll
-                    for (int v = 0; v < 16; v++)
-                        *(float4 *)(crow + col0 + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-                } else {
+                        for (int v = 0; v < 8; v++)
+                            *(float4 *)(crow + col0 + 4 * v) =
+                                make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                    } else {
 #pragma unroll
-                    for (int v = 0; v < 64; v++)
-                        if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                        for (int v = 0; v < 32; v++)
+                            if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                    }
                 }
             }
         }
@@ -562,18 +592,39 @@ int64_t max_offset(const GemmBatch &bt, const int64_t *s) {
     return o;
 }
 
-template <bool TA, bool TB>
+template <bool TA, bool TB, int BN_>
 int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
-    auto k = tf32x3_gemm_kernel<TA, TB>;
-    static bool attr = false;
-    if (!attr) {
-        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-        attr = true;
+    auto k = tf32x3_gemm_kernel<TA, TB, BN_>;
+    static bool attr[64] = {false};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64 || !attr[dev]) {
+        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile<BN_>::SMEM_BYTES));
+        if (dev >= 0 && dev < 64) attr[dev] = true;
     }
-    dim3 grid((unsigned)((P.N + BN - 1) / BN), (unsigned)((P.M + BM - 1) / BM), (unsigned)batches);
-    k<<<grid, THREADS, SMEM_BYTES, s>>>(maps, C, P);
+    dim3 grid((unsigned)((P.N + BN_ - 1) / BN_), (unsigned)((P.M + BM - 1) / BM), (unsigned)batches);
+    k<<<grid, THREADS, Tile<BN_>::SMEM_BYTES, s>>>(maps, C, P);
     ZC_LAUNCHED("tf32x3_gemm_kernel");
     return ZPUCUDA_OK;
+}
+
+// Tile width for an m x n x batches problem: the 256-wide tile does a
+// 128 x 256 tile in ~1.75x the time of a 128 x 128 one; pick the width whose
+// whole waves of tiles over the SMs take less time.
+int choose_bn(int64_t m, int64_t n, int64_t batches) {
+    if (n <= 128) return 128;
+    const int64_t sms = num_sms();
+    const int64_t rows = (m + BM - 1) / BM;
+    const int64_t w128 = (rows * ((n + 127) / 128) * batches + sms - 1) / sms;
+    const int64_t w256 = (rows * ((n + 255) / 256) * batches + sms - 1) / sms;
+    return 1.75 * (double)w256 < (double)w128 ? 256 : 128;
+}
+
+template <int BN_>
+int dispatch_tf32x3(bool ta, bool tb, const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
+    if (!ta && !tb) return launch_tf32x3<false, false, BN_>(maps, C, P, batches, s);
+    if (!ta && tb) return launch_tf32x3<false, true, BN_>(maps, C, P, batches, s);
+    if (ta && !tb) return launch_tf32x3<true, false, BN_>(maps, C, P, batches, s);
+    return launch_tf32x3<true, true, BN_>(maps, C, P, batches, s);
 }
 
 }  // namespace
@@ -615,10 +666,11 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
         const int64_t b_inner = tb ? k : n, b_rows = tb ? n : k;
         const int64_t na = mat_a ? max_offset(bt, bt.sa) / mat_a + 1 : 1;
         const int64_t nb = mat_b ? max_offset(bt, bt.sb) / mat_b + 1 : 1;
+        const int bn = choose_bn(m, n, batches);
         Maps maps;
         memset(&maps, 0, sizeof maps);
         tc = make_map(&maps.a, A, a_inner, a_rows, lda, na, mat_a, ta ? 32 : BM, !ta) &&
-             make_map(&maps.b, B, b_inner, b_rows, ldb, nb, mat_b, tb ? BN : 32, tb);
+             make_map(&maps.b, B, b_inner, b_rows, ldb, nb, mat_b, tb ? bn : 32, tb);
         if (tc) {
             Params P;
             memset(&P, 0, sizeof P);
@@ -629,14 +681,12 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
             P.stride_c = stride_c;
             P.mat_a = mat_a;
             P.mat_b = mat_b;
-            P.nmma = (int32_t)(n >= BN ? BN : (n + 15) / 16 * 16);
+            P.nmma = (int32_t)(n >= bn ? bn : (n + 15) / 16 * 16);
             P.idesc = make_idesc(ta, tb, P.nmma);
             P.epi = epi;
             P.bt = bt;
-            if (!ta && !tb) return launch_tf32x3<false, false>(maps, C, P, batches, s);
-            if (!ta && tb) return launch_tf32x3<false, true>(maps, C, P, batches, s);
-            if (ta && !tb) return launch_tf32x3<true, false>(maps, C, P, batches, s);
-            return launch_tf32x3<true, true>(maps, C, P, batches, s);
+            return bn == 256 ? dispatch_tf32x3<256>(ta, tb, maps, C, P, batches, s)
+                             : dispatch_tf32x3<128>(ta, tb, maps, C, P, batches, s);
         }
     }
     dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16), (unsigned)batches);
