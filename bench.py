@@ -459,8 +459,8 @@ def _only_gemm(kind, steps, warmup):
         n, bsz = 1024, 0
         A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
         B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
-    elif kind == "f32_4096":
-        n, bsz = 4096, 0
+    elif kind in ("f32_4096", "f32_8192"):
+        n, bsz = int(kind[4:]), 0
         A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
         B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
     elif kind == "f32_batched":
@@ -480,7 +480,8 @@ def _only_gemm(kind, steps, warmup):
 
 ONLY_CASES = {
     "chain": None, "mlp": None,
-    "gemm_f32_1024": "f32_1024", "gemm_f32_4096": "f32_4096", "gemm_f32_batched": "f32_batched",
+    "gemm_f32_1024": "f32_1024", "gemm_f32_4096": "f32_4096", "gemm_f32_8192": "f32_8192",
+    "gemm_f32_batched": "f32_batched",
     "gemm_f64_4096": "f64_4096",
 }
 
