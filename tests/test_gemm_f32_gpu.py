@@ -121,3 +121,32 @@ def test_nan_propagates_like_the_fma_chain(zc):
     assert np.array_equal(np.isnan(got), np.isnan(want))
     fin = ~np.isnan(want)
     assert rel_fro(got[fin], want[fin]) <= TOL
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("m,k,n", [(256, 8192, 16), (1024, 1024, 1024), (300, 3000, 40), (128, 100000 // 8, 8)])
+def test_split_k_shapes(zc, ta, tb, m, k, n):
+    """Few output tiles and a long K: the K range is split across CTAs and the
+    partials added in split order."""
+    rng = np.random.default_rng(m + k + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    want = zo.gemm(a, b)
+    A = dev(a.T.copy()) if ta else dev(a)
+    B = dev(b.T.copy()) if tb else dev(b)
+    got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+    check_no_device_error(zc)
+    assert rel_fro(got, want) <= TOL, (m, k, n, ta, tb, rel_fro(got, want))
+    again = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+    assert np.array_equal(got, again)  # deterministic
+
+
+def test_split_k_batched(zc):
+    rng = np.random.default_rng(11)
+    a = rng.uniform(-1, 1, (3, 128, 4096)).astype(np.float32)
+    b = rng.uniform(-1, 1, (3, 4096, 64)).astype(np.float32)
+    got = zc.gemm(dev(a), dev(b)).cpu().numpy()
+    check_no_device_error(zc)
+    for i in range(3):
+        assert rel_fro(got[i], zo.gemm(a[i], b[i])) <= TOL

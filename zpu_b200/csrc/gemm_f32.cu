@@ -265,6 +265,8 @@ struct Params {
     int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
     int32_t nmma;          // MMA width: N rounded up to 16, at most BN
     uint32_t idesc;
+    int32_t splits;        // K split across this many CTAs (blockIdx.z = batch * splits + split)
+    int32_t kb_per_split;  // 32-wide K slices per split
     Epilogue epi;
     GemmBatch bt;
 };
@@ -329,10 +331,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t oa, ob;
-    batch_offsets(P.bt, blockIdx.z, &oa, &ob);
+    const int split = (int)(blockIdx.z % (unsigned)P.splits);
+    const int64_t bz = blockIdx.z / (unsigned)P.splits;
+    batch_offsets(P.bt, bz, &oa, &ob);
     const int za = (int)(P.mat_a ? oa / P.mat_a : 0), zb = (int)(P.mat_b ? ob / P.mat_b : 0);
     const int m0 = (int)blockIdx.y * BM, n0 = (int)blockIdx.x * BN;
-    const int KT = (int)((P.K + BK - 1) / BK);
+    const int kb0 = split * P.kb_per_split;  // this CTA's first K slice
+    const int KT = min((int)((P.K + BK - 1) / BK) - kb0, P.kb_per_split);
     const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
 
     if (threadIdx.x == 0) {
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int s = j % RAW;
                 if (j >= RAW && !mb_wait(&empty[s], ((j / RAW) - 1) & 1)) break;
                 mb_expect_tx(&full[s], A_BYTES + B_BYTES);
-                const int k0 = j * BK;
+                const int k0 = (kb0 + j) * BK;
                 if (!TA) tma_load_3d(raw_a(s), &maps.a, k0, m0, za, &full[s]);
                 else
                     for (int c = 0; c < BM / 32; c++) tma_load_3d(raw_a(s) + c * 4096, &maps.a, m0 + 32 * c, k0, za, &full[s]);
@@ -470,7 +475,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t row = (int64_t)m0 + q4 * 32 + lane;
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;");
-            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;
+            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
 #pragma unroll 1
             for (int c = 0; c < T::FOLD_COLS / 32; c++) {
                 const int cl = half * T::FOLD_COLS + c * 32;
@@ -537,6 +542,60 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
 
 // ------------------------------------------------------------- host side
 
+// Split-K: C = epilogue(sum over s of ws[(batch * splits + s)][m][n]), the
+// partials added in split order (deterministic).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ ws, int splits, int64_t m,
+                                                            int64_t n, int64_t batches, float *__restrict__ C,
+                                                            int64_t ldc, int64_t stride_c,
+                                                            const __grid_constant__ Epilogue epi) {
+    const int64_t mn = m * n, total = batches * mn;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / mn, r = (i / n) % m, c = i % n;
+        const float *p = ws + b * splits * mn + r * n + c;
+        float acc = p[0];
+        for (int sp = 1; sp < splits; sp++) acc = __fadd_rn(acc, p[sp * mn]);
+        C[b * stride_c + r * ldc + c] = epi_apply(epi, acc, r, c);
+    }
+}
+
+// Stream-ordered scratch for split-K partials: one memory pool per device
+// that keeps what it has allocated (no release at synchronisation).
+cudaMemPool_t splitk_pool() {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {nullptr};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props;
+        memset(&props, 0, sizeof props);
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        pools[dev] = pool;
+    }
+    return pools[dev];
+}
+
+// K splits for a problem of `tiles` output tiles and KT K slices: enough CTAs
+// to cover the SMs when the tiles alone fill less than half of them, with at
+// least two accumulation chunks per split.
+int choose_splits(int64_t tiles, int64_t KT, int kc) {
+    const int64_t sms = num_sms();
+    if (tiles * 2 > sms) return 1;
+    int64_t sp = sms / tiles;
+    if (sp > KT / (2 * kc)) sp = KT / (2 * kc);
+    if (sp > 16) sp = 16;
+    return sp < 1 ? 1 : (int)sp;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int encode_fn() {
@@ -601,7 +660,7 @@ int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, 
         ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile<BN_>::SMEM_BYTES));
         if (dev >= 0 && dev < 64) attr[dev] = true;
     }
-    dim3 grid((unsigned)((P.N + BN_ - 1) / BN_), (unsigned)((P.M + BM - 1) / BM), (unsigned)batches);
+    dim3 grid((unsigned)((P.N + BN_ - 1) / BN_), (unsigned)((P.M + BM - 1) / BM), (unsigned)(batches * P.splits));
     k<<<grid, THREADS, Tile<BN_>::SMEM_BYTES, s>>>(maps, C, P);
     ZC_LAUNCHED("tf32x3_gemm_kernel");
     return ZPUCUDA_OK;
@@ -685,8 +744,43 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
             P.idesc = make_idesc(ta, tb, P.nmma);
             P.epi = epi;
             P.bt = bt;
-            return bn == 256 ? dispatch_tf32x3<256>(ta, tb, maps, C, P, batches, s)
-                             : dispatch_tf32x3<128>(ta, tb, maps, C, P, batches, s);
+            const int64_t KT = (k + BK - 1) / BK;
+            const int64_t tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn) * batches;
+            int splits = choose_splits(tiles, KT, bn == 256 ? Tile<256>::KC_BLOCKS : Tile<128>::KC_BLOCKS);
+            if (batches * splits > 65535) splits = 1;
+            float *ws = nullptr;
+            cudaMemPool_t pool = splits > 1 ? splitk_pool() : nullptr;
+            if (splits > 1 &&
+                (!pool || cudaMallocFromPoolAsync((void **)&ws, (size_t)(splits * batches * m * n) * sizeof(float),
+                                                  pool, s) != cudaSuccess)) {
+                cudaGetLastError();
+                splits = 1;  // no scratch: one CTA per tile over the whole K
+                ws = nullptr;
+            }
+            P.splits = splits;
+            P.kb_per_split = (int32_t)((KT + splits - 1) / splits);
+            if (splits > 1) {  // every split writes raw partial sums into ws
+                P.splits = splits = (int)((KT + P.kb_per_split - 1) / P.kb_per_split);
+                P.ldc = n;
+                P.stride_c = m * n;
+                P.epi = Epilogue{};
+            }
+            int st = bn == 256 ? dispatch_tf32x3<256>(ta, tb, maps, splits > 1 ? ws : C, P, batches, s)
+                               : dispatch_tf32x3<128>(ta, tb, maps, splits > 1 ? ws : C, P, batches, s);
+            if (splits > 1) {
+                if (st == ZPUCUDA_OK) {
+                    const int64_t total = batches * m * n;
+                    int64_t blocks = (total + 255) / 256;
+                    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+                    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(ws, splits, m, n, batches, C, ldc, stride_c,
+                                                                          epi);
+                    cudaError_t e = cudaGetLastError();
+                    if (e != cudaSuccess) st = cuda_fail(e, "splitk_reduce_kernel");
+                    else count_launch();
+                }
+                cudaFreeAsync(ws, s);
+            }
+            return st;
         }
     }
     dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16), (unsigned)batches);
