@@ -206,40 +206,77 @@ def _time_events(fn, reps, warm=2):
     return e0.elapsed_time(e1) / reps
 
 
-def gemm_configs():
+def _max_over_ranks(ms, world, dev):
+    if world == 1:
+        return ms
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch
+        torch.distributed.barrier()
+
+
+# 2-D output-tile grids for the f64 GEMM at 1, 2, 4, 8 ranks
+F64_GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
+
+
+def gemm_configs(rank=0, world=1, dev="cuda"):
     """The GEMM workloads of the hot path, each timed with CUDA events on
-    device-resident inputs (zpu's RNG streams, seeds per config):
-    1: f32 1024^3 U[-1,1]; 3: vmap-batched 256 x 512^3, N(0, 1/512);
-    5: f64 8192^3 N(0,1)."""
+    device-resident inputs (zpu's RNG streams, seeds per config), max over
+    ranks, no data-path collective:
+    1: f32 1024^3 U[-1,1], replicas (too small to split);
+    3: vmap-batched 256 x 512^3 N(0, 1/512), rank r computes matrices
+       [256 r / N, 256 (r+1) / N);
+    5: f64 8192^3 N(0,1), 2-D output tiles on a 1x1 / 1x2 / 2x2 / 2x4 grid,
+       each rank's A row panel and B column panel staged in its own HBM."""
     import torch
     import zpu_b200 as zc
     tf32, fp64, src = _peak_tflops()
     out = {}
     n = 1024
-    A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0).view(n, n)
-    B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0).view(n, n)
-    C = torch.empty(n, n, device="cuda")
-    ms = _time_events(lambda: zc.matmul(A, B, out=C), 20)
+    A = zc.rng_uniform(0x5EED0001, n * n, -1.0, 1.0, device=dev).view(n, n)
+    B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0, device=dev).view(n, n)
+    C = torch.empty(n, n, device=dev)
+    _barrier(world)
+    ms = _max_over_ranks(_time_events(lambda: zc.matmul(A, B, out=C), 20), world, dev)
     t = 2 * n ** 3 / ms / 1e9
-    out["config1_f32_gemm_1024"] = {"tflops": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3),
-                                    "ceiling_tflops": tf32 / 3, "ceiling_source": src}
+    out["config1_f32_gemm_1024"] = {"tflops_per_replica": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3),
+                                    "ceiling_tflops": tf32 / 3, "ceiling_source": src,
+                                    "parallelism": "replicas (%d)" % world}
     bsz, n = 256, 512
     s = 1.0 / (512.0 ** 0.5)
-    A = (zc.rng_normal(0x5EED0004, bsz * n * n) * s).view(bsz, n, n)
-    B = (zc.rng_normal(0x5EED0005, bsz * n * n) * s).view(bsz, n, n)
-    C = torch.empty(bsz, n, n, device="cuda")
-    ms = _time_events(lambda: zc.matmul(A, B, a_depth=1, b_depth=1, out=C), 10)
+    A = (zc.rng_normal(0x5EED0004, bsz * n * n, device=dev) * s).view(bsz, n, n)
+    B = (zc.rng_normal(0x5EED0005, bsz * n * n, device=dev) * s).view(bsz, n, n)
+    per = bsz // world
+    A, B = A[rank * per:(rank + 1) * per].contiguous(), B[rank * per:(rank + 1) * per].contiguous()
+    C = torch.empty(per, n, n, device=dev)
+    _barrier(world)
+    ms = _max_over_ranks(_time_events(lambda: zc.matmul(A, B, a_depth=1, b_depth=1, out=C), 10), world, dev)
     t = bsz * 2 * n ** 3 / ms / 1e9
-    out["config3_vmap_batched_f32_256x512"] = {"tflops": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3)}
+    out["config3_vmap_batched_f32_256x512"] = {"tflops": t, "ms": ms, "tflops_per_gpu": t / world,
+                                               "frac_of_3xtf32_ceiling_per_gpu": t / world / (tf32 / 3),
+                                               "parallelism": "batch axis over %d GPUs, %d matrices each" % (world, per)}
     del A, B, C
     n = 8192
-    A = zc.rng_normal(0x5EED0008, n * n, dtype=torch.float64).view(n, n)
-    B = zc.rng_normal(0x5EED0009, n * n, dtype=torch.float64).view(n, n)
-    C = torch.empty(n, n, dtype=torch.float64, device="cuda")
-    ms = _time_events(lambda: zc.matmul(A, B, out=C), 3, warm=1)
+    gr, gc = F64_GRIDS.get(world, (1, world))
+    i, j = rank // gc, rank % gc
+    rows, cols = n // gr, n // gc
+    A = zc.rng_normal(0x5EED0008, n * n, dtype=torch.float64, device=dev).view(n, n)[i * rows:(i + 1) * rows].contiguous()
+    B = zc.rng_normal(0x5EED0009, n * n, dtype=torch.float64, device=dev).view(n, n)[:, j * cols:(j + 1) * cols].contiguous()
+    C = torch.empty(rows, cols, dtype=torch.float64, device=dev)
+    torch.cuda.empty_cache()
+    _barrier(world)
+    ms = _max_over_ranks(_time_events(lambda: zc.matmul(A, B, out=C), 3, warm=1), world, dev)
     t = 2 * n ** 3 / ms / 1e9
-    out["config5_f64_gemm_8192"] = {"tflops": t, "ms": ms, "frac_of_fp64_nominal": t / fp64,
-                                    "fp64_peak_tflops": fp64, "fp64_peak_source": "nominal B200"}
+    out["config5_f64_gemm_8192"] = {"tflops": t, "ms": ms, "tflops_per_gpu": t / world,
+                                    "frac_of_fp64_nominal_per_gpu": t / world / fp64, "fp64_peak_tflops": fp64,
+                                    "fp64_peak_source": "nominal B200",
+                                    "parallelism": "2-D output tiles %dx%d" % (gr, gc)}
     del A, B, C
     torch.cuda.empty_cache()
     return out
@@ -292,18 +329,40 @@ def mlp_config(rank, world, steps, warmup, dev):
     torch.cuda.synchronize()
     launches = zc.launch_count() - l0
     ms = e0.elapsed_time(e1) / steps
-    # end to end: pinned host X / labels -> HBM, the step, loss -> host
+    # end to end: every step copies its X / labels from pinned host memory
+    # into HBM and its loss back to the host.  The copies run on a side stream
+    # into two alternating device buffers, so step i+1's input crosses PCIe
+    # while step i computes.
     xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
     lh = torch.empty(1, dtype=torch.float32).pin_memory()
+    xs_, ys_ = [x, torch.empty_like(x)], [y, torch.empty_like(y)]
+    copy_stream = torch.cuda.Stream(device=dev)
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    used = [torch.cuda.Event(), torch.cuda.Event()]
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(steps):
-        x.copy_(xh, non_blocking=True)
-        y.copy_(yh, non_blocking=True)
-        m.train_step(x, y, global_batch=MLP_BATCH)
+    copy_stream.wait_event(e2)
+
+    def issue_copy(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            if i >= 2:
+                copy_stream.wait_event(used[b])
+            xs_[b].copy_(xh, non_blocking=True)
+            ys_[b].copy_(yh, non_blocking=True)
+            copied[b].record(copy_stream)
+
+    issue_copy(0)
+    for i in range(steps):
+        if i + 1 < steps:
+            issue_copy(i + 1)
+        b = i % 2
+        stream.wait_event(copied[b])
+        m.train_step(xs_[b], ys_[b], global_batch=MLP_BATCH)
+        used[b].record(stream)
         m.loss_to(lh.data_ptr())
     e3.record(stream)
     torch.cuda.synchronize()
@@ -438,7 +497,7 @@ def run_ours(args):
         "clocks": clk,
         "warmup_soak_steps": soak,
     }
-    line["other_configs"] = gemm_configs() if world == 1 else {}
+    line["other_configs"] = gemm_configs(rank, world, dev)
     line["other_configs"]["config4_mlp_train_step"] = mlp_config(rank, world, min(args.steps, 20), args.warmup, dev)
     if rank == 0 and world == 1:
         gbs, cores, sample, per = cpu_chain_baseline()
@@ -492,10 +551,20 @@ def run_only(args):
     import torch
     import numpy as np
     import zpu_b200 as zc
-    torch.cuda.set_device(0)
-    zc.check(zc.lib().zpucuda_init(0))
-    if args.only == "mlp":
-        out = mlp_config(0, 1, args.steps, args.warmup, torch.device("cuda", 0))
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    zc.check(zc.lib().zpucuda_init(local))
+    if args.only == "mlp":  # the only case that runs under torchrun (data parallel)
+        if world > 1:
+            import datetime
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                                 device_id=torch.device("cuda", local))
+        out = mlp_config(rank, world, args.steps, args.warmup, torch.device("cuda", local))
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        if rank != 0:
+            return 0
     elif args.only == "chain":
         x = zc.rng_normal(SEED_X, N_ELEM)
         steps_def = [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0), ("mul", [11, 2], 12, -2, 0),

@@ -248,7 +248,7 @@ int zpucuda_nccl_destroy(int64_t timeout_ms);
  * labels) (src/zpu/nn.zig:123-134,190-194), its gradients as
  * zpu.valueAndGrad computes them (src/zpu/transforms.zig:87-148,
  * src/zpu/autodiff.zig:51,323-330,451-454,480-487), and Adam.step with f32
- * moments (src/zpu/optim.zig:149-259), lowered to 13 kernels per step.
+ * moments (src/zpu/optim.zig:149-259), lowered to 14 kernels per step.
  * Parameters are numbered in the reference's argument order: 0 W1 [d_in,d_h1],
  * 1 b1 [d_h1], 2 W2 [d_h1,d_h2], 3 b2 [d_h2], 4 W3 [d_h2,d_out], 5 b3 [d_out],
  * row-major as the reference stores them; the handle owns the parameters,
@@ -258,7 +258,8 @@ int zpucuda_nccl_destroy(int64_t timeout_ms);
  *    to any host or device pointer (numel = the parameter's element count),
  *    asynchronously on `stream`.
  *  array: the device address and length (floats, padding included) of a
- *    whole array -- for callers that exchange it themselves.
+ *    whole array -- for callers that exchange it themselves; param_offset:
+ *    where parameter i starts in it and its row pitch (floats).
  *  adam_config: Adam's lr, beta1, beta2, eps (defaults 1e-3, 0.9, 0.999,
  *    1e-8: optim.AdamConfig); weight decay is not supported.
  *  value_and_grad: gradients of the loss over d_x [batch, d_in] f32 (16-byte
@@ -269,9 +270,13 @@ int zpucuda_nccl_destroy(int64_t timeout_ms);
  *  allreduce_grads: sums the GRAD array and the loss over the device's NCCL
  *    communicator (no-op without one).
  *  adam_step: one Adam.step with the GRAD array (step counter inside).
- *  train_step: value_and_grad, the gradient sum across ranks when the device
- *    has a communicator (two buckets on a side stream, overlapping the last
- *    backward GEMMs), and adam_step.
+ *  train_step: value_and_grad, the gradient exchange when the device has a
+ *    communicator (two buckets on a side stream, overlapping the last
+ *    backward GEMMs), and one Adam.step.  With a communicator each bucket is
+ *    reduce-scattered, every rank updates its 1/world shard and the
+ *    parameters are all-gathered, so afterwards the parameters are complete
+ *    on every rank but the GRAD and ADAM_M/V arrays only in the rank's own
+ *    shards.
  *  loss: copies the last loss (f32) to dst (host or device) on `stream`.
  *  check: synchronous; ZPUCUDA_ERR_INDEX_OUT_OF_RANGE when a label of an
  *    earlier step was outside [0, d_out) (nn.oneHot's error; that row's
@@ -287,6 +292,7 @@ int zpucuda_mlp_param_count(const zpucuda_mlp *h, int64_t *count);
 int zpucuda_mlp_write(zpucuda_mlp *h, int what, int i, const float *src, int64_t numel, void *stream);
 int zpucuda_mlp_read(const zpucuda_mlp *h, int what, int i, float *dst, int64_t numel, void *stream);
 int zpucuda_mlp_array(const zpucuda_mlp *h, int what, float **d_ptr, int64_t *n);
+int zpucuda_mlp_param_offset(const zpucuda_mlp *h, int i, int64_t *offset, int64_t *ld);
 int zpucuda_mlp_adam_config(zpucuda_mlp *h, double lr, double beta1, double beta2, double eps);
 int zpucuda_mlp_value_and_grad(zpucuda_mlp *h, const float *d_x, const int64_t *d_labels, int64_t batch,
                                int64_t global_batch, void *stream);

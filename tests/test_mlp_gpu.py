@@ -149,11 +149,11 @@ def test_padding_stays_zero(zc):
         host = np.empty(n, dtype=np.float32)
         zc.check(L.zpucuda_buf_download(buf, 0, host.ctypes.data, n * 4))
         L.zpucuda_buf_release(buf)
-        # W3 starts after W1 b1 W2 b2 (each rounded up to 64 floats)
-        r = lambda x: (x + 63) // 64 * 64
-        off = r(64 * 96) + r(96) + r(96 * 80) + r(80)
+        off, ld = m.param_offset(4)
+        boff, _ = m.param_offset(5)
+        assert ld == 16 and boff >= off + 80 * 16
         w3 = host[off:off + 80 * 16].reshape(80, 16)
-        b3 = host[off + r(80 * 16):off + r(80 * 16) + 16]
+        b3 = host[boff:boff + 16]
         assert not w3[:, 10:].any() and not b3[10:].any(), what
         if what in (0, 1):
             assert w3[:, :10].any()

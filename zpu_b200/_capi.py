@@ -117,6 +117,7 @@ SIGNATURES = {
     "zpucuda_mlp_write": (I32, [P, I32, I32, P, I64, P]),
     "zpucuda_mlp_read": (I32, [P, I32, I32, P, I64, P]),
     "zpucuda_mlp_array": (I32, [P, I32, C.POINTER(P), C.POINTER(I64)]),
+    "zpucuda_mlp_param_offset": (I32, [P, I32, C.POINTER(I64), C.POINTER(I64)]),
     "zpucuda_mlp_adam_config": (I32, [P, C.c_double, C.c_double, C.c_double, C.c_double]),
     "zpucuda_mlp_value_and_grad": (I32, [P, P, P, I64, I64, P]),
     "zpucuda_mlp_allreduce_grads": (I32, [P, P]),

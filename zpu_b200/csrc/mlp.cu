@@ -6,7 +6,7 @@
 // src/zpu/ops.zig:998-1010), the reverse sweep's rules for matmul, tanh, sum
 // and the broadcast bias (src/zpu/autodiff.zig:51,323-330,451-454,480-487),
 // then Adam.step with f32 moment state (src/zpu/optim.zig:183-259).
-// Here the same arithmetic is lowered to 13 kernel launches over buffers that
+// Here the same arithmetic is lowered to 14 kernel launches over buffers that
 // stay in HBM:
 //   forward   3 GEMMs; bias + tanh run in the first two GEMMs' epilogues,
 //             the bias of the logits in the third's;
@@ -19,7 +19,7 @@
 //             views in the reference, materialised there by toContiguous,
 //             src/zpu/tensor.zig:395-404) are read in place as MN-major
 //             tiles; bias gradients are column sums (unbroadcast);
-//   update    one fused Adam kernel over every parameter.
+//   update    the fused Adam kernel, once per gradient bucket (below).
 // Layout in HBM: parameters, gradients and both Adam moments are one
 // contiguous f32 array each, parameters in the order W1 b1 W2 b2 W3 b3, each
 // starting on a 256-byte boundary.  The output layer is padded to a multiple
@@ -34,7 +34,13 @@
 // batch with the loss scaled by 1/global_batch, and the gradient array is
 // summed across ranks in two buckets on a side stream: [W2 .. end] (plus the
 // loss) as soon as dW2 is done, overlapping the last two backward GEMMs, and
-// [W1, b1] at the end.  Every rank then applies the same Adam update.
+// [W1, b1] at the end.  In the full train step each bucket is reduce-
+// scattered instead, each rank runs Adam on its 1/world shard and the
+// parameters are all-gathered (same bytes, a world-th of the optimizer work),
+// all on the side stream: [W2 .. end] as soon as its sum is in and the g1 GEMM
+// has read W2 (overlapping dW1), [W1, b1] last.  The same per-bucket Adam
+// split runs on one GPU, without the exchange.  (After a data-parallel step
+// a rank's gradient and moment arrays are final only in its own shards.)
 #include <math.h>
 #include <string.h>
 
@@ -50,6 +56,9 @@ constexpr int kXentThreads = 256;
 constexpr int kColThreads = 256;
 constexpr int kColRows = 128;   // rows summed by one column-sum block
 constexpr int64_t kAlign = 64;  // floats: 256-byte parameter alignment
+// floats: the two gradient buckets ([W1, b1] and [W2 .. b3]) are padded to
+// this, so any world size dividing 256 cuts them into float4-aligned shards
+constexpr int64_t kBucketAlign = 1024;
 constexpr int kTail = 64;       // floats after the gradients: [0] = loss
 constexpr int kMaxOut = 64;     // widest output layer the loss kernel takes
 
@@ -285,7 +294,7 @@ struct zpucuda_mlp {
     int64_t t = 0;  // Adam steps taken
     double lr = 1e-3, beta1 = 0.9, beta2 = 0.999, eps = 1e-8;
     cudaStream_t comm_stream = nullptr;
-    cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_done = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_w2 = nullptr, ev_done = nullptr;
     std::mutex mu;
 
     float *loss_ptr() const { return grads + total; }
@@ -309,6 +318,7 @@ void free_mlp(zpucuda_mlp *h) {
     if (h->counters) cudaFree(h->counters);
     if (h->ev_a) cudaEventDestroy(h->ev_a);
     if (h->ev_b) cudaEventDestroy(h->ev_b);
+    if (h->ev_w2) cudaEventDestroy(h->ev_w2);
     if (h->ev_done) cudaEventDestroy(h->ev_done);
     if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
     delete h;
@@ -357,8 +367,16 @@ Epilogue epi(int32_t mode, const float *bias, const float *aux = nullptr, int64_
 
 // Forward, loss and backward.  With `ar` set, the gradient buckets are summed
 // across ranks on the side stream as they become ready.
+AdamConsts adam_consts(zpucuda_mlp *h);
+int adam_range(zpucuda_mlp *h, const AdamConsts &c, int64_t off, int64_t n, cudaStream_t s);
+
+// Forward, loss and backward.  With `ar` set, the gradient buckets are summed
+// across ranks on the side stream as they become ready; with `adam` set, the
+// Adam update of each bucket follows on the side stream too: [W2 .. b3] once
+// its gradients are final and the g1 GEMM has read W2, overlapping dW1, then
+// [W1, b1] at the end.
 int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_t B, int64_t global_b, bool ar,
-                   cudaStream_t s) {
+                   bool adam, cudaStream_t s) {
     const int64_t d0 = h->d[0], d1 = h->d[1], d2 = h->d[2], d3 = h->d[3], d3p = h->d3p;
     const float *W1 = h->params + h->off[0], *b1 = h->params + h->off[1];
     const float *W2 = h->params + h->off[2], *b2 = h->params + h->off[3];
@@ -392,26 +410,60 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     // layer 2
     ZC_TRY(colsum(h, 1, h->ga2, B, d2, d2, gb2, s));
     ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s));
+    cudaStream_t side = h->comm_stream;
+    // With a communicator and Adam in the step, each rank updates only its
+    // 1/world shard of each bucket: reduce-scatter the gradients, Adam on the
+    // shard, all-gather the parameters (the same bytes as an allreduce, and a
+    // world-th of the optimizer work).
+    int rank = 0;
+    const int world = ar ? nccl_world(&rank) : 1;
+    const int64_t nA = h->total - h->off[2], nB = h->off[2];
+    const bool shard = ar && adam && nA % (4 * world) == 0 && nB % (4 * world) == 0;
     if (ar) {
         ZC_CUDA(cudaEventRecord(h->ev_a, s));
-        ZC_CUDA(cudaStreamWaitEvent(h->comm_stream, h->ev_a, 0));
-        ZC_TRY(nccl_allreduce_sum_f32(h->grads + h->off[2], h->total - h->off[2] + 1, h->comm_stream));
+        ZC_CUDA(cudaStreamWaitEvent(side, h->ev_a, 0));
+        if (shard) {
+            ZC_TRY(nccl_reduce_scatter_sum_f32(h->grads + h->off[2], nA / world, side));
+            ZC_TRY(nccl_allreduce_sum_f32(h->loss_ptr(), 1, side));
+        } else {
+            ZC_TRY(nccl_allreduce_sum_f32(h->grads + h->off[2], nA + 1, side));
+        }
     }
     ZC_TRY(gemm(h->ga2, W2, h->ga1, B, d1, d2, d2, d2, d1, false, true, epi(EPI_TANH_GRAD, nullptr, h->a1, d1), s));
+    AdamConsts ac;
+    if (adam) {  // every later kernel on s leaves W2, b2, W3, b3 alone
+        ac = adam_consts(h);
+        ZC_CUDA(cudaEventRecord(h->ev_w2, s));
+        ZC_CUDA(cudaStreamWaitEvent(side, h->ev_w2, 0));
+        if (shard) {
+            ZC_TRY(adam_range(h, ac, h->off[2] + rank * (nA / world), nA / world, side));
+            ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], nA / world, side));
+        } else {
+            ZC_TRY(adam_range(h, ac, h->off[2], nA, side));
+        }
+    }
     // layer 1
     ZC_TRY(colsum(h, 0, h->ga1, B, d1, d1, gb1, s));
     ZC_TRY(gemm(x, h->ga1, gW1, d0, d1, B, d0, d1, d1, true, false, Epilogue{}, s));
-    if (ar) {
+    if (ar || adam) {
         ZC_CUDA(cudaEventRecord(h->ev_b, s));
-        ZC_CUDA(cudaStreamWaitEvent(h->comm_stream, h->ev_b, 0));
-        ZC_TRY(nccl_allreduce_sum_f32(h->grads, h->off[2], h->comm_stream));
-        ZC_CUDA(cudaEventRecord(h->ev_done, h->comm_stream));
+        ZC_CUDA(cudaStreamWaitEvent(side, h->ev_b, 0));
+        if (shard) {
+            ZC_TRY(nccl_reduce_scatter_sum_f32(h->grads, nB / world, side));
+            ZC_TRY(adam_range(h, ac, rank * (nB / world), nB / world, side));
+            ZC_TRY(nccl_all_gather_f32(h->params, nB / world, side));
+        } else {
+            if (ar) ZC_TRY(nccl_allreduce_sum_f32(h->grads, nB, side));
+            if (adam) ZC_TRY(adam_range(h, ac, 0, nB, side));
+        }
+        ZC_CUDA(cudaEventRecord(h->ev_done, side));
         ZC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
     }
     return ZPUCUDA_OK;
 }
 
-int adam_step(zpucuda_mlp *h, cudaStream_t s) {
+// One Adam.step's constants (the step counter advances).
+AdamConsts adam_consts(zpucuda_mlp *h) {
     h->t += 1;
     const double bc1 = 1.0 - zig_pow(h->beta1, (double)h->t);
     const double bc2 = 1.0 - zig_pow(h->beta2, (double)h->t);
@@ -424,14 +476,25 @@ int adam_step(zpucuda_mlp *h, cudaStream_t s) {
     c.bc2 = (float)bc2;
     c.eps = (float)h->eps;
     c.lr = (float)h->lr;
-    const int64_t n4 = h->total / 4;
+    return c;
+}
+
+// Adam over floats [off, off + n) of the arrays (off and n multiples of 4).
+int adam_range(zpucuda_mlp *h, const AdamConsts &c, int64_t off, int64_t n, cudaStream_t s) {
+    const int64_t n4 = n / 4;
     int64_t blocks = (n4 + 255) / 256;
     const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    adam_kernel<<<(unsigned)blocks, 256, 0, s>>>((float4 *)h->params, (const float4 *)h->grads, (float4 *)h->m,
-                                                 (float4 *)h->v, n4, c);
+    if (blocks < 1) return ZPUCUDA_OK;
+    adam_kernel<<<(unsigned)blocks, 256, 0, s>>>((float4 *)(h->params + off), (const float4 *)(h->grads + off),
+                                                 (float4 *)(h->m + off), (float4 *)(h->v + off), n4, c);
     ZC_LAUNCHED("adam_kernel");
     return ZPUCUDA_OK;
+}
+
+int adam_step(zpucuda_mlp *h, cudaStream_t s) {
+    const AdamConsts c = adam_consts(h);
+    return adam_range(h, c, 0, h->total, s);
 }
 
 int check_step_args(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_t B, int64_t global_b) {
@@ -483,10 +546,11 @@ extern "C" int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int6
         h->rows[i] = r[i];
         h->cols[i] = c[i];
         h->ld[i] = l[i];
+        if (i == 2) o = round_up(o, kBucketAlign);  // bucket [W2 .. b3] starts here
         h->off[i] = o;
         o += round_up(r[i] * l[i], kAlign);
     }
-    h->total = o;
+    h->total = round_up(o, kBucketAlign);
     const int64_t R = (max_batch + kColRows - 1) / kColRows;
     const int64_t widths[3] = {d_h1, d_h2, h->d3p};
     int64_t n_counters = 2;
@@ -520,6 +584,7 @@ extern "C" int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int6
                                  cudaStreamCreateWithFlags(&h->comm_stream, cudaStreamNonBlocking),
                                  cudaEventCreateWithFlags(&h->ev_a, cudaEventDisableTiming),
                                  cudaEventCreateWithFlags(&h->ev_b, cudaEventDisableTiming),
+                                 cudaEventCreateWithFlags(&h->ev_w2, cudaEventDisableTiming),
                                  cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming)};
         for (cudaError_t x : e)
             if (x != cudaSuccess && !st) st = cuda_fail(x, "mlp_create setup");
@@ -541,6 +606,13 @@ extern "C" void zpucuda_mlp_destroy(zpucuda_mlp *h) {
 extern "C" int zpucuda_mlp_param_numel(const zpucuda_mlp *h, int i, int64_t *numel) {
     if (!h || !numel || i < 0 || i > 5) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_param_numel");
     *numel = h->rows[i] * h->cols[i];
+    return ZPUCUDA_OK;
+}
+
+extern "C" int zpucuda_mlp_param_offset(const zpucuda_mlp *h, int i, int64_t *offset, int64_t *ld) {
+    if (!h || !offset || !ld || i < 0 || i > 5) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_param_offset");
+    *offset = h->off[i];
+    *ld = h->ld[i];
     return ZPUCUDA_OK;
 }
 
@@ -594,7 +666,7 @@ extern "C" int zpucuda_mlp_value_and_grad(zpucuda_mlp *h, const float *d_x, cons
                                           int64_t global_batch, void *stream) {
     ZC_TRY(check_step_args(h, d_x, d_labels, batch, global_batch));
     std::lock_guard<std::mutex> lk(h->mu);
-    return value_and_grad(h, d_x, d_labels, batch, global_batch, false, resolve_stream(stream));
+    return value_and_grad(h, d_x, d_labels, batch, global_batch, false, false, resolve_stream(stream));
 }
 
 extern "C" int zpucuda_mlp_allreduce_grads(zpucuda_mlp *h, void *stream) {
@@ -615,8 +687,7 @@ extern "C" int zpucuda_mlp_train_step(zpucuda_mlp *h, const float *d_x, const in
     ZC_TRY(check_step_args(h, d_x, d_labels, batch, global_batch));
     std::lock_guard<std::mutex> lk(h->mu);
     cudaStream_t s = resolve_stream(stream);
-    ZC_TRY(value_and_grad(h, d_x, d_labels, batch, global_batch, nccl_world(nullptr) > 1, s));
-    return adam_step(h, s);
+    return value_and_grad(h, d_x, d_labels, batch, global_batch, nccl_world(nullptr) > 1, true, s);
 }
 
 extern "C" int zpucuda_mlp_loss(const zpucuda_mlp *h, float *dst, void *stream) {

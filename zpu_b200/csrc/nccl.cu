@@ -31,6 +31,9 @@ struct NcclApi {
     ncclResult_t (*init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
     ncclResult_t (*async_error)(ncclComm_t, ncclResult_t *);
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                   cudaStream_t);
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*abort)(ncclComm_t);
     ncclResult_t (*finalize)(ncclComm_t);
     ncclResult_t (*destroy)(ncclComm_t);
@@ -68,6 +71,8 @@ int load_api() {
     g_api.init_rank_config = (decltype(g_api.init_rank_config))sym("ncclCommInitRankConfig");
     g_api.async_error = (decltype(g_api.async_error))sym("ncclCommGetAsyncError");
     g_api.all_reduce = (decltype(g_api.all_reduce))sym("ncclAllReduce");
+    g_api.reduce_scatter = (decltype(g_api.reduce_scatter))sym("ncclReduceScatter");
+    g_api.all_gather = (decltype(g_api.all_gather))sym("ncclAllGather");
     g_api.abort = (decltype(g_api.abort))sym("ncclCommAbort");
     g_api.finalize = (decltype(g_api.finalize))sym("ncclCommFinalize");
     g_api.destroy = (decltype(g_api.destroy))sym("ncclCommDestroy");
@@ -121,6 +126,34 @@ int nccl_allreduce_sum_f32(float *d, int64_t count, cudaStream_t s) {
     ncclResult_t r = g_api.all_reduce(d, d, (size_t)count, ncclFloat32, ncclSum, c, s);
     if (r == ncclInProgress) return settle(c, 60000, "ncclAllReduce");
     if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+    return ZPUCUDA_OK;
+}
+
+// In-place reduce-scatter: d holds world * count floats; this rank's summed
+// block lands at d + rank * count.
+int nccl_reduce_scatter_sum_f32(float *d, int64_t count, cudaStream_t s) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices || !g_comms[dev].comm)
+        return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "no NCCL communicator on this device (zpucuda_nccl_init)");
+    if (count <= 0) return ZPUCUDA_OK;
+    ncclComm_t c = g_comms[dev].comm;
+    ncclResult_t r = g_api.reduce_scatter(d, d + (int64_t)g_comms[dev].rank * count, (size_t)count, ncclFloat32,
+                                          ncclSum, c, s);
+    if (r == ncclInProgress) return settle(c, 60000, "ncclReduceScatter");
+    if (r != ncclSuccess) return nccl_fail(r, "ncclReduceScatter");
+    return ZPUCUDA_OK;
+}
+
+// In-place all-gather: every rank's block d + rank * count goes to all.
+int nccl_all_gather_f32(float *d, int64_t count, cudaStream_t s) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices || !g_comms[dev].comm)
+        return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "no NCCL communicator on this device (zpucuda_nccl_init)");
+    if (count <= 0) return ZPUCUDA_OK;
+    ncclComm_t c = g_comms[dev].comm;
+    ncclResult_t r = g_api.all_gather(d + (int64_t)g_comms[dev].rank * count, d, (size_t)count, ncclFloat32, c, s);
+    if (r == ncclInProgress) return settle(c, 60000, "ncclAllGather");
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
     return ZPUCUDA_OK;
 }
 

@@ -9,5 +9,9 @@ namespace zc {
 int nccl_world(int *rank);
 // In-place sum over the communicator on stream `s`.
 int nccl_allreduce_sum_f32(float *d, int64_t count, cudaStream_t s);
+// In place over world * count floats: rank r ends with the sum of block r.
+int nccl_reduce_scatter_sum_f32(float *d, int64_t count, cudaStream_t s);
+// In place over world * count floats: block r of rank r goes to every rank.
+int nccl_all_gather_f32(float *d, int64_t count, cudaStream_t s);
 
 }  // namespace zc

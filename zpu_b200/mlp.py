@@ -106,6 +106,12 @@ class MLP:
         check(lib().zpucuda_mlp_array(self._h, what, C.byref(p), C.byref(n)))
         return p.value, n.value
 
+    def param_offset(self, i):
+        """(offset, row pitch) of parameter i inside the arrays, in floats."""
+        o, ld = C.c_int64(), C.c_int64()
+        check(lib().zpucuda_mlp_param_offset(self._h, i, C.byref(o), C.byref(ld)))
+        return o.value, ld.value
+
     def init_xavier(self, seed0=XAVIER_SEED0, stream=None):
         """Xavier-uniform weights W_l ~ U(-sqrt(6/(in+out)), +sqrt(6/(in+out)))
         from rng.Rng(seed0 + l).uniformRange on the device, zero biases."""
