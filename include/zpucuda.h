@@ -303,6 +303,13 @@ int zpucuda_mlp_train_step(zpucuda_mlp *h, const float *d_x, const int64_t *d_la
 int zpucuda_mlp_loss(const zpucuda_mlp *h, float *dst, void *stream);
 int zpucuda_mlp_check(zpucuda_mlp *h);
 int64_t zpucuda_mlp_steps(const zpucuda_mlp *h);
+/* 1 when train_step exchanges dW2 over peer memory (its GEMM stores each
+ * tile into the owning rank's inbox across NVLink, set up through CUDA IPC at
+ * the first data-parallel step), 0 when every gradient goes through NCCL.
+ * By default it is used from 6 ranks on (below that NCCL's reduce-scatter
+ * hides under the next GEMM); ZPUCUDA_MLP_PEER_EXCHANGE=1 / =0, set alike on
+ * every rank, forces it on / off. */
+int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h);
 
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot

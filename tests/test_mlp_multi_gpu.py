@@ -2,7 +2,8 @@
 join on one.
 
 Each rank is a child process bound to its own GPU; the 128-byte NCCL id
-travels through a gloo process group.  After two train steps on halves of
+travels through a gloo process group.  Run once with dW2 exchanged over peer
+memory by its GEMM and once with NCCL alone.  After two train steps on halves of
 the batch (gradients summed over NCCL in the library's two buckets) every
 rank's parameters must equal each other bit for bit and match a one-GPU
 full-batch run within 1e-5 (the halves' partial sums re-associate).
@@ -53,7 +54,7 @@ RANK_SCRIPT = textwrap.dedent("""
     for _ in range(steps):
         m.train_step(xs, ys, global_batch=B)
     loss = m.loss()
-    np.savez(out, loss=np.float32(loss), *m.params())
+    np.savez(out, loss=np.float32(loss), mode=np.int32(m.exchange_mode()), *m.params())
     m.close()
     zm.nccl_destroy()
     dist.barrier()
@@ -61,7 +62,11 @@ RANK_SCRIPT = textwrap.dedent("""
 """)
 
 
-def test_two_gpu_train_steps_match_one_gpu(tmp_path):
+@pytest.mark.parametrize("peer", ["1", "0"])
+def test_two_gpu_train_steps_match_one_gpu(tmp_path, peer):
+    """peer "1": dW2 goes from its GEMM's tile stores into the owner's inbox
+    over NVLink (the exchange must be active); "0": every gradient through
+    NCCL's reduce-scatter."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import zpu_b200 as zc
@@ -69,7 +74,8 @@ def test_two_gpu_train_steps_match_one_gpu(tmp_path):
     from oracle import zpu_oracle as zo
     script = tmp_path / "rank.py"
     script.write_text(RANK_SCRIPT.format(root=ROOT, dims=DIMS, B=B, steps=STEPS))
-    env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()), NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()), NCCL_NVLS_ENABLE="0",
+               ZPUCUDA_MLP_PEER_EXCHANGE=peer)
     procs = [subprocess.Popen([sys.executable, str(script), str(r), "2", str(tmp_path / ("r%d.npz" % r))], env=env)
              for r in range(2)]
     try:
@@ -80,6 +86,7 @@ def test_two_gpu_train_steps_match_one_gpu(tmp_path):
                 p.kill()
     assert rcs == [0, 0]
     r0, r1 = np.load(tmp_path / "r0.npz"), np.load(tmp_path / "r1.npz")
+    assert int(r0["mode"]) == int(r1["mode"]) == int(peer)
     # one GPU, the whole batch
     zc.check(zc.lib().zpucuda_init(0))
     X = zo.uniform_range(0x5EED0800, B * DIMS[0], 0.0, 1.0).reshape(B, DIMS[0])

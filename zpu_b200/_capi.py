@@ -126,6 +126,7 @@ SIGNATURES = {
     "zpucuda_mlp_loss": (I32, [P, P, P]),
     "zpucuda_mlp_check": (I32, [P]),
     "zpucuda_mlp_steps": (I64, [P]),
+    "zpucuda_mlp_exchange_mode": (I32, [P]),
 }
 
 

@@ -46,12 +46,21 @@ enum EpiMode : int32_t {
     EPI_BIAS_TANH = 1,  // tanh(c + bias[col])
     EPI_TANH_GRAD = 2,  // c * (1 - y*y), y = aux[row, col] (a tanh output)
     EPI_BIAS = 3,       // c + bias[col]
+    EPI_SCATTER = 4,    // c, stored into the inbox of the rank that owns the row
 };
+constexpr int kMaxPeers = 8;
 struct Epilogue {
     int32_t mode = EPI_STORE;
     const float *bias = nullptr;
     const float *aux = nullptr;
     int64_t ldaux = 0;
+    // EPI_SCATTER: rank r owns rows [r * rows_per_owner, (r + 1) * rows_per_owner)
+    // and receives them in peer[r] (its inbox, mapped into this process),
+    // slot `src` of `world`: row i of the product lands at
+    // peer[r] + (src * rows_per_owner + i - r * rows_per_owner) * ldc.
+    float *peer[kMaxPeers] = {};
+    int64_t rows_per_owner = 0;
+    int32_t src = 0, world = 0;
 };
 
 // op(A)[m,k] @ op(B)[k,n] -> C[m,n] (ldc), per batch; trans flags as in

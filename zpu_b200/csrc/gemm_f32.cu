@@ -290,7 +290,7 @@ __device__ __forceinline__ float epi_apply(const Epilogue &e, float c, int64_t r
 
 // The epilogue on 32 consecutive columns of one row, all inside C.
 __device__ __forceinline__ void epi_apply32(const Epilogue &e, float (&acc)[32], int64_t row, int64_t col0) {
-    if (e.mode == EPI_STORE) return;
+    if (e.mode == EPI_STORE || e.mode == EPI_SCATTER) return;
     if (e.mode == EPI_TANH_GRAD) {
         const float *y = e.aux + row * e.ldaux + col0;
         if ((((uintptr_t)y) & 15) == 0) {
@@ -472,10 +472,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mb_arrive(&tfree[folded % NBUF]);
                 folded++;
             }
+            // Store: each lane holds 32 columns of its own row and writes them
+            // with float4 stores.  For EPI_SCATTER (rows that live in a peer's
+            // inbox) the warp first turns its 32 x 32 piece around in shared
+            // memory (the pipeline's buffers are idle once the last chunk is
+            // folded) and writes it a row at a time, 128 contiguous bytes per
+            // instruction, so NVLink carries full-size writes.
             const int64_t row = (int64_t)m0 + q4 * 32 + lane;
+            const bool staged = P.epi.mode == EPI_SCATTER;
+            const int64_t row0 = (int64_t)m0 + q4 * 32;
+            float *stage = (float *)(smem + (size_t)(warp - 8) * (32 * 33 * sizeof(float)));
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;");
-            float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
 #pragma unroll 1
             for (int c = 0; c < T::FOLD_COLS / 32; c++) {
                 const int cl = half * T::FOLD_COLS + c * 32;
@@ -483,19 +491,37 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float acc[32];
                 tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)cl, acc);
                 const int64_t col0 = (int64_t)n0 + cl;
-                if (row < P.M) {
-                    if (col0 + 32 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
-                        epi_apply32(P.epi, acc, row, col0);
+                if (!staged) {
+                    float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
+                    if (row < P.M) {
+                        if (col0 + 32 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
+                            epi_apply32(P.epi, acc, row, col0);
 #pragma unroll
-                        for (int v = 0; v < 8; v++)
-                            *(float4 *)(crow + col0 + 4 * v) =
-                                make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-                    } else {
+                            for (int v = 0; v < 8; v++)
+                                *(float4 *)(crow + col0 + 4 * v) =
+                                    make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                        } else {
 #pragma unroll
-                        for (int v = 0; v < 32; v++)
-                            if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                            for (int v = 0; v < 32; v++)
+                                if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                        }
                     }
+                    continue;
                 }
+#pragma unroll
+                for (int v = 0; v < 32; v++) stage[lane * 33 + v] = acc[v];
+                __syncwarp();
+                const int64_t col = col0 + lane;
+#pragma unroll 4
+                for (int r = 0; r < 32; r++) {
+                    const int64_t rr = row0 + r;
+                    if (rr >= P.M) break;
+                    const int64_t owner = rr / P.epi.rows_per_owner;  // its inbox: over NVLink for a peer
+                    float *dst = P.epi.peer[owner] +
+                                 ((int64_t)P.epi.src * P.epi.rows_per_owner + rr - owner * P.epi.rows_per_owner) * P.ldc;
+                    if (col < P.N) dst[col] = stage[r * 33 + lane];
+                }
+                __syncwarp();
             }
         }
     }
@@ -701,8 +727,16 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
     if (m == 0 || n == 0 || batches == 0) return ZPUCUDA_OK;
     if (!C || ldc < n) return ZPUCUDA_ERR_INVALID_ARGUMENT;
     if (epi.mode != EPI_STORE) {  // the epilogue inputs belong to one matrix
-        if (batches != 1 || epi.mode < 0 || epi.mode > EPI_BIAS) return ZPUCUDA_ERR_INVALID_ARGUMENT;
-        if ((epi.mode == EPI_TANH_GRAD) ? (!epi.aux || epi.ldaux < n) : !epi.bias) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        if (batches != 1 || epi.mode < 0 || epi.mode > EPI_SCATTER) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        if (epi.mode == EPI_SCATTER) {
+            if (epi.world < 1 || epi.world > kMaxPeers || epi.src < 0 || epi.src >= epi.world ||
+                epi.rows_per_owner * epi.world != m)
+                return ZPUCUDA_ERR_INVALID_ARGUMENT;
+            for (int r = 0; r < epi.world; r++)
+                if (!epi.peer[r]) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        } else if ((epi.mode == EPI_TANH_GRAD) ? (!epi.aux || epi.ldaux < n) : !epi.bias) {
+            return ZPUCUDA_ERR_INVALID_ARGUMENT;
+        }
         if (k == 0) return ZPUCUDA_ERR_NOT_SUPPORTED;
     }
     if (k == 0) {  // kernels.zig:346-349: an empty contraction writes zeros
@@ -747,7 +781,7 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
             const int64_t KT = (k + BK - 1) / BK;
             const int64_t tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn) * batches;
             int splits = choose_splits(tiles, KT, bn == 256 ? Tile<256>::KC_BLOCKS : Tile<128>::KC_BLOCKS);
-            if (batches * splits > 65535) splits = 1;
+            if (batches * splits > 65535 || epi.mode == EPI_SCATTER) splits = 1;  // the tile store is the scatter
             float *ws = nullptr;
             cudaMemPool_t pool = splits > 1 ? splitk_pool() : nullptr;
             if (splits > 1 &&
@@ -783,6 +817,7 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
             return st;
         }
     }
+    if (epi.mode == EPI_SCATTER) return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "scatter epilogue needs the TMA path");
     dim3 grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16), (unsigned)batches);
     if ((m + 15) / 16 > 65535) return ZPUCUDA_ERR_NOT_SUPPORTED;
 #define ZC_FG(TA_, TB_) \

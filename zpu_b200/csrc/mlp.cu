@@ -41,10 +41,15 @@
 // has read W2 (overlapping dW1), [W1, b1] last.  The same per-bucket Adam
 // split runs on one GPU, without the exchange.  (After a data-parallel step
 // a rank's gradient and moment arrays are final only in its own shards.)
+// dW2, the bulk of the bytes, does not go through NCCL at all when the ranks
+// can map each other's memory: its GEMM stores every tile into the owning
+// rank's inbox over NVLink (see "dW2 over peer memory" below).
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
+#include <vector>
 
 #include "gemm.cuh"
 #include "nccl.cuh"
@@ -272,6 +277,56 @@ double zig_pow(double x, double y) {
     return ldexp(acc, (int)exp_acc);
 }
 
+constexpr size_t kXferFlagBytes = 4096;  // flags: world x u64, error word at byte 2048
+constexpr uint32_t kXferSpin = 1u << 24;  // ~256 ns each: a few seconds
+
+struct XferFlags {
+    unsigned long long *flag[kMaxPeers];  // rank r's flag array, mapped here
+};
+
+__global__ void xfer_signal_kernel(const __grid_constant__ XferFlags f, int world, int src,
+                                   unsigned long long epoch) {
+    __threadfence_system();
+    for (int r = 0; r < world; r++)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f.flag[r] + src), "l"(epoch) : "memory");
+}
+
+// out[i] = sum over s of inbox[s * n + i], s in rank order, once every rank's
+// flag shows `epoch`; a wait that runs out sets *err and writes nothing.
+__global__ void __launch_bounds__(256) xfer_reduce_kernel(const float4 *__restrict__ inbox, int world, int64_t n4,
+                                                          float4 *__restrict__ out,
+                                                          const unsigned long long *flags,
+                                                          unsigned long long epoch, unsigned int *err) {
+    __shared__ int ready;
+    if (threadIdx.x == 0) {
+        int ok = 0;
+        for (uint32_t it = 0; it < kXferSpin && !ok; it++) {
+            ok = 1;
+            for (int r = 0; r < world; r++) {
+                unsigned long long v;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + r) : "memory");
+                if (v < epoch) ok = 0;
+            }
+            if (!ok) __nanosleep(256);
+        }
+        if (!ok) atomicOr(err, 1u);
+        ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        float4 a = __ldcg(inbox + i);
+        for (int s = 1; s < world; s++) {
+            const float4 b = __ldcg(inbox + (int64_t)s * n4 + i);
+            a.x = __fadd_rn(a.x, b.x);
+            a.y = __fadd_rn(a.y, b.y);
+            a.z = __fadd_rn(a.z, b.z);
+            a.w = __fadd_rn(a.w, b.w);
+        }
+        out[i] = a;
+    }
+}
+
 }  // namespace
 }  // namespace zc
 
@@ -295,6 +350,13 @@ struct zpucuda_mlp {
     double lr = 1e-3, beta1 = 0.9, beta2 = 0.999, eps = 1e-8;
     cudaStream_t comm_stream = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_w2 = nullptr, ev_done = nullptr;
+    // dW2 exchange over peer memory (data parallel): one allocation per rank,
+    // [flags | inbox], opened on every peer through CUDA IPC
+    int peer_state = 0;  // 0 not set up, 1 in use, -1 not available
+    int peer_world = 0, peer_rank = 0;
+    uint8_t *xfer = nullptr;                    // this rank's [flags | inbox]
+    uint8_t *peer_base[kMaxPeers] = {};         // every rank's allocation, mapped here
+    unsigned long long epoch = 0;               // dW2 exchanges so far
     std::mutex mu;
 
     float *loss_ptr() const { return grads + total; }
@@ -315,6 +377,9 @@ void free_mlp(zpucuda_mlp *h) {
                      h->xent_partials};
     for (float *b : bufs)
         if (b) cudaFree(b);
+    for (int r = 0; r < kMaxPeers; r++)
+        if (h->peer_base[r] && h->peer_base[r] != h->xfer) cudaIpcCloseMemHandle(h->peer_base[r]);
+    if (h->xfer) cudaFree(h->xfer);
     if (h->counters) cudaFree(h->counters);
     if (h->ev_a) cudaEventDestroy(h->ev_a);
     if (h->ev_b) cudaEventDestroy(h->ev_b);
@@ -365,10 +430,95 @@ Epilogue epi(int32_t mode, const float *bias, const float *aux = nullptr, int64_
         if (st_) return st_;   \
     } while (0)
 
-// Forward, loss and backward.  With `ar` set, the gradient buckets are summed
-// across ranks on the side stream as they become ready.
 AdamConsts adam_consts(zpucuda_mlp *h);
 int adam_range(zpucuda_mlp *h, const AdamConsts &c, int64_t off, int64_t n, cudaStream_t s);
+
+// ---------------------------------------------------- dW2 over peer memory
+//
+// The data-parallel step's largest gradient, dW2 [d_h1, d_h2], is
+// reduce-scattered by its own GEMM: rank r owns rows [r R, (r+1) R)
+// (R = d_h1 / world), and the GEMM's tile store writes every row straight into
+// slot `src` of its owner's inbox -- across NVLink for a peer -- so the
+// exchange overlaps the math tile by tile (gemm_f32.cu, EPI_SCATTER).  The
+// GEMM is followed on the same stream by a one-thread kernel that publishes
+// this step's epoch to every rank's flag for `src` (system-scope release after
+// a system fence); the owner's reduction waits (bounded) until every flag
+// carries the epoch, then adds the world slots in rank order.  The next
+// step's GEMM cannot overwrite an inbox early: it starts only after this
+// step's parameter all-gather, which needs every owner's reduced shard.
+unsigned int *xfer_error(const zpucuda_mlp *h) { return (unsigned int *)(h->xfer + 2048); }
+float *xfer_inbox(const zpucuda_mlp *h, int r) { return (float *)(h->peer_base[r] + kXferFlagBytes); }
+
+// Sets up the dW2 exchange once (every rank at the same point of its first
+// data-parallel step): allocate [flags | inbox], swap IPC handles with an
+// NCCL all-gather, open the peers' allocations, and agree across ranks
+// (an allreduce of the outcome) so that either all use it or none.
+// Used by default from kPeerExchangeMinWorld ranks on: with fewer, NCCL's
+// reduce-scatter of dW2 hides completely under the g1 GEMM on the side stream
+// while the tile stores sit inside dW2's GEMM (measured on B200: 3 % slower at
+// 2 and 4 ranks, 11 % faster at 8).  ZPUCUDA_MLP_PEER_EXCHANGE=1 / =0 (the
+// same on every rank) forces it on / off.
+constexpr int kPeerExchangeMinWorld = 6;
+int peer_setup(zpucuda_mlp *h, int world, int rank, cudaStream_t s) {
+    h->peer_state = -1;
+    const char *env = getenv("ZPUCUDA_MLP_PEER_EXCHANGE");
+    const bool want = env && env[0] ? env[0] != '0' : world >= kPeerExchangeMinWorld;
+    if (!want || world < 2 || world > kMaxPeers || h->d[1] % world || ((h->d[1] / world) * h->d[2]) % 4)
+        return ZPUCUDA_OK;
+    const size_t bytes = kXferFlagBytes + (size_t)h->d[1] * (size_t)h->d[2] * sizeof(float);
+    float ok = 1.0f;
+    cudaIpcMemHandle_t mine;
+    memset(&mine, 0, sizeof mine);
+    if (cudaMalloc((void **)&h->xfer, bytes) != cudaSuccess ||
+        cudaMemset(h->xfer, 0, kXferFlagBytes) != cudaSuccess || cudaIpcGetMemHandle(&mine, h->xfer) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0.0f;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    float *d_ex = nullptr;  // world handles (16 floats each) + the agreement word
+    ZC_CUDA(cudaMalloc((void **)&d_ex, (size_t)(world * 16 + 1) * sizeof(float)));
+    ZC_CUDA(cudaMemcpyAsync(d_ex + rank * 16, &mine, 64, cudaMemcpyHostToDevice, s));
+    int st = nccl_all_gather_f32(d_ex, 16, s);
+    std::vector<cudaIpcMemHandle_t> all(world);
+    if (!st) st = cudaMemcpyAsync(all.data(), d_ex, (size_t)world * 64, cudaMemcpyDeviceToHost, s) == cudaSuccess
+                      ? ZPUCUDA_OK
+                      : cuda_fail(cudaGetLastError(), "copy IPC handles");
+    if (!st) st = cudaStreamSynchronize(s) == cudaSuccess ? ZPUCUDA_OK : cuda_fail(cudaGetLastError(), "sync");
+    h->peer_base[rank] = h->xfer;
+    for (int r = 0; r < world && !st && ok != 0.0f; r++) {
+        if (r == rank) continue;
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0.0f;
+            break;
+        }
+        h->peer_base[r] = (uint8_t *)p;
+    }
+    if (!st) st = cudaMemcpyAsync(d_ex + world * 16, &ok, sizeof ok, cudaMemcpyHostToDevice, s) == cudaSuccess
+                      ? ZPUCUDA_OK
+                      : cuda_fail(cudaGetLastError(), "agreement word");
+    if (!st) st = nccl_allreduce_sum_f32(d_ex + world * 16, 1, s);
+    float agreed = 0.0f;
+    if (!st) st = cudaMemcpyAsync(&agreed, d_ex + world * 16, sizeof agreed, cudaMemcpyDeviceToHost, s) == cudaSuccess
+                      ? ZPUCUDA_OK
+                      : cuda_fail(cudaGetLastError(), "agreement word");
+    if (!st) st = cudaStreamSynchronize(s) == cudaSuccess ? ZPUCUDA_OK : cuda_fail(cudaGetLastError(), "sync");
+    cudaFree(d_ex);
+    if (st || agreed != (float)world) {  // someone could not map a peer: everyone keeps NCCL
+        for (int r = 0; r < kMaxPeers; r++) {
+            if (h->peer_base[r] && h->peer_base[r] != h->xfer) cudaIpcCloseMemHandle(h->peer_base[r]);
+            h->peer_base[r] = nullptr;
+        }
+        if (h->xfer) cudaFree(h->xfer);
+        h->xfer = nullptr;
+        return st;
+    }
+    h->peer_world = world;
+    h->peer_rank = rank;
+    h->peer_state = 1;
+    return ZPUCUDA_OK;
+}
 
 // Forward, loss and backward.  With `ar` set, the gradient buckets are summed
 // across ranks on the side stream as they become ready; with `adam` set, the
@@ -384,6 +534,9 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     float *gW1 = h->grads + h->off[0], *gb1 = h->grads + h->off[1];
     float *gW2 = h->grads + h->off[2], *gb2 = h->grads + h->off[3];
     float *gW3 = h->grads + h->off[4], *gb3 = h->grads + h->off[5];
+    int rank = 0;
+    const int world = ar ? nccl_world(&rank) : 1;
+    if (ar && adam && world > 1 && h->peer_state == 0) ZC_TRY(peer_setup(h, world, rank, h->comm_stream));
 
     // forward: dense -> tanh -> dense -> tanh -> dense
     ZC_TRY(gemm(x, W1, h->a1, B, d1, d0, d0, d1, d1, false, false, epi(EPI_BIAS_TANH, b1), s));
@@ -409,20 +562,48 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     ZC_TRY(gemm(h->gl, W3, h->ga2, B, d2, d3p, d3p, d3p, d2, false, true, epi(EPI_TANH_GRAD, nullptr, h->a2, d2), s));
     // layer 2
     ZC_TRY(colsum(h, 1, h->ga2, B, d2, d2, gb2, s));
-    ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s));
+    const int64_t nA = h->total - h->off[2], nB = h->off[2], nA3 = h->total - h->off[3];
+    const bool shard = ar && adam && nA % (4 * world) == 0 && nB % (4 * world) == 0;
+    const bool fused = shard && h->peer_state == 1 && h->peer_world == world && nA3 % (4 * world) == 0;
+    const int64_t w2_shard = d1 / world * d2;  // floats of dW2 a rank owns (fused)
+    if (fused) {  // dW2's tiles go straight into their owners' inboxes
+        Epilogue se;
+        se.mode = EPI_SCATTER;
+        for (int r = 0; r < world; r++) se.peer[r] = xfer_inbox(h, r);
+        se.rows_per_owner = d1 / world;
+        se.src = rank;
+        se.world = world;
+        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, se, s));
+        XferFlags f;
+        memset(&f, 0, sizeof f);
+        for (int r = 0; r < world; r++) f.flag[r] = (unsigned long long *)h->peer_base[r];
+        h->epoch += 1;
+        xfer_signal_kernel<<<1, 1, 0, s>>>(f, world, rank, h->epoch);
+        ZC_LAUNCHED("xfer_signal_kernel");
+    } else {
+        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s));
+    }
     cudaStream_t side = h->comm_stream;
     // With a communicator and Adam in the step, each rank updates only its
     // 1/world shard of each bucket: reduce-scatter the gradients, Adam on the
     // shard, all-gather the parameters (the same bytes as an allreduce, and a
     // world-th of the optimizer work).
-    int rank = 0;
-    const int world = ar ? nccl_world(&rank) : 1;
-    const int64_t nA = h->total - h->off[2], nB = h->off[2];
-    const bool shard = ar && adam && nA % (4 * world) == 0 && nB % (4 * world) == 0;
     if (ar) {
         ZC_CUDA(cudaEventRecord(h->ev_a, s));
         ZC_CUDA(cudaStreamWaitEvent(side, h->ev_a, 0));
-        if (shard) {
+        if (fused) {
+            // b2, W3, b3 and the loss (70 K floats) in one NCCL allreduce; dW2 is
+            // already in the inboxes: add this rank's slots as soon as every
+            // peer's flag is up, overlapping the g1 GEMM
+            ZC_TRY(nccl_allreduce_sum_f32(h->grads + h->off[3], nA3 + 1, side));
+            const int64_t n4 = w2_shard / 4;
+            int64_t blocks = (n4 + 255) / 256;
+            if (blocks > (int64_t)num_sms() * 4) blocks = (int64_t)num_sms() * 4;
+            xfer_reduce_kernel<<<(unsigned)blocks, 256, 0, side>>>(
+                (const float4 *)xfer_inbox(h, rank), world, n4, (float4 *)(h->grads + h->off[2] + rank * w2_shard),
+                (const unsigned long long *)h->xfer, h->epoch, xfer_error(h));
+            ZC_LAUNCHED("xfer_reduce_kernel");
+        } else if (shard) {
             ZC_TRY(nccl_reduce_scatter_sum_f32(h->grads + h->off[2], nA / world, side));
             ZC_TRY(nccl_allreduce_sum_f32(h->loss_ptr(), 1, side));
         } else {
@@ -435,7 +616,11 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         ac = adam_consts(h);
         ZC_CUDA(cudaEventRecord(h->ev_w2, s));
         ZC_CUDA(cudaStreamWaitEvent(side, h->ev_w2, 0));
-        if (shard) {
+        if (fused) {  // Adam on this rank's dW2 rows, gather W2; b2, W3, b3 everywhere
+            ZC_TRY(adam_range(h, ac, h->off[2] + rank * w2_shard, w2_shard, side));
+            ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], w2_shard, side));
+            ZC_TRY(adam_range(h, ac, h->off[3], nA3, side));
+        } else if (shard) {
             ZC_TRY(adam_range(h, ac, h->off[2] + rank * (nA / world), nA / world, side));
             ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], nA / world, side));
         } else {
@@ -546,7 +731,7 @@ extern "C" int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int6
         h->rows[i] = r[i];
         h->cols[i] = c[i];
         h->ld[i] = l[i];
-        if (i == 2) o = round_up(o, kBucketAlign);  // bucket [W2 .. b3] starts here
+        if (i == 2 || i == 3) o = round_up(o, kBucketAlign);  // buckets [W2 .. b3] and [b2 .. b3] start here
         h->off[i] = o;
         o += round_up(r[i] * l[i], kAlign);
     }
@@ -704,7 +889,13 @@ extern "C" int zpucuda_mlp_check(zpucuda_mlp *h) {
         ZC_CUDA(cudaMemset(h->label_error(), 0, sizeof e));
         return set_error(ZPUCUDA_ERR_INDEX_OUT_OF_RANGE, "a label was outside [0, classes) (nn.oneHot)");
     }
+    if (h->xfer) {
+        ZC_CUDA(cudaMemcpy(&e, xfer_error(h), sizeof e, cudaMemcpyDeviceToHost));
+        if (e) return set_error(ZPUCUDA_ERR_TIMEOUT, "a peer's dW2 tiles did not arrive in time");
+    }
     return ZPUCUDA_OK;
 }
 
 extern "C" int64_t zpucuda_mlp_steps(const zpucuda_mlp *h) { return h ? h->t : -1; }
+
+extern "C" int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h) { return h && h->peer_state == 1 ? 1 : 0; }

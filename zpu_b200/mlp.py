@@ -168,6 +168,11 @@ class MLP:
     def steps(self):
         return lib().zpucuda_mlp_steps(self._h)
 
+    def exchange_mode(self):
+        """1 when dW2 travels over peer memory from its GEMM, 0 when all
+        gradients go through NCCL."""
+        return lib().zpucuda_mlp_exchange_mode(self._h)
+
     def sync(self):
         import torch
         torch.cuda.synchronize()
