@@ -183,7 +183,8 @@ typedef struct zpucuda_plan zpucuda_plan;
 /* Lowers a built jit plan (the output of jit.build, src/zpu/jit.zig:130-256):
  * maximal runs of element-wise steps (prims.isElementwise,
  * src/zpu/prims.zig:198) that end in at most one sum / prod / max / min over
- * all axes or the last axis become ONE fused kernel each (no intermediate
+ * all axes or over any one axis (keepdims or not) become ONE fused kernel
+ * each (no intermediate
  * HBM traffic); matmul steps become GEMM launches.  Region kernels come from
  * a catalogue generated at build time, with a one-pass bytecode kernel for
  * regions outside it.  Steps outside that set make creation fail with

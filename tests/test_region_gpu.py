@@ -273,3 +273,36 @@ def test_launch_counter_counts_region_launches(zc):
         p.run([x])
     torch.cuda.synchronize()
     assert zc.launch_count() - before == 3
+
+
+@pytest.mark.parametrize("axis,keep", [(0, 0), (1, 0), (1, 1), (-3, 1), (2, 0)])
+@pytest.mark.parametrize("prim", ["sum", "max_reduce", "min_reduce", "prod_op"])
+def test_reductions_over_any_axis(zc, axis, keep, prim):
+    """sum / prod / max / min over one axis of a 3-D region (ops.reduceOp,
+    src/zpu/ops.zig:820-869): the element-wise output and the reduction in
+    one kernel; an axis other than the last walks it in row order."""
+    shape = (7, 33, 65)
+    x = zo.uniform_range(21, 7 * 33 * 65, 0.5, 1.5).reshape(shape)
+    p = zc.Plan([(1, zc.F32, shape)], [],
+                [("sqrt", [1], 10, -2, 0), (prim, [10], 11, axis, keep)], [11, 10])
+    red, s = p.run([torch.from_numpy(x).cuda()])
+    want_s = zo.unary("sqrt", x)
+    assert ulp_diff_f32(s.cpu().numpy(), want_s).max() <= 4
+    fn = {"sum": np.sum, "max_reduce": np.max, "min_reduce": np.min, "prod_op": np.prod}[prim]
+    want = fn(want_s.astype(np.float64), axis=axis, keepdims=bool(keep))
+    assert red.shape == want.shape, (red.shape, want.shape)
+    assert np.allclose(red.cpu().numpy(), want, rtol=2e-6, atol=0), prim
+
+
+def test_axis0_sum_matches_the_snapshot(zc, golden):
+    """The reference's reduce/sum-axis0 snapshot (spread12 as 3 x 4, f64):
+    the device walks the rows in order as zpu does, within the snapshot's
+    1e-9."""
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    snapv = golden["snapshots"]["zpu/reduce/sum-axis0"]
+    p = zc.Plan([(1, zc.F64, (3, 4))], [], [("sum", [1], 10, 0, 0)], [10])
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    want = np.array(snapv["values"])
+    g = got.cpu().numpy()
+    assert g.shape == (4,)
+    assert np.all(np.abs(g - want) <= snapv["tol"] * np.maximum(1, np.maximum(np.abs(g), np.abs(want))))

@@ -229,11 +229,14 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 for (int i = 0; i < o.shape.rank; i++) o.shape.dims[i] = 1;
             } else {
                 int ax = st.axis < 0 ? st.axis + a.shape.rank : st.axis;
-                if (ax != a.shape.rank - 1 || a.shape.rank == 0)
-                    return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "only full and last-axis reductions are fused");
+                if (ax < 0 || ax >= a.shape.rank) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "reduction axis");
                 o.shape = a.shape;
-                if (st.keepdims) o.shape.dims[ax] = 1;
-                else o.shape.rank -= 1;
+                if (st.keepdims) {
+                    o.shape.dims[ax] = 1;
+                } else {  // drop axis ax
+                    for (int d = ax; d + 1 < a.shape.rank; d++) o.shape.dims[d] = a.shape.dims[d + 1];
+                    o.shape.rank -= 1;
+                }
             }
         } else if (st.prim == PRIM_MATMUL && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
@@ -466,11 +469,21 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                      : red_prim == PRIM_MAX_REDUCE ? RED_MAX : RED_MIN;
             P.reduce_all = red_axis == ZPUCUDA_AXIS_NONE;
             P.reduce_reg = reg[red_in];
-            P.inner = P.reduce_all ? P.numel : (rshape.rank ? rshape.dims[rshape.rank - 1] : 1);
-            P.outer = P.reduce_all ? 1 : (P.inner ? P.numel / P.inner : 1);
-            if (!P.reduce_all && P.inner == 0) {
+            const int rax = P.reduce_all ? -1 : (red_axis < 0 ? red_axis + rshape.rank : red_axis);
+            if (!P.reduce_all && rax != rshape.rank - 1) {  // [outer, red_len, inner]
+                P.reduce_mid = 1;
+                P.red_len = rshape.dims[rax];
                 P.outer = 1;
-                for (int d = 0; d < rshape.rank - 1; d++) P.outer *= rshape.dims[d];
+                P.inner = 1;
+                for (int d = 0; d < rax; d++) P.outer *= rshape.dims[d];
+                for (int d = rax + 1; d < rshape.rank; d++) P.inner *= rshape.dims[d];
+            } else {
+                P.inner = P.reduce_all ? P.numel : (rshape.rank ? rshape.dims[rshape.rank - 1] : 1);
+                P.outer = P.reduce_all ? 1 : (P.inner ? P.numel / P.inner : 1);
+                if (!P.reduce_all && P.inner == 0) {
+                    P.outer = 1;
+                    for (int d = 0; d < rshape.rank - 1; d++) P.outer *= rshape.dims[d];
+                }
             }
             L.has_red = true;
             L.red = materialise(red_out_id);
@@ -478,7 +491,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             char buf[64];
             snprintf(buf, sizeof buf, ";out=r%d;red=%s%s", P.reduce_reg,
                      red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max" : "min",
-                     P.reduce_all ? "" : "_rows");
+                     P.reduce_all ? "" : P.reduce_mid ? "_axis" : "_rows");
             sig += buf;
             if (P.reduce_all) {
                 void *w = nullptr;

@@ -207,7 +207,11 @@ __device__ __forceinline__ void store_outputs(const RegionProgram &p, const Regi
 }
 
 // MODE 0: element-wise outputs only; 1: plus a full reduction; 2: plus a
-// reduction over the last axis (one warp per row).
+// reduction over the last axis (one warp per row); 3: plus a reduction over
+// an axis that is not the last: the region is [outer, red_len, inner], one
+// thread per output element walks the reduced axis in order (the row-order
+// walk of ops.reduceKernel, src/zpu/ops.zig:746-752), threads of a warp on
+// consecutive inner indices so every step of the walk is one coalesced load.
 template <class T, int MODE>
 __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_constant__ RegionProgram p,
                                                                 const __grid_constant__ RegionIO io) {
@@ -245,6 +249,20 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
         for (unsigned b = 0; b < gridDim.x; b++) v = red_combine(p.reduce, v, __ldcg(io.partials + b));
         *(T *)io.red_out = (T)v;
         *io.ticket = 0u;
+    } else if (MODE == 3) {
+        const int64_t n_out = p.outer * p.inner;
+        for (int64_t o = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; o < n_out;
+             o += (int64_t)gridDim.x * kInterpThreads) {
+            const int64_t a = o / p.inner, c = o - a * p.inner;
+            double acc = red_identity(p.reduce);
+            for (int64_t k = 0; k < p.red_len; k++) {
+                const int64_t i = (a * p.red_len + k) * p.inner + c;
+                eval<T>(p, io, i, r);
+                store_outputs<T>(p, io, i, r);
+                acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
+            }
+            ((T *)io.red_out)[o] = (T)acc;
+        }
     } else {
         const int lane = threadIdx.x & 31;
         const int64_t warps = (int64_t)gridDim.x * (kInterpThreads / 32);
@@ -275,6 +293,12 @@ int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
         if (g > sms * 8) g = sms * 8;
         if (g < 1) g = 1;
         interp_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+    } else if (p.reduce_mid) {
+        const int64_t n_out = p.outer * p.inner;
+        if (n_out == 0) return ZPUCUDA_OK;
+        int64_t g = (n_out + kInterpThreads - 1) / kInterpThreads;
+        if (g > sms * 8) g = sms * 8;
+        interp_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else {
         if (p.outer == 0) return ZPUCUDA_OK;
         int64_t g = (p.outer + (kInterpThreads / 32) - 1) / (kInterpThreads / 32);

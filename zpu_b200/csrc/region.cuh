@@ -47,8 +47,10 @@ struct RegionProgram {
     int64_t numel;
     int64_t outer;       // rows of a row reduction (numel / inner; set even when inner == 0)
     int32_t reduce;      // RED_*
-    int32_t reduce_all;  // 1: all axes -> 1 value; 0: last axis -> numel / inner values
-    int64_t inner;       // last-axis length for row reductions
+    int32_t reduce_all;  // 1: all axes -> 1 value; 0: one axis (below)
+    int64_t inner;       // last-axis length for row reductions; axes after the reduced one (reduce_mid)
+    int32_t reduce_mid;  // 1: the reduced axis is not the last: [outer, red_len, inner] -> [outer, inner]
+    int64_t red_len;     // length of that axis
     int32_t reduce_reg;
     int32_t n_out;  // element-wise outputs written to HBM
     int32_t out_reg[RP_MAX_OUT];
