@@ -306,3 +306,54 @@ def test_axis0_sum_matches_the_snapshot(zc, golden):
     g = got.cpu().numpy()
     assert g.shape == (4,)
     assert np.all(np.abs(g - want) <= snapv["tol"] * np.maximum(1, np.maximum(np.abs(g), np.abs(want))))
+
+
+def _tanh_sum_plan(zc, region, n):
+    if region == "tanh_sq_affine":
+        return chain_plan(zc, n, True)
+    if region == "tanh_sq":
+        steps = [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0), ("sum", [11], 12, -2, 0)]
+        return zc.Plan([(1, zc.F32, (n,))], [], steps, [12])
+    return zc.Plan([(1, zc.F32, (n,))], [], [("tanh", [1], 10, -2, 0), ("sum", [10], 11, -2, 0)], [11])
+
+
+@pytest.mark.parametrize("region", ["tanh_sq_affine", "tanh_sq", "tanh"])
+@pytest.mark.parametrize("n,frac", [(N_FULL, 0.3), ((1 << 25) + 7, 1.0), ((1 << 25) + 7, 0.001),
+                                    (N_FULL + 5, 0.0), ((1 << 24) + 1, 0.5), (4099, 0.5)])
+def test_tanh_sums_count_every_element_once(zc, region, n, frac):
+    """Full sums through tanh at sizes that reach every part of the fused
+    kernel (unrolled grid-stride iterations, the float4 tail, the n % 4
+    elements).  With x in {0, +-16, +-inf} every tanh value is exactly 0 or
+    +-1 (tanh(16) rounds to 1 in f32) and every partial sum is exact, so the
+    result must be the exactly rounded count: an element dropped or counted
+    twice anywhere shows."""
+    g = torch.Generator(device="cuda").manual_seed(n * 1000 + int(frac * 1000))
+    r = torch.rand(n, device="cuda", generator=g)
+    neg = torch.rand(n, device="cuda", generator=g) < 0.5
+    inf = torch.rand(n, device="cuda", generator=g) < 0.05
+    big = r < frac
+    mag = torch.where(inf, torch.tensor(float("inf"), device="cuda"), torch.tensor(16.0, device="cuda"))
+    x = torch.where(big, torch.where(neg, -mag, mag), torch.zeros((), device="cuda")).float().contiguous()
+    k = int(big.sum())
+    kneg = int((big & neg).sum())
+    p = _tanh_sum_plan(zc, region, n)
+    assert ("catalogue %s+sum" % region) in p.describe()
+    (got,) = p.run([x])
+    got = float(got.cpu())
+    if region == "tanh_sq_affine":
+        want = 0.5 * k - 0.25 * n  # each element: tanh * 0.5 - 0.25 with tanh 0 or 1
+    elif region == "tanh_sq":
+        want = float(k)
+    else:
+        want = float(k - 2 * kneg)
+    assert got == float(np.float32(want)), (got, want, k)
+
+
+def test_tanh_sum_propagates_nan(zc):
+    n = N_FULL
+    x = torch.zeros(n, device="cuda")
+    x[12345678] = float("nan")
+    x[(1 << 25) + 3] = 16.0
+    for region in ("tanh_sq_affine", "tanh_sq", "tanh"):
+        (got,) = _tanh_sum_plan(zc, region, n).run([x])
+        assert math.isnan(float(got.cpu())), region
