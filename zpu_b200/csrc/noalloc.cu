@@ -61,7 +61,7 @@ extern "C" int zpucuda_chain_tanh_sq_affine_sum_noalloc(const float *d_x, int64_
     ZC_CHECK(n >= 0 && d_a && d_b && d_out && (d_x || n == 0), ZPUCUDA_ERR_INVALID_ARGUMENT);
     if (((uintptr_t)d_x & 15u) != 0)
         return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "zpucuda_chain_tanh_sq_affine_sum_noalloc: d_x must be 16-byte aligned");
-    const int grid = num_sms() * fused_blocks_per_sm();
+    const int grid = fused_grid<Region_tanh_sq_affine, true>();
     if (grid > kNoAllocMaxBlocks)
         return set_error(ZPUCUDA_ERR_NOT_SUPPORTED,
                          "zpucuda_chain_tanh_sq_affine_sum_noalloc: this launch needs " + std::to_string(grid) +

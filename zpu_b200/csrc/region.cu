@@ -29,6 +29,16 @@ int fused_blocks_per_sm() {
     return v;
 }
 
+int fused_sum_blocks_per_sm(int occupancy) {
+    static const int env = [] {
+        const char *e = getenv("ZPUCUDA_REGION_BPS");
+        const int x = e ? atoi(e) : 0;
+        return (x >= 1 && x <= 16) ? x : 0;
+    }();
+    if (env) return env;
+    return (occupancy >= 1 && occupancy <= 16) ? occupancy : fused_blocks_per_sm();
+}
+
 int bulk_blocks_per_sm() {
     static int v = [] {
         const char *e = getenv("ZPUCUDA_REGION_BULK_BPS");

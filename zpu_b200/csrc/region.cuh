@@ -513,6 +513,29 @@ __global__ void __launch_bounds__(kBulkThreads) fused_sum_bulk_kernel(const __gr
 // for tuning sweeps.
 int fused_blocks_per_sm();
 int bulk_blocks_per_sm();
+// Blocks per SM of a register-loop full sum: ZPUCUDA_REGION_BPS when set,
+// else the kernel's own resident blocks per SM (`occupancy`), so the grid is
+// one wave (measured on the 2^26 tanh chain: 5190 GB/s at its 5 resident
+// blocks per SM against 4940 at 12; element-wise regions run best at 12).
+int fused_sum_blocks_per_sm(int occupancy);
+
+// The grid launch_fused_f32 uses for the register-loop kernel of F.
+template <class F, bool SUM>
+int fused_grid() {
+    int per_sm = fused_blocks_per_sm();
+    if (SUM) {
+        static const int occ = [] {
+            int nb = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fused_f32_kernel<F, SUM>, kFusedThreads, 0) !=
+                cudaSuccess)
+                nb = 0;
+            return nb;
+        }();
+        per_sm = fused_sum_blocks_per_sm(occ);
+    }
+    int grid = num_sms() * per_sm;
+    return grid > kMaxRegionBlocks ? kMaxRegionBlocks : grid;
+}
 
 // SUM: the region ends in a full sum.  BULK (full sums only): stream through
 // the bulk-copy pipeline -- the generator picks it for regions with no
@@ -538,8 +561,7 @@ int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s)
         return ZPUCUDA_OK;
     }
     auto k = fused_f32_kernel<F, SUM>;
-    int grid = num_sms() * fused_blocks_per_sm();
-    if (grid > kMaxRegionBlocks) grid = kMaxRegionBlocks;
+    const int grid = fused_grid<F, SUM>();
     k<<<grid, kFusedThreads, 0, s>>>(io, p.numel);
     ZC_LAUNCHED("fused region kernel");
     return ZPUCUDA_OK;
