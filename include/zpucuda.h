@@ -49,8 +49,9 @@ enum {
     ZPUCUDA_ERR_INVALID_ARGUMENT = 16    /* NULL pointer, negative size, ... */
 };
 
-/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13). */
-enum { ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1 };
+/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13).  I64 is
+ * produced only by argmax / argmin steps of a plan. */
+enum { ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1, ZPUCUDA_I64 = 3 };
 
 /* prims.AXIS_NONE (src/zpu/prims.zig:169). */
 #define ZPUCUDA_AXIS_NONE (-2)
@@ -183,9 +184,12 @@ typedef struct zpucuda_plan zpucuda_plan;
 /* Lowers a built jit plan (the output of jit.build, src/zpu/jit.zig:130-256):
  * maximal runs of element-wise steps (prims.isElementwise,
  * src/zpu/prims.zig:198) that end in at most one sum / prod / max / min over
- * all axes or over any one axis (keepdims or not) become ONE fused kernel
- * each (no intermediate
- * HBM traffic); matmul steps become GEMM launches.  Region kernels come from
+ * all axes or over any one axis (keepdims or not), or one argmax / argmin
+ * (i64 result, ops.argReduce, src/zpu/ops.zig:931-975), become ONE fused
+ * kernel each (no intermediate HBM traffic).  Reduction axes follow
+ * ops.axesMaskOf (ops.zig:630-642): with batch_depth d, AXIS_NONE folds the
+ * payload axes [d, rank) and a non-negative axis counts from axis d.  Matmul
+ * steps become GEMM launches.  Region kernels come from
  * a catalogue generated at build time, with a one-pass bytecode kernel for
  * regions outside it.  Steps outside that set make creation fail with
  * ZPUCUDA_ERR_NOT_SUPPORTED. */

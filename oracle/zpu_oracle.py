@@ -225,6 +225,73 @@ def reduce_max(x):
     return np.float32(lib().zo_reduce_maxmin_f32(_p(x), x.size, 1))
 
 
+AXIS_NONE = -2
+
+
+def reduced_axes(ndim, axis, depth=0):
+    """ops.axesMaskOf (src/zpu/ops.zig:630-642) as a tuple of axes: AXIS_NONE
+    folds the payload axes [depth, ndim); a non-negative axis counts from the
+    first payload axis, a negative one from the last."""
+    if axis == AXIS_NONE:
+        return tuple(range(min(depth, ndim), ndim))
+    a = axis + depth if axis >= 0 else axis + ndim
+    if a < 0 or a >= ndim:
+        raise ValueError("InvalidAxis")
+    return (a,)
+
+
+def arg_reduce(x, axis=AXIS_NONE, depth=0, want_max=True):
+    """ops.argReduce (src/zpu/ops.zig:931-975): the reduced elements of each
+    output are visited in row order; the first seeds `best`, a later one
+    replaces it only when strictly greater (argmax) / smaller (argmin), so
+    ties keep the first index and a NaN never replaces (a NaN first element
+    pins the answer to 0).  Values compare as f64 (readF64).  Returns i64 with
+    the folded axes dropped."""
+    x = np.asarray(x).astype(np.float64)
+    axes = reduced_axes(x.ndim, axis, depth)
+    keep = [d for d in range(x.ndim) if d not in axes]
+    y = np.transpose(x, keep + list(axes))  # folded axes last, in row order
+    out_shape = tuple(x.shape[d] for d in keep)
+    y = y.reshape(out_shape + (-1,))
+    n = y.shape[-1]
+    best = np.zeros(out_shape)
+    idx = np.zeros(out_shape, dtype=np.int64)
+    for k in range(n):
+        v = y[..., k]
+        if k == 0:
+            better = np.ones(out_shape, dtype=bool)
+        else:
+            with np.errstate(invalid="ignore"):
+                better = v > best if want_max else v < best
+        best = np.where(better, v, best)
+        idx = np.where(better, k, idx)
+    return idx
+
+
+def reduce_axis(x, prim, axis=AXIS_NONE, keepdims=False, depth=0):
+    """ops.reduceOp (src/zpu/ops.zig:820-869) for sum / prod / max / min over
+    the axes axesMaskOf gives, as an f64 reference (order-free; the
+    tolerances of the tests that use it cover the summation order)."""
+    x = np.asarray(x).astype(np.float64)
+    axes = reduced_axes(x.ndim, axis, depth)
+    fn = {"sum": np.sum, "prod_op": np.prod, "max_reduce": np.max, "min_reduce": np.min}[prim]
+    return fn(x, axis=axes, keepdims=bool(keepdims))
+
+
+def mean(x, axis=AXIS_NONE, keepdims=False, depth=0):
+    """ops.mean (src/zpu/ops.zig:894-908): sum, then times 1/count."""
+    x = np.asarray(x).astype(np.float64)
+    axes = reduced_axes(x.ndim, axis, depth)
+    count = int(np.prod([x.shape[a] for a in axes])) if axes else 1
+    return reduce_axis(x, "sum", axis, keepdims, depth) * (1.0 / count)
+
+
+def variance(x, axis=AXIS_NONE, keepdims=False, depth=0):
+    """ops.variance (src/zpu/ops.zig:914-922): mean(square(x - mean(x, keep)))."""
+    m = mean(x, axis, True, depth)
+    return mean(np.square(np.asarray(x, dtype=np.float64) - m), axis, keepdims, depth)
+
+
 def sum_f64(x):
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     return lib().zo_sum_f64_of_f32(_p(x), x.size)

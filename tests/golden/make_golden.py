@@ -23,6 +23,13 @@ CASES = {
     "transforms/jit-replay": 1e-9, # tests/snap/zpu.zig:288
     "reduce/sum-all": 1e-9,        # tests/snap/zpu.zig:85
     "reduce/sum-axis0": 1e-9,      # tests/snap/zpu.zig:86
+    "reduce/sum-axis1-keepdims": 1e-9,  # tests/snap/zpu.zig:87
+    "reduce/max-axis1": 1e-9,      # tests/snap/zpu.zig:88
+    "reduce/min-axis0": 1e-9,      # tests/snap/zpu.zig:89
+    "reduce/mean-axis1": 1e-9,     # tests/snap/zpu.zig:90
+    "reduce/variance-axis1": 1e-9, # tests/snap/zpu.zig:91
+    "reduce/prod-axis1": 1e-9,     # tests/snap/zpu.zig:92
+    "reduce/argmax-axis1": 0.0,    # tests/snap/zpu.zig:93
     "ops/tanh": 1e-9,              # tests/snap/zpu.zig:62
     "ops/exp": 1e-9,               # tests/snap/zpu.zig:60
     "ops/sigmoid": 1e-9,           # tests/snap/zpu.zig:61
@@ -108,6 +115,25 @@ def main(ref):
          "b": [1, 2, 3, 4], "b_shape": [2, 2], "want": [7, 10, 15, 22, 1, 2, 3, 4], "tol": 1e-12},
     ]
 
+    # src/zpu/tests.zig:116-124: reductions of [[1,2,3],[4,5,6]] (f64);
+    # examples/audit_edge_cases.zig:138-144: argmax of a length-5 f32 vector
+    reduce_known = [
+        {"name": "sum axis 0", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "sum", "axis": 0,
+         "keepdims": 0, "want": [5, 7, 9], "want_shape": [3], "tol": 1e-12},
+        {"name": "sum axis -1", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "sum", "axis": -1,
+         "keepdims": 0, "want": [6, 15], "want_shape": [2], "tol": 1e-12},
+        {"name": "sum axis 1 keepdims", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "sum", "axis": 1,
+         "keepdims": 1, "want": [6, 15], "want_shape": [2, 1], "tol": 1e-12},
+        {"name": "max axis 0", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "max_reduce", "axis": 0,
+         "keepdims": 0, "want": [4, 5, 6], "want_shape": [3], "tol": 1e-12},
+        {"name": "min axis 1", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "min_reduce", "axis": 1,
+         "keepdims": 0, "want": [1, 4], "want_shape": [2], "tol": 1e-12},
+        {"name": "argmax axis -1", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "prim": "argmax", "axis": -1,
+         "keepdims": 0, "want": [2, 2], "want_shape": [2], "tol": 0.0},
+        {"name": "argmax of a vector (f32)", "x": [1.0, 5.0, 3.0, 2.0, 4.0], "shape": [5], "dtype": "f32",
+         "prim": "argmax", "axis": 0, "keepdims": 0, "want": [1], "want_shape": [], "tol": 0.0},
+    ]
+
     # src/zpu/kernels.zig:512-543: gemm vs the naive triple loop at 1e-12 on
     # these shapes, inputs a[i] = (i % 7) * 0.5 - 1, b[i] = (i % 5) * 0.25 - 0.5.
     gemm_shapes = [[1, 1, 1], [3, 4, 5], [32, 7, 128], [35, 9, 133], [2, 33, 2]]
@@ -124,6 +150,7 @@ def main(ref):
         "jit_steps": jit_steps,
         "inputs": inputs,
         "known_answers": known,
+        "reduce_known": reduce_known,
         "gemm_shapes": gemm_shapes,
         "reduce_lengths": reduce_lengths,
     }

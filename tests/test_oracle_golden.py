@@ -88,6 +88,59 @@ def test_reduction_snapshots(golden):
     snap_close(want, col, tol)
 
 
+@pytest.mark.parametrize("name,fn", [
+    ("sum-axis1-keepdims", lambda x: zo.reduce_axis(x, "sum", 1, True)),
+    ("max-axis1", lambda x: zo.reduce_axis(x, "max_reduce", 1)),
+    ("min-axis0", lambda x: zo.reduce_axis(x, "min_reduce", 0)),
+    ("prod-axis1", lambda x: zo.reduce_axis(x, "prod_op", 1)),
+    ("mean-axis1", lambda x: zo.mean(x, 1)),
+    ("variance-axis1", lambda x: zo.variance(x, 1)),
+    ("argmax-axis1", lambda x: zo.arg_reduce(x, 1)),
+])
+def test_axis_reduction_snapshots(golden, name, fn):
+    """tests/snap/zpu.zig:87-93 on spread(12) as 3 x 4 (f64)."""
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    want, tol, shape = snap(golden, "zpu/reduce/" + name)
+    got = fn(x)
+    assert list(np.shape(got)) == shape, (np.shape(got), shape)
+    snap_close(want, got, tol)
+
+
+def test_reduction_known_answers(golden):
+    """src/zpu/tests.zig:116-124 and examples/audit_edge_cases.zig:138-144."""
+    for case in golden["reduce_known"]:
+        x = np.array(case["x"], dtype=np.float32 if case.get("dtype") == "f32" else np.float64)
+        x = x.reshape(case["shape"])
+        if case["prim"] in ("argmax", "argmin"):
+            got = zo.arg_reduce(x, case["axis"], want_max=case["prim"] == "argmax")
+        else:
+            got = zo.reduce_axis(x, case["prim"], case["axis"], case["keepdims"])
+        assert list(np.shape(got)) == case["want_shape"], case["name"]
+        assert np.all(np.abs(np.asarray(got, np.float64).ravel() - case["want"]) <= case["tol"]), case["name"]
+
+
+def test_arg_reduce_scan_rules():
+    """ops.argReduce's sequential rules (src/zpu/ops.zig:961-969): strict
+    comparison (ties keep the first), NaN never replaces, a NaN first element
+    pins 0, -0.0 ties +0.0; AXIS_NONE with a vmap depth folds payload axes."""
+    nan = float("nan")
+    assert zo.arg_reduce(np.array([1.0, 3.0, 3.0, 2.0]), 0) == 1
+    assert zo.arg_reduce(np.array([1.0, 3.0, 3.0, 2.0]), 0, want_max=False) == 0
+    assert zo.arg_reduce(np.array([nan, 5.0, 7.0]), 0) == 0
+    assert zo.arg_reduce(np.array([nan, 5.0, 7.0]), 0, want_max=False) == 0
+    assert zo.arg_reduce(np.array([1.0, nan, 7.0, nan]), 0) == 2
+    assert zo.arg_reduce(np.array([nan, nan]), 0) == 0
+    assert zo.arg_reduce(np.array([-0.0, 0.0]), 0) == 0
+    assert zo.arg_reduce(np.array([-np.inf, -np.inf]), 0) == 0
+    assert zo.arg_reduce(np.zeros((2, 0)), 1).tolist() == [0, 0]
+    x = np.array([[1.0, 9.0, 2.0, 9.0], [4.0, 1.0, 4.0, 0.0]])
+    assert zo.arg_reduce(x, zo.AXIS_NONE).shape == ()
+    assert zo.arg_reduce(x, zo.AXIS_NONE) == 1
+    assert zo.arg_reduce(x, zo.AXIS_NONE, depth=1).tolist() == [1, 0]
+    assert zo.arg_reduce(x, 0, depth=1).tolist() == [1, 0]
+    assert zo.arg_reduce(x, -1, want_max=False).tolist() == [0, 3]
+
+
 def _log_softmax_rows(x):
     out = np.empty_like(x)
     sm = np.empty_like(x)

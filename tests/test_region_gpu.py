@@ -357,3 +357,112 @@ def test_tanh_sum_propagates_nan(zc):
     for region in ("tanh_sq_affine", "tanh_sq", "tanh"):
         (got,) = _tanh_sum_plan(zc, region, n).run([x])
         assert math.isnan(float(got.cpu())), region
+
+
+def _snapshot_plan(zc, name):
+    """The jit plan each tests/snap/zpu.zig:87-93 case records (3 x 4 f64):
+    mean and variance are their ops.zig:894-922 compositions with 1/count as
+    a captured rank-0 blob."""
+    c = [(2, np.float64(0.25))]
+    one = {"sum-axis1-keepdims": ("sum", 1, 1), "max-axis1": ("max_reduce", 1, 0),
+           "min-axis0": ("min_reduce", 0, 0), "prod-axis1": ("prod_op", 1, 0), "argmax-axis1": ("argmax", 1, 0)}
+    args = [(1, zc.F64, (3, 4))]
+    if name in one:
+        prim, axis, keep = one[name]
+        return zc.Plan(args, [], [(prim, [1], 10, axis, keep)], [10])
+    if name == "mean-axis1":
+        return zc.Plan(args, c, [("sum", [1], 10, 1, 0), ("mul", [10, 2], 11, -2, 0)], [11])
+    steps = [("sum", [1], 10, 1, 1), ("mul", [10, 2], 11, -2, 0), ("sub", [1, 11], 12, -2, 0),
+             ("square", [12], 13, -2, 0), ("sum", [13], 14, 1, 0), ("mul", [14, 2], 15, -2, 0)]
+    return zc.Plan(args, c, steps, [15])
+
+
+@pytest.mark.parametrize("name", ["sum-axis1-keepdims", "max-axis1", "min-axis0", "prod-axis1", "mean-axis1",
+                                  "variance-axis1", "argmax-axis1"])
+def test_axis_reductions_match_the_snapshots(zc, golden, name):
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    snapv = golden["snapshots"]["zpu/reduce/" + name]
+    (got,) = _snapshot_plan(zc, name).run([torch.from_numpy(x).cuda()])
+    g = got.cpu().numpy()
+    assert list(g.shape) == snapv["shape"], (g.shape, snapv["shape"])
+    want = np.array(snapv["values"])
+    if name == "argmax-axis1":
+        assert got.dtype == torch.int64
+        assert g.ravel().tolist() == want.astype(np.int64).tolist()
+    else:
+        g = g.ravel()
+        assert np.all(np.abs(g - want) <= snapv["tol"] * np.maximum(1, np.maximum(np.abs(g), np.abs(want))))
+
+
+def test_reduction_known_answers_on_device(zc, golden):
+    for case in golden["reduce_known"]:
+        f32 = case.get("dtype") == "f32"
+        x = np.array(case["x"], dtype=np.float32 if f32 else np.float64).reshape(case["shape"])
+        p = zc.Plan([(1, zc.F32 if f32 else zc.F64, tuple(case["shape"]))], [],
+                    [(case["prim"], [1], 10, case["axis"], case["keepdims"])], [10])
+        (got,) = p.run([torch.from_numpy(x).cuda()])
+        assert list(got.shape) == case["want_shape"], case["name"]
+        g = got.cpu().numpy().astype(np.float64).ravel()
+        assert np.all(np.abs(g - case["want"]) <= case["tol"]), (case["name"], g)
+
+
+@pytest.mark.parametrize("axis", [-2, 0, 1, 2, -1])
+@pytest.mark.parametrize("prim", ["argmax", "argmin"])
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_arg_reductions_match_the_oracle(zc, axis, prim, dt):
+    """argmax / argmin fused with an element-wise producer (abs, so +-v tie)
+    over small integers (many ties), NaNs at scattered places and at the
+    start of some rows: the index zpu's sequential scan returns."""
+    rng = np.random.default_rng(7 + axis)
+    shape = (9, 37, 70)
+    npdt = np.float32 if dt == "f32" else np.float64
+    x = rng.integers(-6, 7, size=shape).astype(npdt)
+    nan_at = rng.random(shape) < 0.01
+    x[nan_at] = np.nan
+    x[0, 0, :] = np.nan  # position 0 of every axis-2 row of x[0, 0]
+    x[:, 0, 0] = np.nan  # position 0 along axis 0 / 1 for some outputs
+    p = zc.Plan([(1, zc.F32 if dt == "f32" else zc.F64, shape)], [],
+                [("abs", [1], 10, -2, 0), (prim, [10], 11, axis, 0)], [11, 10])
+    red, a = p.run([torch.from_numpy(x).cuda()])
+    want = zo.arg_reduce(np.abs(x), axis, want_max=prim == "argmax")
+    assert red.dtype == torch.int64
+    assert tuple(red.shape) == want.shape
+    assert np.array_equal(red.cpu().numpy(), want)
+    assert np.array_equal(a.cpu().numpy(), np.abs(x), equal_nan=True)
+
+
+@pytest.mark.parametrize("prim", ["argmax", "argmin"])
+def test_full_arg_reduction_across_blocks(zc, prim):
+    """A full argmax over 2^22 + 5 elements (many blocks): the extreme value
+    planted at several places, the first of them wins; a NaN at index 0
+    gives 0."""
+    n = (1 << 22) + 5
+    x = zo.uniform_range(33, n, -1.0, 1.0)
+    v = 7.5 if prim == "argmax" else -7.5
+    places = [3_000_001, 17, 4_194_300, 1_048_576]
+    x[places] = v
+    p = zc.Plan([(1, zc.F32, (n,))], [], [(prim, [1], 10, -2, 0)], [10])
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    assert int(got.cpu()) == min(places)
+    x[0] = np.nan
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    assert int(got.cpu()) == 0
+
+
+@pytest.mark.parametrize("prim,axis,keep", [("sum", -2, 0), ("sum", -2, 1), ("max_reduce", 0, 0), ("sum", -1, 1),
+                                            ("argmax", -2, 0), ("argmin", 1, 0)])
+def test_reductions_fold_payload_axes_under_vmap(zc, prim, axis, keep):
+    """With batch_depth 1 (vmap) AXIS_NONE folds the payload axes only and a
+    non-negative axis counts from the first payload axis (ops.axesMaskOf,
+    src/zpu/ops.zig:630-642)."""
+    shape = (4, 6, 10)
+    x = zo.uniform_range(5, int(np.prod(shape)), -2.0, 2.0).reshape(shape)
+    p = zc.Plan([(1, zc.F32, shape, 1)], [], [(prim, [1], 10, axis, keep)], [10])
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    if prim in ("argmax", "argmin"):
+        want = zo.arg_reduce(x, axis, depth=1, want_max=prim == "argmax")
+        assert np.array_equal(got.cpu().numpy(), want)
+    else:
+        want = zo.reduce_axis(x, prim, axis, keep, depth=1)
+        assert tuple(got.shape) == want.shape
+        assert np.allclose(got.cpu().numpy(), want, rtol=2e-6, atol=1e-6)

@@ -7,7 +7,7 @@ a CPU path when the library is missing -- importing the operations raises.
 """
 import ctypes as C
 
-from ._capi import (AXIS_NONE, F32, F64, PRIM, Blob, Step, Tensor, Value, ZpuCudaError, check,
+from ._capi import (AXIS_NONE, DT_I64, F32, F64, PRIM, Blob, Step, Tensor, Value, ZpuCudaError, check,
                     exported_names, lib)
 
 __all__ = ["lib", "check", "ZpuCudaError", "Plan", "gemm", "matmul", "matmul_shape", "stream_of",
@@ -43,6 +43,8 @@ def dtype_code(t):
 
 def torch_dtype(code):
     torch = _torch()
+    if code == DT_I64:
+        return torch.int64
     return torch.float32 if code == F32 else torch.float64
 
 
@@ -133,14 +135,16 @@ class Plan:
     """A lowered jit plan (zpucuda_plan_*)."""
 
     def __init__(self, args, blobs, steps, out_ids):
-        """args: [(id, dtype_code, shape)], blobs: [(id, numpy array)],
-        steps: [(prim, [input ids], out id, axis, keepdims)], out_ids: [id]."""
+        """args: [(id, dtype_code, shape[, batch_depth])], blobs: [(id, numpy
+        array)], steps: [(prim, [input ids], out id, axis, keepdims)],
+        out_ids: [id].  batch_depth is Tensor.batch_depth (vmap's leading
+        axes, src/zpu/tensor.zig:79-89): reductions fold payload axes only."""
         import numpy as np
         L = lib()
         self._keep = []
         va = (Value * max(1, len(args)))()
-        for i, (vid, dt, shape) in enumerate(args):
-            _fill_value(va[i], vid, dt, shape)
+        for i, a in enumerate(args):
+            _fill_value(va[i], a[0], a[1], a[2], a[3] if len(a) > 3 else 0)
         bl = (Blob * max(1, len(blobs)))()
         for i, (vid, arr) in enumerate(blobs):
             arr = np.ascontiguousarray(arr)
@@ -209,10 +213,10 @@ class Plan:
             self.handle = None
 
 
-def _fill_value(v, vid, dt, shape):
+def _fill_value(v, vid, dt, shape, depth=0):
     v.id = vid
     v.dtype = dt
     v.rank = len(shape)
     for i, s in enumerate(shape):
         v.dims[i] = s
-    v.batch_depth = 0
+    v.batch_depth = depth

@@ -14,6 +14,7 @@ LIB_PATH = os.environ.get("ZPUCUDA_LIB") or os.path.join(HERE, "libzpucuda.so")
 MAX_RANK = 8
 AXIS_NONE = -2
 F64, F32 = 0, 1
+DT_I64 = 3  # zpu DType.i64: argmax / argmin results
 
 STATUS = {
     0: "ok", 1: "OutOfMemory", 2: "ShapeMismatch", 3: "DTypeMismatch", 4: "RankTooLarge",
@@ -31,7 +32,7 @@ PRIM = {
     "ceil": 28, "round": 29, "trunc": 30, "sign": 31, "isnan": 32, "isinf": 33,
     "isfinite": 34, "add": 35, "sub": 36, "mul": 37, "div": 38, "pow": 39, "maximum": 40,
     "minimum": 41, "atan2": 42, "hypot": 43, "mod_op": 44, "eq": 45, "where": 55,
-    "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "matmul": 80,
+    "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "argmax": 64, "argmin": 65, "matmul": 80,
     "constant": 87, "copy": 88,
 }
 

@@ -29,6 +29,8 @@ enum {
     PRIM_PROD = 59,
     PRIM_MAX_REDUCE = 60,
     PRIM_MIN_REDUCE = 61,
+    PRIM_ARGMAX = 64,
+    PRIM_ARGMIN = 65,
     PRIM_MATMUL = 80,
 };
 
@@ -43,7 +45,9 @@ const char *kPrimNames[] = {
 // src/zpu/prims.zig:198, minus predicates and the selection ops).
 bool region_unary(int p) { return p >= 0 && p <= 31; }
 bool region_binary(int p) { return p >= 35 && p <= 44; }
-bool region_reduce(int p) { return p >= PRIM_SUM && p <= PRIM_MIN_REDUCE; }
+bool arg_reduce(int p) { return p == PRIM_ARGMAX || p == PRIM_ARGMIN; }
+bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p); }
+bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
 
 struct Shape {
     int rank = 0;
@@ -133,7 +137,7 @@ struct zpucuda_plan {
 
 namespace {
 
-size_t itemsize(int dt) { return dt == ZPUCUDA_F64 ? 8 : 4; }
+size_t itemsize(int dt) { return dt == ZPUCUDA_F32 ? 4 : 8; }
 
 int lower_fail(zpucuda_plan *p, int st, const std::string &why) {
     delete p;
@@ -143,6 +147,22 @@ int lower_fail(zpucuda_plan *p, int st, const std::string &why) {
 std::string prim_name(int p) {
     if (p >= 0 && p < (int)(sizeof(kPrimNames) / sizeof(kPrimNames[0]))) return kPrimNames[p];
     return "prim" + std::to_string(p);
+}
+
+// The axes a reduction folds (ops.axesMaskOf, src/zpu/ops.zig:630-642):
+// AXIS_NONE folds the payload axes [depth, rank); a non-negative axis counts
+// from the first payload axis, a negative one from the last axis.  The folded
+// axes are the contiguous range [*first, *last] (empty for a rank-0 value).
+bool reduced_axes(const Shape &s, int depth, int axis, int *first, int *last) {
+    if (axis == ZPUCUDA_AXIS_NONE) {
+        *first = depth < s.rank ? depth : s.rank;
+        *last = s.rank - 1;
+        return true;
+    }
+    const int a = axis >= 0 ? axis + depth : axis + s.rank;
+    if (a < 0 || a >= s.rank) return false;
+    *first = *last = a;
+    return true;
 }
 
 }  // namespace
@@ -214,6 +234,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         const Value &a = vals[st.ins[0]];
         o.dtype = a.dtype;
         o.depth = a.depth;
+        if ((region_unary(st.prim) || region_binary(st.prim) || region_reduce(st.prim)) && !float_dtype(a.dtype))
+            return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a non-float value");
         if (region_unary(st.prim) && st.n_inputs == 1) {
             o.shape = a.shape;
         } else if (region_binary(st.prim) && st.n_inputs == 2) {
@@ -224,20 +246,21 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             o.depth = std::max(a.depth, b.depth);
             if (!broadcast(a.shape, b.shape, &o.shape)) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
         } else if (region_reduce(st.prim) && st.n_inputs == 1) {
-            if (st.axis == ZPUCUDA_AXIS_NONE) {
-                o.shape.rank = st.keepdims ? a.shape.rank : 0;
-                for (int i = 0; i < o.shape.rank; i++) o.shape.dims[i] = 1;
-            } else {
-                int ax = st.axis < 0 ? st.axis + a.shape.rank : st.axis;
-                if (ax < 0 || ax >= a.shape.rank) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "reduction axis");
-                o.shape = a.shape;
-                if (st.keepdims) {
-                    o.shape.dims[ax] = 1;
-                } else {  // drop axis ax
-                    for (int d = ax; d + 1 < a.shape.rank; d++) o.shape.dims[d] = a.shape.dims[d + 1];
-                    o.shape.rank -= 1;
+            // ops.reduceOutShape (src/zpu/ops.zig:644-660); argmax / argmin
+            // never keep the folded axes and give i64 (ops.zig:931-934)
+            int r0 = 0, r1 = -1;
+            if (!reduced_axes(a.shape, a.depth, st.axis, &r0, &r1))
+                return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "reduction axis");
+            const bool keep = st.keepdims && !arg_reduce(st.prim);
+            o.shape.rank = 0;
+            for (int d = 0; d < a.shape.rank; d++) {
+                if (d >= r0 && d <= r1) {
+                    if (keep) o.shape.dims[o.shape.rank++] = 1;
+                } else {
+                    o.shape.dims[o.shape.rank++] = a.shape.dims[d];
                 }
             }
+            if (arg_reduce(st.prim)) o.dtype = ZPUCUDA_I64;
         } else if (st.prim == PRIM_MATMUL && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
             if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed-dtype matmul");
@@ -426,7 +449,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         int nreg = P.n_in;
         int n_insn = P.n_in;
         bool has_red = false;
-        int red_prim = -1, red_axis = ZPUCUDA_AXIS_NONE;
+        int red_prim = -1, red_axis = ZPUCUDA_AXIS_NONE, red_depth = 0;
         uint64_t red_in = 0, red_out_id = 0;
         for (int m : member) {
             const zpucuda_step &st = steps[m];
@@ -434,6 +457,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 has_red = true;
                 red_prim = st.prim;
                 red_axis = st.axis;
+                red_depth = vals[st.ins[0]].depth;
                 red_in = st.ins[0];
                 red_out_id = st.out;
                 continue;
@@ -466,31 +490,38 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         }
         if (has_red) {
             P.reduce = red_prim == PRIM_SUM ? RED_SUM : red_prim == PRIM_PROD ? RED_PROD
-                     : red_prim == PRIM_MAX_REDUCE ? RED_MAX : RED_MIN;
-            P.reduce_all = red_axis == ZPUCUDA_AXIS_NONE;
+                     : red_prim == PRIM_MAX_REDUCE ? RED_MAX : red_prim == PRIM_MIN_REDUCE ? RED_MIN
+                     : red_prim == PRIM_ARGMAX ? RED_ARGMAX : RED_ARGMIN;
             P.reduce_reg = reg[red_in];
-            const int rax = P.reduce_all ? -1 : (red_axis < 0 ? red_axis + rshape.rank : red_axis);
-            if (!P.reduce_all && rax != rshape.rank - 1) {  // [outer, red_len, inner]
-                P.reduce_mid = 1;
-                P.red_len = rshape.dims[rax];
+            // the folded axes [r0, r1] split the region into [outer, red_len, inner]
+            int r0 = 0, r1 = -1;
+            reduced_axes(rshape, red_depth, red_axis, &r0, &r1);
+            int64_t outer = 1, red_len = 1, inner = 1;
+            for (int d = 0; d < rshape.rank; d++) {
+                if (d < r0) outer *= rshape.dims[d];
+                else if (d <= r1) red_len *= rshape.dims[d];
+                else inner *= rshape.dims[d];
+            }
+            P.reduce_all = (outer == 1 && inner == 1) ? 1 : 0;
+            if (P.reduce_all) {
+                P.inner = P.numel;
                 P.outer = 1;
-                P.inner = 1;
-                for (int d = 0; d < rax; d++) P.outer *= rshape.dims[d];
-                for (int d = rax + 1; d < rshape.rank; d++) P.inner *= rshape.dims[d];
-            } else {
-                P.inner = P.reduce_all ? P.numel : (rshape.rank ? rshape.dims[rshape.rank - 1] : 1);
-                P.outer = P.reduce_all ? 1 : (P.inner ? P.numel / P.inner : 1);
-                if (!P.reduce_all && P.inner == 0) {
-                    P.outer = 1;
-                    for (int d = 0; d < rshape.rank - 1; d++) P.outer *= rshape.dims[d];
-                }
+            } else if (inner != 1) {  // an axis before the last: [outer, red_len, inner]
+                P.reduce_mid = 1;
+                P.red_len = red_len;
+                P.outer = outer;
+                P.inner = inner;
+            } else {  // the trailing axes: rows of red_len
+                P.inner = red_len;
+                P.outer = outer;
             }
             L.has_red = true;
             L.red = materialise(red_out_id);
             if (L.red.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
             char buf[64];
             snprintf(buf, sizeof buf, ";out=r%d;red=%s%s", P.reduce_reg,
-                     red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max" : "min",
+                     red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max"
+                     : red_prim == PRIM_MIN_REDUCE ? "min" : red_prim == PRIM_ARGMAX ? "argmax" : "argmin",
                      P.reduce_all ? "" : P.reduce_mid ? "_axis" : "_rows");
             sig += buf;
             if (P.reduce_all) {
@@ -564,7 +595,7 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
 static size_t value_bytes(const zpucuda_value &v) {
     size_t n = 1;
     for (int d = 0; d < v.rank; d++) n *= (size_t)v.dims[d];
-    return n * (v.dtype == ZPUCUDA_F64 ? 8 : 4);
+    return n * (v.dtype == ZPUCUDA_F32 ? 4 : 8);
 }
 
 int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs, void *stream) {

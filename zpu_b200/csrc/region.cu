@@ -290,9 +290,135 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
     }
 }
 
+// ------------------------------------------------ argmax / argmin regions
+//
+// ops.argReduce (src/zpu/ops.zig:931-975) scans the reduced elements in row
+// order: the first seeds the best value, a later one replaces it only when
+// strictly greater (argmax) or smaller (argmin).  So ties keep the first
+// index, a NaN never replaces the best, and a NaN at position 0 keeps index
+// 0 whatever follows.  In parallel every thread scans its positions in
+// ascending order keeping the first strict best among the non-NaN values;
+// partial results merge by value and, on equal values, by the smaller index
+// (the order-free form of the same rule); a NaN at position 0 gives 0.
+struct ArgAcc {
+    double best;
+    int64_t idx;   // -1: no non-NaN value seen
+    int64_t nan0;  // 1: the value at position 0 is NaN
+};
+__device__ __forceinline__ ArgAcc arg_empty() { return ArgAcc{0.0, -1, 0}; }
+__device__ __forceinline__ void arg_take(ArgAcc &a, double v, int64_t k, bool want_max) {
+    if (isnan(v)) {
+        if (k == 0) a.nan0 = 1;
+        return;
+    }
+    if (a.idx < 0 || (want_max ? v > a.best : v < a.best)) {
+        a.best = v;
+        a.idx = k;
+    }
+}
+__device__ __forceinline__ ArgAcc arg_merge(ArgAcc a, const ArgAcc &b, bool want_max) {
+    a.nan0 |= b.nan0;
+    if (b.idx < 0) return a;
+    bool take_b;
+    if (a.idx < 0) take_b = true;
+    else if (want_max ? b.best > a.best : b.best < a.best) take_b = true;
+    else if (want_max ? a.best > b.best : a.best < b.best) take_b = false;
+    else take_b = b.idx < a.idx;
+    if (take_b) {
+        a.best = b.best;
+        a.idx = b.idx;
+    }
+    return a;
+}
+__device__ __forceinline__ int64_t arg_result(const ArgAcc &a) { return (a.nan0 || a.idx < 0) ? 0 : a.idx; }
+__device__ __forceinline__ ArgAcc arg_warp(ArgAcc a, bool want_max) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgAcc b;
+        b.best = __shfl_xor_sync(0xffffffffu, a.best, o);
+        b.idx = __shfl_xor_sync(0xffffffffu, a.idx, o);
+        b.nan0 = __shfl_xor_sync(0xffffffffu, a.nan0, o);
+        a = arg_merge(a, b, want_max);
+    }
+    return a;
+}
+
+// MODE as interp_kernel (1: all axes, 2: trailing axes, one warp per row,
+// 3: an inner axis, one thread per output); the output is i64.
+template <class T, int MODE>
+__global__ void __launch_bounds__(kInterpThreads) interp_arg_kernel(const __grid_constant__ RegionProgram p,
+                                                                    const __grid_constant__ RegionIO io) {
+    T r[RP_MAX_REG];
+    const bool want_max = p.reduce == RED_ARGMAX;
+    int64_t *out = (int64_t *)io.red_out;
+    if (MODE == 1) {
+        ArgAcc acc = arg_empty();
+        for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
+             i += (int64_t)gridDim.x * kInterpThreads) {
+            eval<T>(p, io, i, r);
+            store_outputs<T>(p, io, i, r);
+            arg_take(acc, (double)r[p.reduce_reg], i, want_max);
+        }
+        __shared__ ArgAcc part[kInterpThreads / 32];
+        __shared__ bool last;
+        acc = arg_warp(acc, want_max);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+        __syncthreads();
+        double *best = io.partials;
+        int64_t *idx = (int64_t *)(io.partials + kMaxRegionBlocks);
+        int64_t *nan0 = idx + kMaxRegionBlocks;
+        if (threadIdx.x == 0) {
+            ArgAcc b = part[0];
+            for (int w = 1; w < kInterpThreads / 32; w++) b = arg_merge(b, part[w], want_max);
+            best[blockIdx.x] = b.best;
+            idx[blockIdx.x] = b.idx;
+            nan0[blockIdx.x] = b.nan0;
+            __threadfence();
+            last = atomicAdd(io.ticket, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (!last || threadIdx.x != 0) return;
+        __threadfence();
+        ArgAcc v = arg_empty();
+        for (unsigned b = 0; b < gridDim.x; b++)
+            v = arg_merge(v, ArgAcc{__ldcg(best + b), __ldcg(idx + b), __ldcg(nan0 + b)}, want_max);
+        out[0] = arg_result(v);
+        *io.ticket = 0u;
+    } else if (MODE == 3) {
+        const int64_t n_out = p.outer * p.inner;
+        for (int64_t o = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; o < n_out;
+             o += (int64_t)gridDim.x * kInterpThreads) {
+            const int64_t a = o / p.inner, c = o - a * p.inner;
+            ArgAcc acc = arg_empty();
+            for (int64_t k = 0; k < p.red_len; k++) {
+                const int64_t i = (a * p.red_len + k) * p.inner + c;
+                eval<T>(p, io, i, r);
+                store_outputs<T>(p, io, i, r);
+                arg_take(acc, (double)r[p.reduce_reg], k, want_max);
+            }
+            out[o] = arg_result(acc);
+        }
+    } else {
+        const int lane = threadIdx.x & 31;
+        const int64_t warps = (int64_t)gridDim.x * (kInterpThreads / 32);
+        for (int64_t row = ((int64_t)blockIdx.x * kInterpThreads + threadIdx.x) >> 5; row < p.outer; row += warps) {
+            ArgAcc acc = arg_empty();
+            for (int64_t j = lane; j < p.inner; j += 32) {
+                const int64_t i = row * p.inner + j;
+                eval<T>(p, io, i, r);
+                store_outputs<T>(p, io, i, r);
+                arg_take(acc, (double)r[p.reduce_reg], j, want_max);
+            }
+            acc = arg_warp(acc, want_max);
+            if (lane == 0) out[row] = arg_result(acc);
+        }
+    }
+}
+
 template <class T>
 int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
     const int sms = num_sms();
+    const bool arg = p.reduce == RED_ARGMAX || p.reduce == RED_ARGMIN;
     if (p.reduce == RED_NONE) {
         if (p.numel == 0) return ZPUCUDA_OK;
         int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
@@ -302,18 +428,21 @@ int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
         int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
         if (g > sms * 8) g = sms * 8;
         if (g < 1) g = 1;
-        interp_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else if (p.reduce_mid) {
         const int64_t n_out = p.outer * p.inner;
         if (n_out == 0) return ZPUCUDA_OK;
         int64_t g = (n_out + kInterpThreads - 1) / kInterpThreads;
         if (g > sms * 8) g = sms * 8;
-        interp_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else {
         if (p.outer == 0) return ZPUCUDA_OK;
         int64_t g = (p.outer + (kInterpThreads / 32) - 1) / (kInterpThreads / 32);
         if (g > sms * 8) g = sms * 8;
-        interp_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     }
     ZC_LAUNCHED("region bytecode kernel");
     return ZPUCUDA_OK;

@@ -24,7 +24,7 @@ constexpr int RP_MAX_REG = 32;
 constexpr int RP_MAX_RANK = 8;
 
 enum : int8_t { IN_FULL = 0, IN_SCALAR = 1, IN_ROW = 2, IN_GENERAL = 3 };
-enum : int32_t { RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4 };
+enum : int32_t { RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4, RED_ARGMAX = 5, RED_ARGMIN = 6 };
 enum : uint8_t { OPC_LOAD = 250 };
 
 struct Insn {
@@ -66,10 +66,11 @@ struct RegionIO {
     unsigned int *error;    // set (never cleared by a kernel) when a bounded wait runs out
 };
 
-// Scratch a full reduction needs: a ticket word, an error word, one double
-// per block.
+// Scratch a full reduction needs: a ticket word, an error word, then one
+// double per block (an arg reduction uses three arrays of kMaxRegionBlocks
+// 8-byte words: best value, index, leading-NaN flag).
 constexpr int kMaxRegionBlocks = 148 * 16;
-constexpr size_t kRegionWorkspaceBytes = 256 + sizeof(double) * kMaxRegionBlocks;
+constexpr size_t kRegionWorkspaceBytes = 256 + 3 * sizeof(double) * kMaxRegionBlocks;
 
 typedef int (*FusedLaunch)(const RegionProgram &p, const RegionIO &io, cudaStream_t s);
 struct CatalogueEntry {
