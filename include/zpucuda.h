@@ -49,9 +49,13 @@ enum {
     ZPUCUDA_ERR_INVALID_ARGUMENT = 16    /* NULL pointer, negative size, ... */
 };
 
-/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13).  I64 is
- * produced only by argmax / argmin steps of a plan. */
-enum { ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1, ZPUCUDA_I64 = 3 };
+/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13).  GEMM,
+ * plans and the RNG take F64 / F32 (plans give I64 from argmax / argmin);
+ * zpucuda_tensor_copy takes all nine.  BOOL is one byte, 0 or 1. */
+enum {
+    ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1, ZPUCUDA_F16 = 2, ZPUCUDA_I64 = 3, ZPUCUDA_I32 = 4,
+    ZPUCUDA_I16 = 5, ZPUCUDA_I8 = 6, ZPUCUDA_U8 = 7, ZPUCUDA_BOOL = 8
+};
 
 /* prims.AXIS_NONE (src/zpu/prims.zig:169). */
 #define ZPUCUDA_AXIS_NONE (-2)
@@ -148,6 +152,20 @@ typedef struct zpucuda_tensor {
  * must be row-major or transposed (unit stride on one of them); anything else
  * returns ZPUCUDA_ERR_NON_CONTIGUOUS and the caller materialises it. */
 int zpucuda_matmul_shape(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out);
+/* Tensor.clone, Tensor.toContiguous and ops.cast on HBM
+ * (src/zpu/tensor.zig:356-361,395-404, src/zpu/ops.zig:2062-2071): writes
+ * the elements of the view `src` in logical (row-major) order into the
+ * contiguous buffer dst->data of type dst->dtype, each as zpu's
+ * writeF64(readLogical) does -- widened to f64, then narrowed: floats round
+ * to nearest; integer types take 0 for NaN, else clamp to their range and
+ * truncate toward zero (i64 saturates at 2^63, where zpu is undefined);
+ * BOOL is v != 0.  src may have any strides (negative from flip, 0 from
+ * broadcast); dst must have src's dims and must not overlap it; its strides
+ * are set to the contiguous ones.  clone: dst->dtype == src->dtype;
+ * toContiguous: the same, called only for a non-contiguous src (zpu returns
+ * a contiguous tensor itself); cast: another dtype (zpu returns the input
+ * for an equal one). */
+int zpucuda_tensor_copy(const zpucuda_tensor *src, zpucuda_tensor *dst, void *stream);
 int zpucuda_matmul(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out,
                    void *stream);
 

@@ -292,6 +292,47 @@ def variance(x, axis=AXIS_NONE, keepdims=False, depth=0):
     return mean(np.square(np.asarray(x, dtype=np.float64) - m), axis, keepdims, depth)
 
 
+# zpu DType order (src/zpu/dtype.zig:4-13) as numpy types
+DTYPES = [np.float64, np.float32, np.float16, np.int64, np.int32, np.int16, np.int8, np.uint8, np.bool_]
+
+
+def to_f64(x):
+    """scalar.toF64 (src/zpu/scalar.zig:7-15) element-wise."""
+    return np.asarray(x).astype(np.float64)
+
+
+def from_f64(v, dt):
+    """scalar.fromF64 (src/zpu/scalar.zig:17-27) element-wise: floats round to
+    nearest, bool is v != 0, an integer type takes 0 for NaN, else clamps to
+    [minInt, maxInt] (as f64) and truncates toward zero.  For i64 the clamp
+    bound (f64)maxInt = 2^63 is out of range (undefined in Zig); the device
+    saturates it to maxInt, and so does this restatement."""
+    v = np.asarray(v, dtype=np.float64)
+    dt = np.dtype(dt)
+    if dt.kind == "f":
+        with np.errstate(over="ignore"):
+            return v.astype(dt)
+    if dt.kind == "b":
+        return v != 0
+    info = np.iinfo(dt)
+    nan = np.isnan(v)
+    c = np.clip(np.where(nan, 0.0, v), float(info.min), float(info.max))
+    t = np.trunc(c)
+    if dt == np.int64:
+        top = t >= 2.0 ** 63
+        out = np.where(top, 0.0, t).astype(np.int64)
+        out[top] = info.max
+        return out
+    return t.astype(dt)
+
+
+def tensor_copy(x, dt):
+    """Tensor.clone / toContiguous / ops.cast (src/zpu/tensor.zig:356-404,
+    src/zpu/ops.zig:2062-2071): writeF64(i, readLogical(n, i)) for every i
+    of the logical order -- a numpy view gives that order itself."""
+    return from_f64(to_f64(np.ascontiguousarray(x)), dt)
+
+
 def sum_f64(x):
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     return lib().zo_sum_f64_of_f32(_p(x), x.size)

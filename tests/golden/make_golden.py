@@ -43,6 +43,9 @@ CASES = {
     "nn/softmax": 1e-9,            # tests/snap/zpu.zig:142
     "optim/adam-step1": 1e-9,      # tests/snap/zpu.zig:340
     "optim/adam-step10": 1e-9,     # tests/snap/zpu.zig:342
+    "tensor/bools": 0.0,           # tests/snap/zpu.zig:48 (cast of spread(6) to bool)
+    "shape/transpose": 1e-9,       # tests/snap/zpu.zig:96
+    "shape/flip": 1e-9,            # tests/snap/zpu.zig:97
     "rng/normal-seed12345": 0.0,   # tests/snap/zpu.zig:355
     "rng/uniform-seed12345": 0.0,  # tests/snap/zpu.zig:358
 }
@@ -86,6 +89,7 @@ def main(ref):
         "spd3": [4.0, 1.0, 0.5, 1.0, 3.0, 0.25, 0.5, 0.25, 2.0],
         "rhs3": [1.0, 2.0, 3.0],
         # tests/snap/zpu.zig:28-36 (x = spread(8) for ops, spread(12) as 3x4 for reductions)
+        "spread6": spread(6),
         "spread8": spread(8),
         "spread12": spread(12),
         # tests/snap/zpu.zig:137-141

@@ -298,3 +298,25 @@ def test_mlp_gradient_finite_difference():
             dn = f64_loss(ps)
             fd = (up - dn) / (2 * h)
             assert abs(grads[pi].ravel()[idx] - fd) < 1e-4, (pi, idx, grads[pi].ravel()[idx], fd)
+
+
+def test_cast_and_view_snapshots(golden):
+    """tests/snap/zpu.zig:48,96-97: cast(spread(6), bool); the transpose and
+    flip views of spread(12) as 3 x 4 read in logical order."""
+    want, tol, shape = snap(golden, "zpu/tensor/bools")
+    got = zo.tensor_copy(np.array(golden["inputs"]["spread6"]), np.bool_)
+    assert got.astype(np.float64).tolist() == want.tolist()
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    want, tol, shape = snap(golden, "zpu/shape/transpose")
+    snap_close(want, zo.tensor_copy(x.T, np.float64), tol)
+    want, tol, shape = snap(golden, "zpu/shape/flip")
+    snap_close(want, zo.tensor_copy(x[:, ::-1], np.float64), tol)
+
+
+def test_from_f64_rules():
+    """scalar.fromF64 (src/zpu/scalar.zig:17-27) by hand."""
+    v = np.array([np.nan, 2.9, -2.9, 300.0, -300.0, np.inf, -np.inf, -0.0])
+    assert zo.from_f64(v, np.uint8).tolist() == [0, 2, 0, 255, 0, 255, 0, 0]
+    assert zo.from_f64(v, np.int8).tolist() == [0, 2, -2, 127, -128, 127, -128, 0]
+    assert zo.from_f64(v, np.bool_).tolist() == [True, True, True, True, True, True, True, False]
+    assert zo.from_f64(np.array([2.0 ** 63, -2.0 ** 64]), np.int64).tolist() == [2 ** 63 - 1, -2 ** 63]

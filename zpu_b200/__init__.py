@@ -81,13 +81,39 @@ def tensor_desc(t, batch_depth=0):
     """zpucuda_tensor for a torch tensor view (strides in elements)."""
     d = Tensor()
     d.data = t.data_ptr()
-    d.dtype = dtype_code(t)
+    d.dtype = dtype_code(t) if t.is_floating_point() and t.dtype != _torch().float16 else storage_code(t)
     d.rank = t.dim()
     for i in range(t.dim()):
         d.dims[i] = t.shape[i]
         d.strides[i] = t.stride(i)
     d.batch_depth = batch_depth
     return d
+
+
+def storage_code(t):
+    """zpu DType code (src/zpu/dtype.zig:4-13) of a torch tensor's element type."""
+    torch = _torch()
+    codes = {torch.float64: 0, torch.float32: 1, torch.float16: 2, torch.int64: 3, torch.int32: 4,
+             torch.int16: 5, torch.int8: 6, torch.uint8: 7, torch.bool: 8}
+    if t.dtype not in codes:
+        raise ZpuCudaError(9, "dtype %s" % t.dtype)
+    return codes[t.dtype]
+
+
+def tensor_copy(src, out, stream=None):
+    """Tensor.clone / toContiguous / ops.cast on device: the elements of the
+    view `src` (a torch tensor, or a zpucuda_tensor descriptor for views torch
+    cannot express, e.g. negative strides) in logical order into the
+    contiguous torch tensor `out`, converted to out's type as zpu converts."""
+    if isinstance(src, Tensor):
+        d = src
+    else:
+        d = tensor_desc(src)
+        d.dtype = storage_code(src)
+    o = tensor_desc(out)
+    o.dtype = storage_code(out)
+    check(lib().zpucuda_tensor_copy(C.byref(d), C.byref(o), stream_of(stream)))
+    return out
 
 
 def matmul_shape(a, b, a_depth=0, b_depth=0):

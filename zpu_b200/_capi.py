@@ -106,6 +106,7 @@ SIGNATURES = {
     "zpucuda_rng_normal": (I32, [U64, I32, P, I64, P]),
     "zpucuda_rng_randint": (I32, [U64, P, I64, I64, I64, P]),
     "zpucuda_chain_tanh_sq_affine_sum_noalloc": (I32, [P, I64, P, P, P, P]),
+    "zpucuda_tensor_copy": (I32, [P, P, P]),
     "zpucuda_nccl_unique_id": (I32, [P]),
     "zpucuda_nccl_init": (I32, [I32, I32, P, I64]),
     "zpucuda_nccl_allreduce_f32": (I32, [P, I64, P]),
