@@ -49,9 +49,10 @@ enum {
     ZPUCUDA_ERR_INVALID_ARGUMENT = 16    /* NULL pointer, negative size, ... */
 };
 
-/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13).  GEMM,
- * plans and the RNG take F64 / F32 (plans give I64 from argmax / argmin);
- * zpucuda_tensor_copy takes all nine.  BOOL is one byte, 0 or 1. */
+/* Element types: zpu's DType enum order (src/zpu/dtype.zig:4-13).  GEMM
+ * and the RNG take F64 / F32; plans take F64 / F32 / BOOL values (predicates
+ * and any / all give BOOL, argmax / argmin give I64); zpucuda_tensor_copy
+ * takes all nine.  BOOL is one byte, 0 or 1. */
 enum {
     ZPUCUDA_F64 = 0, ZPUCUDA_F32 = 1, ZPUCUDA_F16 = 2, ZPUCUDA_I64 = 3, ZPUCUDA_I32 = 4,
     ZPUCUDA_I16 = 5, ZPUCUDA_I8 = 6, ZPUCUDA_U8 = 7, ZPUCUDA_BOOL = 8
@@ -187,7 +188,7 @@ typedef struct zpucuda_step {
     uint64_t ins[3];
     uint64_t out;
     int32_t axis;     /* Attrs.axis, ZPUCUDA_AXIS_NONE for a full reduction */
-    int32_t keepdims; /* Attrs.withKeepDims */
+    int32_t flags;    /* Attrs.flags: bit 0 KEEP_DIMS (reductions), bit 5 REVERSE (cumsum) */
 } zpucuda_step;
 
 /* jit.Blob (src/zpu/jit.zig:39-42): a constant folded at build time; its
@@ -203,11 +204,14 @@ typedef struct zpucuda_plan zpucuda_plan;
  * maximal runs of element-wise steps (prims.isElementwise,
  * src/zpu/prims.zig:198) that end in at most one sum / prod / max / min over
  * all axes or over any one axis (keepdims or not), or one argmax / argmin
- * (i64 result, ops.argReduce, src/zpu/ops.zig:931-975), become ONE fused
+ * (i64 result, ops.argReduce, src/zpu/ops.zig:931-975), or one any / all
+ * (BOOL result) become ONE fused
  * kernel each (no intermediate HBM traffic).  Reduction axes follow
  * ops.axesMaskOf (ops.zig:630-642): with batch_depth d, AXIS_NONE folds the
  * payload axes [d, rank) and a non-negative axis counts from axis d.  Matmul
- * steps become GEMM launches.  Region kernels come from
+ * steps become GEMM launches; cumsum steps (ops.cumsum, src/zpu/ops.zig:
+ * 2032-2060: f64 running sum along one axis, rounded per element) a scan
+ * launch each.  Region kernels come from
  * a catalogue generated at build time, with a one-pass bytecode kernel for
  * regions outside it.  Steps outside that set make creation fail with
  * ZPUCUDA_ERR_NOT_SUPPORTED. */

@@ -292,6 +292,65 @@ def variance(x, axis=AXIS_NONE, keepdims=False, depth=0):
     return mean(np.square(np.asarray(x, dtype=np.float64) - m), axis, keepdims, depth)
 
 
+def predicate(prim, a, b=None):
+    """The predicates on f64 values (scalar.pred1F / pred2F,
+    src/zpu/scalar.zig:235-259; logicalNot is eq(a, 0), ops.zig:516-520):
+    comparisons by IEEE rules, logical ops on truthiness v != 0 (NaN is
+    true).  Returns bool with numpy broadcasting."""
+    a = np.asarray(a).astype(np.float64)
+    if prim == "isnan":
+        return np.isnan(a)
+    if prim == "isinf":
+        return np.isinf(a)
+    if prim == "isfinite":
+        return np.isfinite(a)
+    if prim == "logical_not":
+        return a == 0
+    b = np.asarray(b).astype(np.float64)
+    with np.errstate(invalid="ignore"):
+        return {"eq": np.equal, "ne": np.not_equal, "lt": np.less, "le": np.less_equal, "gt": np.greater,
+                "ge": np.greater_equal,
+                "logical_and": lambda x, y: (x != 0) & (y != 0),
+                "logical_or": lambda x, y: (x != 0) | (y != 0),
+                "logical_xor": lambda x, y: (x != 0) != (y != 0)}[prim](a, b)
+
+
+def where(cond, a, b):
+    """ops.where (src/zpu/ops.zig:572-590): a where cond != 0 (NaN is true),
+    else b, all three broadcast."""
+    return np.where(np.asarray(cond).astype(np.float64) != 0, a, b)
+
+
+def reduce_bool(x, kind, axis=AXIS_NONE, keepdims=False, depth=0):
+    """ops.any / ops.all (src/zpu/ops.zig:883-888, 838-853): the reduction of
+    x != 0 over the axes axesMaskOf gives; empty axes give false / true."""
+    t = np.asarray(x).astype(np.float64) != 0
+    axes = reduced_axes(t.ndim, axis, depth)
+    fn = np.any if kind == "any_reduce" else np.all
+    return fn(t, axis=axes, keepdims=bool(keepdims))
+
+
+def cumsum(x, axis, reverse=False, depth=0):
+    """ops.cumsum (src/zpu/ops.zig:2032-2060): along ops.realAxis (a
+    non-negative axis counts from the first payload axis, no AXIS_NONE), a
+    running f64 sum, each prefix rounded to x's type; `reverse` from the end."""
+    x = np.asarray(x)
+    ax = axis + depth if axis >= 0 else axis + x.ndim
+    if ax < 0 or ax >= x.ndim:
+        raise ValueError("InvalidAxis")
+    v = np.moveaxis(x.astype(np.float64), ax, -1)
+    if reverse:
+        v = v[..., ::-1]
+    acc = np.zeros(v.shape[:-1])
+    out = np.empty_like(v)
+    for d in range(v.shape[-1]):  # sequential, as zpu adds
+        acc = acc + v[..., d]
+        out[..., d] = acc
+    if reverse:
+        out = out[..., ::-1]
+    return np.moveaxis(out, -1, ax).astype(x.dtype)
+
+
 # zpu DType order (src/zpu/dtype.zig:4-13) as numpy types
 DTYPES = [np.float64, np.float32, np.float16, np.int64, np.int32, np.int16, np.int8, np.uint8, np.bool_]
 

@@ -30,6 +30,8 @@ CASES = {
     "reduce/variance-axis1": 1e-9, # tests/snap/zpu.zig:91
     "reduce/prod-axis1": 1e-9,     # tests/snap/zpu.zig:92
     "reduce/argmax-axis1": 0.0,    # tests/snap/zpu.zig:93
+    "reduce/cumsum-axis1": 1e-9,   # tests/snap/zpu.zig:94
+    "reduce/cumsum-reverse": 1e-9, # tests/snap/zpu.zig:95
     "ops/tanh": 1e-9,              # tests/snap/zpu.zig:62
     "ops/exp": 1e-9,               # tests/snap/zpu.zig:60
     "ops/sigmoid": 1e-9,           # tests/snap/zpu.zig:61
@@ -39,6 +41,9 @@ CASES = {
     "ops/square-rsqrt": 1e-9,      # tests/snap/zpu.zig:65
     "ops/sqrt-abs": 1e-9,          # tests/snap/zpu.zig:64
     "ops/maximum": 1e-9,           # tests/snap/zpu.zig:68
+    "ops/where": 1e-9,             # tests/snap/zpu.zig:69-73 (where(gt(x, 0), x, neg(x)))
+    "ops/clamp": 1e-9,             # tests/snap/zpu.zig:74
+    "ops/lerp": 1e-9,              # tests/snap/zpu.zig:75
     "nn/log-softmax": 1e-9,        # tests/snap/zpu.zig:143
     "nn/softmax": 1e-9,            # tests/snap/zpu.zig:142
     "optim/adam-step1": 1e-9,      # tests/snap/zpu.zig:340
@@ -138,6 +143,21 @@ def main(ref):
          "prim": "argmax", "axis": 0, "keepdims": 0, "want": [1], "want_shape": [], "tol": 0.0},
     ]
 
+    # src/zpu/tests.zig:97-101 (a = 1..6 as 2 x 3) and :873-877 (lt of the
+    # i64 [1, 2, 3, 4] against 3, any / all; the f64 values compare alike)
+    # src/zpu/tests.zig:125-126: cumsum of [[1,2,3],[4,5,6]] along axis 1
+    cumsum_known = [
+        {"x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "axis": 1, "reverse": False, "want": [1, 3, 6, 4, 9, 15]},
+        {"x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "axis": 1, "reverse": True, "want": [6, 5, 3, 15, 11, 6]},
+    ]
+    pred_known = [
+        {"name": "gt(a, 3)", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3], "want": [0, 0, 0, 1, 1, 1]},
+        {"name": "where(gt(a, 3), a, neg(a))", "x": [1, 2, 3, 4, 5, 6], "shape": [2, 3],
+         "want": [-1, -2, -3, 4, 5, 6]},
+        {"name": "any(lt(i, 3))", "x": [1, 2, 3, 4], "shape": [2, 2], "want": [1]},
+        {"name": "all(lt(i, 3))", "x": [1, 2, 3, 4], "shape": [2, 2], "want": [0]},
+    ]
+
     # src/zpu/kernels.zig:512-543: gemm vs the naive triple loop at 1e-12 on
     # these shapes, inputs a[i] = (i % 7) * 0.5 - 1, b[i] = (i % 5) * 0.25 - 0.5.
     gemm_shapes = [[1, 1, 1], [3, 4, 5], [32, 7, 128], [35, 9, 133], [2, 33, 2]]
@@ -155,6 +175,8 @@ def main(ref):
         "inputs": inputs,
         "known_answers": known,
         "reduce_known": reduce_known,
+        "pred_known": pred_known,
+        "cumsum_known": cumsum_known,
         "gemm_shapes": gemm_shapes,
         "reduce_lengths": reduce_lengths,
     }

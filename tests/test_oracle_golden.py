@@ -320,3 +320,52 @@ def test_from_f64_rules():
     assert zo.from_f64(v, np.int8).tolist() == [0, 2, -2, 127, -128, 127, -128, 0]
     assert zo.from_f64(v, np.bool_).tolist() == [True, True, True, True, True, True, True, False]
     assert zo.from_f64(np.array([2.0 ** 63, -2.0 ** 64]), np.int64).tolist() == [2 ** 63 - 1, -2 ** 63]
+
+
+def test_selection_snapshots(golden):
+    """tests/snap/zpu.zig:69-75 on spread(8): where(gt(x, 0), x, -x),
+    clamp (maximum then minimum, ops.zig:593-601), lerp (a + t (b - a),
+    ops.zig:604-610)."""
+    x = np.array(golden["inputs"]["spread8"], dtype=np.float64)
+    want, tol, _ = snap(golden, "zpu/ops/where")
+    snap_close(want, zo.where(zo.predicate("gt", x, 0.0), x, -x), tol)
+    want, tol, _ = snap(golden, "zpu/ops/clamp")
+    snap_close(want, np.minimum(np.maximum(x, -0.5), 0.5), tol)
+    want, tol, _ = snap(golden, "zpu/ops/lerp")
+    snap_close(want, x + 0.25 * (-x - x), tol)
+
+
+def test_predicate_known_answers(golden):
+    """src/zpu/tests.zig:97-101, 873-877."""
+    k = {c["name"]: c for c in golden["pred_known"]}
+    a = np.array(k["gt(a, 3)"]["x"], dtype=np.float64).reshape(2, 3)
+    assert zo.predicate("gt", a, 3.0).astype(np.float64).ravel().tolist() == k["gt(a, 3)"]["want"]
+    w = zo.where(zo.predicate("gt", a, 3.0), a, -a)
+    assert w.ravel().tolist() == k["where(gt(a, 3), a, neg(a))"]["want"]
+    i = np.array(k["any(lt(i, 3))"]["x"], dtype=np.float64).reshape(2, 2)
+    assert [float(zo.reduce_bool(zo.predicate("lt", i, 3.0), "any_reduce"))] == k["any(lt(i, 3))"]["want"]
+    assert [float(zo.reduce_bool(zo.predicate("lt", i, 3.0), "all_reduce"))] == k["all(lt(i, 3))"]["want"]
+
+
+def test_predicate_rules():
+    nan = float("nan")
+    x = np.array([nan, 0.0, -0.0, 1.0, np.inf])
+    assert zo.predicate("eq", x, x).tolist() == [False, True, True, True, True]
+    assert zo.predicate("ne", x, 0.0).tolist() == [True, False, False, True, True]
+    assert zo.predicate("logical_and", x, 1.0).tolist() == [True, False, False, True, True]
+    assert zo.predicate("logical_not", x).tolist() == [False, True, True, False, False]
+    assert zo.where(x, 1.0, 2.0).tolist() == [1.0, 2.0, 2.0, 1.0, 1.0]
+    assert bool(zo.reduce_bool(np.zeros((3, 0)), "all_reduce")) is True
+    assert zo.reduce_bool(np.zeros((3, 0)), "any_reduce", 1).tolist() == [False] * 3
+
+
+def test_cumsum_snapshots_and_known_answers(golden):
+    """tests/snap/zpu.zig:94-95 (spread(12) as 3 x 4) and src/zpu/tests.zig:125-126."""
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    want, tol, _ = snap(golden, "zpu/reduce/cumsum-axis1")
+    snap_close(want, zo.cumsum(x, 1), tol)
+    want, tol, _ = snap(golden, "zpu/reduce/cumsum-reverse")
+    snap_close(want, zo.cumsum(x, 1, reverse=True), tol)
+    for c in golden["cumsum_known"]:
+        a = np.array(c["x"], dtype=np.float64).reshape(c["shape"])
+        assert zo.cumsum(a, c["axis"], c["reverse"]).ravel().tolist() == c["want"]

@@ -466,3 +466,154 @@ def test_reductions_fold_payload_axes_under_vmap(zc, prim, axis, keep):
         want = zo.reduce_axis(x, prim, axis, keep, depth=1)
         assert tuple(got.shape) == want.shape
         assert np.allclose(got.cpu().numpy(), want, rtol=2e-6, atol=1e-6)
+
+
+def test_selection_snapshots_on_device(zc, golden):
+    """tests/snap/zpu.zig:69-75 as jit plans (f64 spread(8)): where(gt(x, 0),
+    x, neg(x)) -- a bool value inside one region --, clamp as maximum then
+    minimum with captured bounds, lerp as a + t (b - a)."""
+    x = np.array(golden["inputs"]["spread8"], dtype=np.float64)
+    xd = torch.from_numpy(x).cuda()
+    args = [(1, zc.F64, (8,))]
+    plans = {
+        "where": zc.Plan(args, [(2, np.float64(0.0))],
+                         [("gt", [1, 2], 10, -2, 0), ("neg", [1], 11, -2, 0), ("where", [10, 1, 11], 12, -2, 0)], [12]),
+        "clamp": zc.Plan(args, [(2, np.float64(-0.5)), (3, np.float64(0.5))],
+                         [("maximum", [1, 2], 10, -2, 0), ("minimum", [10, 3], 11, -2, 0)], [11]),
+        "lerp": zc.Plan(args, [(2, np.float64(0.25))],
+                        [("neg", [1], 10, -2, 0), ("sub", [10, 1], 11, -2, 0), ("mul", [11, 2], 12, -2, 0),
+                         ("add", [1, 12], 13, -2, 0)], [13]),
+    }
+    for name, p in plans.items():
+        assert p.num_kernels() == 1, name
+        (got,) = p.run([xd])
+        s = golden["snapshots"]["zpu/ops/" + name]
+        g = got.cpu().numpy()
+        assert np.all(np.abs(g - s["values"]) <= s["tol"] * np.maximum(1, np.abs(g))), name
+
+
+def test_predicate_known_answers_on_device(zc, golden):
+    k = {c["name"]: c for c in golden["pred_known"]}
+    a = torch.tensor(k["gt(a, 3)"]["x"], dtype=torch.float64, device="cuda").reshape(2, 3)
+    p = zc.Plan([(1, zc.F64, (2, 3))], [(2, np.float64(3.0))],
+                [("gt", [1, 2], 10, -2, 0), ("neg", [1], 11, -2, 0), ("where", [10, 1, 11], 12, -2, 0)], [10, 12])
+    cond, w = p.run([a])
+    assert cond.dtype == torch.bool
+    assert cond.cpu().numpy().astype(np.float64).ravel().tolist() == k["gt(a, 3)"]["want"]
+    assert w.cpu().numpy().ravel().tolist() == k["where(gt(a, 3), a, neg(a))"]["want"]
+    i = torch.tensor(k["any(lt(i, 3))"]["x"], dtype=torch.float64, device="cuda").reshape(2, 2)
+    for prim, key in (("any_reduce", "any(lt(i, 3))"), ("all_reduce", "all(lt(i, 3))")):
+        q = zc.Plan([(1, zc.F64, (2, 2))], [(2, np.float64(3.0))],
+                    [("lt", [1, 2], 10, -2, 0), (prim, [10], 11, -2, 0)], [11])
+        (r,) = q.run([i])
+        assert r.dtype == torch.bool and [float(r.cpu())] == k[key]["want"]
+
+
+PRED2 = ["eq", "ne", "lt", "le", "gt", "ge", "logical_and", "logical_or", "logical_xor"]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_predicates_match_the_oracle(zc, dt):
+    """Every predicate over values with NaN, +-0, +-inf and ties, broadcast
+    against a row; unary predicates; where on a NaN condition."""
+    npdt = np.float32 if dt == "f32" else np.float64
+    code = zc.F32 if dt == "f32" else zc.F64
+    rng = np.random.default_rng(3)
+    x = rng.integers(-2, 3, size=(64, 33)).astype(npdt)
+    x[rng.random(x.shape) < 0.05] = np.nan
+    x[0, :4] = [np.inf, -np.inf, -0.0, 0.0]
+    y = rng.integers(-2, 3, size=(33,)).astype(npdt)
+    y[5] = np.nan
+    xd, yd = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    steps = [(prim, [1, 2], 10 + i, -2, 0) for i, prim in enumerate(PRED2)]
+    steps += [(prim, [1], 20 + i, -2, 0) for i, prim in enumerate(["isnan", "isinf", "isfinite", "logical_not"])]
+    steps += [("where", [1, 1, 2], 30, -2, 0)]  # x itself as the condition: NaN is true
+    outs = [10 + i for i in range(len(PRED2))] + [20, 21, 22, 23, 30]
+    p = zc.Plan([(1, code, (64, 33)), (2, code, (33,))], [], steps, outs)
+    got = p.run([xd, yd])
+    for i, prim in enumerate(PRED2):
+        assert got[i].dtype == torch.bool
+        assert np.array_equal(got[i].cpu().numpy(), zo.predicate(prim, x, y)), prim
+    for i, prim in enumerate(["isnan", "isinf", "isfinite", "logical_not"]):
+        assert np.array_equal(got[len(PRED2) + i].cpu().numpy(), zo.predicate(prim, x)), prim
+    w = got[-1].cpu().numpy()
+    assert np.array_equal(w, zo.where(x, x, np.broadcast_to(y, x.shape)).astype(npdt), equal_nan=True)
+
+
+@pytest.mark.parametrize("prim", ["any_reduce", "all_reduce"])
+@pytest.mark.parametrize("axis,keep", [(-2, 0), (0, 0), (1, 1), (2, 0), (-1, 1)])
+def test_any_all_match_the_oracle(zc, prim, axis, keep):
+    """any / all of a comparison (bool values) and of floats (x != 0, NaN
+    true), over every axis kind, with a bool argument as well."""
+    rng = np.random.default_rng(11)
+    shape = (5, 40, 70)
+    x = (rng.random(shape) < 0.03).astype(np.float32) * rng.choice([1.0, np.nan, -2.0], size=shape).astype(np.float32)
+    x[2] = 1.0  # an all-true slab
+    m = rng.random(shape) < 0.5
+    p = zc.Plan([(1, zc.F32, shape), (2, zc.DT_BOOL, shape)], [(3, np.float32(0.0))],
+                [("ne", [1, 3], 10, -2, 0), (prim, [10], 11, axis, keep), (prim, [1], 12, axis, keep),
+                 ("logical_and", [2, 10], 13, -2, 0), (prim, [13], 14, axis, keep)], [11, 12, 14])
+    a, b, c = p.run([torch.from_numpy(x).cuda(), torch.from_numpy(m).cuda()])
+    want = zo.reduce_bool(zo.predicate("ne", x, 0.0), prim, axis, keep)
+    assert a.dtype == torch.bool and tuple(a.shape) == want.shape
+    assert np.array_equal(a.cpu().numpy(), want)
+    assert np.array_equal(b.cpu().numpy(), zo.reduce_bool(x, prim, axis, keep))
+    assert np.array_equal(c.cpu().numpy(), zo.reduce_bool(m & (x != 0), prim, axis, keep))
+
+
+def test_i64_operands_are_refused(zc):
+    """eq(argmax(logits, 1), labels): an i64 value feeding a comparison is
+    outside the lowering, which says so (NotSupported) at creation."""
+    with pytest.raises(zc.ZpuCudaError) as e:
+        zc.Plan([(1, zc.F32, (8, 10)), (2, zc.F32, (8,))], [],
+                [("argmax", [1], 10, 1, 0), ("eq", [10, 2], 11, -2, 0)], [11])
+    assert e.value.status == 9
+
+
+REVERSE = 32  # prims.Attrs.REVERSE
+
+
+def test_cumsum_snapshots_and_known_answers_on_device(zc, golden):
+    x = torch.tensor(golden["inputs"]["spread12"], dtype=torch.float64, device="cuda").reshape(3, 4)
+    for name, flags in (("cumsum-axis1", 0), ("cumsum-reverse", REVERSE)):
+        p = zc.Plan([(1, zc.F64, (3, 4))], [], [("cumsum", [1], 10, 1, flags)], [10])
+        assert "cumsum" in p.describe()
+        (got,) = p.run([x])
+        s = golden["snapshots"]["zpu/reduce/" + name]
+        g = got.cpu().numpy().ravel()
+        assert np.all(np.abs(g - s["values"]) <= s["tol"] * np.maximum(1, np.abs(g))), name
+    for c in golden["cumsum_known"]:
+        a = torch.tensor(c["x"], dtype=torch.float64, device="cuda").reshape(c["shape"])
+        p = zc.Plan([(1, zc.F64, tuple(c["shape"]))], [], [("cumsum", [1], 10, c["axis"], REVERSE * c["reverse"])],
+                    [10])
+        (got,) = p.run([a])
+        assert got.cpu().numpy().ravel().tolist() == c["want"]
+
+
+@pytest.mark.parametrize("axis", [0, 1, 2, -1, -2])
+@pytest.mark.parametrize("reverse", [0, 1])
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_cumsum_is_bit_exact(zc, axis, reverse, dt):
+    """zpu's f64 running sum rounded per element, along any axis, forward and
+    reverse, fed by an element-wise region and feeding one (exp of the
+    prefix sums) -- every element bit-equal to the oracle."""
+    npdt = np.float32 if dt == "f32" else np.float64
+    shape = (6, 257, 40)
+    x = zo.uniform_range(9, int(np.prod(shape)), -1.0, 1.0, npdt).reshape(shape)
+    code = zc.F32 if dt == "f32" else zc.F64
+    p = zc.Plan([(1, code, shape)], [],
+                [("square", [1], 10, -2, 0), ("cumsum", [10], 11, axis, REVERSE * reverse),
+                 ("neg", [11], 12, -2, 0)], [11, 12])
+    assert p.num_kernels() == 3
+    c, n = p.run([torch.from_numpy(x).cuda()])
+    want = zo.cumsum((x * x).astype(npdt), axis, bool(reverse))
+    assert np.array_equal(c.cpu().numpy(), want)
+    assert np.array_equal(n.cpu().numpy(), -want)
+
+
+def test_cumsum_under_vmap_counts_payload_axes(zc):
+    shape = (3, 5, 7)
+    x = zo.uniform_range(10, 105, -1.0, 1.0, np.float64).reshape(shape)
+    p = zc.Plan([(1, zc.F64, shape, 1)], [], [("cumsum", [1], 10, 0, 0)], [10])  # payload axis 0 = axis 1
+    (got,) = p.run([torch.from_numpy(x).cuda()])
+    assert np.array_equal(got.cpu().numpy(), zo.cumsum(x, 0, depth=1))

@@ -7,7 +7,7 @@ a CPU path when the library is missing -- importing the operations raises.
 """
 import ctypes as C
 
-from ._capi import (AXIS_NONE, DT_I64, F32, F64, PRIM, Blob, Step, Tensor, Value, ZpuCudaError, check,
+from ._capi import (AXIS_NONE, DT_BOOL, DT_I64, F32, F64, PRIM, Blob, Step, Tensor, Value, ZpuCudaError, check,
                     exported_names, lib)
 
 __all__ = ["lib", "check", "ZpuCudaError", "Plan", "gemm", "matmul", "matmul_shape", "stream_of",
@@ -45,6 +45,8 @@ def torch_dtype(code):
     torch = _torch()
     if code == DT_I64:
         return torch.int64
+    if code == DT_BOOL:
+        return torch.bool
     return torch.float32 if code == F32 else torch.float64
 
 
@@ -175,7 +177,8 @@ class Plan:
         for i, (vid, arr) in enumerate(blobs):
             arr = np.ascontiguousarray(arr)
             self._keep.append(arr)
-            _fill_value(bl[i].value, vid, F64 if arr.dtype == np.float64 else F32, arr.shape)
+            code = F64 if arr.dtype == np.float64 else DT_BOOL if arr.dtype == np.bool_ else F32
+            _fill_value(bl[i].value, vid, code, arr.shape)
             bl[i].host_data = arr.ctypes.data
         st = (Step * max(1, len(steps)))()
         for i, (prim, ins, out, axis, keepdims) in enumerate(steps):
@@ -185,7 +188,7 @@ class Plan:
                 st[i].ins[k] = x
             st[i].out = out
             st[i].axis = axis
-            st[i].keepdims = int(keepdims)
+            st[i].flags = int(keepdims)  # Attrs.flags: 1 = KEEP_DIMS, 32 = REVERSE
         oi = (C.c_uint64 * len(out_ids))(*out_ids)
         h = C.c_void_p()
         check(L.zpucuda_plan_create(va, len(args), bl, len(blobs), st, len(steps), oi, len(out_ids),

@@ -15,6 +15,7 @@ MAX_RANK = 8
 AXIS_NONE = -2
 F64, F32 = 0, 1
 DT_I64 = 3  # zpu DType.i64: argmax / argmin results
+DT_BOOL = 8  # zpu DType.bool (one byte): predicates, any / all
 
 STATUS = {
     0: "ok", 1: "OutOfMemory", 2: "ShapeMismatch", 3: "DTypeMismatch", 4: "RankTooLarge",
@@ -31,8 +32,10 @@ PRIM = {
     "atanh": 22, "erf": 23, "sigmoid": 24, "softplus": 25, "relu": 26, "floor": 27,
     "ceil": 28, "round": 29, "trunc": 30, "sign": 31, "isnan": 32, "isinf": 33,
     "isfinite": 34, "add": 35, "sub": 36, "mul": 37, "div": 38, "pow": 39, "maximum": 40,
-    "minimum": 41, "atan2": 42, "hypot": 43, "mod_op": 44, "eq": 45, "where": 55,
-    "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "argmax": 64, "argmin": 65, "matmul": 80,
+    "minimum": 41, "atan2": 42, "hypot": 43, "mod_op": 44, "eq": 45, "ne": 46, "lt": 47, "le": 48,
+    "gt": 49, "ge": 50, "logical_and": 51, "logical_or": 52, "logical_xor": 53, "logical_not": 54,
+    "where": 55, "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "any_reduce": 62,
+    "all_reduce": 63, "argmax": 64, "argmin": 65, "cumsum": 78, "matmul": 80,
     "constant": 87, "copy": 88,
 }
 
@@ -57,7 +60,7 @@ class Value(C.Structure):
 
 class Step(C.Structure):
     _fields_ = [("prim", C.c_int32), ("n_inputs", C.c_int32), ("ins", C.c_uint64 * 3),
-                ("out", C.c_uint64), ("axis", C.c_int32), ("keepdims", C.c_int32)]
+                ("out", C.c_uint64), ("axis", C.c_int32), ("flags", C.c_int32)]
 
 
 class Blob(C.Structure):

@@ -29,25 +29,43 @@ enum {
     PRIM_PROD = 59,
     PRIM_MAX_REDUCE = 60,
     PRIM_MIN_REDUCE = 61,
+    PRIM_ANY = 62,
+    PRIM_ALL = 63,
     PRIM_ARGMAX = 64,
     PRIM_ARGMIN = 65,
+    PRIM_LOGICAL_NOT = 54,
+    PRIM_WHERE = 55,
+    PRIM_CUMSUM = 78,
     PRIM_MATMUL = 80,
 };
+constexpr int32_t kFlagReverse = 1 << 5;  // prims.Attrs.REVERSE
 
 const char *kPrimNames[] = {
     "neg", "abs", "exp", "expm1", "log", "log1p", "sqrt", "rsqrt", "square", "recip", "cbrt",
     "sin", "cos", "tan", "asin", "acos", "atan", "sinh", "cosh", "tanh", "asinh", "acosh",
     "atanh", "erf", "sigmoid", "softplus", "relu", "floor", "ceil", "round", "trunc", "sign",
     "isnan", "isinf", "isfinite", "add", "sub", "mul", "div", "pow", "maximum", "minimum",
-    "atan2", "hypot", "mod_op"};
+    "atan2", "hypot", "mod_op", "eq", "ne", "lt", "le", "gt", "ge", "logical_and", "logical_or",
+    "logical_xor", "logical_not", "where", "clamp", "lerp", "sum", "prod_op", "max_reduce", "min_reduce",
+    "any_reduce", "all_reduce", "argmax", "argmin"};
 
 // The element-wise prims a region kernel evaluates (prims.isElementwise,
-// src/zpu/prims.zig:198, minus predicates and the selection ops).
-bool region_unary(int p) { return p >= 0 && p <= 31; }
-bool region_binary(int p) { return p >= 35 && p <= 44; }
+// src/zpu/prims.zig:198): float math, the predicates (bool results:
+// isnan / isinf / isfinite, comparisons, logical ops) and `where`.
+bool math_unary(int p) { return p >= 0 && p <= 31; }
+bool pred_unary(int p) { return (p >= 32 && p <= 34) || p == PRIM_LOGICAL_NOT; }
+bool math_binary(int p) { return p >= 35 && p <= 44; }
+bool pred_binary(int p) { return p >= 45 && p <= 53; }
+bool region_unary(int p) { return math_unary(p) || pred_unary(p); }
+bool region_binary(int p) { return math_binary(p) || pred_binary(p); }
 bool arg_reduce(int p) { return p == PRIM_ARGMAX || p == PRIM_ARGMIN; }
-bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p); }
+bool bool_reduce(int p) { return p == PRIM_ANY || p == PRIM_ALL; }
+bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p) || bool_reduce(p); }
 bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
+// Bool values ride in a region's float registers: two values fit one region
+// unless both are floats of different types.  -1: no float type required.
+int carrier_of(int dt) { return float_dtype(dt) ? dt : -1; }
+bool carriers_agree(int a, int b) { return a < 0 || b < 0 || a == b; }
 
 struct Shape {
     int rank = 0;
@@ -99,7 +117,7 @@ struct Value {
 };
 
 struct Launch {
-    enum { REGION, MATMUL } kind = REGION;
+    enum { REGION, MATMUL, CUMSUM } kind = REGION;
     RegionProgram prog;
     const CatalogueEntry *cat = nullptr;
     std::string signature;
@@ -110,6 +128,10 @@ struct Launch {
     // matmul
     Slot ma, mb, mc;
     zpucuda_tensor ta, tb, tc;
+    // cumsum: [outer, dim, inner] along the middle axis
+    int32_t dtype = 0;
+    int64_t outer = 0, dim = 0, inner = 0;
+    bool reverse = false;
     std::string text;
 };
 
@@ -137,7 +159,7 @@ struct zpucuda_plan {
 
 namespace {
 
-size_t itemsize(int dt) { return dt == ZPUCUDA_F32 ? 4 : 8; }
+size_t itemsize(int dt) { return dt == ZPUCUDA_F32 ? 4 : dt == ZPUCUDA_BOOL ? 1 : 8; }
 
 int lower_fail(zpucuda_plan *p, int st, const std::string &why) {
     delete p;
@@ -191,7 +213,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
     };
     for (int i = 0; i < n_args; i++) {
         if (args[i].rank < 0 || args[i].rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "arg rank");
-        if (args[i].dtype != ZPUCUDA_F32 && args[i].dtype != ZPUCUDA_F64) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "arg dtype");
+        if (!float_dtype(args[i].dtype) && args[i].dtype != ZPUCUDA_BOOL) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "arg dtype");
         Value &v = add_value(args[i]);
         v.is_arg = true;
         v.arg_index = i;
@@ -201,7 +223,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
     for (int i = 0; i < n_blobs; i++) {
         const zpucuda_value &bv = blobs[i].value;
         if (bv.rank < 0 || bv.rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "blob rank");
-        if (bv.dtype != ZPUCUDA_F32 && bv.dtype != ZPUCUDA_F64) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "blob dtype");
+        if (!float_dtype(bv.dtype) && bv.dtype != ZPUCUDA_BOOL) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "blob dtype");
         Value &v = add_value(bv);
         v.is_blob = true;
         v.blob_index = i;
@@ -234,24 +256,47 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         const Value &a = vals[st.ins[0]];
         o.dtype = a.dtype;
         o.depth = a.depth;
-        if ((region_unary(st.prim) || region_binary(st.prim) || region_reduce(st.prim)) && !float_dtype(a.dtype))
-            return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a non-float value");
+        // operand types: float math and the numeric reductions take floats;
+        // predicates, `where`'s condition and any / all also take bools
+        // (truthiness v != 0, ops.zig:516, 572-590, 845-853)
+        const bool takes_bool = pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim) ||
+                                st.prim == PRIM_WHERE;
+        for (int k = 0; k < st.n_inputs && (region_unary(st.prim) || region_binary(st.prim) ||
+                                            region_reduce(st.prim) || st.prim == PRIM_WHERE);
+             k++) {
+            const int dt = vals[st.ins[k]].dtype;
+            const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0));
+            if (!ok) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a value of dtype " + std::to_string(dt));
+        }
+        if (pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim)) o.dtype = ZPUCUDA_BOOL;
         if (region_unary(st.prim) && st.n_inputs == 1) {
             o.shape = a.shape;
         } else if (region_binary(st.prim) && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
-            if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
+            if (!carriers_agree(carrier_of(a.dtype), carrier_of(b.dtype)) ||
+                (math_binary(st.prim) && a.dtype != b.dtype))
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
             if (a.depth != b.depth && a.shape.rank && b.shape.rank)
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "vmap depth mismatch in an element-wise step");
             o.depth = std::max(a.depth, b.depth);
             if (!broadcast(a.shape, b.shape, &o.shape)) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
+        } else if (st.prim == PRIM_WHERE && st.n_inputs == 3) {
+            // where(cond, a, b): a / b broadcast, then with cond; a's type
+            const Value &x = vals[st.ins[1]], &y = vals[st.ins[2]];
+            if (x.dtype != y.dtype || !carriers_agree(carrier_of(a.dtype), x.dtype))
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in where");
+            Shape xy;
+            if (!broadcast(x.shape, y.shape, &xy) || !broadcast(xy, a.shape, &o.shape))
+                return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
+            o.dtype = x.dtype;
+            o.depth = std::max(a.depth, std::max(x.depth, y.depth));
         } else if (region_reduce(st.prim) && st.n_inputs == 1) {
             // ops.reduceOutShape (src/zpu/ops.zig:644-660); argmax / argmin
             // never keep the folded axes and give i64 (ops.zig:931-934)
             int r0 = 0, r1 = -1;
             if (!reduced_axes(a.shape, a.depth, st.axis, &r0, &r1))
                 return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "reduction axis");
-            const bool keep = st.keepdims && !arg_reduce(st.prim);
+            const bool keep = (st.flags & 1) && !arg_reduce(st.prim);
             o.shape.rank = 0;
             for (int d = 0; d < a.shape.rank; d++) {
                 if (d >= r0 && d <= r1) {
@@ -261,6 +306,12 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 }
             }
             if (arg_reduce(st.prim)) o.dtype = ZPUCUDA_I64;
+        } else if (st.prim == PRIM_CUMSUM && st.n_inputs == 1) {
+            // ops.realAxis (src/zpu/ops.zig:1466-1471): vmap-aware, no AXIS_NONE
+            if (!float_dtype(a.dtype)) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "cumsum of a non-float value");
+            const int ax = st.axis >= 0 ? st.axis + a.depth : st.axis + a.shape.rank;
+            if (ax < 0 || ax >= a.shape.rank) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "cumsum axis");
+            o.shape = a.shape;
         } else if (st.prim == PRIM_MATMUL && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
             if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed-dtype matmul");
@@ -356,6 +407,30 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             s++;
             continue;
         }
+        if (st0.prim == PRIM_CUMSUM) {
+            Launch L;
+            L.kind = Launch::CUMSUM;
+            const Value &a = vals[st0.ins[0]];
+            L.ma = a.slot;
+            L.dtype = a.dtype;
+            const int ax = st0.axis >= 0 ? st0.axis + a.depth : st0.axis + a.shape.rank;
+            L.outer = 1;
+            L.inner = 1;
+            for (int d = 0; d < ax; d++) L.outer *= a.shape.dims[d];
+            for (int d = ax + 1; d < a.shape.rank; d++) L.inner *= a.shape.dims[d];
+            L.dim = a.shape.dims[ax];
+            L.reverse = (st0.flags & kFlagReverse) != 0;
+            L.mc = materialise(st0.out);
+            if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            char buf[160];
+            snprintf(buf, sizeof buf, "  kernel %zu: cumsum %s axis %d%s (%%%llu = cumsum(%%%llu))\n",
+                     plan->launches.size(), a.dtype == ZPUCUDA_F64 ? "f64" : "f32", ax, L.reverse ? " reverse" : "",
+                     (unsigned long long)st0.out, (unsigned long long)st0.ins[0]);
+            L.text = buf;
+            plan->launches.push_back(L);
+            s++;
+            continue;
+        }
         // a region: element-wise steps over one shape, at most one trailing reduction
         Launch L;
         RegionProgram &P = L.prog;
@@ -368,25 +443,36 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         bool have_shape = false;
         int e = s;
         // first pass: which steps join
+        // the float type a step computes in: its output's, else its inputs'
+        auto step_carrier = [&](const zpucuda_step &st) {
+            int c = carrier_of(vals[st.out].dtype);
+            for (int k = 0; k < st.n_inputs && c < 0; k++) c = carrier_of(vals[st.ins[k]].dtype);
+            return c;
+        };
         for (; e < n_steps; e++) {
             const zpucuda_step &st = steps[e];
             const Value &ov = vals[st.out];
-            if (region_unary(st.prim) || region_binary(st.prim)) {
-                if (have_shape && (!(ov.shape == rshape) || ov.dtype != rdtype)) break;
-                if (!have_shape) { rshape = ov.shape; rdtype = ov.dtype; have_shape = true; }
+            if (region_unary(st.prim) || region_binary(st.prim) || st.prim == PRIM_WHERE) {
+                const int c = step_carrier(st);
+                if (have_shape && (!(ov.shape == rshape) || !carriers_agree(c, rdtype))) break;
+                if (!have_shape) { rshape = ov.shape; have_shape = true; }
+                if (rdtype < 0) rdtype = c;
                 member.push_back(e);
                 continue;
             }
             if (region_reduce(st.prim)) {
                 const Value &iv = vals[st.ins[0]];
                 bool inside = std::find(member.begin(), member.end(), iv.producer) != member.end();
-                if (member.empty() || inside) {
-                    if (!have_shape) { rshape = iv.shape; rdtype = iv.dtype; have_shape = true; }
-                    if (inside || member.empty()) { member.push_back(e); e++; }
+                if ((member.empty() || inside) && carriers_agree(carrier_of(iv.dtype), rdtype)) {
+                    if (!have_shape) { rshape = iv.shape; have_shape = true; }
+                    if (rdtype < 0) rdtype = carrier_of(iv.dtype);
+                    member.push_back(e);
+                    e++;
                 }
             }
             break;
         }
+        if (rdtype < 0) rdtype = ZPUCUDA_F32;  // only bools: carried as f32
         if (member.empty()) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "step " + std::to_string(s) + " cannot start a region");
         P.dtype = rdtype;
         P.rank = rshape.rank;
@@ -411,7 +497,9 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         for (int k = 0; k < P.n_in; k++) {
             Value &iv = vals[loads[k]];
             if (!iv.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "region input not materialised");
-            if (iv.dtype != rdtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in a region");
+            if (iv.dtype != rdtype && iv.dtype != ZPUCUDA_BOOL)
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in a region");
+            P.in_bool[k] = iv.dtype == ZPUCUDA_BOOL;
             reg[loads[k]] = k;
             P.insn[k] = Insn{OPC_LOAD, (uint8_t)k, (uint8_t)k, 0};
             L.ins.push_back(iv.slot);
@@ -463,10 +551,13 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 continue;
             }
             if (nreg >= RP_MAX_REG || n_insn >= RP_MAX_INSN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
-            Insn in{(uint8_t)st.prim, (uint8_t)nreg, (uint8_t)reg[st.ins[0]], (uint8_t)(st.n_inputs > 1 ? reg[st.ins[1]] : 0)};
+            Insn in{(uint8_t)st.prim, (uint8_t)nreg, (uint8_t)reg[st.ins[0]], (uint8_t)(st.n_inputs > 1 ? reg[st.ins[1]] : 0),
+                    (uint8_t)(st.n_inputs > 2 ? reg[st.ins[2]] : 0)};
             P.insn[n_insn++] = in;
-            char buf[64];
-            if (st.n_inputs > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b);
+            char buf[80];
+            if (st.n_inputs > 2)
+                snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b, in.c);
+            else if (st.n_inputs > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b);
             else snprintf(buf, sizeof buf, ";r%d=%s(r%d)", nreg, prim_name(st.prim).c_str(), in.a);
             sig += buf;
             reg[st.out] = nreg++;
@@ -482,6 +573,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 if (std::find(member.begin(), member.end(), u) == member.end()) needed = true;
             if (needed) {
                 if (P.n_out >= RP_MAX_OUT) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region has too many outputs");
+                P.out_bool[P.n_out] = vals[st.out].dtype == ZPUCUDA_BOOL;
                 P.out_reg[P.n_out++] = reg[st.out];
                 Slot sl = materialise(st.out);
                 if (sl.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
@@ -491,7 +583,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         if (has_red) {
             P.reduce = red_prim == PRIM_SUM ? RED_SUM : red_prim == PRIM_PROD ? RED_PROD
                      : red_prim == PRIM_MAX_REDUCE ? RED_MAX : red_prim == PRIM_MIN_REDUCE ? RED_MIN
-                     : red_prim == PRIM_ARGMAX ? RED_ARGMAX : RED_ARGMIN;
+                     : red_prim == PRIM_ARGMAX ? RED_ARGMAX : red_prim == PRIM_ARGMIN ? RED_ARGMIN
+                     : red_prim == PRIM_ANY ? RED_ANY : RED_ALL;
             P.reduce_reg = reg[red_in];
             // the folded axes [r0, r1] split the region into [outer, red_len, inner]
             int r0 = 0, r1 = -1;
@@ -521,7 +614,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             char buf[64];
             snprintf(buf, sizeof buf, ";out=r%d;red=%s%s", P.reduce_reg,
                      red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max"
-                     : red_prim == PRIM_MIN_REDUCE ? "min" : red_prim == PRIM_ARGMAX ? "argmax" : "argmin",
+                     : red_prim == PRIM_MIN_REDUCE ? "min" : red_prim == PRIM_ARGMAX ? "argmax"
+                     : red_prim == PRIM_ARGMIN ? "argmin" : red_prim == PRIM_ANY ? "any" : "all",
                      P.reduce_all ? "" : P.reduce_mid ? "_axis" : "_rows");
             sig += buf;
             if (P.reduce_all) {
@@ -539,8 +633,11 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             sig += buf;
         }
         L.signature = sig;
+        bool any_bool = false;
+        for (int k = 0; k < P.n_in; k++) any_bool |= P.in_bool[k] != 0;
+        for (int o = 0; o < P.n_out; o++) any_bool |= P.out_bool[o] != 0;
         const bool catalogue_shape = ((!has_red && P.n_out == 1) || (has_red && P.reduce == RED_SUM && P.reduce_all && P.n_out == 0)) &&
-                                     kinds.find_first_of("RG") == std::string::npos;
+                                     kinds.find_first_of("RG") == std::string::npos && !any_bool;
         L.cat = catalogue_shape ? catalogue_find(sig.c_str()) : nullptr;
         L.text = "  kernel " + std::to_string(plan->launches.size()) + ": region " +
                  (L.cat ? std::string("[catalogue ") + L.cat->name + "]" : std::string("[bytecode]")) + " " + sig + "\n";
@@ -574,6 +671,8 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
             b.data = ptr(L.mb);
             c.data = ptr(L.mc);
             st = matmul_device(&a, &b, &c, s);
+        } else if (L.kind == Launch::CUMSUM) {
+            st = cumsum_launch(L.dtype, ptr(L.ma), ptr(L.mc), L.outer, L.dim, L.inner, L.reverse, s);
         } else {
             RegionIO io;
             memset(&io, 0, sizeof io);
@@ -595,7 +694,7 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
 static size_t value_bytes(const zpucuda_value &v) {
     size_t n = 1;
     for (int d = 0; d < v.rank; d++) n *= (size_t)v.dims[d];
-    return n * (v.dtype == ZPUCUDA_F32 ? 4 : 8);
+    return n * (v.dtype == ZPUCUDA_F32 ? 4 : v.dtype == ZPUCUDA_BOOL ? 1 : 8);
 }
 
 int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs, void *stream) {

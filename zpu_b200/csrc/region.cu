@@ -96,6 +96,12 @@ __device__ double unary_f64(int op, double x) {
     case 29: return round(x);
     case 30: return trunc(x);
     case 31: return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : 0.0);
+    // unary predicates (scalar.pred1F, src/zpu/scalar.zig:252-259) and
+    // logical_not (ops.logicalNot: x == 0, ops.zig:516-520), as 1 / 0
+    case 32: return isnan(x) ? 1.0 : 0.0;
+    case 33: return isinf(x) ? 1.0 : 0.0;
+    case 34: return isfinite(x) ? 1.0 : 0.0;
+    case 54: return x == 0.0 ? 1.0 : 0.0;
     default: return nan("");
     }
 }
@@ -134,6 +140,17 @@ __device__ __forceinline__ double binary_f64(int op, double a, double b) {
     case 42: return atan2(a, b);
     case 43: return hypot(a, b);
     case 44: return mod_f64(a, b);
+    // comparisons and logical ops on f64 values (scalar.pred2F,
+    // src/zpu/scalar.zig:235-249), as 1 / 0; truthiness is v != 0 (NaN is true)
+    case 45: return a == b ? 1.0 : 0.0;
+    case 46: return a != b ? 1.0 : 0.0;
+    case 47: return a < b ? 1.0 : 0.0;
+    case 48: return a <= b ? 1.0 : 0.0;
+    case 49: return a > b ? 1.0 : 0.0;
+    case 50: return a >= b ? 1.0 : 0.0;
+    case 51: return (a != 0.0 && b != 0.0) ? 1.0 : 0.0;
+    case 52: return (a != 0.0 || b != 0.0) ? 1.0 : 0.0;
+    case 53: return ((a != 0.0) != (b != 0.0)) ? 1.0 : 0.0;
     default: return nan("");
     }
 }
@@ -159,21 +176,23 @@ template <> __device__ __forceinline__ double bin<double>(int op, double a, doub
 
 template <class T>
 __device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io, int k, int64_t i) {
-    const T *src = (const T *)io.in[k];
+    int64_t off;
     switch (p.in_kind[k]) {
-    case IN_FULL: return src[i];
-    case IN_SCALAR: return src[0];
-    case IN_ROW: return src[i % p.in_numel[k]];
+    case IN_FULL: off = i; break;
+    case IN_SCALAR: off = 0; break;
+    case IN_ROW: off = i % p.in_numel[k]; break;
     default: {
-        int64_t rem = i, off = 0;
+        int64_t rem = i;
+        off = 0;
         for (int d = p.rank - 1; d >= 0; d--) {
             const int64_t idx = rem % p.dims[d];
             rem /= p.dims[d];
             off += idx * p.in_strides[k][d];
         }
-        return src[off];
     }
     }
+    if (p.in_bool[k]) return ((const uint8_t *)io.in[k])[off] ? (T)1 : (T)0;
+    return ((const T *)io.in[k])[off];
 }
 
 template <class T>
@@ -181,7 +200,8 @@ __device__ __forceinline__ void eval(const RegionProgram &p, const RegionIO &io,
     for (int k = 0; k < p.n_insn; k++) {
         const Insn in = p.insn[k];
         if (in.op == OPC_LOAD) r[in.dst] = load_in<T>(p, io, in.a, i);
-        else if (in.op < 35) r[in.dst] = un<T>(in.op, r[in.a]);
+        else if (in.op == 55) r[in.dst] = r[in.a] != (T)0 ? r[in.b] : r[in.c];  // where: ops.zig:572-590
+        else if (in.op < 35 || in.op == 54) r[in.dst] = un<T>(in.op, r[in.a]);
         else r[in.dst] = bin<T>(in.op, r[in.a], r[in.b]);
     }
 }
@@ -191,6 +211,7 @@ __device__ __forceinline__ double red_identity(int red) {
     case RED_PROD: return 1.0;
     case RED_MAX: return -INFINITY;
     case RED_MIN: return INFINITY;
+    case RED_ALL: return 1.0;
     default: return 0.0;
     }
 }
@@ -200,6 +221,10 @@ __device__ __forceinline__ double red_combine(int red, double acc, double v) {
     case RED_PROD: return acc * v;
     case RED_MAX: return isnan(v) || isnan(acc) ? (isnan(acc) ? acc : v) : (v > acc ? v : acc);
     case RED_MIN: return isnan(v) || isnan(acc) ? (isnan(acc) ? acc : v) : (v < acc ? v : acc);
+    // any / all of x != 0 (ops.reduceOp on a non-bool input takes ne(x, 0)
+    // first, ops.zig:845-853)
+    case RED_ANY: return (acc != 0.0 || v != 0.0) ? 1.0 : 0.0;
+    case RED_ALL: return (acc != 0.0 && v != 0.0) ? 1.0 : 0.0;
     default: return acc + v;
     }
 }
@@ -213,7 +238,16 @@ constexpr int kInterpThreads = 256;
 
 template <class T>
 __device__ __forceinline__ void store_outputs(const RegionProgram &p, const RegionIO &io, int64_t i, const T *r) {
-    for (int o = 0; o < p.n_out; o++) ((T *)io.out[o])[i] = r[p.out_reg[o]];
+    for (int o = 0; o < p.n_out; o++) {
+        if (p.out_bool[o]) ((uint8_t *)io.out[o])[i] = r[p.out_reg[o]] != (T)0;
+        else ((T *)io.out[o])[i] = r[p.out_reg[o]];
+    }
+}
+// The reduced value at output index `i`: any / all store a bool byte.
+template <class T>
+__device__ __forceinline__ void store_red(const RegionProgram &p, const RegionIO &io, int64_t i, double v) {
+    if (p.reduce == RED_ANY || p.reduce == RED_ALL) ((uint8_t *)io.red_out)[i] = v != 0.0;
+    else ((T *)io.red_out)[i] = (T)v;
 }
 
 // MODE 0: element-wise outputs only; 1: plus a full reduction; 2: plus a
@@ -257,7 +291,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
         __threadfence();
         double v = red_identity(p.reduce);
         for (unsigned b = 0; b < gridDim.x; b++) v = red_combine(p.reduce, v, __ldcg(io.partials + b));
-        *(T *)io.red_out = (T)v;
+        store_red<T>(p, io, 0, v);
         *io.ticket = 0u;
     } else if (MODE == 3) {
         const int64_t n_out = p.outer * p.inner;
@@ -271,7 +305,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
                 store_outputs<T>(p, io, i, r);
                 acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
             }
-            ((T *)io.red_out)[o] = (T)acc;
+            store_red<T>(p, io, o, acc);
         }
     } else {
         const int lane = threadIdx.x & 31;
@@ -285,7 +319,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
                 acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
             }
             acc = warp_reduce(p.reduce, acc);
-            if (lane == 0) ((T *)io.red_out)[row] = (T)acc;
+            if (lane == 0) store_red<T>(p, io, row, acc);
         }
     }
 }
@@ -445,6 +479,42 @@ int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
         else interp_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     }
     ZC_LAUNCHED("region bytecode kernel");
+    return ZPUCUDA_OK;
+}
+
+// ------------------------------------------------------------------ cumsum
+//
+// One thread per (outer, inner) column walks the axis in order with zpu's f64
+// accumulator, so every prefix has zpu's bits; threads of a warp take
+// consecutive inner indices (coalesced when inner >= 32; for the last axis
+// each thread streams its own row, sequential sectors through L1).
+template <class T>
+__global__ void __launch_bounds__(256) cumsum_kernel(const T *__restrict__ x, T *__restrict__ y, int64_t outer,
+                                                     int64_t dim, int64_t inner, int reverse) {
+    const int64_t cols = outer * inner;
+    for (int64_t c = (int64_t)blockIdx.x * 256 + threadIdx.x; c < cols; c += (int64_t)gridDim.x * 256) {
+        const int64_t o = c / inner, i = c - o * inner;
+        const int64_t base = o * dim * inner + i;
+        double acc = 0.0;
+        for (int64_t d = 0; d < dim; d++) {
+            const int64_t idx = base + (reverse ? dim - 1 - d : d) * inner;
+            acc += (double)x[idx];
+            y[idx] = (T)acc;
+        }
+    }
+}
+
+int cumsum_launch(int dtype, const void *x, void *y, int64_t outer, int64_t dim, int64_t inner, bool reverse,
+                  cudaStream_t s) {
+    const int64_t cols = outer * inner;
+    if (cols == 0 || dim == 0) return ZPUCUDA_OK;
+    int64_t g = (cols + 255) / 256;
+    if (g > (int64_t)num_sms() * 16) g = (int64_t)num_sms() * 16;
+    if (dtype == ZPUCUDA_F64)
+        cumsum_kernel<double><<<(int)g, 256, 0, s>>>((const double *)x, (double *)y, outer, dim, inner, reverse);
+    else
+        cumsum_kernel<float><<<(int)g, 256, 0, s>>>((const float *)x, (float *)y, outer, dim, inner, reverse);
+    ZC_LAUNCHED("cumsum_kernel");
     return ZPUCUDA_OK;
 }
 

@@ -19,17 +19,20 @@ namespace zc {
 
 constexpr int RP_MAX_INSN = 48;
 constexpr int RP_MAX_IN = 8;
-constexpr int RP_MAX_OUT = 4;
+constexpr int RP_MAX_OUT = 16;
 constexpr int RP_MAX_REG = 32;
 constexpr int RP_MAX_RANK = 8;
 
 enum : int8_t { IN_FULL = 0, IN_SCALAR = 1, IN_ROW = 2, IN_GENERAL = 3 };
-enum : int32_t { RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4, RED_ARGMAX = 5, RED_ARGMIN = 6 };
+enum : int32_t {
+    RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4, RED_ARGMAX = 5, RED_ARGMIN = 6,
+    RED_ANY = 7, RED_ALL = 8  // bool results (ops.reduceBoolKernel)
+};
 enum : uint8_t { OPC_LOAD = 250 };
 
 struct Insn {
     uint8_t op;  // prims.Prim code, or OPC_LOAD
-    uint8_t dst, a, b;
+    uint8_t dst, a, b, c;  // c: the third operand of `where`
 };
 
 // One lowered region.  Loads come first (r0..r(n_in-1)), then one register
@@ -54,6 +57,11 @@ struct RegionProgram {
     int32_t reduce_reg;
     int32_t n_out;  // element-wise outputs written to HBM
     int32_t out_reg[RP_MAX_OUT];
+    // Bool values (predicates, zpu's one-byte DType.bool) ride in the
+    // region's float registers as 0 / 1: bool inputs load a byte, bool
+    // outputs store (v != 0) as a byte.
+    uint8_t in_bool[RP_MAX_IN];
+    uint8_t out_bool[RP_MAX_OUT];
 };
 
 // Launch-time arguments of a region kernel.
@@ -567,6 +575,12 @@ int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s)
     ZC_LAUNCHED("fused region kernel");
     return ZPUCUDA_OK;
 }
+
+// ops.cumsum (src/zpu/ops.zig:2032-2060) of a contiguous [outer, dim, inner]
+// tensor along the middle axis into y: a running f64 sum, each prefix
+// rounded to the element type; `reverse` runs from the end.
+int cumsum_launch(int dtype, const void *x, void *y, int64_t outer, int64_t dim, int64_t inner, bool reverse,
+                  cudaStream_t s);
 
 // The lookup the lowering uses: nullptr when `sig` is not catalogued.
 const CatalogueEntry *catalogue_find(const char *sig);
