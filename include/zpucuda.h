@@ -337,6 +337,16 @@ int64_t zpucuda_mlp_steps(const zpucuda_mlp *h);
  * hides under the next GEMM); ZPUCUDA_MLP_PEER_EXCHANGE=1 / =0, set alike on
  * every rank, forces it on / off. */
 int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h);
+/* Phase trace of the step (diagnostics): with tracing on, each
+ * value_and_grad / train_step records timing events at its phase boundaries;
+ * zpucuda_mlp_trace_read waits (bounded) for the last traced step and writes
+ * up to 12 times in ms from its start: [0] start, [1] forward GEMMs, [2]
+ * loss, [3] layer-3 backward + db2, [4] dW2 GEMM, [5] g1 GEMM, [6] db1 + dW1
+ * GEMM, [7] end (main stream); [8] bucket [W2 ..] summed, [9] its Adam and
+ * all-gather, [10] bucket [W1, b1] summed, [11] its Adam and all-gather
+ * (side stream; -1 where a point was not reached, e.g. on one rank). */
+int zpucuda_mlp_trace(zpucuda_mlp *h, int on);
+int zpucuda_mlp_trace_read(zpucuda_mlp *h, float *ms, int n);
 
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot

@@ -223,3 +223,25 @@ def test_full_size_step_against_torch_fp32(zc):
     assert np.array_equal(xd[:2].cpu().numpy().ravel(), zo.uniform_range(0x5EED0006, 2 * 784, 0.0, 1.0))
     m.close()
     torch.cuda.empty_cache()
+
+
+def test_phase_trace_orders_the_step(zc):
+    """zpucuda_mlp_trace: one GPU, so no gradient exchange (point 8 is never
+    reached); the main-stream points come in step order, the step's end waits
+    for the side stream's Adam, and tracing leaves the results unchanged."""
+    dims, B = (128, 256, 128, 10), 512
+    X, labels, params = problem(dims, B, 0x5EED0900)
+    xd, ld = dev(X), dev(labels)
+    a, b = make(zc, dims, B, params), make(zc, dims, B, params)
+    b.trace(True)
+    for _ in range(2):
+        a.train_step(xd, ld)
+        b.train_step(xd, ld)
+    t = b.trace_read()
+    assert t[0] == 0.0
+    assert all(t[i] > 0 for i in range(1, 8)) and all(t[i] <= t[i + 1] for i in range(0, 7)), t
+    assert t[8] == -1.0
+    assert 0 < t[9] <= t[11] <= t[7] and t[10] <= t[11], t
+    for x, y in zip(a.params(), b.params()):
+        assert np.array_equal(x, y)
+    b.trace(False)

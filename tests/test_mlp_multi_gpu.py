@@ -62,11 +62,12 @@ RANK_SCRIPT = textwrap.dedent("""
 """)
 
 
-@pytest.mark.parametrize("peer", ["1", "0"])
-def test_two_gpu_train_steps_match_one_gpu(tmp_path, peer):
+@pytest.mark.parametrize("peer,last_ar", [("1", "0"), ("0", "0"), ("1", "1")])
+def test_two_gpu_train_steps_match_one_gpu(tmp_path, peer, last_ar):
     """peer "1": dW2 goes from its GEMM's tile stores into the owner's inbox
     over NVLink (the exchange must be active); "0": every gradient through
-    NCCL's reduce-scatter."""
+    NCCL's reduce-scatter.  last_ar "1": the last bucket [W1, b1] as one
+    allreduce with Adam on every rank instead of reduce-scatter + all-gather."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import zpu_b200 as zc
@@ -75,7 +76,7 @@ def test_two_gpu_train_steps_match_one_gpu(tmp_path, peer):
     script = tmp_path / "rank.py"
     script.write_text(RANK_SCRIPT.format(root=ROOT, dims=DIMS, B=B, steps=STEPS))
     env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()), NCCL_NVLS_ENABLE="0",
-               ZPUCUDA_MLP_PEER_EXCHANGE=peer)
+               ZPUCUDA_MLP_PEER_EXCHANGE=peer, ZPUCUDA_MLP_LAST_BUCKET_ALLREDUCE=last_ar)
     procs = [subprocess.Popen([sys.executable, str(script), str(r), "2", str(tmp_path / ("r%d.npz" % r))], env=env)
              for r in range(2)]
     try:

@@ -132,6 +132,8 @@ SIGNATURES = {
     "zpucuda_mlp_check": (I32, [P]),
     "zpucuda_mlp_steps": (I64, [P]),
     "zpucuda_mlp_exchange_mode": (I32, [P]),
+    "zpucuda_mlp_trace": (I32, [P, I32]),
+    "zpucuda_mlp_trace_read": (I32, [P, P, I32]),
 }
 
 

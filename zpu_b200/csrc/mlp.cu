@@ -48,7 +48,9 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <chrono>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "gemm.cuh"
@@ -332,6 +334,12 @@ __global__ void __launch_bounds__(256) xfer_reduce_kernel(const float4 *__restri
 
 using namespace zc;
 
+// Phase boundaries the trace records, in this order: main stream -- start,
+// forward GEMMs, loss, layer-3 backward + db2, dW2 GEMM, g1 GEMM, db1 + dW1
+// GEMM, end (side stream joined); side stream -- bucket [W2 ..] summed,
+// its Adam + all-gather, bucket [W1, b1] summed, its Adam + all-gather.
+constexpr int kTracePoints = 12;
+
 struct zpucuda_mlp {
     int device = -1;
     int64_t d[4] = {0, 0, 0, 0};  // d_in, d_h1, d_h2, d_out
@@ -357,6 +365,10 @@ struct zpucuda_mlp {
     uint8_t *xfer = nullptr;                    // this rank's [flags | inbox]
     uint8_t *peer_base[kMaxPeers] = {};         // every rank's allocation, mapped here
     unsigned long long epoch = 0;               // dW2 exchanges so far
+    // phase trace (zpucuda_mlp_trace): timing events at the step's phase
+    // boundaries, on the main stream (kTraceMain) and the side stream
+    bool trace = false;
+    cudaEvent_t tev[kTracePoints] = {};
     std::mutex mu;
 
     float *loss_ptr() const { return grads + total; }
@@ -385,6 +397,8 @@ void free_mlp(zpucuda_mlp *h) {
     if (h->ev_b) cudaEventDestroy(h->ev_b);
     if (h->ev_w2) cudaEventDestroy(h->ev_w2);
     if (h->ev_done) cudaEventDestroy(h->ev_done);
+    for (cudaEvent_t e : h->tev)
+        if (e) cudaEventDestroy(e);
     if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
     delete h;
 }
@@ -459,6 +473,21 @@ float *xfer_inbox(const zpucuda_mlp *h, int r) { return (float *)(h->peer_base[r
 // 2 and 4 ranks, 11 % faster at 8).  ZPUCUDA_MLP_PEER_EXCHANGE=1 / =0 (the
 // same on every rank) forces it on / off.
 constexpr int kPeerExchangeMinWorld = 6;
+
+// The last bucket ([W1, b1], summed after the final GEMM with nothing left to
+// overlap it) as one allreduce with Adam over the whole bucket on every rank,
+// instead of reduce-scatter + Adam on a shard + all-gather: one collective's
+// latency instead of two.  ZPUCUDA_MLP_LAST_BUCKET_ALLREDUCE=1 / =0 (the same
+// on every rank) forces it on / off; the default is off.
+bool last_bucket_allreduce(int world) {
+    static const int env = [] {
+        const char *e = getenv("ZPUCUDA_MLP_LAST_BUCKET_ALLREDUCE");
+        return e && e[0] ? (e[0] != '0' ? 1 : 0) : -1;
+    }();
+    (void)world;
+    return env == 1;
+}
+
 int peer_setup(zpucuda_mlp *h, int world, int rank, cudaStream_t s) {
     h->peer_state = -1;
     const char *env = getenv("ZPUCUDA_MLP_PEER_EXCHANGE");
@@ -525,6 +554,13 @@ int peer_setup(zpucuda_mlp *h, int world, int rank, cudaStream_t s) {
 // Adam update of each bucket follows on the side stream too: [W2 .. b3] once
 // its gradients are final and the g1 GEMM has read W2, overlapping dW1, then
 // [W1, b1] at the end.
+// Records trace point i on stream st when the trace is on.
+inline int tmark(zpucuda_mlp *h, int i, cudaStream_t st) {
+    if (!h->trace) return ZPUCUDA_OK;
+    ZC_CUDA(cudaEventRecord(h->tev[i], st));
+    return ZPUCUDA_OK;
+}
+
 int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_t B, int64_t global_b, bool ar,
                    bool adam, cudaStream_t s) {
     const int64_t d0 = h->d[0], d1 = h->d[1], d2 = h->d[2], d3 = h->d[3], d3p = h->d3p;
@@ -539,9 +575,11 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     if (ar && adam && world > 1 && h->peer_state == 0) ZC_TRY(peer_setup(h, world, rank, h->comm_stream));
 
     // forward: dense -> tanh -> dense -> tanh -> dense
+    ZC_TRY(tmark(h, 0, s));
     ZC_TRY(gemm(x, W1, h->a1, B, d1, d0, d0, d1, d1, false, false, epi(EPI_BIAS_TANH, b1), s));
     ZC_TRY(gemm(h->a1, W2, h->a2, B, d2, d1, d1, d2, d2, false, false, epi(EPI_BIAS_TANH, b2), s));
     ZC_TRY(gemm(h->a2, W3, h->logits, B, d3p, d2, d2, d3p, d3p, false, false, epi(EPI_BIAS, b3), s));
+    ZC_TRY(tmark(h, 1, s));
 
     // loss and d(loss)/d(logits)
     const float inv_b = (float)(1.0 / (double)global_b);
@@ -555,6 +593,7 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
                                                          h->xent_partials, h->xent_ticket(), h->loss_ptr(),
                                                          h->label_error());
     ZC_LAUNCHED("xent_kernel");
+    ZC_TRY(tmark(h, 2, s));
 
     // layer 3: dW3 = a2^T gl, db3 = colsum(gl), g_a2 = (gl W3^T) * (1 - a2^2)
     ZC_TRY(gemm(h->a2, h->gl, gW3, d2, d3p, B, d2, d3p, d3p, true, false, Epilogue{}, s));
@@ -562,6 +601,7 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     ZC_TRY(gemm(h->gl, W3, h->ga2, B, d2, d3p, d3p, d3p, d2, false, true, epi(EPI_TANH_GRAD, nullptr, h->a2, d2), s));
     // layer 2
     ZC_TRY(colsum(h, 1, h->ga2, B, d2, d2, gb2, s));
+    ZC_TRY(tmark(h, 3, s));
     const int64_t nA = h->total - h->off[2], nB = h->off[2], nA3 = h->total - h->off[3];
     const bool shard = ar && adam && nA % (4 * world) == 0 && nB % (4 * world) == 0;
     const bool fused = shard && h->peer_state == 1 && h->peer_world == world && nA3 % (4 * world) == 0;
@@ -583,6 +623,7 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     } else {
         ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s));
     }
+    ZC_TRY(tmark(h, 4, s));
     cudaStream_t side = h->comm_stream;
     // With a communicator and Adam in the step, each rank updates only its
     // 1/world shard of each bucket: reduce-scatter the gradients, Adam on the
@@ -609,8 +650,10 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         } else {
             ZC_TRY(nccl_allreduce_sum_f32(h->grads + h->off[2], nA + 1, side));
         }
+        ZC_TRY(tmark(h, 8, side));
     }
     ZC_TRY(gemm(h->ga2, W2, h->ga1, B, d1, d2, d2, d2, d1, false, true, epi(EPI_TANH_GRAD, nullptr, h->a1, d1), s));
+    ZC_TRY(tmark(h, 5, s));
     AdamConsts ac;
     if (adam) {  // every later kernel on s leaves W2, b2, W3, b3 alone
         ac = adam_consts(h);
@@ -626,24 +669,30 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         } else {
             ZC_TRY(adam_range(h, ac, h->off[2], nA, side));
         }
+        ZC_TRY(tmark(h, 9, side));
     }
     // layer 1
     ZC_TRY(colsum(h, 0, h->ga1, B, d1, d1, gb1, s));
     ZC_TRY(gemm(x, h->ga1, gW1, d0, d1, B, d0, d1, d1, true, false, Epilogue{}, s));
+    ZC_TRY(tmark(h, 6, s));
     if (ar || adam) {
         ZC_CUDA(cudaEventRecord(h->ev_b, s));
         ZC_CUDA(cudaStreamWaitEvent(side, h->ev_b, 0));
-        if (shard) {
+        if (shard && !last_bucket_allreduce(world)) {
             ZC_TRY(nccl_reduce_scatter_sum_f32(h->grads, nB / world, side));
+            ZC_TRY(tmark(h, 10, side));
             ZC_TRY(adam_range(h, ac, rank * (nB / world), nB / world, side));
             ZC_TRY(nccl_all_gather_f32(h->params, nB / world, side));
         } else {
             if (ar) ZC_TRY(nccl_allreduce_sum_f32(h->grads, nB, side));
+            ZC_TRY(tmark(h, 10, side));
             if (adam) ZC_TRY(adam_range(h, ac, 0, nB, side));
         }
+        ZC_TRY(tmark(h, 11, side));
         ZC_CUDA(cudaEventRecord(h->ev_done, side));
         ZC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
     }
+    ZC_TRY(tmark(h, 7, s));
     return ZPUCUDA_OK;
 }
 
@@ -899,3 +948,37 @@ extern "C" int zpucuda_mlp_check(zpucuda_mlp *h) {
 extern "C" int64_t zpucuda_mlp_steps(const zpucuda_mlp *h) { return h ? h->t : -1; }
 
 extern "C" int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h) { return h && h->peer_state == 1 ? 1 : 0; }
+
+extern "C" int zpucuda_mlp_trace(zpucuda_mlp *h, int on) {
+    ZC_CHECK(h, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    std::lock_guard<std::mutex> g(h->mu);
+    if (on)
+        for (cudaEvent_t &e : h->tev)
+            if (!e) ZC_CUDA(cudaEventCreate(&e));
+    h->trace = on != 0;
+    return ZPUCUDA_OK;
+}
+
+extern "C" int zpucuda_mlp_trace_read(zpucuda_mlp *h, float *ms, int n) {
+    ZC_CHECK(h && ms && n >= 0, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    std::lock_guard<std::mutex> g(h->mu);
+    ZC_CHECK(h->tev[0], ZPUCUDA_ERR_NOT_SUPPORTED);
+    // bounded wait for the traced step's last point
+    for (int64_t spins = 0;; spins++) {
+        const cudaError_t e = cudaEventQuery(h->tev[7]);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "cudaEventQuery");
+        if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_mlp_trace_read: step did not end");
+        std::this_thread::sleep_for(std::chrono::microseconds(10));
+    }
+    for (int i = 0; i < n && i < kTracePoints; i++) {
+        float t = -1.0f;  // -1: the point was not recorded in the traced step
+        if (i == 0) t = 0.0f;
+        else if (cudaEventElapsedTime(&t, h->tev[0], h->tev[i]) != cudaSuccess) {
+            cudaGetLastError();
+            t = -1.0f;
+        }
+        ms[i] = t;
+    }
+    return ZPUCUDA_OK;
+}

@@ -83,7 +83,7 @@ struct View {
 };
 
 constexpr int kCopyThreads = 256;
-constexpr int kTile = 32;
+constexpr int kTile = 64;  // transpose tile: 16 loads in flight per thread
 
 template <class S, class D, bool CONTIG>
 __global__ void __launch_bounds__(kCopyThreads) copy_gather_kernel(const __grid_constant__ View v, D *dst, int64_t n) {
@@ -105,10 +105,10 @@ __global__ void __launch_bounds__(kCopyThreads) copy_gather_kernel(const __grid_
 }
 
 // View [batch..., R, C] whose axis R has unit stride and axis C stride ld:
-// block (32, 8) moves one 32 x 32 tile, reading 32 consecutive rows of a
-// column (unit stride) and writing 32 consecutive columns of a row.
+// block (32, 8) moves one 64 x 64 tile, each warp reading 32 consecutive rows
+// of a column (unit stride) and writing 32 consecutive columns of a row.
 template <class S, class D>
-__global__ void __launch_bounds__(kTile * 8) copy_transpose_kernel(const __grid_constant__ View v, D *dst, int64_t R,
+__global__ void __launch_bounds__(256) copy_transpose_kernel(const __grid_constant__ View v, D *dst, int64_t R,
                                                                    int64_t C, int64_t ld) {
     __shared__ S tile[kTile][kTile + 1];
     const S *src = (const S *)v.data;
@@ -127,16 +127,20 @@ __global__ void __launch_bounds__(kTile * 8) copy_transpose_kernel(const __grid_
         const int64_t r0 = (int64_t)blockIdx.y * kTile, c0 = (int64_t)blockIdx.x * kTile;
         const int tx = threadIdx.x, ty = threadIdx.y;
 #pragma unroll
-        for (int j = 0; j < kTile; j += 8) {
-            const int64_t r = r0 + tx, c = c0 + ty + j;
-            if (r < R && c < C) tile[ty + j][tx] = src[boff + r + c * ld];
-        }
+        for (int j = 0; j < kTile; j += 8)
+#pragma unroll
+            for (int h = 0; h < kTile; h += 32) {
+                const int64_t r = r0 + tx + h, c = c0 + ty + j;
+                if (r < R && c < C) tile[ty + j][tx + h] = src[boff + r + c * ld];
+            }
         __syncthreads();
 #pragma unroll
-        for (int j = 0; j < kTile; j += 8) {
-            const int64_t r = r0 + ty + j, c = c0 + tx;
-            if (r < R && c < C) dst[(b * R + r) * C + c] = convert<S, D>(tile[tx][ty + j]);
-        }
+        for (int j = 0; j < kTile; j += 8)
+#pragma unroll
+            for (int h = 0; h < kTile; h += 32) {
+                const int64_t r = r0 + ty + j, c = c0 + tx + h;
+                if (r < R && c < C) dst[(b * R + r) * C + c] = convert<S, D>(tile[tx + h][ty + j]);
+            }
         __syncthreads();
     }
 }
@@ -163,7 +167,7 @@ int launch_copy(const View &v, void *dst, int64_t n, bool contig, cudaStream_t s
         const int64_t gx = (C + kTile - 1) / kTile, gy = (R + kTile - 1) / kTile;
         if (gy <= 65535 && gx <= 0x7fffffff) {
             const int gz = (int)(nb < 65535 ? nb : 65535);
-            copy_transpose_kernel<S, D><<<dim3((unsigned)gx, (unsigned)gy, gz), dim3(kTile, 8), 0, s>>>(
+            copy_transpose_kernel<S, D><<<dim3((unsigned)gx, (unsigned)gy, gz), dim3(32, 8), 0, s>>>(
                 v, (D *)dst, R, C, v.strides[r - 1]);
             ZC_LAUNCHED("tensor copy (tiled transpose)");
             return ZPUCUDA_OK;

@@ -168,6 +168,17 @@ class MLP:
     def steps(self):
         return lib().zpucuda_mlp_steps(self._h)
 
+    def trace(self, on=True):
+        """Record the step's phase boundaries (zpucuda_mlp_trace)."""
+        check(lib().zpucuda_mlp_trace(self._h, int(on)))
+
+    def trace_read(self):
+        """Times (ms from the step's start) of the last traced step's phase
+        boundaries, in zpucuda_mlp_trace_read's order (-1: not reached)."""
+        buf = (C.c_float * 12)()
+        check(lib().zpucuda_mlp_trace_read(self._h, buf, 12))
+        return [float(v) for v in buf]
+
     def exchange_mode(self):
         """1 when dW2 travels over peer memory from its GEMM, 0 when all
         gradients go through NCCL."""
