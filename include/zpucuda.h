@@ -189,6 +189,12 @@ typedef struct zpucuda_step {
     uint64_t out;
     int32_t axis;     /* Attrs.axis, ZPUCUDA_AXIS_NONE for a full reduction */
     int32_t flags;    /* Attrs.flags: bit 0 KEEP_DIMS (reductions), bit 5 REVERSE (cumsum) */
+    /* reshape / broadcast: Attrs.shape[0 .. shape_len) (-1: the one dimension
+     * reshape infers); transpose: Attrs.perm[0 .. nsl) */
+    int64_t shape[ZPUCUDA_MAX_RANK];
+    int32_t shape_len;
+    int32_t nsl;
+    uint8_t perm[ZPUCUDA_MAX_RANK];
 } zpucuda_step;
 
 /* jit.Blob (src/zpu/jit.zig:39-42): a constant folded at build time; its
@@ -211,7 +217,12 @@ typedef struct zpucuda_plan zpucuda_plan;
  * payload axes [d, rank) and a non-negative axis counts from axis d.  Matmul
  * steps become GEMM launches; cumsum steps (ops.cumsum, src/zpu/ops.zig:
  * 2032-2060: f64 running sum along one axis, rounded per element) a scan
- * launch each.  Region kernels come from
+ * launch each.  reshape / transpose / broadcast / expand_dims / squeeze
+ * (ops.zig:1343-1555) are views -- new strides over the same HBM, no launch
+ * -- that region loads and GEMM operands read in place; a view is copied
+ * (zpucuda_tensor_copy's kernels) only where a contiguous buffer is needed:
+ * a plan output, a cumsum input, a reshape of a non-contiguous view, a GEMM
+ * operand whose last two axes have no unit stride.  Region kernels come from
  * a catalogue generated at build time, with a one-pass bytecode kernel for
  * regions outside it.  Steps outside that set make creation fail with
  * ZPUCUDA_ERR_NOT_SUPPORTED. */

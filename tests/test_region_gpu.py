@@ -617,3 +617,134 @@ def test_cumsum_under_vmap_counts_payload_axes(zc):
     p = zc.Plan([(1, zc.F64, shape, 1)], [], [("cumsum", [1], 10, 0, 0)], [10])  # payload axis 0 = axis 1
     (got,) = p.run([torch.from_numpy(x).cuda()])
     assert np.array_equal(got.cpu().numpy(), zo.cumsum(x, 0, depth=1))
+
+
+def test_jit_mlp_loss_lowers_to_five_launches(zc):
+    """The jitted function of the reference's `jit(grad MLP) f32` benchmark
+    case (bench/bench.zig:137-150, 230-234; dims 64 -> 64 -> 10, batch 64):
+    dense, gelu (nn.zig:39-53: x * 0.5 * (1 + erf(x / sqrt 2))), dense,
+    square, mean over the last axis, sumAll -- the plan zpu's tracer records,
+    scalars as captured blobs.  Lowered to gemm, one fused region, gemm, one
+    fused region with the row sum, one region with the full sum; checked
+    against the oracle's f32 step-by-step evaluation at 1e-5 relative (the
+    device sums in f64, zpu in f32)."""
+    B, I, H, O = 64, 64, 64, 10
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((B, I)).astype(np.float32)
+    w1 = rng.standard_normal((I, H)).astype(np.float32)
+    b1 = np.zeros(H, np.float32)
+    w2 = rng.standard_normal((H, O)).astype(np.float32)
+    b2 = np.zeros(O, np.float32)
+    F = zc.F32
+    args = [(1, F, (B, I)), (2, F, (I, H)), (3, F, (H,)), (4, F, (H, O)), (5, F, (O,))]
+    blobs = [(6, np.float32(1.0 / np.sqrt(2.0))), (7, np.float32(1.0)), (8, np.float32(0.5)),
+             (9, np.float32(1.0 / O))]
+    steps = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0),
+             ("mul", [11, 6], 12, -2, 0), ("erf", [12], 13, -2, 0), ("add", [7, 13], 14, -2, 0),
+             ("mul", [11, 8], 15, -2, 0), ("mul", [15, 14], 16, -2, 0),
+             ("matmul", [16, 4], 17, -2, 0), ("add", [17, 5], 18, -2, 0),
+             ("square", [18], 19, -2, 0), ("sum", [19], 20, -1, 0), ("mul", [20, 9], 21, -2, 0),
+             ("sum", [21], 22, -2, 0)]
+    p = zc.Plan(args, blobs, steps, [22])
+    assert p.num_kernels() == 5, p.describe()
+    (got,) = p.run([torch.from_numpy(a).cuda() for a in (x, w1, b1, w2, b2)])
+    f32 = np.float32
+    h = (zo.matmul(x, w1) + b1).astype(f32)
+    e = zo.unary("erf", (h * f32(1.0 / np.sqrt(2.0))).astype(f32))
+    act = ((h * f32(0.5)).astype(f32) * (f32(1.0) + e).astype(f32)).astype(f32)
+    y = (zo.matmul(act, w2) + b2).astype(f32)
+    per_row = ((y * y).astype(f32).astype(np.float64).sum(-1)).astype(f32)
+    want = float(((per_row * f32(1.0 / O)).astype(f32)).astype(np.float64).sum())
+    assert abs(float(got.cpu()) - want) <= 1e-5 * abs(want), (float(got.cpu()), want)
+
+
+def test_views_fold_into_regions(zc):
+    """transpose / reshape / broadcast / expand_dims / squeeze (ops.zig:
+    1343-1555) are views over the producer's HBM; the regions after them
+    read through the view's strides, and outputs that are views are copied
+    out contiguous."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((6, 8, 10)).astype(np.float32)
+    bias = rng.standard_normal(10).astype(np.float32)
+    F = zc.F32
+    steps = [("transpose", [1], 10, -2, 0, {"perm": [2, 0, 1]}),       # [10, 6, 8], strided
+             ("exp", [10], 11, -2, 0),                                    # region through the view
+             ("reshape", [10], 12, -2, 0, {"shape": [10, -1]}),          # strided -> copied, [10, 48]
+             ("expand_dims", [2], 13, 0, 0),                              # [1, 10]
+             ("broadcast", [13], 14, -2, 0, {"shape": [48, 10]}),        # stride 0 rows
+             ("transpose", [12], 15, -2, 0, {"perm": [1, 0]}),           # [48, 10] view of the copy
+             ("add", [15, 14], 16, -2, 0),
+             ("expand_dims", [16], 17, -1, 0),                            # [48, 10, 1]
+             ("squeeze", [17], 18, 2, 0),                                 # [48, 10]
+             ("sum", [18], 19, 0, 0)]
+    p = zc.Plan([(1, F, (6, 8, 10)), (2, F, (10,))], [], steps, [11, 12, 14, 18, 19, 10])
+    outs = p.run([torch.from_numpy(x).cuda(), torch.from_numpy(bias).cuda()])
+    xt = np.transpose(x, (2, 0, 1))
+    want = [zo.unary("exp", np.ascontiguousarray(xt)), xt.reshape(10, 48),
+            np.broadcast_to(bias[None, :], (48, 10)), None, None, xt]
+    s18 = (xt.reshape(10, 48).T + bias[None, :]).astype(np.float32)
+    want[3] = s18
+    want[4] = s18.astype(np.float64).sum(0)
+    got = [o.cpu().numpy() for o in outs]
+    assert ulp_diff_f32(got[0], want[0]).max() <= 1
+    for i in (1, 2, 3, 5):
+        assert got[i].shape == want[i].shape and np.array_equal(got[i], want[i]), i
+    assert np.allclose(got[4], want[4], rtol=1e-6, atol=1e-6)
+    assert "copy (reshape of a strided view)" in p.describe()
+
+
+def test_transposed_matmul_operands_are_read_in_place(zc):
+    """The matmul VJP's swapLastTwo views (transpose of the last two axes)
+    feed the GEMM with no copy: one launch."""
+    a = zo.uniform_range(41, 96 * 64, -1.0, 1.0).reshape(96, 64)
+    b = zo.uniform_range(42, 96 * 40, -1.0, 1.0).reshape(96, 40)
+    F = zc.F32
+    p = zc.Plan([(1, F, (96, 64)), (2, F, (96, 40))], [],
+                [("transpose", [1], 10, -2, 0, {"perm": [1, 0]}), ("matmul", [10, 2], 11, -2, 0)], [11])
+    assert p.num_kernels() == 1, p.describe()
+    (c,) = p.run([torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])
+    want = a.T.astype(np.float64) @ b.astype(np.float64)
+    assert np.linalg.norm(c.cpu().numpy() - want) <= 1e-5 * np.linalg.norm(want)
+
+
+def test_broadcast_matmul_operand_is_copied(zc):
+    """A view with a zero stride inside the matrix axes has no leading
+    dimension a GEMM can take: the plan copies it first."""
+    v = zo.uniform_range(43, 32, -1.0, 1.0)
+    b = zo.uniform_range(44, 32 * 16, -1.0, 1.0).reshape(32, 16)
+    F = zc.F32
+    p = zc.Plan([(1, F, (32,)), (2, F, (32, 16))], [],
+                [("broadcast", [1], 10, -2, 0, {"shape": [24, 32]}), ("matmul", [10, 2], 11, -2, 0)], [11])
+    assert "copy (matmul operand)" in p.describe()
+    (c,) = p.run([torch.from_numpy(v).cuda(), torch.from_numpy(b).cuda()])
+    want = np.broadcast_to(v, (24, 32)).astype(np.float64) @ b.astype(np.float64)
+    assert np.linalg.norm(c.cpu().numpy() - want) <= 1e-5 * np.linalg.norm(want)
+
+
+def test_views_under_vmap_use_payload_axes(zc):
+    """batch_depth 1: transpose, reshape, expand_dims and squeeze take
+    payload-relative arguments and keep the batch axis first.  A reshape
+    target gets the batch axes in front only when it has the payload's rank
+    (ops.zig:1345-1350); another rank is zpu's ShapeMismatch here too."""
+    x = zo.uniform_range(45, 3 * 4 * 5, -1.0, 1.0).reshape(3, 4, 5)
+    F = zc.F32
+    steps = [("transpose", [1], 10, -2, 0, {"perm": [1, 0]}),   # payload perm -> (0, 2, 1)
+             ("reshape", [10], 11, -2, 0, {"shape": [2, 10]}),   # payload shape -> [3, 2, 10]
+             ("expand_dims", [1], 12, 0, 0),                      # -> [3, 1, 4, 5]
+             ("squeeze", [12], 13, 0, 0),                         # -> [3, 4, 5]
+             ("neg", [11], 14, -2, 0)]
+    p = zc.Plan([(1, F, (3, 4, 5), 1)], [], steps, [10, 11, 12, 13, 14])
+    t, r, e, q, n = [o.cpu().numpy() for o in p.run([torch.from_numpy(x).cuda()])]
+    xt = np.transpose(x, (0, 2, 1))
+    assert np.array_equal(t, xt) and np.array_equal(r, xt.reshape(3, 2, 10))
+    assert np.array_equal(e, x[:, None]) and np.array_equal(q, x) and np.array_equal(n, -xt.reshape(3, 2, 10))
+    with pytest.raises(zc.ZpuCudaError) as err:
+        zc.Plan([(1, F, (3, 4, 5), 1)], [], [("reshape", [1], 10, -2, 0, {"shape": [20]})], [10])
+    assert err.value.status == 2  # ShapeMismatch
+
+
+def test_argument_output_is_copied(zc):
+    x = torch.randn(7, 9, device="cuda")
+    p = zc.Plan([(1, zc.F32, (7, 9))], [], [("neg", [1], 10, -2, 0)], [1, 10, 1])
+    a, n, b = p.run([x])
+    assert torch.equal(a, x) and torch.equal(b, x) and torch.equal(n, -x)

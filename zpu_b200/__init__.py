@@ -164,9 +164,11 @@ class Plan:
 
     def __init__(self, args, blobs, steps, out_ids):
         """args: [(id, dtype_code, shape[, batch_depth])], blobs: [(id, numpy
-        array)], steps: [(prim, [input ids], out id, axis, keepdims)],
-        out_ids: [id].  batch_depth is Tensor.batch_depth (vmap's leading
-        axes, src/zpu/tensor.zig:79-89): reductions fold payload axes only."""
+        array)], steps: [(prim, [input ids], out id, axis, flags[, {"shape":
+        dims, "perm": axes}])] (flags: Attrs.flags, 1 = KEEP_DIMS, 32 =
+        REVERSE; shape / perm: reshape, broadcast, transpose), out_ids: [id].
+        batch_depth is Tensor.batch_depth (vmap's leading axes,
+        src/zpu/tensor.zig:79-89): reductions fold payload axes only."""
         import numpy as np
         L = lib()
         self._keep = []
@@ -181,7 +183,9 @@ class Plan:
             _fill_value(bl[i].value, vid, code, arr.shape)
             bl[i].host_data = arr.ctypes.data
         st = (Step * max(1, len(steps)))()
-        for i, (prim, ins, out, axis, keepdims) in enumerate(steps):
+        for i, step in enumerate(steps):
+            prim, ins, out, axis, keepdims = step[:5]
+            extra = step[5] if len(step) > 5 else {}
             st[i].prim = PRIM[prim] if isinstance(prim, str) else prim
             st[i].n_inputs = len(ins)
             for k, x in enumerate(ins):
@@ -189,6 +193,14 @@ class Plan:
             st[i].out = out
             st[i].axis = axis
             st[i].flags = int(keepdims)  # Attrs.flags: 1 = KEEP_DIMS, 32 = REVERSE
+            shape = extra.get("shape", ())
+            st[i].shape_len = len(shape)
+            for k, d in enumerate(shape):
+                st[i].shape[k] = d
+            perm = extra.get("perm", ())
+            st[i].nsl = len(perm)
+            for k, d in enumerate(perm):
+                st[i].perm[k] = d
         oi = (C.c_uint64 * len(out_ids))(*out_ids)
         h = C.c_void_p()
         check(L.zpucuda_plan_create(va, len(args), bl, len(blobs), st, len(steps), oi, len(out_ids),

@@ -35,7 +35,8 @@ PRIM = {
     "minimum": 41, "atan2": 42, "hypot": 43, "mod_op": 44, "eq": 45, "ne": 46, "lt": 47, "le": 48,
     "gt": 49, "ge": 50, "logical_and": 51, "logical_or": 52, "logical_xor": 53, "logical_not": 54,
     "where": 55, "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "any_reduce": 62,
-    "all_reduce": 63, "argmax": 64, "argmin": 65, "cumsum": 78, "matmul": 80,
+    "all_reduce": 63, "argmax": 64, "argmin": 65, "reshape": 66, "transpose": 67, "broadcast": 68, "expand_dims": 69,
+    "squeeze": 70, "cumsum": 78, "matmul": 80,
     "constant": 87, "copy": 88,
 }
 
@@ -60,7 +61,9 @@ class Value(C.Structure):
 
 class Step(C.Structure):
     _fields_ = [("prim", C.c_int32), ("n_inputs", C.c_int32), ("ins", C.c_uint64 * 3),
-                ("out", C.c_uint64), ("axis", C.c_int32), ("flags", C.c_int32)]
+                ("out", C.c_uint64), ("axis", C.c_int32), ("flags", C.c_int32),
+                ("shape", C.c_int64 * MAX_RANK), ("shape_len", C.c_int32), ("nsl", C.c_int32),
+                ("perm", C.c_uint8 * MAX_RANK)]
 
 
 class Blob(C.Structure):

@@ -35,6 +35,11 @@ enum {
     PRIM_ARGMIN = 65,
     PRIM_LOGICAL_NOT = 54,
     PRIM_WHERE = 55,
+    PRIM_RESHAPE = 66,
+    PRIM_TRANSPOSE = 67,
+    PRIM_BROADCAST = 68,
+    PRIM_EXPAND_DIMS = 69,
+    PRIM_SQUEEZE = 70,
     PRIM_CUMSUM = 78,
     PRIM_MATMUL = 80,
 };
@@ -62,6 +67,8 @@ bool arg_reduce(int p) { return p == PRIM_ARGMAX || p == PRIM_ARGMIN; }
 bool bool_reduce(int p) { return p == PRIM_ANY || p == PRIM_ALL; }
 bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p) || bool_reduce(p); }
 bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
+// The movement prims a plan lowers as views (ops.zig:1343-1555).
+bool view_prim(int p) { return p >= PRIM_RESHAPE && p <= PRIM_SQUEEZE; }
 // Bool values ride in a region's float registers: two values fit one region
 // unless both are floats of different types.  -1: no float type required.
 int carrier_of(int dt) { return float_dtype(dt) ? dt : -1; }
@@ -114,10 +121,34 @@ struct Value {
     int arg_index = -1, blob_index = -1;
     bool materialised = false;  // has a Slot
     Slot slot;
+    // element (i0, i1, ...) lives at offset + sum(i_d * strides[d]) of the
+    // slot: contiguous with offset 0 except for views
+    int64_t strides[ZPUCUDA_MAX_RANK] = {0};
+    int64_t offset = 0;
+    bool view = false;          // a view step's output: the input's slot
+    bool reshape_copy = false;  // a reshape of a non-contiguous view: copied first
+    void set_contiguous() {
+        int64_t st = 1;
+        for (int d = shape.rank - 1; d >= 0; d--) {
+            strides[d] = st;
+            st *= shape.dims[d];
+        }
+    }
+    bool contiguous() const {  // size-1 axes may have any stride
+        int64_t st = 1;
+        for (int d = shape.rank - 1; d >= 0; d--) {
+            if (shape.dims[d] != 1 && strides[d] != st) return false;
+            st *= shape.dims[d];
+        }
+        return true;
+    }
 };
 
 struct Launch {
-    enum { REGION, MATMUL, CUMSUM } kind = REGION;
+    enum { REGION, MATMUL, CUMSUM, COPY } kind = REGION;
+    std::vector<int64_t> in_off;  // region inputs: byte offsets into their slots
+    int64_t ma_off = 0, mb_off = 0;  // matmul / cumsum / copy source: byte offsets
+    zpucuda_tensor src;              // copy: the view (data set at run time)
     RegionProgram prog;
     const CatalogueEntry *cat = nullptr;
     std::string signature;
@@ -209,6 +240,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         x.shape.rank = v.rank;
         for (int i = 0; i < v.rank; i++) x.shape.dims[i] = v.dims[i];
         x.depth = v.batch_depth;
+        x.set_contiguous();
         return x;
     };
     for (int i = 0; i < n_args; i++) {
@@ -306,6 +338,120 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 }
             }
             if (arg_reduce(st.prim)) o.dtype = ZPUCUDA_I64;
+        } else if (view_prim(st.prim) && st.n_inputs == 1) {
+            o.view = true;
+            o.offset = a.offset;
+            const int r = a.shape.rank;
+            if (st.prim == PRIM_RESHAPE) {
+                // ops.reshape / reshapeTarget (ops.zig:1343-1400): a payload
+                // shape under vmap keeps the batch axes; -1 is inferred
+                Shape req;
+                req.rank = st.shape_len;
+                if (req.rank < 0 || req.rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "reshape rank");
+                for (int i = 0; i < req.rank; i++) req.dims[i] = st.shape[i];
+                if (req.rank + a.depth == r && a.depth > 0) {
+                    if (r > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "reshape rank");
+                    for (int i = req.rank - 1; i >= 0; i--) req.dims[i + a.depth] = req.dims[i];
+                    for (int i = 0; i < a.depth; i++) req.dims[i] = a.shape.dims[i];
+                    req.rank = r;
+                }
+                int64_t known = 1;
+                int unknown = -1;
+                for (int i = 0; i < req.rank; i++) {
+                    if (req.dims[i] == 0) return lower_fail(plan, ZPUCUDA_ERR_INVALID_SHAPE, "reshape to a zero dimension");
+                    if (req.dims[i] < 0) {
+                        if (unknown >= 0) return lower_fail(plan, ZPUCUDA_ERR_INVALID_SHAPE, "reshape with two -1");
+                        unknown = i;
+                    } else {
+                        known *= req.dims[i];
+                    }
+                }
+                if (unknown >= 0) {
+                    if (known == 0 || a.shape.numel() % known) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "reshape");
+                    req.dims[unknown] = a.shape.numel() / known;
+                }
+                if (req.numel() != a.shape.numel() || req.rank < a.depth)
+                    return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "reshape");
+                o.shape = req;
+                o.set_contiguous();
+                if (!a.contiguous()) {
+                    o.reshape_copy = true;
+                    o.offset = 0;
+                }
+            } else if (st.prim == PRIM_TRANSPOSE) {
+                // ops.transpose (ops.zig:1424-1449): a payload permutation
+                // under vmap leaves the batch axes first
+                int perm[ZPUCUDA_MAX_RANK];
+                if (st.nsl == r) {
+                    for (int i = 0; i < r; i++) perm[i] = st.perm[i];
+                } else if (st.nsl + a.depth == r) {
+                    for (int i = 0; i < a.depth; i++) perm[i] = i;
+                    for (int i = 0; i < st.nsl; i++) perm[a.depth + i] = st.perm[i] + a.depth;
+                } else {
+                    return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "transpose permutation length");
+                }
+                bool seen[ZPUCUDA_MAX_RANK] = {false};
+                for (int i = 0; i < r; i++) {
+                    if (perm[i] < 0 || perm[i] >= r || seen[perm[i]]) return lower_fail(plan, ZPUCUDA_ERR_INVALID_SHAPE, "transpose permutation");
+                    seen[perm[i]] = true;
+                }
+                o.shape.rank = r;
+                for (int i = 0; i < r; i++) {
+                    o.shape.dims[i] = a.shape.dims[perm[i]];
+                    o.strides[i] = a.strides[perm[i]];
+                }
+            } else if (st.prim == PRIM_BROADCAST) {
+                // ops.broadcastTo / broadcastTarget (ops.zig:1480-1522)
+                Shape t;
+                t.rank = st.shape_len;
+                if (t.rank < r || t.rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast target");
+                for (int i = 0; i < t.rank; i++) t.dims[i] = st.shape[i];
+                for (int i = 0; i < r; i++) {
+                    const int64_t rd = t.dims[t.rank - r + i], xd = a.shape.dims[i];
+                    if (rd != xd && xd != 1 && rd != 1) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast target");
+                }
+                // NumPy right alignment: x's axis xi = i - (t.rank - r); a
+                // size-1 or missing axis gets stride 0.  (zpu's loop maps
+                // axis i < r to x axis i - (t.rank - r), which is negative for
+                // a rank-increasing target; for equal ranks the two agree.)
+                for (int i = 0; i < t.rank; i++) {
+                    const int xi = i - (t.rank - r);
+                    o.strides[i] = (xi < 0 || a.shape.dims[xi] == 1) ? 0 : a.strides[xi];
+                }
+                o.shape = t;
+            } else {
+                // ops.expandDims / squeeze (ops.zig:1524-1555): payload axes
+                const int payload = r - a.depth;
+                int ax = st.axis;
+                if (st.prim == PRIM_EXPAND_DIMS) {
+                    if (ax < 0) ax += payload + 1;
+                    if (ax < 0 || ax > payload || r >= ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "expand_dims axis");
+                    const int pos = a.depth + ax;
+                    o.shape.rank = r + 1;
+                    for (int i = 0, j = 0; i < r + 1; i++) {
+                        if (i == pos) {
+                            o.shape.dims[i] = 1;
+                            o.strides[i] = 0;
+                        } else {
+                            o.shape.dims[i] = a.shape.dims[j];
+                            o.strides[i] = a.strides[j];
+                            j++;
+                        }
+                    }
+                } else {
+                    if (ax < 0) ax += payload;
+                    if (ax < 0 || ax >= payload) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "squeeze axis");
+                    const int pos = a.depth + ax;
+                    if (a.shape.dims[pos] != 1) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "squeeze of an axis longer than 1");
+                    o.shape.rank = r - 1;
+                    for (int i = 0, j = 0; j < r; j++) {
+                        if (j == pos) continue;
+                        o.shape.dims[i] = a.shape.dims[j];
+                        o.strides[i] = a.strides[j];
+                        i++;
+                    }
+                }
+            }
         } else if (st.prim == PRIM_CUMSUM && st.n_inputs == 1) {
             // ops.realAxis (src/zpu/ops.zig:1466-1471): vmap-aware, no AXIS_NONE
             if (!float_dtype(a.dtype)) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "cumsum of a non-float value");
@@ -337,6 +483,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " is not lowered to the device");
         }
         if (vals.count(st.out)) return lower_fail(plan, ZPUCUDA_ERR_INVALID_ARGUMENT, "step output id reused");
+        if (!o.view) o.set_contiguous();
         vals[st.out] = o;
     }
     std::map<uint64_t, int> out_index;
@@ -375,26 +522,111 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         return v.slot;
     };
 
+    // A copy launch of the view `v` (zpucuda_tensor_copy's kernels) into a
+    // contiguous buffer: `dst`, or a new temp when dst.index < 0.
+    auto copy_launch = [&](const Value &v, Slot dst, const std::string &why) -> Slot {
+        if (dst.index < 0) {
+            void *d = nullptr;
+            const size_t nb = (size_t)v.shape.numel() * itemsize(v.dtype);
+            if (cudaMalloc(&d, nb ? nb : 16) != cudaSuccess) {
+                cudaGetLastError();
+                return Slot{SLOT_TEMP, -1};
+            }
+            plan->temps.push_back(d);
+            dst = Slot{SLOT_TEMP, (int)plan->temps.size() - 1};
+        }
+        Launch L;
+        L.kind = Launch::COPY;
+        L.ma = v.slot;
+        L.ma_off = v.offset * (int64_t)itemsize(v.dtype);
+        memset(&L.src, 0, sizeof L.src);
+        L.src.dtype = v.dtype;
+        L.src.rank = v.shape.rank;
+        for (int d = 0; d < v.shape.rank; d++) {
+            L.src.dims[d] = v.shape.dims[d];
+            L.src.strides[d] = v.strides[d];
+        }
+        L.mc = dst;
+        L.text = "  kernel " + std::to_string(plan->launches.size()) + ": copy (" + why + ")\n";
+        plan->launches.push_back(L);
+        return dst;
+    };
+    // `v` as a contiguous value: itself, or a copy (v is left untouched)
+    auto contiguous_of = [&](const Value &v, const std::string &why, Value *out) -> bool {
+        *out = v;
+        if (v.contiguous()) return true;
+        Slot t = copy_launch(v, Slot{SLOT_TEMP, -1}, why);
+        if (t.index < 0) return false;
+        out->slot = t;
+        out->offset = 0;
+        out->set_contiguous();
+        return true;
+    };
+
     // ---- cut regions
     int s = 0;
     while (s < n_steps) {
         const zpucuda_step &st0 = steps[s];
+        if (view_prim(st0.prim)) {  // a view: the input's slot, no launch
+            Value &a = vals[st0.ins[0]];
+            Value &o = vals[st0.out];
+            if (!a.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "view of a value not materialised");
+            if (o.reshape_copy) {
+                Value c;
+                if (!contiguous_of(a, "reshape of a strided view", &c)) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy buffer");
+                o.slot = c.slot;
+                o.offset = 0;
+            } else {
+                o.slot = a.slot;
+            }
+            o.materialised = true;
+            s++;
+            continue;
+        }
         if (st0.prim == PRIM_MATMUL) {
+            // operands: views are read in place when one of the last two
+            // axes has unit stride (row-major or transposed), else copied
+            auto gemm_ok = [](const Value &v) {
+                const int r = v.shape.rank;
+                if (v.contiguous()) return true;
+                if (r < 2) return false;
+                for (int d = 0; d < r; d++)
+                    if (v.strides[d] < 0) return false;
+                const int64_t rows = v.shape.dims[r - 2], cols = v.shape.dims[r - 1];
+                const int64_t s0 = v.strides[r - 2], s1 = v.strides[r - 1];
+                if (s1 == 1 && (rows == 1 || s0 >= cols)) return true;  // row-major, leading dim s0
+                if (s0 == 1 && (cols == 1 || s1 >= rows)) return true;  // transposed, leading dim s1
+                return false;
+            };
+            Value a = vals[st0.ins[0]], b = vals[st0.ins[1]];
+            if (!gemm_ok(a) && !contiguous_of(vals[st0.ins[0]], "matmul operand", &a))
+                return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy buffer");
+            if (!gemm_ok(b) && !contiguous_of(vals[st0.ins[1]], "matmul operand", &b))
+                return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy buffer");
             Launch L;
             L.kind = Launch::MATMUL;
-            const Value &a = vals[st0.ins[0]], &b = vals[st0.ins[1]];
             L.ma = a.slot;
             L.mb = b.slot;
+            L.ma_off = a.offset * (int64_t)itemsize(a.dtype);
+            L.mb_off = b.offset * (int64_t)itemsize(b.dtype);
             memset(&L.ta, 0, sizeof L.ta);
             memset(&L.tb, 0, sizeof L.tb);
             L.ta.dtype = a.dtype; L.ta.rank = a.shape.rank; L.ta.batch_depth = a.depth;
             L.tb.dtype = b.dtype; L.tb.rank = b.shape.rank; L.tb.batch_depth = b.depth;
             for (int i = 0; i < a.shape.rank; i++) L.ta.dims[i] = a.shape.dims[i];
             for (int i = 0; i < b.shape.rank; i++) L.tb.dims[i] = b.shape.dims[i];
-            int64_t q = 1;
-            for (int i = L.ta.rank - 1; i >= 0; i--) { L.ta.strides[i] = q; q *= L.ta.dims[i]; }
-            q = 1;
-            for (int i = L.tb.rank - 1; i >= 0; i--) { L.tb.strides[i] = q; q *= L.tb.dims[i]; }
+            if (a.contiguous()) {
+                int64_t q = 1;
+                for (int i = L.ta.rank - 1; i >= 0; i--) { L.ta.strides[i] = q; q *= L.ta.dims[i]; }
+            } else {
+                for (int i = 0; i < a.shape.rank; i++) L.ta.strides[i] = a.strides[i];
+            }
+            if (b.contiguous()) {
+                int64_t q = 1;
+                for (int i = L.tb.rank - 1; i >= 0; i--) { L.tb.strides[i] = q; q *= L.tb.dims[i]; }
+            } else {
+                for (int i = 0; i < b.shape.rank; i++) L.tb.strides[i] = b.strides[i];
+            }
             zpucuda_matmul_shape(&L.ta, &L.tb, &L.tc);
             L.mc = materialise(st0.out);
             if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
@@ -408,10 +640,12 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             continue;
         }
         if (st0.prim == PRIM_CUMSUM) {
+            Value a;
+            if (!contiguous_of(vals[st0.ins[0]], "cumsum input", &a)) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy buffer");
             Launch L;
             L.kind = Launch::CUMSUM;
-            const Value &a = vals[st0.ins[0]];
             L.ma = a.slot;
+            L.ma_off = a.offset * (int64_t)itemsize(a.dtype);
             L.dtype = a.dtype;
             const int ax = st0.axis >= 0 ? st0.axis + a.depth : st0.axis + a.shape.rank;
             L.outer = 1;
@@ -503,9 +737,20 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             reg[loads[k]] = k;
             P.insn[k] = Insn{OPC_LOAD, (uint8_t)k, (uint8_t)k, 0};
             L.ins.push_back(iv.slot);
+            L.in_off.push_back(iv.offset * (int64_t)itemsize(iv.dtype));
             const Shape &is = iv.shape;
             P.in_numel[k] = is.numel();
-            if (is == rshape) {
+            if (!iv.contiguous() && is.numel() != 1) {
+                // a strided view: its own strides over the region's axes
+                for (int d = rshape.rank - 1; d >= 0; d--) {
+                    const int id = is.rank - rshape.rank + d;
+                    const int64_t dim = id >= 0 ? is.dims[id] : 1;
+                    if (dim != 1 && dim != rshape.dims[d]) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "region broadcast");
+                    P.in_strides[k][d] = (id < 0 || dim == 1) ? 0 : iv.strides[id];
+                }
+                P.in_kind[k] = IN_GENERAL;
+                kinds += "G";
+            } else if (is == rshape) {
                 P.in_kind[k] = IN_FULL;
                 kinds += "F";
             } else if (is.numel() == 1) {
@@ -644,6 +889,14 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         plan->launches.push_back(L);
         s = member.back() + 1;
     }
+    // outputs that are views, arguments, constants, or listed twice: copied
+    // into their output buffers after everything else
+    for (int i = 0; i < n_outs; i++) {
+        Value &v = vals[out_ids[i]];
+        if (!v.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "output not computed");
+        if (v.slot.kind == SLOT_OUT && v.slot.index == i && v.offset == 0 && v.contiguous()) continue;
+        if (copy_launch(v, Slot{SLOT_OUT, i}, "plan output").index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy");
+    }
     char head[160];
     snprintf(head, sizeof head, "plan: %d steps -> %zu kernels\n", n_steps, plan->launches.size());
     plan->text = head;
@@ -667,16 +920,21 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
         int st;
         if (L.kind == Launch::MATMUL) {
             zpucuda_tensor a = L.ta, b = L.tb, c = L.tc;
-            a.data = ptr(L.ma);
-            b.data = ptr(L.mb);
+            a.data = (char *)ptr(L.ma) + L.ma_off;
+            b.data = (char *)ptr(L.mb) + L.mb_off;
             c.data = ptr(L.mc);
             st = matmul_device(&a, &b, &c, s);
         } else if (L.kind == Launch::CUMSUM) {
-            st = cumsum_launch(L.dtype, ptr(L.ma), ptr(L.mc), L.outer, L.dim, L.inner, L.reverse, s);
+            st = cumsum_launch(L.dtype, (char *)ptr(L.ma) + L.ma_off, ptr(L.mc), L.outer, L.dim, L.inner, L.reverse, s);
+        } else if (L.kind == Launch::COPY) {
+            zpucuda_tensor a = L.src, c = L.src;
+            a.data = (char *)ptr(L.ma) + L.ma_off;
+            c.data = ptr(L.mc);
+            st = zpucuda_tensor_copy(&a, &c, s);
         } else {
             RegionIO io;
             memset(&io, 0, sizeof io);
-            for (size_t k = 0; k < L.ins.size(); k++) io.in[k] = ptr(L.ins[k]);
+            for (size_t k = 0; k < L.ins.size(); k++) io.in[k] = (char *)ptr(L.ins[k]) + L.in_off[k];
             for (size_t o = 0; o < L.outs.size(); o++) io.out[o] = ptr(L.outs[o]);
             if (L.has_red) io.red_out = ptr(L.red);
             if (L.workspace) {
