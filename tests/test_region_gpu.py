@@ -748,3 +748,28 @@ def test_argument_output_is_copied(zc):
     p = zc.Plan([(1, zc.F32, (7, 9))], [], [("neg", [1], 10, -2, 0)], [1, 10, 1])
     a, n, b = p.run([x])
     assert torch.equal(a, x) and torch.equal(b, x) and torch.equal(n, -x)
+
+
+def test_flip_copy_and_cast_steps(zc):
+    """flip / reverse (negative-stride views, ops.zig:2019-2030, 2198), copy
+    (the input itself) and cast_op (a converting copy, ops.zig:2062-2071 --
+    Attrs.axis is the type): an i64 argument cast to f32 feeds a region, and
+    a flipped view feeds a region, a GEMM (copied: negative strides) and an
+    output."""
+    x = zo.uniform_range(51, 12 * 7, -3.0, 3.0).reshape(12, 7)
+    lab = np.arange(12, dtype=np.int64) * 3 - 5
+    w = zo.uniform_range(52, 7 * 5, -1.0, 1.0).reshape(7, 5)
+    F = zc.F32
+    steps = [("flip", [1], 10, 0, 0), ("abs", [10], 11, -2, 0), ("reverse", [10], 12, -1, 0),
+             ("copy", [12], 13, -2, 0), ("cast_op", [2], 14, zc.F32, 0), ("mul", [14, 14], 15, -2, 0),
+             ("matmul", [10, 3], 16, -2, 0), ("cast_op", [1], 17, zc.F32, 0), ("cast_op", [1], 18, zc.DT_BOOL, 0)]
+    p = zc.Plan([(1, F, (12, 7)), (2, zc.DT_I64, (12,)), (3, F, (7, 5))], [], steps, [10, 11, 13, 15, 16, 17, 18])
+    outs = [o.cpu().numpy() for o in p.run([torch.from_numpy(a).cuda() for a in (x, lab, w)])]
+    xf = x[::-1]
+    assert np.array_equal(outs[0], xf) and np.array_equal(outs[1], np.abs(xf))
+    assert np.array_equal(outs[2], xf[:, ::-1])
+    lf = lab.astype(np.float32)
+    assert np.array_equal(outs[3], lf * lf)
+    want = xf.astype(np.float64) @ w.astype(np.float64)
+    assert np.linalg.norm(outs[4] - want) <= 1e-5 * np.linalg.norm(want)
+    assert np.array_equal(outs[5], x) and outs[6].dtype == np.bool_ and np.array_equal(outs[6], x != 0)

@@ -42,12 +42,10 @@ def dtype_code(t):
 
 
 def torch_dtype(code):
+    """torch dtype of a zpu DType code (src/zpu/dtype.zig:4-13)."""
     torch = _torch()
-    if code == DT_I64:
-        return torch.int64
-    if code == DT_BOOL:
-        return torch.bool
-    return torch.float32 if code == F32 else torch.float64
+    return [torch.float64, torch.float32, torch.float16, torch.int64, torch.int32, torch.int16, torch.int8,
+            torch.uint8, torch.bool][code]
 
 
 def rng_normal(seed, n, dtype=None, device="cuda", out=None, stream=None):

@@ -36,8 +36,8 @@ PRIM = {
     "gt": 49, "ge": 50, "logical_and": 51, "logical_or": 52, "logical_xor": 53, "logical_not": 54,
     "where": 55, "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "any_reduce": 62,
     "all_reduce": 63, "argmax": 64, "argmin": 65, "reshape": 66, "transpose": 67, "broadcast": 68, "expand_dims": 69,
-    "squeeze": 70, "cumsum": 78, "matmul": 80,
-    "constant": 87, "copy": 88,
+    "squeeze": 70, "flip": 77, "cumsum": 78, "reverse": 79, "matmul": 80,
+    "constant": 87, "copy": 88, "cast_op": 89,
 }
 
 

@@ -40,7 +40,12 @@ enum {
     PRIM_BROADCAST = 68,
     PRIM_EXPAND_DIMS = 69,
     PRIM_SQUEEZE = 70,
+    PRIM_FLIP = 77,
     PRIM_CUMSUM = 78,
+    PRIM_REVERSE = 79,
+    PRIM_CONSTANT = 87,
+    PRIM_COPY = 88,
+    PRIM_CAST = 89,
     PRIM_MATMUL = 80,
 };
 constexpr int32_t kFlagReverse = 1 << 5;  // prims.Attrs.REVERSE
@@ -68,7 +73,13 @@ bool bool_reduce(int p) { return p == PRIM_ANY || p == PRIM_ALL; }
 bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p) || bool_reduce(p); }
 bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
 // The movement prims a plan lowers as views (ops.zig:1343-1555).
-bool view_prim(int p) { return p >= PRIM_RESHAPE && p <= PRIM_SQUEEZE; }
+// flip / reverse mirror one axis (negative stride); copy and constant replay
+// as their input (ops.zig:2195-2198).
+bool view_prim(int p) {
+    return (p >= PRIM_RESHAPE && p <= PRIM_SQUEEZE) || p == PRIM_FLIP || p == PRIM_REVERSE || p == PRIM_COPY ||
+           p == PRIM_CONSTANT;
+}
+bool any_dtype(int dt) { return dt >= ZPUCUDA_F64 && dt <= ZPUCUDA_BOOL; }
 // Bool values ride in a region's float registers: two values fit one region
 // unless both are floats of different types.  -1: no float type required.
 int carrier_of(int dt) { return float_dtype(dt) ? dt : -1; }
@@ -149,6 +160,7 @@ struct Launch {
     std::vector<int64_t> in_off;  // region inputs: byte offsets into their slots
     int64_t ma_off = 0, mb_off = 0;  // matmul / cumsum / copy source: byte offsets
     zpucuda_tensor src;              // copy: the view (data set at run time)
+    int32_t dst_dtype = 0;           // copy: the output's element type (a cast converts)
     RegionProgram prog;
     const CatalogueEntry *cat = nullptr;
     std::string signature;
@@ -190,7 +202,15 @@ struct zpucuda_plan {
 
 namespace {
 
-size_t itemsize(int dt) { return dt == ZPUCUDA_F32 ? 4 : dt == ZPUCUDA_BOOL ? 1 : 8; }
+// zpu's DType sizes (src/zpu/dtype.zig:4-13)
+size_t itemsize(int dt) {
+    switch (dt) {
+    case ZPUCUDA_F64: case ZPUCUDA_I64: return 8;
+    case ZPUCUDA_F32: case ZPUCUDA_I32: return 4;
+    case ZPUCUDA_F16: case ZPUCUDA_I16: return 2;
+    default: return 1;
+    }
+}
 
 int lower_fail(zpucuda_plan *p, int st, const std::string &why) {
     delete p;
@@ -245,7 +265,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
     };
     for (int i = 0; i < n_args; i++) {
         if (args[i].rank < 0 || args[i].rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "arg rank");
-        if (!float_dtype(args[i].dtype) && args[i].dtype != ZPUCUDA_BOOL) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "arg dtype");
+        if (!any_dtype(args[i].dtype)) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "arg dtype");
         Value &v = add_value(args[i]);
         v.is_arg = true;
         v.arg_index = i;
@@ -400,6 +420,18 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                     o.shape.dims[i] = a.shape.dims[perm[i]];
                     o.strides[i] = a.strides[perm[i]];
                 }
+            } else if (st.prim == PRIM_COPY || st.prim == PRIM_CONSTANT) {
+                o.shape = a.shape;
+                for (int i = 0; i < r; i++) o.strides[i] = a.strides[i];
+            } else if (st.prim == PRIM_FLIP || st.prim == PRIM_REVERSE) {
+                // ops.flip (ops.zig:2019-2030): realAxis, stride negated, the
+                // offset moved to the axis's last element
+                const int ax = st.axis >= 0 ? st.axis + a.depth : st.axis + r;
+                if (ax < 0 || ax >= r) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "flip axis");
+                o.shape = a.shape;
+                for (int i = 0; i < r; i++) o.strides[i] = a.strides[i];
+                o.strides[ax] = -a.strides[ax];
+                o.offset = a.offset + (a.shape.dims[ax] > 0 ? a.shape.dims[ax] - 1 : 0) * a.strides[ax];
             } else if (st.prim == PRIM_BROADCAST) {
                 // ops.broadcastTo / broadcastTarget (ops.zig:1480-1522)
                 Shape t;
@@ -451,6 +483,17 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                         i++;
                     }
                 }
+            }
+        } else if (st.prim == PRIM_CAST && st.n_inputs == 1) {
+            // ops.cast (ops.zig:2062-2071; the type is Attrs.axis): the input
+            // itself for its own type, else a converting copy
+            if (!any_dtype(st.axis)) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "cast target dtype");
+            o.shape = a.shape;
+            o.dtype = st.axis;
+            if (st.axis == a.dtype) {
+                o.view = true;
+                o.offset = a.offset;
+                for (int i = 0; i < a.shape.rank; i++) o.strides[i] = a.strides[i];
             }
         } else if (st.prim == PRIM_CUMSUM && st.n_inputs == 1) {
             // ops.realAxis (src/zpu/ops.zig:1466-1471): vmap-aware, no AXIS_NONE
@@ -524,7 +567,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
 
     // A copy launch of the view `v` (zpucuda_tensor_copy's kernels) into a
     // contiguous buffer: `dst`, or a new temp when dst.index < 0.
-    auto copy_launch = [&](const Value &v, Slot dst, const std::string &why) -> Slot {
+    auto copy_launch = [&](const Value &v, Slot dst, const std::string &why, int dst_dtype = -1) -> Slot {
         if (dst.index < 0) {
             void *d = nullptr;
             const size_t nb = (size_t)v.shape.numel() * itemsize(v.dtype);
@@ -547,6 +590,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             L.src.strides[d] = v.strides[d];
         }
         L.mc = dst;
+        L.dst_dtype = dst_dtype < 0 ? v.dtype : dst_dtype;
         L.text = "  kernel " + std::to_string(plan->launches.size()) + ": copy (" + why + ")\n";
         plan->launches.push_back(L);
         return dst;
@@ -567,6 +611,21 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
     int s = 0;
     while (s < n_steps) {
         const zpucuda_step &st0 = steps[s];
+        if (st0.prim == PRIM_CAST) {
+            Value &a = vals[st0.ins[0]];
+            Value &o = vals[st0.out];
+            if (!a.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "cast of a value not materialised");
+            if (o.view) {  // cast to its own type: the input itself
+                o.slot = a.slot;
+            } else {
+                const Slot dst = materialise(st0.out);
+                if (dst.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+                if (copy_launch(a, dst, "cast", o.dtype).index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy");
+            }
+            o.materialised = true;
+            s++;
+            continue;
+        }
         if (view_prim(st0.prim)) {  // a view: the input's slot, no launch
             Value &a = vals[st0.ins[0]];
             Value &o = vals[st0.out];
@@ -930,6 +989,7 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
             zpucuda_tensor a = L.src, c = L.src;
             a.data = (char *)ptr(L.ma) + L.ma_off;
             c.data = ptr(L.mc);
+            c.dtype = L.dst_dtype;
             st = zpucuda_tensor_copy(&a, &c, s);
         } else {
             RegionIO io;
@@ -952,7 +1012,7 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
 static size_t value_bytes(const zpucuda_value &v) {
     size_t n = 1;
     for (int d = 0; d < v.rank; d++) n *= (size_t)v.dims[d];
-    return n * (v.dtype == ZPUCUDA_F32 ? 4 : v.dtype == ZPUCUDA_BOOL ? 1 : 8);
+    return n * itemsize(v.dtype);
 }
 
 int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs, void *stream) {
