@@ -195,6 +195,11 @@ typedef struct zpucuda_step {
     int32_t shape_len;
     int32_t nsl;
     uint8_t perm[ZPUCUDA_MAX_RANK];
+    /* slice: Attrs.starts / Attrs.lens (in `shape`) / Attrs.steps [0 .. nsl),
+     * the ranges sliceAttrs records (resolved: element j of axis i is
+     * starts[i] + j * steps[i], j < lens[i]) */
+    int64_t starts[ZPUCUDA_MAX_RANK];
+    int64_t steps[ZPUCUDA_MAX_RANK];
 } zpucuda_step;
 
 /* jit.Blob (src/zpu/jit.zig:39-42): a constant folded at build time; its
@@ -217,8 +222,8 @@ typedef struct zpucuda_plan zpucuda_plan;
  * payload axes [d, rank) and a non-negative axis counts from axis d.  Matmul
  * steps become GEMM launches; cumsum steps (ops.cumsum, src/zpu/ops.zig:
  * 2032-2060: f64 running sum along one axis, rounded per element) a scan
- * launch each.  reshape / transpose / broadcast / expand_dims / squeeze
- * (ops.zig:1343-1555) are views -- new strides over the same HBM, no launch
+ * launch each.  reshape / transpose / broadcast / expand_dims / squeeze /
+ * slice / flip (ops.zig:1343-1635, 2019-2030) are views -- new strides over the same HBM, no launch
  * -- that region loads and GEMM operands read in place; a view is copied
  * (zpucuda_tensor_copy's kernels) only where a contiguous buffer is needed:
  * a plan output, a cumsum input, a reshape of a non-contiguous view, a GEMM

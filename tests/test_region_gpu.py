@@ -773,3 +773,27 @@ def test_flip_copy_and_cast_steps(zc):
     want = xf.astype(np.float64) @ w.astype(np.float64)
     assert np.linalg.norm(outs[4] - want) <= 1e-5 * np.linalg.norm(want)
     assert np.array_equal(outs[5], x) and outs[6].dtype == np.bool_ and np.array_equal(outs[6], x != 0)
+
+
+def test_slice_views(zc):
+    """slice from its recorded ranges (ops.zig:1587-1635): element j of axis
+    i at starts[i] + j * steps[i]; positive and negative steps, feeding a
+    region and copied out; payload ranges under vmap."""
+    x = zo.uniform_range(61, 10 * 12, -2.0, 2.0).reshape(10, 12)
+    F = zc.F32
+    steps = [("slice", [1], 10, -2, 0, {"starts": [2, 1], "shape": [4, 5], "steps": [2, 2]}),
+             ("slice", [1], 11, -2, 0, {"starts": [9, 11], "shape": [3, 4], "steps": [-3, -2]}),
+             ("neg", [10], 12, -2, 0), ("abs", [11], 13, -2, 0)]
+    p = zc.Plan([(1, F, (10, 12))], [], steps, [10, 11, 12, 13])
+    a, b, c, d = [o.cpu().numpy() for o in p.run([torch.from_numpy(x).cuda()])]
+    sa, sb = x[2:10:2, 1:11:2], x[9:0:-3, 11:3:-2]
+    assert np.array_equal(a, sa) and np.array_equal(b, sb)
+    assert np.array_equal(c, -sa) and np.array_equal(d, np.abs(sb))
+    y = zo.uniform_range(62, 3 * 6 * 4, -1.0, 1.0).reshape(3, 6, 4)
+    q = zc.Plan([(1, F, (3, 6, 4), 1)], [],
+                [("slice", [1], 10, -2, 0, {"starts": [1, 3], "shape": [2, 1], "steps": [3, 1]})], [10])
+    (r,) = q.run([torch.from_numpy(y).cuda()])
+    assert np.array_equal(r.cpu().numpy(), y[:, 1:6:3, 3:4])
+    with pytest.raises(zc.ZpuCudaError) as err:
+        zc.Plan([(1, F, (10, 12))], [], [("slice", [1], 10, -2, 0, {"starts": [8, 0], "shape": [2, 1], "steps": [2, 1]})], [10])
+    assert err.value.status == 8  # IndexOutOfRange: 8 + 2 is past the axis

@@ -199,6 +199,11 @@ class Plan:
             st[i].nsl = len(perm)
             for k, d in enumerate(perm):
                 st[i].perm[k] = d
+            if "starts" in extra:  # slice: starts, lens (as "shape"), steps
+                st[i].nsl = len(extra["starts"])
+                for k in range(len(extra["starts"])):
+                    st[i].starts[k] = extra["starts"][k]
+                    st[i].steps[k] = extra["steps"][k]
         oi = (C.c_uint64 * len(out_ids))(*out_ids)
         h = C.c_void_p()
         check(L.zpucuda_plan_create(va, len(args), bl, len(blobs), st, len(steps), oi, len(out_ids),

@@ -36,7 +36,7 @@ PRIM = {
     "gt": 49, "ge": 50, "logical_and": 51, "logical_or": 52, "logical_xor": 53, "logical_not": 54,
     "where": 55, "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "any_reduce": 62,
     "all_reduce": 63, "argmax": 64, "argmin": 65, "reshape": 66, "transpose": 67, "broadcast": 68, "expand_dims": 69,
-    "squeeze": 70, "flip": 77, "cumsum": 78, "reverse": 79, "matmul": 80,
+    "squeeze": 70, "slice": 71, "flip": 77, "cumsum": 78, "reverse": 79, "matmul": 80,
     "constant": 87, "copy": 88, "cast_op": 89,
 }
 
@@ -63,7 +63,8 @@ class Step(C.Structure):
     _fields_ = [("prim", C.c_int32), ("n_inputs", C.c_int32), ("ins", C.c_uint64 * 3),
                 ("out", C.c_uint64), ("axis", C.c_int32), ("flags", C.c_int32),
                 ("shape", C.c_int64 * MAX_RANK), ("shape_len", C.c_int32), ("nsl", C.c_int32),
-                ("perm", C.c_uint8 * MAX_RANK)]
+                ("perm", C.c_uint8 * MAX_RANK), ("starts", C.c_int64 * MAX_RANK),
+                ("steps", C.c_int64 * MAX_RANK)]
 
 
 class Blob(C.Structure):

@@ -40,6 +40,7 @@ enum {
     PRIM_BROADCAST = 68,
     PRIM_EXPAND_DIMS = 69,
     PRIM_SQUEEZE = 70,
+    PRIM_SLICE = 71,
     PRIM_FLIP = 77,
     PRIM_CUMSUM = 78,
     PRIM_REVERSE = 79,
@@ -76,7 +77,7 @@ bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
 // flip / reverse mirror one axis (negative stride); copy and constant replay
 // as their input (ops.zig:2195-2198).
 bool view_prim(int p) {
-    return (p >= PRIM_RESHAPE && p <= PRIM_SQUEEZE) || p == PRIM_FLIP || p == PRIM_REVERSE || p == PRIM_COPY ||
+    return (p >= PRIM_RESHAPE && p <= PRIM_SLICE) || p == PRIM_FLIP || p == PRIM_REVERSE || p == PRIM_COPY ||
            p == PRIM_CONSTANT;
 }
 bool any_dtype(int dt) { return dt >= ZPUCUDA_F64 && dt <= ZPUCUDA_BOOL; }
@@ -419,6 +420,38 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 for (int i = 0; i < r; i++) {
                     o.shape.dims[i] = a.shape.dims[perm[i]];
                     o.strides[i] = a.strides[perm[i]];
+                }
+            } else if (st.prim == PRIM_SLICE) {
+                // ops.sliceView with the ranges sliceAttrs records
+                // (ops.zig:1587-1635): element j of axis i at starts[i] +
+                // j * steps[i], j < lens[i]; payload ranges under vmap leave
+                // the batch axes whole.  (zpu's replay rebuilds Range(start,
+                // start + len, step), which agrees for step 1.)
+                int64_t st0[ZPUCUDA_MAX_RANK], ln[ZPUCUDA_MAX_RANK], sp[ZPUCUDA_MAX_RANK];
+                if (st.nsl == r) {
+                    for (int i = 0; i < r; i++) { st0[i] = st.starts[i]; ln[i] = st.shape[i]; sp[i] = st.steps[i]; }
+                } else if (st.nsl + a.depth == r) {
+                    for (int i = 0; i < a.depth; i++) { st0[i] = 0; ln[i] = a.shape.dims[i]; sp[i] = 1; }
+                    for (int i = 0; i < st.nsl; i++) {
+                        st0[a.depth + i] = st.starts[i];
+                        ln[a.depth + i] = st.shape[i];
+                        sp[a.depth + i] = st.steps[i];
+                    }
+                } else {
+                    return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "slice ranges");
+                }
+                o.shape.rank = r;
+                for (int i = 0; i < r; i++) {
+                    const int64_t d = a.shape.dims[i];
+                    if (sp[i] == 0 || ln[i] < 0) return lower_fail(plan, ZPUCUDA_ERR_INVALID_SHAPE, "slice range");
+                    if (ln[i] > 0) {
+                        const int64_t last = st0[i] + (ln[i] - 1) * sp[i];
+                        if (st0[i] < 0 || st0[i] >= d || last < 0 || last >= d)
+                            return lower_fail(plan, ZPUCUDA_ERR_INDEX_OUT_OF_RANGE, "slice range");
+                        o.offset += st0[i] * a.strides[i];
+                    }
+                    o.shape.dims[i] = ln[i];
+                    o.strides[i] = a.strides[i] * sp[i];
                 }
             } else if (st.prim == PRIM_COPY || st.prim == PRIM_CONSTANT) {
                 o.shape = a.shape;
