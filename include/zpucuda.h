@@ -200,6 +200,10 @@ typedef struct zpucuda_step {
      * starts[i] + j * steps[i], j < lens[i]) */
     int64_t starts[ZPUCUDA_MAX_RANK];
     int64_t steps[ZPUCUDA_MAX_RANK];
+    /* pad: Attrs.pads_lo (in `starts`) / Attrs.pads_hi [0 .. nsl) and the
+     * fill value Attrs.scalar */
+    int64_t pads_hi[ZPUCUDA_MAX_RANK];
+    double scalar;
 } zpucuda_step;
 
 /* jit.Blob (src/zpu/jit.zig:39-42): a constant folded at build time; its
@@ -222,8 +226,10 @@ typedef struct zpucuda_plan zpucuda_plan;
  * payload axes [d, rank) and a non-negative axis counts from axis d.  Matmul
  * steps become GEMM launches; cumsum steps (ops.cumsum, src/zpu/ops.zig:
  * 2032-2060: f64 running sum along one axis, rounded per element) a scan
- * launch each.  reshape / transpose / broadcast / expand_dims / squeeze /
- * slice / flip (ops.zig:1343-1635, 2019-2030) are views -- new strides over the same HBM, no launch
+ * launch each; concat / stack / pad / take / scatter_add (ops.zig:1665-1797,
+ * 1995-2017) copy, fill, gather and scatter launches.  reshape / transpose /
+ * broadcast / expand_dims / squeeze / slice / flip (ops.zig:1343-1635,
+ * 2019-2030) are views -- new strides over the same HBM, no launch
  * -- that region loads and GEMM operands read in place; a view is copied
  * (zpucuda_tensor_copy's kernels) only where a contiguous buffer is needed:
  * a plan output, a cumsum input, a reshape of a non-contiguous view, a GEMM
@@ -248,6 +254,11 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
 int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs,
                           void *stream);
 int zpucuda_plan_output(const zpucuda_plan *plan, int i, zpucuda_value *value);
+/* Index errors of the plan's take / scatter_add launches (zpu's
+ * IndexOutOfRange, ops.zig:1735-1741) since the last check: waits for the
+ * stream (bounded) and returns ZPUCUDA_ERR_INDEX_OUT_OF_RANGE once for them,
+ * else ZPUCUDA_OK.  zpucuda_plan_run_host checks by itself. */
+int zpucuda_plan_check(zpucuda_plan *plan, void *stream);
 int zpucuda_plan_num_steps(const zpucuda_plan *plan);   /* jit.Plan.numSteps */
 int zpucuda_plan_num_kernels(const zpucuda_plan *plan); /* launches per run */
 /* Plan.describe (src/zpu/jit.zig:71-83) plus the lowering: one line per

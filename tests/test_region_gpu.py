@@ -797,3 +797,58 @@ def test_slice_views(zc):
     with pytest.raises(zc.ZpuCudaError) as err:
         zc.Plan([(1, F, (10, 12))], [], [("slice", [1], 10, -2, 0, {"starts": [8, 0], "shape": [2, 1], "steps": [2, 1]})], [10])
     assert err.value.status == 8  # IndexOutOfRange: 8 + 2 is past the axis
+
+
+def test_concat_stack_and_pad(zc):
+    """ops.concat / stack / pad (ops.zig:1665-1695, 1995-2017): copies into
+    parts of a new buffer, reading strided views as they are."""
+    rng = np.random.default_rng(71)
+    a = rng.standard_normal((4, 5)).astype(np.float32)
+    b = rng.standard_normal((3, 5)).astype(np.float32)
+    c = rng.standard_normal((5, 4)).astype(np.float32)
+    F = zc.F32
+    steps = [("concat_op", [1, 2], 10, 0, 0),
+             ("transpose", [3], 11, -2, 0, {"perm": [1, 0]}),          # [4, 5], strided
+             ("concat_op", [1, 11], 12, 1, 0),                           # [4, 10]
+             ("stack_op", [1, 11], 13, 1, 0),                            # [4, 2, 5]
+             ("stack_op", [1, 11], 14, -1, 0),                           # [4, 5, 2]
+             ("pad", [1], 15, -2, 0, {"pads": [(1, 2), (0, 3)], "scalar": -7.0}),
+             ("neg", [12], 16, -2, 0)]
+    p = zc.Plan([(1, F, (4, 5)), (2, F, (3, 5)), (3, F, (5, 4))], [], steps, [10, 12, 13, 14, 15, 16])
+    got = [o.cpu().numpy() for o in p.run([torch.from_numpy(v).cuda() for v in (a, b, c)])]
+    ct = c.T
+    want = [np.concatenate([a, b], 0), np.concatenate([a, ct], 1), np.stack([a, ct], 1), np.stack([a, ct], -1),
+            np.pad(a, ((1, 2), (0, 3)), constant_values=-7.0), -np.concatenate([a, ct], 1)]
+    for g, w in zip(got, want):
+        assert g.shape == w.shape and np.array_equal(g, w)
+
+
+def test_take_and_scatter_add(zc):
+    """ops.take / scatterAdd (ops.zig:1697-1797): indices of any numeric type
+    truncated toward zero, negatives counted from the end once; scatter_add
+    starts from zeros and adds repeated indices in order, each sum in f64
+    rounded to f32; a bad index is IndexOutOfRange through plan.check()."""
+    rng = np.random.default_rng(72)
+    x = rng.standard_normal((6, 8)).astype(np.float32)
+    idx = np.array([[0, -1], [5, 2], [3, 3]], dtype=np.int64)
+    fidx = np.array([2.7, -1.2], dtype=np.float32)
+    sidx = np.array([0, 2, 0, 5, 2], dtype=np.int32)  # plan arg dtype 4 = DType.i32
+    upd = rng.standard_normal((5, 8)).astype(np.float32)
+    F = zc.F32
+    p = zc.Plan([(1, F, (6, 8)), (2, zc.DT_I64, (3, 2)), (3, F, (2,)), (4, 4, (5,)), (5, F, (5, 8))], [],
+                [("take", [1, 2], 10, 0, 0), ("take", [1, 3], 11, 1, 0), ("scatter_add", [1, 4, 5], 12, 0, 0)],
+                [10, 11, 12])
+    t0, t1, sc = [o.cpu().numpy() for o in p.run([torch.from_numpy(v).cuda() for v in (x, idx, fidx, sidx, upd)])]
+    assert np.array_equal(t0, x[np.where(idx < 0, idx + 6, idx)])
+    assert np.array_equal(t1, x[:, [2, 7]])
+    want = np.zeros((6, 8), np.float32)
+    for t, j in enumerate(sidx):
+        want[j] = (want[j].astype(np.float64) + upd[t].astype(np.float64)).astype(np.float32)
+    assert np.array_equal(sc, want)
+    p.check()  # no bad index so far
+    bad = zc.Plan([(1, F, (6, 8)), (2, zc.DT_I64, (2,))], [], [("take", [1, 2], 10, 0, 0)], [10])
+    bad.run([torch.from_numpy(x).cuda(), torch.tensor([1, 6], device="cuda")])
+    with pytest.raises(zc.ZpuCudaError) as err:
+        bad.check()
+    assert err.value.status == 8  # IndexOutOfRange
+    bad.check()  # reported once

@@ -204,6 +204,12 @@ class Plan:
                 for k in range(len(extra["starts"])):
                     st[i].starts[k] = extra["starts"][k]
                     st[i].steps[k] = extra["steps"][k]
+            if "pads" in extra:  # pad: [(lo, hi)] per axis and the fill value
+                st[i].nsl = len(extra["pads"])
+                for k, (lo, hi) in enumerate(extra["pads"]):
+                    st[i].starts[k] = lo
+                    st[i].pads_hi[k] = hi
+                st[i].scalar = float(extra.get("scalar", 0.0))
         oi = (C.c_uint64 * len(out_ids))(*out_ids)
         h = C.c_void_p()
         check(L.zpucuda_plan_create(va, len(args), bl, len(blobs), st, len(steps), oi, len(out_ids),
@@ -218,6 +224,11 @@ class Plan:
 
     def num_steps(self):
         return lib().zpucuda_plan_num_steps(self.handle)
+
+    def check(self, stream=None):
+        """zpucuda_plan_check: raises IndexOutOfRange for a bad take /
+        scatter_add index since the last check."""
+        check(lib().zpucuda_plan_check(self.handle, stream_of(stream)))
 
     def num_kernels(self):
         return lib().zpucuda_plan_num_kernels(self.handle)

@@ -36,7 +36,8 @@ PRIM = {
     "gt": 49, "ge": 50, "logical_and": 51, "logical_or": 52, "logical_xor": 53, "logical_not": 54,
     "where": 55, "sum": 58, "prod_op": 59, "max_reduce": 60, "min_reduce": 61, "any_reduce": 62,
     "all_reduce": 63, "argmax": 64, "argmin": 65, "reshape": 66, "transpose": 67, "broadcast": 68, "expand_dims": 69,
-    "squeeze": 70, "slice": 71, "flip": 77, "cumsum": 78, "reverse": 79, "matmul": 80,
+    "squeeze": 70, "slice": 71, "concat_op": 72, "stack_op": 73, "take": 74, "scatter_add": 75,
+    "pad": 76, "flip": 77, "cumsum": 78, "reverse": 79, "matmul": 80,
     "constant": 87, "copy": 88, "cast_op": 89,
 }
 
@@ -64,7 +65,7 @@ class Step(C.Structure):
                 ("out", C.c_uint64), ("axis", C.c_int32), ("flags", C.c_int32),
                 ("shape", C.c_int64 * MAX_RANK), ("shape_len", C.c_int32), ("nsl", C.c_int32),
                 ("perm", C.c_uint8 * MAX_RANK), ("starts", C.c_int64 * MAX_RANK),
-                ("steps", C.c_int64 * MAX_RANK)]
+                ("steps", C.c_int64 * MAX_RANK), ("pads_hi", C.c_int64 * MAX_RANK), ("scalar", C.c_double)]
 
 
 class Blob(C.Structure):
@@ -114,6 +115,7 @@ SIGNATURES = {
     "zpucuda_rng_randint": (I32, [U64, P, I64, I64, I64, P]),
     "zpucuda_chain_tanh_sq_affine_sum_noalloc": (I32, [P, I64, P, P, P, P]),
     "zpucuda_tensor_copy": (I32, [P, P, P]),
+    "zpucuda_plan_check": (I32, [P, P]),
     "zpucuda_nccl_unique_id": (I32, [P]),
     "zpucuda_nccl_init": (I32, [I32, I32, P, I64]),
     "zpucuda_nccl_allreduce_f32": (I32, [P, I64, P]),

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "region.cuh"
+#include "tensor_ops.cuh"
 
 namespace zc {
 int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, cudaStream_t s);
@@ -41,6 +42,11 @@ enum {
     PRIM_EXPAND_DIMS = 69,
     PRIM_SQUEEZE = 70,
     PRIM_SLICE = 71,
+    PRIM_CONCAT = 72,
+    PRIM_STACK = 73,
+    PRIM_TAKE = 74,
+    PRIM_SCATTER_ADD = 75,
+    PRIM_PAD = 76,
     PRIM_FLIP = 77,
     PRIM_CUMSUM = 78,
     PRIM_REVERSE = 79,
@@ -157,7 +163,15 @@ struct Value {
 };
 
 struct Launch {
-    enum { REGION, MATMUL, CUMSUM, COPY } kind = REGION;
+    enum { REGION, MATMUL, CUMSUM, COPY, COPYV, FILL, TAKE, SCATTER } kind = REGION;
+    // COPYV: src view (ma + ma_off) into the dst view (mc + mc_off, dst's
+    // strides); FILL: mc with `scalar`; TAKE / SCATTER: ma = x or updates,
+    // mb = indices, mc = out, [outer, sdim, inner] and k
+    zpucuda_tensor dst;
+    int64_t mc_off = 0;
+    double scalar = 0.0;
+    int32_t idx_dtype = 0;
+    int64_t k = 0;
     std::vector<int64_t> in_off;  // region inputs: byte offsets into their slots
     int64_t ma_off = 0, mb_off = 0;  // matmul / cumsum / copy source: byte offsets
     zpucuda_tensor src;              // copy: the view (data set at run time)
@@ -191,8 +205,10 @@ struct zpucuda_plan {
     std::vector<void *> blobs;  // HBM copies of folded constants
     std::vector<void *> temps;  // intermediates that cross launches
     std::vector<void *> workspaces;
+    unsigned int *err = nullptr;  // index errors of take / scatter_add launches
     std::string text;
     ~zpucuda_plan() {
+        if (err) cudaFree(err);
         for (void *p : blobs) cudaFree(p);
         for (void *p : temps) cudaFree(p);
         for (void *p : workspaces) cudaFree(p);
@@ -517,6 +533,66 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                     }
                 }
             }
+        } else if ((st.prim == PRIM_CONCAT || st.prim == PRIM_STACK) && st.n_inputs == 2) {
+            // ops.concat (ops.zig:1665-1687; realAxis, equal ranks, the other
+            // axes equal) and ops.stack (expand_dims of both, then concat)
+            const Value &b = vals[st.ins[1]];
+            if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "concat of different dtypes");
+            Shape sa = a.shape, sb = b.shape;
+            if (st.prim == PRIM_STACK) {
+                for (Shape *sh : {&sa, &sb}) {
+                    const int payload = sh->rank - (sh == &sa ? a.depth : b.depth);
+                    int ax = st.axis < 0 ? st.axis + payload + 1 : st.axis;
+                    if (ax < 0 || ax > payload || sh->rank >= ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "stack axis");
+                    const int pos = (sh == &sa ? a.depth : b.depth) + ax;
+                    for (int d = sh->rank; d > pos; d--) sh->dims[d] = sh->dims[d - 1];
+                    sh->dims[pos] = 1;
+                    sh->rank += 1;
+                }
+            }
+            if (sa.rank != sb.rank) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "concat ranks");
+            const int ax = st.axis >= 0 ? st.axis + a.depth : st.axis + sa.rank;
+            if (ax < 0 || ax >= sa.rank) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "concat axis");
+            for (int d = 0; d < sa.rank; d++)
+                if (d != ax && sa.dims[d] != sb.dims[d]) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "concat shapes");
+            o.shape = sa;
+            o.shape.dims[ax] = sa.dims[ax] + sb.dims[ax];
+            o.depth = std::max(a.depth, b.depth);
+        } else if (st.prim == PRIM_PAD && st.n_inputs == 1) {
+            // ops.pad (ops.zig:1995-2017): one (lo, hi) per axis
+            if (st.nsl != a.shape.rank) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "pad widths");
+            o.shape = a.shape;
+            for (int d = 0; d < a.shape.rank; d++) {
+                if (st.starts[d] < 0 || st.pads_hi[d] < 0) return lower_fail(plan, ZPUCUDA_ERR_INVALID_SHAPE, "pad widths");
+                o.shape.dims[d] += st.starts[d] + st.pads_hi[d];
+            }
+        } else if ((st.prim == PRIM_TAKE && st.n_inputs == 2) || (st.prim == PRIM_SCATTER_ADD && st.n_inputs == 3)) {
+            // ops.take / scatterAdd (ops.zig:1697-1797): a plain axis of x
+            const Value &ix = vals[st.ins[1]];
+            if (a.depth > 0 && ix.depth > 0) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "take under two vmaps");
+            const int r = a.shape.rank;
+            const int ax = st.axis < 0 ? st.axis + r : st.axis;
+            if (ax < 0 || ax >= r) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "take axis");
+            if (ix.dtype != ZPUCUDA_I64 && ix.dtype != ZPUCUDA_I32 && !float_dtype(ix.dtype))
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "index dtype");
+            if (st.prim == PRIM_TAKE) {
+                if (r - 1 + ix.shape.rank > ZPUCUDA_MAX_RANK) return lower_fail(plan, ZPUCUDA_ERR_RANK_TOO_LARGE, "take rank");
+                o.shape.rank = 0;
+                for (int d = 0; d < ax; d++) o.shape.dims[o.shape.rank++] = a.shape.dims[d];
+                for (int d = 0; d < ix.shape.rank; d++) o.shape.dims[o.shape.rank++] = ix.shape.dims[d];
+                for (int d = ax + 1; d < r; d++) o.shape.dims[o.shape.rank++] = a.shape.dims[d];
+                o.depth = std::max(a.depth, ix.depth);
+            } else {
+                const Value &u = vals[st.ins[2]];
+                int64_t outer = 1, inner = 1;
+                for (int d = 0; d < ax; d++) outer *= a.shape.dims[d];
+                for (int d = ax + 1; d < r; d++) inner *= a.shape.dims[d];
+                if (u.dtype != a.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "scatter_add updates dtype");
+                if (u.shape.numel() != outer * ix.shape.numel() * inner)
+                    return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "scatter_add updates");
+                if (a.dtype == ZPUCUDA_BOOL) return lower_fail(plan, ZPUCUDA_ERR_DTYPE_MISMATCH, "scatter_add on bool");
+                o.shape = a.shape;
+            }
         } else if (st.prim == PRIM_CAST && st.n_inputs == 1) {
             // ops.cast (ops.zig:2062-2071; the type is Attrs.axis): the input
             // itself for its own type, else a converting copy
@@ -644,6 +720,124 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
     int s = 0;
     while (s < n_steps) {
         const zpucuda_step &st0 = steps[s];
+        // descriptor of a value's view (data set at run time)
+        auto desc_of = [](const Value &v) {
+            zpucuda_tensor t;
+            memset(&t, 0, sizeof t);
+            t.dtype = v.dtype;
+            t.rank = v.shape.rank;
+            for (int d = 0; d < v.shape.rank; d++) {
+                t.dims[d] = v.shape.dims[d];
+                t.strides[d] = v.strides[d];
+            }
+            return t;
+        };
+        auto need_err = [&]() -> bool {
+            if (plan->err) return true;
+            if (cudaMalloc(&plan->err, sizeof(unsigned int)) != cudaSuccess ||
+                cudaMemset(plan->err, 0, sizeof(unsigned int)) != cudaSuccess) {
+                cudaGetLastError();
+                plan->err = nullptr;
+                return false;
+            }
+            return true;
+        };
+        // a COPYV launch of `src` into the part of out slot `dst` at element
+        // offset `off` with out's contiguous strides `ost`
+        auto copy_into = [&](const Value &src, const zpucuda_tensor &sdesc, Slot dst, const int64_t *ost, int64_t off,
+                             const char *why) {
+            Launch L;
+            L.kind = Launch::COPYV;
+            L.ma = src.slot;
+            L.ma_off = src.offset * (int64_t)itemsize(src.dtype);
+            L.src = sdesc;
+            L.dst = sdesc;
+            for (int d = 0; d < sdesc.rank; d++) L.dst.strides[d] = ost[d];
+            L.mc = dst;
+            L.mc_off = off * (int64_t)itemsize(src.dtype);
+            L.text = "  kernel " + std::to_string(plan->launches.size()) + ": copy (" + why + ")\n";
+            plan->launches.push_back(L);
+        };
+        if (st0.prim == PRIM_CONCAT || st0.prim == PRIM_STACK) {
+            const Value &a = vals[st0.ins[0]], &b = vals[st0.ins[1]];
+            Value &o = vals[st0.out];
+            if (!a.materialised || !b.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "concat input not materialised");
+            const Slot dst = materialise(st0.out);
+            if (dst.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            zpucuda_tensor sa = desc_of(a), sb = desc_of(b);
+            if (st0.prim == PRIM_STACK)  // a length-1 axis (stride 0) at the stack position
+                for (zpucuda_tensor *t : {&sa, &sb}) {
+                    const int depth = t == &sa ? a.depth : b.depth, payload = t->rank - depth;
+                    const int pos = depth + (st0.axis < 0 ? st0.axis + payload + 1 : st0.axis);
+                    for (int d = t->rank; d > pos; d--) {
+                        t->dims[d] = t->dims[d - 1];
+                        t->strides[d] = t->strides[d - 1];
+                    }
+                    t->dims[pos] = 1;
+                    t->strides[pos] = 0;
+                    t->rank += 1;
+                }
+            const int ax = st0.axis >= 0 ? st0.axis + a.depth : st0.axis + sa.rank;
+            copy_into(a, sa, dst, o.strides, 0, "concat, first part");
+            copy_into(b, sb, dst, o.strides, sa.dims[ax] * o.strides[ax], "concat, second part");
+            o.materialised = true;
+            s++;
+            continue;
+        }
+        if (st0.prim == PRIM_PAD) {
+            const Value &a = vals[st0.ins[0]];
+            Value &o = vals[st0.out];
+            if (!a.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "pad input not materialised");
+            const Slot dst = materialise(st0.out);
+            if (dst.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            Launch F;
+            F.kind = Launch::FILL;
+            F.mc = dst;
+            F.dtype = o.dtype;
+            F.k = o.shape.numel();
+            F.scalar = st0.scalar;
+            F.text = "  kernel " + std::to_string(plan->launches.size()) + ": fill (pad)\n";
+            plan->launches.push_back(F);
+            int64_t off = 0;
+            for (int d = 0; d < o.shape.rank; d++) off += st0.starts[d] * o.strides[d];
+            copy_into(a, desc_of(a), dst, o.strides, off, "pad interior");
+            o.materialised = true;
+            s++;
+            continue;
+        }
+        if (st0.prim == PRIM_TAKE || st0.prim == PRIM_SCATTER_ADD) {
+            const bool take = st0.prim == PRIM_TAKE;
+            const Value &x0 = vals[st0.ins[0]];
+            Value &o = vals[st0.out];
+            Value x, ix, up;
+            if (!x0.materialised || !vals[st0.ins[1]].materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "take input not materialised");
+            if ((take && !contiguous_of(x0, "take input", &x)) || !contiguous_of(vals[st0.ins[1]], "indices", &ix) ||
+                (!take && !contiguous_of(vals[st0.ins[2]], "scatter_add updates", &up)) || !need_err())
+                return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "copy buffer");
+            Launch L;
+            L.kind = take ? Launch::TAKE : Launch::SCATTER;
+            const int r = x0.shape.rank;
+            const int ax = st0.axis < 0 ? st0.axis + r : st0.axis;
+            L.outer = 1;
+            L.inner = 1;
+            for (int d = 0; d < ax; d++) L.outer *= x0.shape.dims[d];
+            for (int d = ax + 1; d < r; d++) L.inner *= x0.shape.dims[d];
+            L.dim = x0.shape.dims[ax];
+            L.k = ix.shape.numel();
+            L.dtype = x0.dtype;
+            L.idx_dtype = ix.dtype;
+            L.ma = take ? x.slot : up.slot;
+            L.ma_off = take ? x.offset * (int64_t)itemsize(x.dtype) : up.offset * (int64_t)itemsize(up.dtype);
+            L.mb = ix.slot;
+            L.mb_off = ix.offset * (int64_t)itemsize(ix.dtype);
+            L.mc = materialise(st0.out);
+            if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
+            L.text = "  kernel " + std::to_string(plan->launches.size()) + (take ? ": take" : ": scatter_add") + "\n";
+            plan->launches.push_back(L);
+            o.materialised = true;
+            s++;
+            continue;
+        }
         if (st0.prim == PRIM_CAST) {
             Value &a = vals[st0.ins[0]];
             Value &o = vals[st0.out];
@@ -1018,6 +1212,19 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
             st = matmul_device(&a, &b, &c, s);
         } else if (L.kind == Launch::CUMSUM) {
             st = cumsum_launch(L.dtype, (char *)ptr(L.ma) + L.ma_off, ptr(L.mc), L.outer, L.dim, L.inner, L.reverse, s);
+        } else if (L.kind == Launch::COPYV) {
+            zpucuda_tensor a = L.src, c = L.dst;
+            a.data = (char *)ptr(L.ma) + L.ma_off;
+            c.data = (char *)ptr(L.mc) + L.mc_off;
+            st = copy_view(a, c, s);
+        } else if (L.kind == Launch::FILL) {
+            st = fill_value(L.dtype, ptr(L.mc), L.k, L.scalar, s);
+        } else if (L.kind == Launch::TAKE) {
+            st = take_launch(L.dtype, (char *)ptr(L.ma) + L.ma_off, L.idx_dtype, (char *)ptr(L.mb) + L.mb_off,
+                             ptr(L.mc), L.outer, L.dim, L.inner, L.k, plan->err, s);
+        } else if (L.kind == Launch::SCATTER) {
+            st = scatter_add_launch(L.dtype, L.idx_dtype, (char *)ptr(L.mb) + L.mb_off, (char *)ptr(L.ma) + L.ma_off,
+                                    ptr(L.mc), L.outer, L.dim, L.inner, L.k, plan->err, s);
         } else if (L.kind == Launch::COPY) {
             zpucuda_tensor a = L.src, c = L.src;
             a.data = (char *)ptr(L.ma) + L.ma_off;
@@ -1040,6 +1247,17 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
         if (st) return st;
     }
     return ZPUCUDA_OK;
+}
+
+// The plan's take / scatter_add index-error word, read and cleared (the
+// stream has drained): IndexOutOfRange once when set.
+static int take_index_error(zpucuda_plan *plan) {
+    if (!plan->err) return ZPUCUDA_OK;
+    unsigned int e = 0;
+    ZC_CUDA(cudaMemcpy(&e, plan->err, sizeof e, cudaMemcpyDeviceToHost));
+    if (!e) return ZPUCUDA_OK;
+    ZC_CUDA(cudaMemset(plan->err, 0, sizeof e));
+    return set_error(ZPUCUDA_ERR_INDEX_OUT_OF_RANGE, "a take / scatter_add index was out of range (ops.take)");
 }
 
 static size_t value_bytes(const zpucuda_value &v) {
@@ -1076,9 +1294,22 @@ int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void
     // bounded wait on this stream
     for (int64_t spins = 0;; spins++) {
         cudaError_t e = cudaStreamQuery(s);
-        if (e == cudaSuccess) return ZPUCUDA_OK;
+        if (e == cudaSuccess) return take_index_error(plan);
         if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
         if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_plan_run_host: stream did not drain");
+        if (spins > 1000) usleep(10);
+    }
+}
+
+int zpucuda_plan_check(zpucuda_plan *plan, void *stream) {
+    ZC_CHECK(plan, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    if (!plan->err) return ZPUCUDA_OK;
+    cudaStream_t s = resolve_stream(stream);
+    for (int64_t spins = 0;; spins++) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return take_index_error(plan);
+        if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+        if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_plan_check: stream did not drain");
         if (spins > 1000) usleep(10);
     }
 }

@@ -17,6 +17,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "tensor_ops.cuh"
 
 namespace zc {
 namespace {
@@ -196,6 +197,147 @@ int launch_from(const View &v, int dst_dt, void *dst, int64_t n, bool contig, cu
     }
 }
 
+// dst[dst view] <- src[src view], one thread per element of the shared dims.
+template <class S, class D>
+__global__ void __launch_bounds__(kCopyThreads) copy_view_kernel(const __grid_constant__ View v, const __grid_constant__ View w,
+                                                                 int64_t n) {
+    const S *src = (const S *)v.data;
+    D *dst = (D *)w.data;
+    for (int64_t i = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kCopyThreads) {
+        int64_t rem = i, so = 0, dof = 0;
+        for (int a = v.rank - 1; a >= 0; a--) {
+            const int64_t d = v.dims[a];
+            const int64_t q = rem / d, idx = rem - q * d;
+            so += idx * v.strides[a];
+            dof += idx * w.strides[a];
+            rem = q;
+        }
+        dst[dof] = convert<S, D>(src[so]);
+    }
+}
+
+template <class T>
+__global__ void __launch_bounds__(kCopyThreads) fill_kernel(T *dst, int64_t n, double v) {
+    const T x = from_f64<T>(v);
+    for (int64_t i = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kCopyThreads)
+        dst[i] = x;
+}
+
+// ops.take / scatterAdd index: trunc(toF64(v)), negatives counted from the
+// end once; -1 when out of range
+template <class I>
+__device__ __forceinline__ int64_t resolve_index(I raw, int64_t sdim) {
+    const double v = to_f64<I>(raw);
+    if (!(v > -9.2e18 && v < 9.2e18)) return -1;  // NaN / beyond i64
+    int64_t iv = (int64_t)v;                      // toward zero, as @intFromFloat
+    if (iv < 0) iv += sdim;
+    return (iv < 0 || iv >= sdim) ? -1 : iv;
+}
+
+template <class T, class I>
+__global__ void __launch_bounds__(kCopyThreads) take_kernel(const T *x, const I *indices, T *out, int64_t outer,
+                                                            int64_t sdim, int64_t inner, int64_t k, unsigned int *err) {
+    const int64_t n = outer * k * inner;
+    for (int64_t j = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; j < n; j += (int64_t)gridDim.x * kCopyThreads) {
+        const int64_t i = j % inner, t = (j / inner) % k, o = j / (inner * k);
+        const int64_t ix = resolve_index<I>(indices[t], sdim);
+        if (ix < 0) {
+            atomicOr(err, 1u);
+            out[j] = from_f64<T>(0.0);
+        } else {
+            out[j] = convert<T, T>(x[(o * sdim + ix) * inner + i]);
+        }
+    }
+}
+
+template <class T, class I>
+__global__ void __launch_bounds__(kCopyThreads) scatter_add_kernel(const I *indices, const T *updates, T *out,
+                                                                   int64_t outer, int64_t sdim, int64_t inner, int64_t k,
+                                                                   unsigned int *err) {
+    const int64_t cols = outer * inner;
+    for (int64_t c = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; c < cols; c += (int64_t)gridDim.x * kCopyThreads) {
+        const int64_t o = c / inner, i = c - o * inner;
+        for (int64_t t = 0; t < k; t++) {
+            const int64_t ix = resolve_index<I>(indices[t], sdim);
+            if (ix < 0) {
+                atomicOr(err, 1u);
+                continue;
+            }
+            T *d = out + (o * sdim + ix) * inner + i;
+            *d = from_f64<T>(to_f64<T>(*d) + to_f64<T>(updates[(o * k + t) * inner + i]));
+        }
+    }
+}
+
+View view_of(const zpucuda_tensor &t) {
+    View v;
+    v.data = (const char *)t.data;
+    v.rank = t.rank;
+    for (int a = 0; a < ZPUCUDA_MAX_RANK; a++) {
+        v.dims[a] = a < t.rank ? t.dims[a] : 1;
+        v.strides[a] = a < t.rank ? t.strides[a] : 0;
+    }
+    return v;
+}
+
+int grid_for(int64_t n) {
+    int64_t g = (n + kCopyThreads - 1) / kCopyThreads;
+    if (g > (int64_t)num_sms() * 16) g = (int64_t)num_sms() * 16;
+    return g < 1 ? 1 : (int)g;
+}
+
+template <class S>
+int copy_view_from(const View &v, const View &w, int dst_dtype, int64_t n, cudaStream_t s) {
+    const int g = grid_for(n);
+    switch (dst_dtype) {
+    case 0: copy_view_kernel<S, double><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 1: copy_view_kernel<S, float><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 2: copy_view_kernel<S, __half><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 3: copy_view_kernel<S, int64_t><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 4: copy_view_kernel<S, int32_t><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 5: copy_view_kernel<S, int16_t><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 6: copy_view_kernel<S, int8_t><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    case 7: copy_view_kernel<S, uint8_t><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    default: copy_view_kernel<S, Bool8><<<g, kCopyThreads, 0, s>>>(v, w, n); break;
+    }
+    ZC_LAUNCHED("copy_view_kernel");
+    return ZPUCUDA_OK;
+}
+
+template <class T>
+int take_typed(const void *x, int idx_dtype, const void *indices, void *out, int64_t outer, int64_t sdim,
+               int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
+    const int g = grid_for(outer * k * inner);
+    const T *xx = (const T *)x;
+    T *oo = (T *)out;
+    switch (idx_dtype) {
+    case ZPUCUDA_I64: take_kernel<T, int64_t><<<g, kCopyThreads, 0, s>>>(xx, (const int64_t *)indices, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_I32: take_kernel<T, int32_t><<<g, kCopyThreads, 0, s>>>(xx, (const int32_t *)indices, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_F32: take_kernel<T, float><<<g, kCopyThreads, 0, s>>>(xx, (const float *)indices, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_F64: take_kernel<T, double><<<g, kCopyThreads, 0, s>>>(xx, (const double *)indices, oo, outer, sdim, inner, k, err); break;
+    default: return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "take: index dtype");
+    }
+    ZC_LAUNCHED("take_kernel");
+    return ZPUCUDA_OK;
+}
+
+template <class T>
+int scatter_typed(int idx_dtype, const void *indices, const void *updates, void *out, int64_t outer, int64_t sdim,
+                  int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
+    const int g = grid_for(outer * inner);
+    const T *uu = (const T *)updates;
+    T *oo = (T *)out;
+    switch (idx_dtype) {
+    case ZPUCUDA_I64: scatter_add_kernel<T, int64_t><<<g, kCopyThreads, 0, s>>>((const int64_t *)indices, uu, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_I32: scatter_add_kernel<T, int32_t><<<g, kCopyThreads, 0, s>>>((const int32_t *)indices, uu, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_F32: scatter_add_kernel<T, float><<<g, kCopyThreads, 0, s>>>((const float *)indices, uu, oo, outer, sdim, inner, k, err); break;
+    case ZPUCUDA_F64: scatter_add_kernel<T, double><<<g, kCopyThreads, 0, s>>>((const double *)indices, uu, oo, outer, sdim, inner, k, err); break;
+    default: return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "scatter_add: index dtype");
+    }
+    ZC_LAUNCHED("scatter_add_kernel");
+    return ZPUCUDA_OK;
+}
+
 }  // namespace
 }  // namespace zc
 
@@ -251,3 +393,76 @@ extern "C" int zpucuda_tensor_copy(const zpucuda_tensor *src, zpucuda_tensor *ds
     default: return launch_from<Bool8>(v, dst->dtype, dst->data, n, contig, s);
     }
 }
+
+namespace zc {
+
+int copy_view(const zpucuda_tensor &src, const zpucuda_tensor &dst, cudaStream_t s) {
+    int64_t n = 1;
+    for (int a = 0; a < src.rank; a++) n *= src.dims[a];
+    if (n == 0) return ZPUCUDA_OK;
+    const View v = view_of(src), w = view_of(dst);
+    switch (src.dtype) {
+    case 0: return copy_view_from<double>(v, w, dst.dtype, n, s);
+    case 1: return copy_view_from<float>(v, w, dst.dtype, n, s);
+    case 2: return copy_view_from<__half>(v, w, dst.dtype, n, s);
+    case 3: return copy_view_from<int64_t>(v, w, dst.dtype, n, s);
+    case 4: return copy_view_from<int32_t>(v, w, dst.dtype, n, s);
+    case 5: return copy_view_from<int16_t>(v, w, dst.dtype, n, s);
+    case 6: return copy_view_from<int8_t>(v, w, dst.dtype, n, s);
+    case 7: return copy_view_from<uint8_t>(v, w, dst.dtype, n, s);
+    default: return copy_view_from<Bool8>(v, w, dst.dtype, n, s);
+    }
+}
+
+int fill_value(int dtype, void *dst, int64_t n, double v, cudaStream_t s) {
+    if (n == 0) return ZPUCUDA_OK;
+    const int g = grid_for(n);
+    switch (dtype) {
+    case 0: fill_kernel<double><<<g, kCopyThreads, 0, s>>>((double *)dst, n, v); break;
+    case 1: fill_kernel<float><<<g, kCopyThreads, 0, s>>>((float *)dst, n, v); break;
+    case 2: fill_kernel<__half><<<g, kCopyThreads, 0, s>>>((__half *)dst, n, v); break;
+    case 3: fill_kernel<int64_t><<<g, kCopyThreads, 0, s>>>((int64_t *)dst, n, v); break;
+    case 4: fill_kernel<int32_t><<<g, kCopyThreads, 0, s>>>((int32_t *)dst, n, v); break;
+    case 5: fill_kernel<int16_t><<<g, kCopyThreads, 0, s>>>((int16_t *)dst, n, v); break;
+    case 6: fill_kernel<int8_t><<<g, kCopyThreads, 0, s>>>((int8_t *)dst, n, v); break;
+    case 7: fill_kernel<uint8_t><<<g, kCopyThreads, 0, s>>>((uint8_t *)dst, n, v); break;
+    default: fill_kernel<Bool8><<<g, kCopyThreads, 0, s>>>((Bool8 *)dst, n, v); break;
+    }
+    ZC_LAUNCHED("fill_kernel");
+    return ZPUCUDA_OK;
+}
+
+int take_launch(int dtype, const void *x, int idx_dtype, const void *indices, void *out, int64_t outer, int64_t sdim,
+                int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
+    if (outer * k * inner == 0) return ZPUCUDA_OK;
+    switch (dtype) {
+    case 0: return take_typed<double>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 1: return take_typed<float>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 2: return take_typed<__half>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 3: return take_typed<int64_t>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 4: return take_typed<int32_t>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 5: return take_typed<int16_t>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 6: return take_typed<int8_t>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    case 7: return take_typed<uint8_t>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    default: return take_typed<Bool8>(x, idx_dtype, indices, out, outer, sdim, inner, k, err, s);
+    }
+}
+
+int scatter_add_launch(int dtype, int idx_dtype, const void *indices, const void *updates, void *out, int64_t outer,
+                       int64_t sdim, int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
+    ZC_CUDA(cudaMemsetAsync(out, 0, (size_t)(outer * sdim * inner) * dtype_size(dtype), s));
+    if (outer * inner == 0 || k == 0) return ZPUCUDA_OK;
+    switch (dtype) {
+    case 0: return scatter_typed<double>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 1: return scatter_typed<float>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 2: return scatter_typed<__half>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 3: return scatter_typed<int64_t>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 4: return scatter_typed<int32_t>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 5: return scatter_typed<int16_t>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 6: return scatter_typed<int8_t>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    case 7: return scatter_typed<uint8_t>(idx_dtype, indices, updates, out, outer, sdim, inner, k, err, s);
+    default: return set_error(ZPUCUDA_ERR_DTYPE_MISMATCH, "scatter_add on bool");
+    }
+}
+
+}  // namespace zc
