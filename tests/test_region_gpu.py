@@ -852,3 +852,43 @@ def test_take_and_scatter_add(zc):
         bad.check()
     assert err.value.status == 8  # IndexOutOfRange
     bad.check()  # reported once
+
+
+def test_value_and_grad_trace_of_an_mlp(zc):
+    """A jit(valueAndGrad) trace of dense -> tanh -> dense -> meanAll(square)
+    as zpu's autodiff records it (autodiff.zig: matmul VJP through
+    swapLastTwo views, add's VJP as unbroadcast sums, tanh's VJP as
+    g * (1 - a^2), meanAll's as a broadcast scalar): ten launches -- the
+    transposes are views read by the GEMMs in place -- and the loss and all
+    four gradients within 1e-4 of torch's f64 autograd."""
+    B, I, H, O = 48, 20, 32, 6
+    rng = np.random.default_rng(81)
+    x, w1, b1 = (rng.standard_normal(s).astype(np.float32) for s in ((B, I), (I, H), (H,)))
+    w2, b2 = (rng.standard_normal(s).astype(np.float32) * 0.3 for s in ((H, O), (O,)))
+    F = zc.F32
+    args = [(1, F, (B, I)), (2, F, (I, H)), (3, F, (H,)), (4, F, (H, O)), (5, F, (O,))]
+    blobs = [(6, np.float32(1.0 / (B * O))), (7, np.float32(2.0)), (8, np.float32(1.0))]
+    T = {"perm": [1, 0]}
+    steps = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0), ("tanh", [11], 12, -2, 0),
+             ("matmul", [12, 4], 13, -2, 0), ("add", [13, 5], 14, -2, 0), ("square", [14], 15, -2, 0),
+             ("sum", [15], 16, -2, 0), ("mul", [16, 6], 17, -2, 0),
+             # backward
+             ("broadcast", [6], 20, -2, 0, {"shape": [B, O]}), ("mul", [14, 7], 21, -2, 0),
+             ("mul", [20, 21], 22, -2, 0), ("sum", [22], 23, 0, 0),
+             ("transpose", [4], 24, -2, 0, T), ("matmul", [22, 24], 25, -2, 0),
+             ("transpose", [12], 26, -2, 0, T), ("matmul", [26, 22], 27, -2, 0),
+             ("square", [12], 28, -2, 0), ("sub", [8, 28], 29, -2, 0), ("mul", [25, 29], 30, -2, 0),
+             ("sum", [30], 31, 0, 0), ("transpose", [1], 32, -2, 0, T), ("matmul", [32, 30], 33, -2, 0)]
+    p = zc.Plan(args, blobs, steps, [17, 33, 31, 27, 23])
+    assert p.num_kernels() == 10, p.describe()
+    assert "copy" not in p.describe()
+    loss, gw1, gb1, gw2, gb2 = [o.cpu().numpy().astype(np.float64)
+                                for o in p.run([torch.from_numpy(v).cuda() for v in (x, w1, b1, w2, b2)])]
+    ts = [torch.tensor(v, dtype=torch.float64, requires_grad=True) for v in (x, w1, b1, w2, b2)]
+    y = torch.tanh(ts[0] @ ts[1] + ts[2]) @ ts[3] + ts[4]
+    ref = (y * y).mean()
+    ref.backward()
+    assert abs(loss.item() - ref.item()) <= 1e-4 * abs(ref.item())
+    for g, t in zip((gw1, gb1, gw2, gb2), ts[1:]):
+        w = t.grad.numpy()
+        assert np.linalg.norm(g - w) <= 1e-4 * np.linalg.norm(w)
