@@ -109,11 +109,51 @@ def test_lowering_keeps_needed_intermediates_and_splits_on_shape(capi):
 
 
 def test_lowering_rejects_unsupported_prims(capi):
+    """solve / inv / det / cholesky / triangular_solve / conv: zpu's own jit
+    replay refuses them (ops.zig:2197-2199), and so does the lowering."""
     import zpu_b200 as zc
-    args = [(1, zc.F32, (4,))]
-    with pytest.raises(zc.ZpuCudaError) as e:
-        zc.Plan(args, [], [(74, [1], 10, -2, 0)], [10])  # take
-    assert e.value.name == "NotSupported"
+    args = [(1, zc.F32, (4, 4)), (2, zc.F32, (4,))]
+    for prim in (81, 82, 83, 84, 86):
+        with pytest.raises(zc.ZpuCudaError) as e:
+            zc.Plan(args, [], [(prim, [1, 2], 10, -2, 0)], [10])
+        assert e.value.name == "NotSupported"
+
+
+def test_abi_struct_layouts_match_the_header(capi, tmp_path):
+    """Every struct the ctypes binding mirrors has the header's size and
+    field offsets (a C probe compiled here with gcc)."""
+    from zpu_b200 import _capi
+    structs = {"zpucuda_step": _capi.Step, "zpucuda_value": _capi.Value, "zpucuda_tensor": _capi.Tensor,
+               "zpucuda_blob": _capi.Blob}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "zpucuda.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append('printf("%s %%zu\\n", sizeof(%s));' % (cname, cname))
+        for fname, _ in cls._fields_:
+            lines.append('printf("%s.%s %%zu\\n", offsetof(%s, %s));' % (cname, fname, cname, fname))
+    lines.append("return 0; }")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines())
+    for cname, cls in structs.items():
+        assert int(got[cname]) == C.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert int(got["%s.%s" % (cname, fname)]) == getattr(cls, fname).offset, (cname, fname)
+
+
+def test_lowering_of_views_is_host_logic(capi):
+    """A transposed GEMM operand is read in place (one launch, no copy), and
+    a transpose under vmap permutes the payload axes only."""
+    import zpu_b200 as zc
+    T = {"perm": [1, 0]}
+    p = zc.Plan([(1, zc.F32, (16, 8)), (2, zc.F32, (16, 4))], [],
+                [("transpose", [1], 10, -2, 0, T), ("matmul", [10, 2], 11, -2, 0)], [11])
+    assert p.num_kernels() == 1 and "copy" not in p.describe()
+    assert p.outputs == [(zc.F32, (8, 4))]
+    q = zc.Plan([(1, zc.F32, (3, 4, 5), 1)], [],
+                [("transpose", [1], 10, -2, 0, T), ("neg", [10], 11, -2, 0)], [11])
+    assert q.outputs == [(zc.F32, (3, 5, 4))]
 
 
 def test_matmul_shape_logic_matches_ops_matmul(capi):
