@@ -858,9 +858,10 @@ def test_value_and_grad_trace_of_an_mlp(zc):
     """A jit(valueAndGrad) trace of dense -> tanh -> dense -> meanAll(square)
     as zpu's autodiff records it (autodiff.zig: matmul VJP through
     swapLastTwo views, add's VJP as unbroadcast sums, tanh's VJP as
-    g * (1 - a^2), meanAll's as a broadcast scalar): ten launches -- the
-    transposes are views read by the GEMMs in place -- and the loss and all
-    four gradients within 1e-4 of torch's f64 autograd."""
+    g * (1 - a^2), meanAll's as a broadcast scalar): nine launches -- the
+    transposes are views read by the GEMMs in place, the forward bias + tanh
+    and bias run in the GEMM epilogues -- and the loss and all four gradients
+    within 1e-4 of torch's f64 autograd."""
     B, I, H, O = 48, 20, 32, 6
     rng = np.random.default_rng(81)
     x, w1, b1 = (rng.standard_normal(s).astype(np.float32) for s in ((B, I), (I, H), (H,)))
@@ -880,8 +881,9 @@ def test_value_and_grad_trace_of_an_mlp(zc):
              ("square", [12], 28, -2, 0), ("sub", [8, 28], 29, -2, 0), ("mul", [25, 29], 30, -2, 0),
              ("sum", [30], 31, 0, 0), ("transpose", [1], 32, -2, 0, T), ("matmul", [32, 30], 33, -2, 0)]
     p = zc.Plan(args, blobs, steps, [17, 33, 31, 27, 23])
-    assert p.num_kernels() == 10, p.describe()
-    assert "copy" not in p.describe()
+    assert p.num_kernels() == 9, p.describe()
+    d = p.describe()
+    assert "copy" not in d and "bias + tanh epilogue" in d and "+ bias epilogue" in d, d
     loss, gw1, gb1, gw2, gb2 = [o.cpu().numpy().astype(np.float64)
                                 for o in p.run([torch.from_numpy(v).cuda() for v in (x, w1, b1, w2, b2)])]
     ts = [torch.tensor(v, dtype=torch.float64, requires_grad=True) for v in (x, w1, b1, w2, b2)]
@@ -892,3 +894,33 @@ def test_value_and_grad_trace_of_an_mlp(zc):
     for g, t in zip((gw1, gb1, gw2, gb2), ts[1:]):
         w = t.grad.numpy()
         assert np.linalg.norm(g - w) <= 1e-4 * np.linalg.norm(w)
+
+
+def test_matmul_bias_tanh_fuse_into_the_gemm_epilogue(zc):
+    """matmul -> add(row bias) -> tanh with each value used only by the next
+    runs as one GEMM whose epilogue adds the bias and takes tanh; when the
+    sum is needed elsewhere only the bias fuses, and a product used twice
+    keeps its own region."""
+    rng = np.random.default_rng(91)
+    x = rng.standard_normal((40, 24)).astype(np.float32)
+    w = rng.standard_normal((24, 36)).astype(np.float32) * 0.3
+    b = rng.standard_normal(36).astype(np.float32)
+    F = zc.F32
+    args = [(1, F, (40, 24)), (2, F, (24, 36)), (3, F, (36,))]
+    mm = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0), ("tanh", [11], 12, -2, 0)]
+    ref_h = x.astype(np.float64) @ w.astype(np.float64) + b
+    cases = [([12], 1, "bias + tanh epilogue"), ([11, 12], 2, "+ bias epilogue"),
+             ([12, 10], 2, None)]  # the product is an output: no fusion
+    for outs, kernels, tag in cases:
+        p = zc.Plan(args, [], mm, outs)
+        d = p.describe()
+        assert p.num_kernels() == kernels, d
+        if tag:
+            assert tag in d, d
+        else:
+            assert "epilogue" not in d, d
+        got = dict(zip(outs, [o.cpu().numpy().astype(np.float64)
+                              for o in p.run([torch.from_numpy(v).cuda() for v in (x, w, b)])]))
+        assert np.max(np.abs(got[12] - np.tanh(ref_h))) <= 2e-5
+        if 11 in got:
+            assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)

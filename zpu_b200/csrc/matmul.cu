@@ -174,6 +174,24 @@ int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tens
                            P.lda, P.ldb, P.n, P.ta, P.tb, P.batch, P.m * P.n, s);
 }
 
+// The same product with an epilogue on each element (f32, one matrix: the
+// GEMM's epilogues belong to one matrix) -- the jit lowering's matmul + bias
+// [+ tanh] fusion.
+int matmul_device_epi(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, const Epilogue &epi,
+                      cudaStream_t s) {
+    Plan P;
+    int st = plan_matmul(a, b, &P);
+    if (st) return st;
+    if (!out || !out->data || !a->data || !b->data) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if (a->dtype != ZPUCUDA_F32 || out->dtype != ZPUCUDA_F32 || batch_count(P.batch) != 1)
+        return ZPUCUDA_ERR_NOT_SUPPORTED;
+    if (out->rank != P.out_rank) return ZPUCUDA_ERR_SHAPE_MISMATCH;
+    for (int i = 0; i < P.out_rank; i++)
+        if (out->dims[i] != P.out_dims[i]) return ZPUCUDA_ERR_SHAPE_MISMATCH;
+    return gemm_f32_device_epi((const float *)a->data, (const float *)b->data, (float *)out->data, P.m, P.n, P.k,
+                               P.lda, P.ldb, P.n, P.ta, P.tb, P.batch, P.m * P.n, epi, s);
+}
+
 }  // namespace zc
 
 using namespace zc;

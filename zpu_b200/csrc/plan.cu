@@ -13,11 +13,14 @@
 #include <string>
 #include <vector>
 
+#include "gemm.cuh"
 #include "region.cuh"
 #include "tensor_ops.cuh"
 
 namespace zc {
 int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, cudaStream_t s);
+int matmul_device_epi(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, const Epilogue &epi,
+                      cudaStream_t s);
 }
 
 using namespace zc;
@@ -174,6 +177,9 @@ struct Launch {
     int64_t k = 0;
     std::vector<int64_t> in_off;  // region inputs: byte offsets into their slots
     int64_t ma_off = 0, mb_off = 0;  // matmul / cumsum / copy source: byte offsets
+    int32_t epi_mode = 0;            // matmul: EPI_BIAS / EPI_BIAS_TANH fused, 0 none
+    Slot bias;                       // its bias vector
+    int64_t bias_off = 0;
     zpucuda_tensor src;              // copy: the view (data set at run time)
     int32_t dst_dtype = 0;           // copy: the output's element type (a cast converts)
     RegionProgram prog;
@@ -914,15 +920,47 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 for (int i = 0; i < b.shape.rank; i++) L.tb.strides[i] = b.strides[i];
             }
             zpucuda_matmul_shape(&L.ta, &L.tb, &L.tc);
-            L.mc = materialise(st0.out);
+            // matmul -> add(row bias) [-> tanh], each value used only by the
+            // next: the f32 GEMM's bias / bias + tanh epilogue writes the last
+            // one (one pass over the output instead of three)
+            uint64_t final_id = st0.out;
+            int fused = 0;
+            const Value &mo = vals[st0.out];
+            auto only_user = [&](uint64_t id, int step) {
+                auto it = users.find(id);
+                return !out_index.count(id) && it != users.end() && it->second.size() == 1 && it->second[0] == step;
+            };
+            if (a.dtype == ZPUCUDA_F32 && mo.shape.rank == 2 && a.shape.rank <= 2 && b.shape.rank <= 2 &&
+                s + 1 < n_steps && only_user(st0.out, s + 1)) {
+                const zpucuda_step &ad = steps[s + 1];
+                const uint64_t other = ad.n_inputs == 2 ? (ad.ins[0] == st0.out ? ad.ins[1] : ad.ins[0]) : 0;
+                if (ad.prim == 35 && ad.n_inputs == 2 && other != st0.out && vals.count(other)) {
+                    const Value &bv = vals[other];
+                    const Value &ao = vals[ad.out];
+                    const int64_t n = mo.shape.dims[1];
+                    if (bv.dtype == ZPUCUDA_F32 && bv.materialised && bv.contiguous() && bv.shape.numel() == n &&
+                        (bv.shape.rank == 1 || (bv.shape.rank == 2 && bv.shape.dims[0] == 1)) && ao.shape == mo.shape) {
+                        fused = 1;
+                        final_id = ad.out;
+                        L.bias = bv.slot;
+                        L.bias_off = bv.offset * 4;
+                        if (s + 2 < n_steps && steps[s + 2].prim == 19 && steps[s + 2].n_inputs == 1 &&
+                            steps[s + 2].ins[0] == ad.out && only_user(ad.out, s + 2))
+                            fused = 2, final_id = steps[s + 2].out;
+                    }
+                }
+            }
+            L.epi_mode = fused == 2 ? EPI_BIAS_TANH : fused == 1 ? EPI_BIAS : 0;
+            L.mc = materialise(final_id);
             if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
             char buf[160];
             snprintf(buf, sizeof buf, "  kernel %zu: gemm %s (%%%llu = matmul(%%%llu, %%%llu))\n", plan->launches.size(),
                      a.dtype == ZPUCUDA_F64 ? "f64 dmma" : "f32 3xtf32", (unsigned long long)st0.out,
                      (unsigned long long)st0.ins[0], (unsigned long long)st0.ins[1]);
             L.text = buf;
+            if (fused) L.text.insert(L.text.size() - 1, fused == 2 ? " + bias + tanh epilogue" : " + bias epilogue");
             plan->launches.push_back(L);
-            s++;
+            s += 1 + fused;
             continue;
         }
         if (st0.prim == PRIM_CUMSUM) {
@@ -1209,7 +1247,14 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
             a.data = (char *)ptr(L.ma) + L.ma_off;
             b.data = (char *)ptr(L.mb) + L.mb_off;
             c.data = ptr(L.mc);
-            st = matmul_device(&a, &b, &c, s);
+            if (L.epi_mode) {
+                Epilogue e;
+                e.mode = L.epi_mode;
+                e.bias = (const float *)((char *)ptr(L.bias) + L.bias_off);
+                st = matmul_device_epi(&a, &b, &c, e, s);
+            } else {
+                st = matmul_device(&a, &b, &c, s);
+            }
         } else if (L.kind == Launch::CUMSUM) {
             st = cumsum_launch(L.dtype, (char *)ptr(L.ma) + L.ma_off, ptr(L.mc), L.outer, L.dim, L.inner, L.reverse, s);
         } else if (L.kind == Launch::COPYV) {
