@@ -503,6 +503,17 @@ def run_ours(args):
         gbs, cores, sample, per = cpu_chain_baseline()
         line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
                                 "sample": sample + " (oracle restatement of zpu's jit.Plan.runAll)"}
+        # the checker on the timed input: the device's sum against zpu's own
+        # f32 summation order and the f64 sum of the same element values
+        from oracle import zpu_oracle as zo
+        s32, s64, t = zo.jit_chain_tanh_sq_affine_sum(x.cpu().numpy(), A, B, want_vector=True)
+        got = float(out.cpu())
+        scale = zo.abssum_f64(t)
+        line["cpu_baseline"]["parity"] = {
+            "device_sum": got, "zpu_f32_order_sum": float(s32), "f64_sum": s64,
+            "abs_diff_vs_f64": abs(got - s64), "abs_diff_vs_zpu_f32_order": abs(got - float(s32)),
+            "tolerance": "|device - f64| <= 1e-6 * sum|t_i|", "bound": 1e-6 * scale,
+            "within": abs(got - s64) <= 1e-6 * scale}
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

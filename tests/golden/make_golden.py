@@ -51,6 +51,10 @@ CASES = {
     "tensor/bools": 0.0,           # tests/snap/zpu.zig:48 (cast of spread(6) to bool)
     "shape/transpose": 1e-9,       # tests/snap/zpu.zig:96
     "shape/flip": 1e-9,            # tests/snap/zpu.zig:97
+    "shape/pad": 1e-9,             # tests/snap/zpu.zig:98 (pads (1,0),(0,2), value -1)
+    "shape/take": 1e-9,            # tests/snap/zpu.zig:99 (i32 indices [2,0,2], axis 0)
+    "shape/concat": 1e-9,          # tests/snap/zpu.zig:100 (x with itself, axis 1)
+    "shape/stack": 1e-9,           # tests/snap/zpu.zig:101 (x with itself, axis 0)
     "rng/normal-seed12345": 0.0,   # tests/snap/zpu.zig:355
     "rng/uniform-seed12345": 0.0,  # tests/snap/zpu.zig:358
 }

@@ -369,3 +369,15 @@ def test_cumsum_snapshots_and_known_answers(golden):
     for c in golden["cumsum_known"]:
         a = np.array(c["x"], dtype=np.float64).reshape(c["shape"])
         assert zo.cumsum(a, c["axis"], c["reverse"]).ravel().tolist() == c["want"]
+
+
+def test_data_movement_snapshots(golden):
+    """tests/snap/zpu.zig:98-101 on spread(12) as 3 x 4: pad, take, concat,
+    stack (numpy's own semantics restate zpu's here)."""
+    x = np.array(golden["inputs"]["spread12"], dtype=np.float64).reshape(3, 4)
+    cases = {"pad": np.pad(x, ((1, 0), (0, 2)), constant_values=-1.0), "take": x[[2, 0, 2]],
+             "concat": np.concatenate([x, x], 1), "stack": np.stack([x, x], 0)}
+    for name, got in cases.items():
+        want, tol, shape = snap(golden, "zpu/shape/" + name)
+        assert list(got.shape) == shape, name
+        snap_close(want, got, tol)

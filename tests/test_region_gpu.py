@@ -924,3 +924,18 @@ def test_matmul_bias_tanh_fuse_into_the_gemm_epilogue(zc):
         assert np.max(np.abs(got[12] - np.tanh(ref_h))) <= 2e-5
         if 11 in got:
             assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)
+
+
+def test_data_movement_snapshots_on_device(zc, golden):
+    """The reference's shape/{pad,take,concat,stack} snapshots as plan steps."""
+    x = torch.tensor(golden["inputs"]["spread12"], dtype=torch.float64, device="cuda").reshape(3, 4)
+    idx = torch.tensor([2, 0, 2], dtype=torch.int32, device="cuda")
+    D = zc.F64
+    p = zc.Plan([(1, D, (3, 4)), (2, 4, (3,))], [],
+                [("pad", [1], 10, -2, 0, {"pads": [(1, 0), (0, 2)], "scalar": -1.0}), ("take", [1, 2], 11, 0, 0),
+                 ("concat_op", [1, 1], 12, 1, 0), ("stack_op", [1, 1], 13, 0, 0)], [10, 11, 12, 13])
+    for name, o in zip(("pad", "take", "concat", "stack"), p.run([x, idx])):
+        s = golden["snapshots"]["zpu/shape/" + name]
+        g = o.cpu().numpy()
+        assert list(g.shape) == s["shape"], name
+        assert np.all(np.abs(g.ravel() - s["values"]) <= s["tol"] * np.maximum(1, np.abs(g.ravel()))), name
