@@ -1,9 +1,17 @@
 // jit-plan lowering: turns the steps of a built jit.Plan (src/zpu/jit.zig:
-// 30-36, 130-256) into a short list of launches -- one fused kernel per
-// element-wise(+reduction) region, one GEMM per matmul step -- and replays
-// that list on every run (the device counterpart of Plan.runAll,
-// jit.zig:99-126, which interprets one ops.applyPrim per step and
-// materialises every intermediate).
+// 30-36, 130-256) into a short list of launches and replays that list on
+// every run (the device counterpart of Plan.runAll, jit.zig:99-126, which
+// interprets one ops.applyPrim per step and materialises every
+// intermediate):
+//   * one fused kernel per element-wise(+reduction) region; bool values
+//     (predicates, any / all) ride in the region's float registers;
+//   * one GEMM per matmul step, with a following row-bias add (and tanh)
+//     in its epilogue when nothing else reads the intermediates;
+//   * movement prims (reshape, transpose, broadcast, expand_dims, squeeze,
+//     slice, flip, copy) as views -- strides and an offset over the
+//     producer's buffer -- read in place by regions and GEMMs, copied only
+//     where a contiguous buffer is needed;
+//   * cumsum, cast, concat / stack / pad, take and scatter_add launches.
 #include <stdio.h>
 #include <string.h>
 #include <unistd.h>
