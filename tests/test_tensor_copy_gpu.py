@@ -73,34 +73,48 @@ def test_transposed_views_take_the_tiled_path(zc, dst):
         assert same_bits(out.cpu().numpy(), want), shape
 
 
-@pytest.mark.parametrize("dst", [torch.float32, torch.int32, torch.float64])
-@pytest.mark.parametrize("src", [np.float32, np.int32])
-def test_transposed_four_byte_views(zc, src, dst):
-    """4-byte sources: 16-byte aligned views (every dim a multiple of 4,
-    ragged 64-tiles) take the 16-byte transpose when the output is 4 bytes
-    too; a one-element offset, an odd ld, a flipped column axis (negative
-    ld) and a broadcast batch axis (stride 0) cover both kernels' addressing."""
-    def values(n):
-        v = zo.uniform_range(21, n, -3.0e7, 3.0e7)
-        return v.astype(src)  # i32 beyond 2^24: f32 rounds
+def spread_values(k, n):
+    """n values of zpu type k spread over most of its range."""
+    dt = zo.DTYPES[k]
+    u = zo.uniform_range(21, n, -1.0, 1.0)
+    kind = np.dtype(dt).kind
+    if kind == "f":
+        return (u * (3.0e4 if dt == np.float16 else 3.0e7)).astype(dt)  # f32 of i32 beyond 2^24 rounds
+    if kind == "b":
+        return u > 0
+    info = np.iinfo(dt)
+    if info.min == 0:
+        return ((u + 1.0) * 0.5 * info.max).astype(dt)
+    return (u * min(info.max, 2 ** 40)).astype(dt)
+
+
+@pytest.mark.parametrize("dst", [torch.float64, torch.float32, torch.float16, torch.int8, torch.bool],
+                         ids=["f64", "f32", "f16", "i8", "bool"])
+@pytest.mark.parametrize("src", range(9), ids=NAMES)
+def test_transposed_aligned_views(zc, src, dst):
+    """16-byte aligned views (every dim a multiple of 16 elements, ragged
+    64-tiles) take the 16-byte transpose for every element size; a
+    one-element offset with an odd ld takes the 1-element kernel; a flipped
+    column axis (negative ld) and a broadcast batch axis (stride 0) cover the
+    addressing of both."""
     cases = []
-    for shape in [(132, 68), (3, 40, 36), (260, 256), (2, 2, 12, 8)]:
-        x = values(int(np.prod(shape))).reshape(shape)
+    for shape in [(144, 80), (3, 48, 32), (272, 256), (2, 2, 16, 32)]:
+        x = spread_values(src, int(np.prod(shape))).reshape(shape)
         cases.append((torch.from_numpy(x).cuda().transpose(-1, -2), np.swapaxes(x, -1, -2)))
-    x = values(67 * 131).reshape(67, 131)  # offset 1 element, ld 131
+    x = spread_values(src, 67 * 131).reshape(67, 131)  # offset 1 element, ld 131
     cases.append((torch.from_numpy(x).cuda()[:, 1:].transpose(0, 1), x[:, 1:].T))
-    x = values(96 * 128).reshape(96, 128)  # [R=128, C=96] view with ld = -128
+    x = spread_values(src, 96 * 128).reshape(96, 128)  # [R=128, C=96] view with ld = -128
     xd = torch.from_numpy(x).cuda()
     d = zc.Tensor()
-    d.data = xd.data_ptr() + (95 * 128) * 4
-    d.dtype = zc.F32 if src == np.float32 else 4  # zpu DType.i32
+    d.data = xd.data_ptr() + (95 * 128) * x.itemsize
+    d.dtype = src
     d.rank = 2
     d.dims[0], d.dims[1] = 128, 96
     d.strides[0], d.strides[1] = 1, -128
     cases.append((d, x[::-1].T))
-    x = values(64 * 72).reshape(64, 72)  # batch axis of stride 0
-    cases.append((torch.from_numpy(x).cuda().expand(3, 64, 72).transpose(-1, -2),
-                  np.broadcast_to(x, (3, 64, 72)).swapaxes(-1, -2)))
+    x = spread_values(src, 64 * 80).reshape(64, 80)  # batch axis of stride 0
+    cases.append((torch.from_numpy(x).cuda().expand(3, 64, 80).transpose(-1, -2),
+                  np.broadcast_to(x, (3, 64, 80)).swapaxes(-1, -2)))
     for view, npv in cases:
         out = torch.empty(npv.shape, dtype=dst, device="cuda")
         zc.tensor_copy(view, out)

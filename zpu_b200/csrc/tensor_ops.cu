@@ -10,8 +10,8 @@
 //   * a tiled transpose for views whose unit-stride axis is the second to
 //     last (the swapLastTwo views of the matmul VJP): 64 x 64 tiles through
 //     shared memory so reads and writes both coalesce, with 16-byte global
-//     accesses when both types are 4 bytes wide and the view is 16-byte
-//     aligned (f32 / i32 at the speed of a plain copy);
+//     accesses when the view is 16-byte aligned (f32 at the speed of a
+//     plain copy);
 //   * cudaMemcpyAsync for a contiguous view of the same type (clone).
 // HBM-bound: 1 read + 1 write per element.
 #include <cuda_fp16.h>
@@ -148,43 +148,47 @@ __global__ void __launch_bounds__(256) copy_transpose_kernel(const __grid_consta
             if (ty + j < rr && tx + h < cc) d[(int64_t)(ty + j) * C + tx + h] = convert<S, D>(tile[tx + h][ty + j]);
 }
 
-// The same transpose with 16-byte global accesses, for 4-byte source and
-// output types whose view is 16-byte aligned (base pointers, ld, the batch
-// strides, R and C all multiples of 4 elements): on the load side lane
-// q = t & 15 reads rows 4q..4q+3 of one column, on the store side it writes
-// columns 4q..4q+3 of one row.  Shared accesses stay 4 bytes wide (pitch 65:
-// at most two lanes per bank).
+// The same transpose with 16-byte global accesses, for views that are
+// 16-byte aligned: base pointers, ld, the batch strides and R multiples of
+// VS = 16 / sizeof(S) elements, C a multiple of VD = 16 / sizeof(D).  On the
+// load side 64 / VS lanes read one column (VS rows each), on the store side
+// 64 / VD lanes write one row (VD columns each); shared accesses stay one
+// element wide (pitch 65).
 template <class S, class D>
 __global__ void __launch_bounds__(256) copy_transpose16_kernel(const __grid_constant__ View v, D *dst, int64_t R,
                                                                      int64_t C, int64_t ld, int64_t b0) {
-    static_assert(sizeof(S) == 4 && sizeof(D) == 4, "16-byte transpose moves 4-byte elements");
-    struct alignas(16) VS { S e[4]; };
-    struct alignas(16) VD { D e[4]; };
+    constexpr int VS = 16 / sizeof(S), VD = 16 / sizeof(D);
+    constexpr int LS = kTile / VS, LD = kTile / VD;  // lanes per column / per row
+    static_assert(VS * sizeof(S) == 16 && VD * sizeof(D) == 16, "element size divides 16");
+    struct alignas(16) VecS { S e[VS]; };
+    struct alignas(16) VecD { D e[VD]; };
     __shared__ S tile[kTile][kTile + 1];  // [column][row]
     const int64_t r0 = (int64_t)blockIdx.y * kTile, c0 = (int64_t)blockIdx.x * kTile;
-    const int rr = (int)min((int64_t)kTile, R - r0), cc = (int)min((int64_t)kTile, C - c0);  // multiples of 4
-    const int q4 = 4 * (threadIdx.x & 15), w = threadIdx.x >> 4;
+    const int rr = (int)min((int64_t)kTile, R - r0), cc = (int)min((int64_t)kTile, C - c0);
+    const int t = threadIdx.x;
     const int64_t b = b0 + blockIdx.z;
     const S *s = (const S *)v.data + batch_offset(v, b) + c0 * ld + r0;
+    const int ql = VS * (t % LS), wl = t / LS;
 #pragma unroll
-    for (int j = 0; j < kTile; j += 16) {
-        const int c = w + j;
-        if (c < cc && q4 < rr) {
-            const VS x = *(const VS *)(s + (int64_t)c * ld + q4);
+    for (int j = 0; j < kTile; j += 256 / LS) {
+        const int c = wl + j;
+        if (c < cc && ql < rr) {
+            const VecS x = *(const VecS *)(s + (int64_t)c * ld + ql);
 #pragma unroll
-            for (int k = 0; k < 4; k++) tile[c][q4 + k] = x.e[k];
+            for (int k = 0; k < VS; k++) tile[c][ql + k] = x.e[k];
         }
     }
     __syncthreads();
     D *d = dst + (b * R + r0) * C + c0;
+    const int qs = VD * (t % LD), ws = t / LD;
 #pragma unroll
-    for (int j = 0; j < kTile; j += 16) {
-        const int r = w + j;
-        if (r < rr && q4 < cc) {
-            VD y;
+    for (int j = 0; j < kTile; j += 256 / LD) {
+        const int r = ws + j;
+        if (r < rr && qs < cc) {
+            VecD y;
 #pragma unroll
-            for (int k = 0; k < 4; k++) y.e[k] = convert<S, D>(tile[q4 + k][r]);
-            *(VD *)(d + (int64_t)r * C + q4) = y;
+            for (int k = 0; k < VD; k++) y.e[k] = convert<S, D>(tile[qs + k][r]);
+            *(VecD *)(d + (int64_t)r * C + qs) = y;
         }
     }
 }
@@ -206,27 +210,23 @@ int launch_copy(const View &v, void *dst, int64_t n, bool contig, cudaStream_t s
     // the tiled transpose: unit stride on the second-to-last axis, not the last
     if (r >= 2 && v.strides[r - 2] == 1 && v.strides[r - 1] != 1 && v.dims[r - 1] > 1 && v.dims[r - 2] > 1) {
         const int64_t R = v.dims[r - 2], C = v.dims[r - 1], ld = v.strides[r - 1];
+        constexpr int64_t VS = 16 / sizeof(S), VD = 16 / sizeof(D);
         int64_t nb = 1;
-        bool aligned16 = (uintptr_t)v.data % 16 == 0 && (uintptr_t)dst % 16 == 0 && R % 4 == 0 && C % 4 == 0 &&
-                         ld % 4 == 0;
+        bool aligned16 = (uintptr_t)v.data % 16 == 0 && (uintptr_t)dst % 16 == 0 && R % VS == 0 && ld % VS == 0 &&
+                         C % VD == 0;
         for (int a = 0; a < r - 2; a++) {
             nb *= v.dims[a];
-            aligned16 = aligned16 && v.strides[a] % 4 == 0;
+            aligned16 = aligned16 && v.strides[a] % VS == 0;
         }
         const int64_t gx = (C + kTile - 1) / kTile, gy = (R + kTile - 1) / kTile;
         if (gy <= 65535 && gx <= 0x7fffffff) {
             // one launch per 65535 batches (the grid's z limit)
             for (int64_t b0 = 0; b0 < nb; b0 += 65535) {
                 const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(nb - b0 < 65535 ? nb - b0 : 65535));
-                bool wide = false;
-                if constexpr (sizeof(S) == 4 && sizeof(D) == 4) {
-                    if (aligned16) {
-                        copy_transpose16_kernel<S, D><<<grid, 256, 0, s>>>(v, (D *)dst, R, C, ld, b0);
-                        ZC_LAUNCHED("tensor copy (tiled transpose, 16-byte)");
-                        wide = true;
-                    }
-                }
-                if (!wide) {
+                if (aligned16) {
+                    copy_transpose16_kernel<S, D><<<grid, 256, 0, s>>>(v, (D *)dst, R, C, ld, b0);
+                    ZC_LAUNCHED("tensor copy (tiled transpose, 16-byte)");
+                } else {
                     copy_transpose_kernel<S, D><<<grid, dim3(32, 8), 0, s>>>(v, (D *)dst, R, C, ld, b0);
                     ZC_LAUNCHED("tensor copy (tiled transpose)");
                 }
