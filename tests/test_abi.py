@@ -119,6 +119,24 @@ def test_lowering_rejects_unsupported_prims(capi):
         assert e.value.name == "NotSupported"
 
 
+def test_lowering_types_i64_operands_as_zpu_promotes(capi):
+    """argmax / argmin give i64 (ops.zig:931-934); an i64 operand against a
+    float gives the float type, two i64 operands only a predicate
+    (DType.promote, dtype.zig:89-104; binaryOutDType, ops.zig:275-285)."""
+    import zpu_b200 as zc
+    F = zc.F32
+    args = [(1, F, (8, 10)), (2, zc.DT_I64, (8,)), (3, F, (8,))]
+    p = zc.Plan(args, [], [("argmax", [1], 10, 1, 0), ("eq", [10, 2], 11, -2, 0), ("mul", [10, 3], 12, -2, 0),
+                           ("gt", [12, 3], 13, -2, 0)], [10, 11, 12, 13])
+    assert p.outputs == [(zc.DT_I64, (8,)), (zc.DT_BOOL, (8,)), (F, (8,)), (zc.DT_BOOL, (8,))]
+    assert "bytecode" in p.describe()
+    for bad in [("add", [10, 2], 11, -2, 0), ("neg", [10], 11, -2, 0), ("sum", [10], 11, -2, 0),
+                ("where", [2, 10, 10], 11, -2, 0)]:
+        with pytest.raises(zc.ZpuCudaError) as e:
+            zc.Plan(args, [], [("argmax", [1], 10, 1, 0), bad], [11])
+        assert e.value.name == "NotSupported", bad
+
+
 def test_abi_struct_layouts_match_the_header(capi, tmp_path):
     """Every struct the ctypes binding mirrors has the header's size and
     field offsets (a C probe compiled here with gcc)."""

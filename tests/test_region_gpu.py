@@ -561,13 +561,37 @@ def test_any_all_match_the_oracle(zc, prim, axis, keep):
     assert np.array_equal(c.cpu().numpy(), zo.reduce_bool(m & (x != 0), prim, axis, keep))
 
 
-def test_i64_operands_are_refused(zc):
-    """eq(argmax(logits, 1), labels): an i64 value feeding a comparison is
-    outside the lowering, which says so (NotSupported) at creation."""
-    with pytest.raises(zc.ZpuCudaError) as e:
-        zc.Plan([(1, zc.F32, (8, 10)), (2, zc.F32, (8,))], [],
-                [("argmax", [1], 10, 1, 0), ("eq", [10, 2], 11, -2, 0)], [11])
-    assert e.value.status == 9
+def test_i64_operands_follow_zpus_promotion(zc):
+    """eq(argmax(logits, 1), labels) -- a classifier's hits -- and i64
+    values against floats: argmax's i64 result feeds the next region as an
+    input read as zpu reads it (readAtF64), each result typed by
+    DType.promote / binaryOutDType (dtype.zig:89-104, ops.zig:275-285);
+    arithmetic of two i64 values (an i64 result) stays outside the lowering."""
+    logits = zo.uniform_range(71, 64 * 10, -3.0, 3.0).reshape(64, 10).astype(np.float32)
+    lab = (np.arange(64, dtype=np.int64) * 7) % 10
+    scale = zo.uniform_range(72, 64, -2.0, 2.0).astype(np.float32)
+    F = zc.F32
+    steps = [("argmax", [1], 10, 1, 0), ("eq", [10, 2], 11, -2, 0), ("cast_op", [11], 12, zc.F32, 0),
+             ("sum", [12], 13, -2, 0), ("mul", [10, 3], 14, -2, 0), ("ge", [10, 3], 15, -2, 0)]
+    p = zc.Plan([(1, F, (64, 10)), (2, zc.DT_I64, (64,)), (3, F, (64,))], [], steps, [10, 11, 13, 14, 15])
+    am, hit, nhit, prod, ge = [o.cpu().numpy() for o in p.run([torch.from_numpy(v).cuda() for v in (logits, lab, scale)])]
+    want = zo.arg_reduce(logits, 1, want_max=True)
+    assert np.array_equal(am, want)
+    assert hit.dtype == np.bool_ and np.array_equal(hit, want == lab) and 0 < hit.sum() < 64
+    assert float(nhit) == float(np.sum(want == lab))
+    wide = want.astype(np.float64)
+    assert prod.dtype == np.float32 and np.array_equal(prod, (wide * scale.astype(np.float64)).astype(np.float32))
+    assert np.array_equal(ge, wide >= scale.astype(np.float64))
+    # two i64 values: compared in f64, exact beyond 2^24
+    x = np.array([2 ** 40 + 1, 2 ** 40, -(2 ** 30) - 3, 5], dtype=np.int64)
+    y = np.array([2 ** 40, 2 ** 40, -(2 ** 30) - 2, 5], dtype=np.int64)
+    q = zc.Plan([(1, zc.DT_I64, (4,)), (2, zc.DT_I64, (4,))], [],
+                [("eq", [1, 2], 10, -2, 0), ("lt", [1, 2], 11, -2, 0)], [10, 11])
+    e, l = [o.cpu().numpy() for o in q.run([torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()])]
+    assert e.tolist() == [False, True, False, True] and l.tolist() == [False, False, True, False]
+    with pytest.raises(zc.ZpuCudaError) as err:
+        zc.Plan([(1, zc.DT_I64, (4,)), (2, zc.DT_I64, (4,))], [], [("add", [1, 2], 10, -2, 0)], [10])
+    assert err.value.status == 9
 
 
 REVERSE = 32  # prims.Attrs.REVERSE

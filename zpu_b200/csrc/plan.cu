@@ -344,11 +344,17 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         // (truthiness v != 0, ops.zig:516, 572-590, 845-853)
         const bool takes_bool = pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim) ||
                                 st.prim == PRIM_WHERE;
+        // i64 values (argmax / argmin results, i64 arguments) enter binary
+        // steps: against a float the result is the float type, against
+        // another i64 only a predicate (DType.promote / binaryOutDType,
+        // dtype.zig:89-104, ops.zig:275-285: floats win, the element is
+        // computed from both operands read as f64)
         for (int k = 0; k < st.n_inputs && (region_unary(st.prim) || region_binary(st.prim) ||
                                             region_reduce(st.prim) || st.prim == PRIM_WHERE);
              k++) {
             const int dt = vals[st.ins[k]].dtype;
-            const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0));
+            const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0)) ||
+                            (dt == ZPUCUDA_I64 && region_binary(st.prim));
             if (!ok) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a value of dtype " + std::to_string(dt));
         }
         if (pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim)) o.dtype = ZPUCUDA_BOOL;
@@ -356,9 +362,14 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             o.shape = a.shape;
         } else if (region_binary(st.prim) && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
+            const bool int_and_float = (a.dtype == ZPUCUDA_I64 && float_dtype(b.dtype)) ||
+                                       (b.dtype == ZPUCUDA_I64 && float_dtype(a.dtype));
             if (!carriers_agree(carrier_of(a.dtype), carrier_of(b.dtype)) ||
-                (math_binary(st.prim) && a.dtype != b.dtype))
+                (math_binary(st.prim) && a.dtype != b.dtype && !int_and_float))
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
+            if (math_binary(st.prim) && a.dtype == ZPUCUDA_I64 && b.dtype == ZPUCUDA_I64)
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " of two i64 values (an i64 result)");
+            if (math_binary(st.prim) && int_and_float) o.dtype = float_dtype(a.dtype) ? a.dtype : b.dtype;
             if (a.depth != b.depth && a.shape.rank && b.shape.rank)
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "vmap depth mismatch in an element-wise step");
             o.depth = std::max(a.depth, b.depth);
@@ -1038,7 +1049,14 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             }
             break;
         }
-        if (rdtype < 0) rdtype = ZPUCUDA_F32;  // only bools: carried as f32
+        if (rdtype < 0) {
+            // no float value: bools ride as f32; i64 operands (predicates of
+            // two i64 values) are compared in f64, exact below 2^53
+            bool any_i64 = false;
+            for (int m : member)
+                for (int k = 0; k < steps[m].n_inputs; k++) any_i64 |= vals[steps[m].ins[k]].dtype == ZPUCUDA_I64;
+            rdtype = any_i64 ? ZPUCUDA_F64 : ZPUCUDA_F32;
+        }
         if (member.empty()) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "step " + std::to_string(s) + " cannot start a region");
         P.dtype = rdtype;
         P.rank = rshape.rank;
@@ -1063,9 +1081,10 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         for (int k = 0; k < P.n_in; k++) {
             Value &iv = vals[loads[k]];
             if (!iv.materialised) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "region input not materialised");
-            if (iv.dtype != rdtype && iv.dtype != ZPUCUDA_BOOL)
+            if (iv.dtype != rdtype && iv.dtype != ZPUCUDA_BOOL && iv.dtype != ZPUCUDA_I64)
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in a region");
             P.in_bool[k] = iv.dtype == ZPUCUDA_BOOL;
+            P.in_i64[k] = iv.dtype == ZPUCUDA_I64;
             reg[loads[k]] = k;
             P.insn[k] = Insn{OPC_LOAD, (uint8_t)k, (uint8_t)k, 0};
             L.ins.push_back(iv.slot);
@@ -1211,7 +1230,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         }
         L.signature = sig;
         bool any_bool = false;
-        for (int k = 0; k < P.n_in; k++) any_bool |= P.in_bool[k] != 0;
+        for (int k = 0; k < P.n_in; k++) any_bool |= P.in_bool[k] != 0 || P.in_i64[k] != 0;
         for (int o = 0; o < P.n_out; o++) any_bool |= P.out_bool[o] != 0;
         const bool catalogue_shape = ((!has_red && P.n_out == 1) || (has_red && P.reduce == RED_SUM && P.reduce_all && P.n_out == 0)) &&
                                      kinds.find_first_of("RG") == std::string::npos && !any_bool;

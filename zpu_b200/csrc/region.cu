@@ -192,6 +192,7 @@ __device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io,
     }
     }
     if (p.in_bool[k]) return ((const uint8_t *)io.in[k])[off] ? (T)1 : (T)0;
+    if (p.in_i64[k]) return (T)__ll2double_rn(((const long long *)io.in[k])[off]);
     return ((const T *)io.in[k])[off];
 }
 

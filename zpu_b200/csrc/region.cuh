@@ -62,6 +62,10 @@ struct RegionProgram {
     // outputs store (v != 0) as a byte.
     uint8_t in_bool[RP_MAX_IN];
     uint8_t out_bool[RP_MAX_OUT];
+    // i64 inputs (argmax / argmin results, i64 arguments) load as int64 and
+    // convert to the region's float type, as zpu reads them (readAtF64):
+    // exact below 2^24 in an f32 region, below 2^53 in an f64 one.
+    uint8_t in_i64[RP_MAX_IN];
 };
 
 // Launch-time arguments of a region kernel.
