@@ -121,17 +121,21 @@ def test_lowering_rejects_unsupported_prims(capi):
 
 def test_lowering_types_i64_operands_as_zpu_promotes(capi):
     """argmax / argmin give i64 (ops.zig:931-934); an i64 operand against a
-    float gives the float type, two i64 operands only a predicate
-    (DType.promote, dtype.zig:89-104; binaryOutDType, ops.zig:275-285)."""
+    float gives the float type; i64 operands alone give i64, f32 for the
+    float-only prims and div, bool for predicates (DType.promote,
+    dtype.zig:89-104; unaryOutDType / binaryOutDType, ops.zig:268-285)."""
     import zpu_b200 as zc
-    F = zc.F32
-    args = [(1, F, (8, 10)), (2, zc.DT_I64, (8,)), (3, F, (8,))]
+    F, I, B = zc.F32, zc.DT_I64, zc.DT_BOOL
+    args = [(1, F, (8, 10)), (2, I, (8,)), (3, F, (8,))]
     p = zc.Plan(args, [], [("argmax", [1], 10, 1, 0), ("eq", [10, 2], 11, -2, 0), ("mul", [10, 3], 12, -2, 0),
-                           ("gt", [12, 3], 13, -2, 0)], [10, 11, 12, 13])
-    assert p.outputs == [(zc.DT_I64, (8,)), (zc.DT_BOOL, (8,)), (F, (8,)), (zc.DT_BOOL, (8,))]
-    assert "bytecode" in p.describe()
-    for bad in [("add", [10, 2], 11, -2, 0), ("neg", [10], 11, -2, 0), ("sum", [10], 11, -2, 0),
-                ("where", [2, 10, 10], 11, -2, 0)]:
+                           ("gt", [12, 3], 13, -2, 0), ("add", [10, 2], 14, -2, 0), ("neg", [14], 15, -2, 0),
+                           ("exp", [10], 16, -2, 0), ("div", [10, 2], 17, -2, 0), ("sign", [2], 18, -2, 0)],
+                [10, 11, 12, 13, 14, 15, 16, 17, 18])
+    shp = (8,)
+    assert p.outputs == [(I, shp), (B, shp), (F, shp), (B, shp), (I, shp), (I, shp), (F, shp), (F, shp), (I, shp)]
+    d = p.describe()
+    assert "bytecode" in d and "to_i64" in d and "catalogue" not in d, d
+    for bad in [("pow", [10, 2], 11, -2, 0), ("sum", [10], 11, -2, 0), ("where", [2, 10, 10], 11, -2, 0)]:
         with pytest.raises(zc.ZpuCudaError) as e:
             zc.Plan(args, [], [("argmax", [1], 10, 1, 0), bad], [11])
         assert e.value.name == "NotSupported", bad

@@ -566,7 +566,7 @@ def test_i64_operands_follow_zpus_promotion(zc):
     values against floats: argmax's i64 result feeds the next region as an
     input read as zpu reads it (readAtF64), each result typed by
     DType.promote / binaryOutDType (dtype.zig:89-104, ops.zig:275-285);
-    arithmetic of two i64 values (an i64 result) stays outside the lowering."""
+    pow of two i64 values stays outside the lowering."""
     logits = zo.uniform_range(71, 64 * 10, -3.0, 3.0).reshape(64, 10).astype(np.float32)
     lab = (np.arange(64, dtype=np.int64) * 7) % 10
     scale = zo.uniform_range(72, 64, -2.0, 2.0).astype(np.float32)
@@ -589,9 +589,40 @@ def test_i64_operands_follow_zpus_promotion(zc):
                 [("eq", [1, 2], 10, -2, 0), ("lt", [1, 2], 11, -2, 0)], [10, 11])
     e, l = [o.cpu().numpy() for o in q.run([torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()])]
     assert e.tolist() == [False, True, False, True] and l.tolist() == [False, False, True, False]
-    with pytest.raises(zc.ZpuCudaError) as err:
-        zc.Plan([(1, zc.DT_I64, (4,)), (2, zc.DT_I64, (4,))], [], [("add", [1, 2], 10, -2, 0)], [10])
+    with pytest.raises(zc.ZpuCudaError) as err:  # pow of two i64 values: zpu's exact integer pow
+        zc.Plan([(1, zc.DT_I64, (4,)), (2, zc.DT_I64, (4,))], [], [("pow", [1, 2], 10, -2, 0)], [10])
     assert err.value.status == 9
+
+
+def test_i64_arithmetic_is_zpus_f64_compute_and_write_back(zc):
+    """Steps of i64 values alone: each element computed from the operands
+    read as f64 and written back as zpu writes an i64 (0 for NaN, clamp,
+    truncate; scalar.zig:7-27) -- recip(2) is 0 before it is multiplied;
+    div and the float-only prims give f32 (ops.zig:268-285)."""
+    a = np.array([7, -7, 2 ** 40 + 3, -(2 ** 52) + 1, 0, 9], dtype=np.int64)
+    b = np.array([2, 3, -5, 4, 1, -9], dtype=np.int64)
+    steps = [("add", [1, 2], 10, -2, 0), ("mul", [1, 2], 11, -2, 0), ("mod_op", [1, 2], 12, -2, 0),
+             ("recip", [2], 13, -2, 0), ("mul", [13, 1], 14, -2, 0), ("neg", [1], 15, -2, 0),
+             ("square", [2], 16, -2, 0), ("maximum", [1, 2], 17, -2, 0), ("sign", [1], 18, -2, 0),
+             ("div", [1, 2], 19, -2, 0), ("exp", [2], 20, -2, 0), ("ne", [15, 1], 21, -2, 0)]
+    p = zc.Plan([(1, zc.DT_I64, (6,)), (2, zc.DT_I64, (6,))], [], steps, list(range(10, 22)))
+    outs = [o.cpu().numpy() for o in p.run([torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()])]
+    af, bf = a.astype(np.float64), b.astype(np.float64)
+
+    def i64(v):
+        return zo.from_f64(v, np.int64)
+
+    rec = i64(zo.unary("recip", bf))
+    want = [i64(zo.binary("add", af, bf)), i64(zo.binary("mul", af, bf)), i64(zo.binary("mod_op", af, bf)), rec,
+            i64(zo.binary("mul", rec.astype(np.float64), af)), i64(zo.unary("neg", af)),
+            i64(zo.unary("square", bf)), i64(zo.binary("maximum", af, bf)), i64(zo.unary("sign", af))]
+    for k, w in enumerate(want):
+        assert outs[k].dtype == np.int64 and np.array_equal(outs[k], w), (steps[k], outs[k], w)
+    assert rec.tolist() == [0, 0, 0, 0, 1, 0] and outs[4].tolist() == [0, 0, 0, 0, 0, 0]
+    assert outs[9].dtype == np.float32
+    np.testing.assert_allclose(outs[9], zo.from_f64(zo.binary("div", af, bf), np.float32), rtol=2.4e-7)
+    np.testing.assert_allclose(outs[10], zo.from_f64(zo.unary("exp", bf), np.float32), rtol=4.8e-7)
+    assert outs[11].dtype == np.bool_ and outs[11].tolist() == [True, True, True, True, False, True]
 
 
 REVERSE = 32  # prims.Attrs.REVERSE

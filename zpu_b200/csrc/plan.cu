@@ -90,6 +90,13 @@ bool arg_reduce(int p) { return p == PRIM_ARGMAX || p == PRIM_ARGMIN; }
 bool bool_reduce(int p) { return p == PRIM_ANY || p == PRIM_ALL; }
 bool region_reduce(int p) { return (p >= PRIM_SUM && p <= PRIM_MIN_REDUCE) || arg_reduce(p) || bool_reduce(p); }
 bool float_dtype(int dt) { return dt == ZPUCUDA_F32 || dt == ZPUCUDA_F64; }
+// prims.isFloatOnly (src/zpu/prims.zig:229-234): of an integer value they
+// give f32 (unaryOutDType, ops.zig:268-273); div joins them for two integers
+// (binaryOutDType, ops.zig:275-285)
+bool float_only(int p) {
+    return (p >= 2 && p <= 7) || (p >= 10 && p <= 25) || p == 42 || p == 43;
+}
+constexpr int PRIM_DIV = 38, PRIM_POW = 39;
 // The movement prims a plan lowers as views (ops.zig:1343-1555).
 // flip / reverse mirror one axis (negative stride); copy and constant replay
 // as their input (ops.zig:2195-2198).
@@ -344,22 +351,25 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         // (truthiness v != 0, ops.zig:516, 572-590, 845-853)
         const bool takes_bool = pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim) ||
                                 st.prim == PRIM_WHERE;
-        // i64 values (argmax / argmin results, i64 arguments) enter binary
-        // steps: against a float the result is the float type, against
-        // another i64 only a predicate (DType.promote / binaryOutDType,
-        // dtype.zig:89-104, ops.zig:275-285: floats win, the element is
-        // computed from both operands read as f64)
+        // i64 values (argmax / argmin results, i64 arguments) enter
+        // element-wise steps, typed as zpu types them (DType.promote,
+        // dtype.zig:89-104: floats win; unaryOutDType / binaryOutDType,
+        // ops.zig:268-285): against a float the float type; of i64 values
+        // alone an i64, except the float-only prims and div (f32) and the
+        // predicates (bool).  Every element is computed from its operands
+        // read as f64; an i64 result is written back as zpu writes it.
         for (int k = 0; k < st.n_inputs && (region_unary(st.prim) || region_binary(st.prim) ||
                                             region_reduce(st.prim) || st.prim == PRIM_WHERE);
              k++) {
             const int dt = vals[st.ins[k]].dtype;
             const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0)) ||
-                            (dt == ZPUCUDA_I64 && region_binary(st.prim));
+                            (dt == ZPUCUDA_I64 && (region_binary(st.prim) || region_unary(st.prim)));
             if (!ok) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a value of dtype " + std::to_string(dt));
         }
         if (pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim)) o.dtype = ZPUCUDA_BOOL;
         if (region_unary(st.prim) && st.n_inputs == 1) {
             o.shape = a.shape;
+            if (a.dtype == ZPUCUDA_I64 && math_unary(st.prim)) o.dtype = float_only(st.prim) ? ZPUCUDA_F32 : ZPUCUDA_I64;
         } else if (region_binary(st.prim) && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
             const bool int_and_float = (a.dtype == ZPUCUDA_I64 && float_dtype(b.dtype)) ||
@@ -367,9 +377,15 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             if (!carriers_agree(carrier_of(a.dtype), carrier_of(b.dtype)) ||
                 (math_binary(st.prim) && a.dtype != b.dtype && !int_and_float))
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
-            if (math_binary(st.prim) && a.dtype == ZPUCUDA_I64 && b.dtype == ZPUCUDA_I64)
-                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " of two i64 values (an i64 result)");
             if (math_binary(st.prim) && int_and_float) o.dtype = float_dtype(a.dtype) ? a.dtype : b.dtype;
+            if (math_binary(st.prim) && a.dtype == ZPUCUDA_I64 && b.dtype == ZPUCUDA_I64) {
+                // pow of two integers: zpu's pow multiplies exactly for an
+                // integral exponent; the device's f64 pow may land an ulp
+                // below an integer, which the i64 write would truncate
+                if (st.prim == PRIM_POW)
+                    return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "pow of two i64 values");
+                o.dtype = (float_only(st.prim) || st.prim == PRIM_DIV) ? ZPUCUDA_F32 : ZPUCUDA_I64;
+            }
             if (a.depth != b.depth && a.shape.rank && b.shape.rank)
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "vmap depth mismatch in an element-wise step");
             o.depth = std::max(a.depth, b.depth);
@@ -1022,8 +1038,13 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         // first pass: which steps join
         // the float type a step computes in: its output's, else its inputs'
         auto step_carrier = [&](const zpucuda_step &st) {
+            // an i64 result, and a predicate of i64 values, are computed in
+            // f64 registers as zpu computes them: exact below 2^53
+            if (vals[st.out].dtype == ZPUCUDA_I64 && !region_reduce(st.prim)) return (int)ZPUCUDA_F64;
             int c = carrier_of(vals[st.out].dtype);
             for (int k = 0; k < st.n_inputs && c < 0; k++) c = carrier_of(vals[st.ins[k]].dtype);
+            for (int k = 0; k < st.n_inputs && c < 0; k++)
+                if (vals[st.ins[k]].dtype == ZPUCUDA_I64) c = ZPUCUDA_F64;
             return c;
         };
         for (; e < n_steps; e++) {
@@ -1156,6 +1177,12 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             else if (st.n_inputs > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b);
             else snprintf(buf, sizeof buf, ";r%d=%s(r%d)", nreg, prim_name(st.prim).c_str(), in.a);
             sig += buf;
+            if (vals[st.out].dtype == ZPUCUDA_I64) {
+                if (n_insn >= RP_MAX_INSN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
+                P.insn[n_insn++] = Insn{OPC_TO_I64, (uint8_t)nreg, (uint8_t)nreg, 0, 0};
+                snprintf(buf, sizeof buf, ";r%d=to_i64(r%d)", nreg, nreg);
+                sig += buf;
+            }
             reg[st.out] = nreg++;
         }
         (void)next_reg_after_loads;
@@ -1170,6 +1197,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             if (needed) {
                 if (P.n_out >= RP_MAX_OUT) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region has too many outputs");
                 P.out_bool[P.n_out] = vals[st.out].dtype == ZPUCUDA_BOOL;
+                P.out_i64[P.n_out] = vals[st.out].dtype == ZPUCUDA_I64;
                 P.out_reg[P.n_out++] = reg[st.out];
                 Slot sl = materialise(st.out);
                 if (sl.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
@@ -1231,7 +1259,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         L.signature = sig;
         bool any_bool = false;
         for (int k = 0; k < P.n_in; k++) any_bool |= P.in_bool[k] != 0 || P.in_i64[k] != 0;
-        for (int o = 0; o < P.n_out; o++) any_bool |= P.out_bool[o] != 0;
+        for (int o = 0; o < P.n_out; o++) any_bool |= P.out_bool[o] != 0 || P.out_i64[o] != 0;
         const bool catalogue_shape = ((!has_red && P.n_out == 1) || (has_red && P.reduce == RED_SUM && P.reduce_all && P.n_out == 0)) &&
                                      kinds.find_first_of("RG") == std::string::npos && !any_bool;
         L.cat = catalogue_shape ? catalogue_find(sig.c_str()) : nullptr;

@@ -196,11 +196,21 @@ __device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io,
     return ((const T *)io.in[k])[off];
 }
 
+// scalar.fromF64 to i64 followed by toF64 (src/zpu/scalar.zig:7-27).
+template <class T>
+__device__ __forceinline__ T to_i64_value(T v) {
+    if (isnan(v)) return (T)0;
+    const T lim = (T)9223372036854775808.0;  // 2^63
+    v = v < -lim ? -lim : (v > lim ? lim : v);
+    return trunc(v);
+}
+
 template <class T>
 __device__ __forceinline__ void eval(const RegionProgram &p, const RegionIO &io, int64_t i, T *r) {
     for (int k = 0; k < p.n_insn; k++) {
         const Insn in = p.insn[k];
         if (in.op == OPC_LOAD) r[in.dst] = load_in<T>(p, io, in.a, i);
+        else if (in.op == OPC_TO_I64) r[in.dst] = to_i64_value<T>(r[in.a]);
         else if (in.op == 55) r[in.dst] = r[in.a] != (T)0 ? r[in.b] : r[in.c];  // where: ops.zig:572-590
         else if (in.op < 35 || in.op == 54) r[in.dst] = un<T>(in.op, r[in.a]);
         else r[in.dst] = bin<T>(in.op, r[in.a], r[in.b]);
@@ -241,6 +251,7 @@ template <class T>
 __device__ __forceinline__ void store_outputs(const RegionProgram &p, const RegionIO &io, int64_t i, const T *r) {
     for (int o = 0; o < p.n_out; o++) {
         if (p.out_bool[o]) ((uint8_t *)io.out[o])[i] = r[p.out_reg[o]] != (T)0;
+        else if (p.out_i64[o]) ((long long *)io.out[o])[i] = __double2ll_rz((double)to_i64_value<T>(r[p.out_reg[o]]));
         else ((T *)io.out[o])[i] = r[p.out_reg[o]];
     }
 }

@@ -28,7 +28,13 @@ enum : int32_t {
     RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4, RED_ARGMAX = 5, RED_ARGMIN = 6,
     RED_ANY = 7, RED_ALL = 8  // bool results (ops.reduceBoolKernel)
 };
-enum : uint8_t { OPC_LOAD = 250 };
+enum : uint8_t {
+    OPC_LOAD = 250,
+    // after a step with an i64 result: the register takes the value zpu
+    // writes and reads back (writeF64 to i64, readAtF64): 0 for NaN, else
+    // clamped to [-2^63, 2^63] and truncated toward zero
+    OPC_TO_I64 = 251,
+};
 
 struct Insn {
     uint8_t op;  // prims.Prim code, or OPC_LOAD
@@ -66,6 +72,9 @@ struct RegionProgram {
     // convert to the region's float type, as zpu reads them (readAtF64):
     // exact below 2^24 in an f32 region, below 2^53 in an f64 one.
     uint8_t in_i64[RP_MAX_IN];
+    // i64 outputs store the register (already an i64 value, OPC_TO_I64) as
+    // int64; 2^63 saturates to maxInt(i64)
+    uint8_t out_i64[RP_MAX_OUT];
 };
 
 // Launch-time arguments of a region kernel.
