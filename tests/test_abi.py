@@ -135,7 +135,11 @@ def test_lowering_types_i64_operands_as_zpu_promotes(capi):
     assert p.outputs == [(I, shp), (B, shp), (F, shp), (B, shp), (I, shp), (I, shp), (F, shp), (F, shp), (I, shp)]
     d = p.describe()
     assert "bytecode" in d and "to_i64" in d and "catalogue" not in d, d
-    for bad in [("pow", [10, 2], 11, -2, 0), ("sum", [10], 11, -2, 0), ("where", [2, 10, 10], 11, -2, 0)]:
+    w = zc.Plan(args + [(4, B, (8,))], [], [("argmax", [1], 10, 1, 0), ("where", [4, 2, 10], 11, -2, 0),
+                                            ("where", [4, 2, 3], 12, -2, 0)], [10, 11, 12])
+    assert w.outputs == [(I, shp), (I, shp), (F, shp)]
+    for bad in [("pow", [10, 2], 11, -2, 0), ("sum", [10], 11, -2, 0), ("where", [2, 10, 10], 11, -2, 0),
+                ("where", [3, 10, 2], 11, -2, 0)]:
         with pytest.raises(zc.ZpuCudaError) as e:
             zc.Plan(args, [], [("argmax", [1], 10, 1, 0), bad], [11])
         assert e.value.name == "NotSupported", bad

@@ -598,7 +598,8 @@ def test_i64_arithmetic_is_zpus_f64_compute_and_write_back(zc):
     """Steps of i64 values alone: each element computed from the operands
     read as f64 and written back as zpu writes an i64 (0 for NaN, clamp,
     truncate; scalar.zig:7-27) -- recip(2) is 0 before it is multiplied;
-    div and the float-only prims give f32 (ops.zig:268-285)."""
+    div and the float-only prims give f32 (ops.zig:268-285); where takes
+    the promoted type of its branches."""
     a = np.array([7, -7, 2 ** 40 + 3, -(2 ** 52) + 1, 0, 9], dtype=np.int64)
     b = np.array([2, 3, -5, 4, 1, -9], dtype=np.int64)
     steps = [("add", [1, 2], 10, -2, 0), ("mul", [1, 2], 11, -2, 0), ("mod_op", [1, 2], 12, -2, 0),
@@ -623,6 +624,14 @@ def test_i64_arithmetic_is_zpus_f64_compute_and_write_back(zc):
     np.testing.assert_allclose(outs[9], zo.from_f64(zo.binary("div", af, bf), np.float32), rtol=2.4e-7)
     np.testing.assert_allclose(outs[10], zo.from_f64(zo.unary("exp", bf), np.float32), rtol=4.8e-7)
     assert outs[11].dtype == np.bool_ and outs[11].tolist() == [True, True, True, True, False, True]
+    # where: DType.promote of the branches (ops.zig:572-576)
+    c = np.array([True, False, True, False, True, False])
+    x = np.array([0.5, -1.5, 2.0, 3.25, -4.0, 9.5], dtype=np.float32)
+    q = zc.Plan([(1, zc.DT_I64, (6,)), (2, zc.DT_I64, (6,)), (3, zc.DT_BOOL, (6,)), (4, zc.F32, (6,))], [],
+                [("where", [3, 1, 2], 10, -2, 0), ("where", [3, 1, 4], 11, -2, 0)], [10, 11])
+    w1, w2 = [o.cpu().numpy() for o in q.run([torch.from_numpy(v).cuda() for v in (a, b, c, x)])]
+    assert w1.dtype == np.int64 and np.array_equal(w1, np.where(c, a, b))
+    assert w2.dtype == np.float32 and np.array_equal(w2, np.where(c, zo.from_f64(af, np.float32), x))
 
 
 REVERSE = 32  # prims.Attrs.REVERSE

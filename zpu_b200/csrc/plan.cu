@@ -363,7 +363,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
              k++) {
             const int dt = vals[st.ins[k]].dtype;
             const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0)) ||
-                            (dt == ZPUCUDA_I64 && (region_binary(st.prim) || region_unary(st.prim)));
+                            (dt == ZPUCUDA_I64 && (region_binary(st.prim) || region_unary(st.prim) ||
+                                                   (st.prim == PRIM_WHERE && k > 0)));
             if (!ok) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a value of dtype " + std::to_string(dt));
         }
         if (pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim)) o.dtype = ZPUCUDA_BOOL;
@@ -391,14 +392,19 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             o.depth = std::max(a.depth, b.depth);
             if (!broadcast(a.shape, b.shape, &o.shape)) return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
         } else if (st.prim == PRIM_WHERE && st.n_inputs == 3) {
-            // where(cond, a, b): a / b broadcast, then with cond; a's type
+            // where(cond, a, b): a / b broadcast, then with cond; the type
+            // DType.promote(a, b) (ops.zig:572-576): i64 when both are i64,
+            // else the float one
             const Value &x = vals[st.ins[1]], &y = vals[st.ins[2]];
-            if (x.dtype != y.dtype || !carriers_agree(carrier_of(a.dtype), x.dtype))
+            const bool xi = x.dtype == ZPUCUDA_I64, yi = y.dtype == ZPUCUDA_I64;
+            const int odt = (xi && yi) ? ZPUCUDA_I64 : xi ? y.dtype : x.dtype;
+            if ((!xi && !yi && x.dtype != y.dtype) ||
+                !carriers_agree(carrier_of(a.dtype), odt == ZPUCUDA_I64 ? ZPUCUDA_F64 : odt))
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in where");
             Shape xy;
             if (!broadcast(x.shape, y.shape, &xy) || !broadcast(xy, a.shape, &o.shape))
                 return lower_fail(plan, ZPUCUDA_ERR_SHAPE_MISMATCH, "broadcast");
-            o.dtype = x.dtype;
+            o.dtype = odt;
             o.depth = std::max(a.depth, std::max(x.depth, y.depth));
         } else if (region_reduce(st.prim) && st.n_inputs == 1) {
             // ops.reduceOutShape (src/zpu/ops.zig:644-660); argmax / argmin
