@@ -174,10 +174,12 @@ template <bool TA, bool TB, int VEC>
 int launch(const double *A, const double *B, double *C, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
            int64_t ldc, const GemmBatch &bt, int64_t stride_c, int64_t batches, cudaStream_t s) {
     auto kern = dgemm_kernel<TA, TB, VEC>;
-    static bool attr_set = false;
-    if (!attr_set) {
+    // the attribute belongs to the current device: set once per device
+    static bool attr[64] = {false};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64 || !attr[dev]) {
         ZC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES));
-        attr_set = true;
+        if (dev >= 0 && dev < 64) attr[dev] = true;
     }
     dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM), (unsigned)batches);
     kern<<<grid, THREADS, SMEM_BYTES, s>>>(A, B, C, m, n, k, lda, ldb, ldc, bt, stride_c);

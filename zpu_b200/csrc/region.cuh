@@ -568,10 +568,12 @@ int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s)
     if (SUM && BULK) {
         auto k = fused_sum_bulk_kernel<F>;
         const size_t smem = (size_t)kBulkStages * FullInputs<F>::N * kBulkTile * sizeof(float);
-        static bool attr = false;
-        if (!attr) {
+        // the attribute belongs to the current device: set once per device
+        static bool attr[64] = {false};
+        const int dev = current_device();
+        if (dev < 0 || dev >= 64 || !attr[dev]) {
             ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attr = true;
+            if (dev >= 0 && dev < 64) attr[dev] = true;
         }
         int per_sm = bulk_blocks_per_sm();
         const int fit = (int)((220u * 1024u) / (smem + 1024));
