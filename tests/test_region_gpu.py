@@ -202,6 +202,42 @@ def test_bytecode_binary_within_4ulp(zc, prim):
     assert ulp_diff_f32(got.cpu().numpy(), want).max() <= 4, prim
 
 
+@pytest.mark.parametrize("n", [1, 4099, (1 << 22) + 5])
+@pytest.mark.parametrize("region", ["sq", "dot", "ident", "affine"])
+def test_catalogue_hbm_bound_full_sums(zc, region, n):
+    """Full sums of the catalogued regions without a transcendental step
+    (x*x, x*y, x, x*a + b) stream through the bulk-copy pipeline kernel
+    (16 KiB tiles, plain loads past the last whole tile).  Integer-valued
+    inputs keep every partial sum exact, so the result is the exact sum: an
+    element dropped or counted twice shows."""
+    g = np.random.default_rng(n * 7 + len(region))
+    x = g.integers(-2, 3, n).astype(np.float32)
+    y = g.integers(-1, 2, n).astype(np.float32)
+    F = zc.F32
+    xd = x.astype(np.float64)
+    blobs, ins = [], [x]
+    if region == "sq":
+        steps, want = [("mul", [1, 1], 10, -2, 0), ("sum", [10], 11, -2, 0)], np.sum(xd * xd)
+    elif region == "dot":
+        steps, want = [("mul", [1, 2], 10, -2, 0), ("sum", [10], 11, -2, 0)], np.sum(xd * y.astype(np.float64))
+        ins = [x, y]
+    elif region == "ident":
+        steps, want = [("sum", [1], 11, -2, 0)], np.sum(xd)
+    else:
+        blobs = [(3, np.float32(2.0)), (4, np.float32(-1.0))]
+        steps = [("mul", [1, 3], 10, -2, 0), ("add", [10, 4], 12, -2, 0), ("sum", [12], 11, -2, 0)]
+        want = np.sum(2.0 * xd - 1.0)
+    args = [(k + 1, F, (n,)) for k in range(len(ins))]
+    p = zc.Plan(args, blobs, steps, [11])
+    # the front end passes a scalar blob as shape (1,): at n = 1 it has the
+    # region's shape and loads as a full input, which no catalogue entry
+    # takes, so that plan runs in the bytecode interpreter
+    if not (region == "affine" and n == 1):
+        assert ("catalogue %s+sum" % region) in p.describe(), p.describe()
+    (got,) = p.run([torch.from_numpy(v).cuda() for v in ins])
+    assert float(got.cpu()) == want
+
+
 def test_row_broadcast_and_row_reductions(zc):
     rows, cols = 37, 129
     x = zo.uniform_range(9, rows * cols, -2, 2).reshape(rows, cols)
