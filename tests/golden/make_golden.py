@@ -19,6 +19,12 @@ CASES = {
     # name -> (snapshot path, tolerance from tests/snap/zpu.zig)
     "linalg/matmul-3x3": 1e-9,     # tests/snap/zpu.zig:118
     "linalg/matvec": 1e-9,         # tests/snap/zpu.zig:119
+    "linalg/norm": 1e-9,           # tests/snap/zpu.zig:124 (sqrt(sum(square(a))))
+    "linalg/trace": 1e-9,          # tests/snap/zpu.zig:125 (sum of the diagonal)
+    "linalg/diag": 1e-9,           # tests/snap/zpu.zig:126
+    "linalg/outer": 1e-9,          # tests/snap/zpu.zig:127 (expandDims(a, -1) * b)
+    "linalg/dot": 1e-9,            # tests/snap/zpu.zig:128 (sum(mul(b, b), -1))
+    "nn/layer-norm": 1e-9,         # tests/snap/zpu.zig:151 (nn.zig:202-222)
     "transforms/vmap": 1e-9,       # tests/snap/zpu.zig:279
     "transforms/jit-replay": 1e-9, # tests/snap/zpu.zig:288
     "reduce/sum-all": 1e-9,        # tests/snap/zpu.zig:85
@@ -103,6 +109,14 @@ def main(ref):
         "spread12": spread(12),
         # tests/snap/zpu.zig:137-141
         "logits3x3": [1.0, 2.0, 3.0, -1.0, 0.0, 0.5, 2.5, -2.5, 0.0],
+        # tests/snap/zpu.zig:127 (outer of [1, 2] and [3, 4, 5])
+        "outer_a": [1.0, 2.0],
+        "outer_b": [3.0, 4.0, 5.0],
+        # tests/snap/zpu.zig:145-151: layerNorm(rows [2, 3], ones(3), bias, 1e-5, -1)
+        "ln_rows": [1.0, 2.0, 3.0, 4.0, 5.0, 6.0],
+        "ln_weight": [1.0, 1.0, 1.0],
+        "ln_bias": [0.5, -0.5, 1.0],
+        "ln_eps": 1e-5,
         # tests/snap/zpu.zig:267-276 (shape [3,2,2] each); f = tanh(matmul(a, b))
         "vmap_a": [1, 2, 3, 4, 0.5, -1, 2, 0.25, 2, 0, -1, 1],
         "vmap_b": [1, 0, 0, 1, 2, -1, 0.5, 1, -1, 1, 1, 0],

@@ -163,6 +163,39 @@ def test_softmax_snapshots(golden):
     snap_close(want, sm, tol)
 
 
+def test_linalg_and_layer_norm_snapshots(golden):
+    """tests/snap/zpu.zig:124-128, 151: compositions of the path's prims as
+    zpu writes them -- norm = sqrt(sum(square(a))), trace = sum(diag(a)),
+    outer = expandDims(a, -1) * b, dot = sum(mul(b, b), -1)
+    (linalg.zig:397-459) and layerNorm (nn.zig:202-222: mean, sub, square,
+    mean, add eps, sqrt, div, mul weight, add bias) -- through the oracle's
+    reductions and f64 element-wise rules."""
+    inp = golden["inputs"]
+    a = np.array(inp["spd3"], dtype=np.float64).reshape(3, 3)
+    b = np.array(inp["rhs3"], dtype=np.float64)
+    d = np.ascontiguousarray(np.diagonal(a))
+    got = {
+        "norm": zo.unary("sqrt", np.asarray(zo.reduce_axis(zo.unary("square", a), "sum"))),
+        "trace": zo.reduce_axis(d, "sum", -1),
+        "diag": d,
+        "outer": zo.binary("mul", np.array(inp["outer_a"])[:, None], np.array(inp["outer_b"])),
+        "dot": zo.reduce_axis(zo.binary("mul", b, b), "sum", -1),
+    }
+    for name, g in got.items():
+        want, tol, shape = snap(golden, "zpu/linalg/" + name)
+        assert list(np.shape(g)) == shape, (name, np.shape(g), shape)
+        snap_close(want, g, tol)
+    x = np.array(inp["ln_rows"], dtype=np.float64).reshape(2, 3)
+    w, bias = np.array(inp["ln_weight"]), np.array(inp["ln_bias"])
+    c = zo.binary("sub", x, zo.mean(x, -1, True))
+    v = zo.mean(zo.unary("square", c), -1, True)
+    den = zo.unary("sqrt", zo.binary("add", v, np.float64(inp["ln_eps"])))
+    ln = zo.binary("add", zo.binary("mul", zo.binary("div", c, den), w), bias)
+    want, tol, shape = snap(golden, "zpu/nn/layer-norm")
+    assert list(ln.shape) == shape
+    snap_close(want, ln, tol)
+
+
 def test_adam_snapshots(golden):
     inp = golden["inputs"]
     p = np.array(inp["adam_params"], dtype=np.float64)
