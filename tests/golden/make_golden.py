@@ -25,6 +25,11 @@ CASES = {
     "linalg/outer": 1e-9,          # tests/snap/zpu.zig:127 (expandDims(a, -1) * b)
     "linalg/dot": 1e-9,            # tests/snap/zpu.zig:128 (sum(mul(b, b), -1))
     "nn/layer-norm": 1e-9,         # tests/snap/zpu.zig:151 (nn.zig:202-222)
+    "grad/arg0": 1e-9,             # tests/snap/zpu.zig:196-202: grad of
+    "grad/arg1": 1e-9,             #   sum(softmax(sigmoid(x.w) + b) * target)
+    "grad/arg2": 1e-9,             #   w.r.t. x, w, b
+    "grad/jvp-value": 1e-9,        # tests/snap/zpu.zig:217 (the function's value)
+    "grad/jvp-tangent": 1e-9,      # tests/snap/zpu.zig:218 (J.v along a tangent of x)
     "transforms/vmap": 1e-9,       # tests/snap/zpu.zig:279
     "transforms/jit-replay": 1e-9, # tests/snap/zpu.zig:288
     "reduce/sum-all": 1e-9,        # tests/snap/zpu.zig:85
@@ -117,6 +122,12 @@ def main(ref):
         "ln_weight": [1.0, 1.0, 1.0],
         "ln_bias": [0.5, -0.5, 1.0],
         "ln_eps": 1e-5,
+        # tests/snap/zpu.zig:190-193, 209: x [2, 3], w [3, 2], b [2], target [2, 2], tangent of x
+        "grad_x": [0.5, -1.0, 2.0, 0.25, -0.5, 1.5],
+        "grad_w": [1.0, -1.0, 0.5, 0.25, 2.0, -0.5],
+        "grad_b": [0.1, -0.2],
+        "grad_target": [1.0, 0.0, 0.25, 0.75],
+        "grad_tangent": [0.3, -0.7, 0.2, 0.4, -0.1, 0.6],
         # tests/snap/zpu.zig:267-276 (shape [3,2,2] each); f = tanh(matmul(a, b))
         "vmap_a": [1, 2, 3, 4, 0.5, -1, 2, 0.25, 2, 0, -1, 1],
         "vmap_b": [1, 0, 0, 1, 2, -1, 0.5, 1, -1, 1, 1, 0],

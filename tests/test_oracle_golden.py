@@ -196,6 +196,36 @@ def test_linalg_and_layer_norm_snapshots(golden):
     snap_close(want, ln, tol)
 
 
+def test_grad_snapshots(golden):
+    """tests/snap/zpu.zig:172-218: the gradient of
+    sum(softmax(sigmoid(x.w) + b) * target) w.r.t. x, w and b, and its jvp
+    along a tangent of x, through the reverse-sweep rules the MLP step uses:
+    the matmul VJPs g.W^T and X^T.g (autodiff.zig:480-487, the oracle's
+    matmul), b's broadcast undone by a sum over the rows (unbroadcast,
+    autodiff.zig:51), and the element-wise and softmax VJPs."""
+    inp = golden["inputs"]
+    x = np.array(inp["grad_x"], dtype=np.float64).reshape(2, 3)
+    w = np.array(inp["grad_w"], dtype=np.float64).reshape(3, 2)
+    b = np.array(inp["grad_b"], dtype=np.float64)
+    t = np.array(inp["grad_target"], dtype=np.float64).reshape(2, 2)
+    tangent = np.array(inp["grad_tangent"], dtype=np.float64).reshape(2, 3)
+    h = zo.unary("sigmoid", zo.matmul(x, w))
+    _, p = _log_softmax_rows(zo.binary("add", h, b))
+    value = zo.reduce_sum(zo.binary("mul", p, t))
+    gz = p * (t - zo.reduce_axis(p * t, "sum", -1, True))  # softmax VJP of d/dp = target
+    ga = gz * h * (1.0 - h)                                # sigmoid VJP
+    grads = [zo.matmul(ga, np.ascontiguousarray(w.T)), zo.matmul(np.ascontiguousarray(x.T), ga),
+             zo.reduce_axis(gz, "sum", 0)]
+    for i, g in enumerate(grads):
+        want, tol, shape = snap(golden, "zpu/grad/arg%d" % i)
+        assert list(g.shape) == shape, (i, g.shape, shape)
+        snap_close(want, g, tol)
+    want, tol, _ = snap(golden, "zpu/grad/jvp-value")
+    snap_close(want, [value], tol)
+    want, tol, _ = snap(golden, "zpu/grad/jvp-tangent")
+    snap_close(want, [zo.reduce_sum(grads[0] * tangent)], tol)
+
+
 def test_adam_snapshots(golden):
     inp = golden["inputs"]
     p = np.array(inp["adam_params"], dtype=np.float64)
