@@ -30,6 +30,7 @@ CASES = {
     "grad/arg2": 1e-9,             #   w.r.t. x, w, b
     "grad/jvp-value": 1e-9,        # tests/snap/zpu.zig:217 (the function's value)
     "grad/jvp-tangent": 1e-9,      # tests/snap/zpu.zig:218 (J.v along a tangent of x)
+    "nn/attention": 1e-9,          # tests/snap/zpu.zig:298-329 (softmax(q.k^T / 2).v, wq = wk = wv)
     "transforms/vmap": 1e-9,       # tests/snap/zpu.zig:279
     "transforms/jit-replay": 1e-9, # tests/snap/zpu.zig:288
     "reduce/sum-all": 1e-9,        # tests/snap/zpu.zig:85
@@ -128,6 +129,9 @@ def main(ref):
         "grad_b": [0.1, -0.2],
         "grad_target": [1.0, 0.0, 0.25, 0.75],
         "grad_tangent": [0.3, -0.7, 0.2, 0.4, -0.1, 0.6],
+        # tests/snap/zpu.zig:317-327: x [4, 3] and the one weight [3, 3]
+        "attn_x": [0.5, -1.0, 2.0, 1.0, 0.5, -0.5, -1.0, 2.0, 0.25, 0.0, 1.0, 1.0],
+        "attn_w": [1.0, 0.0, 0.5, 0.0, 1.0, -0.5, 0.5, 0.5, 1.0],
         # tests/snap/zpu.zig:267-276 (shape [3,2,2] each); f = tanh(matmul(a, b))
         "vmap_a": [1, 2, 3, 4, 0.5, -1, 2, 0.25, 2, 0, -1, 1],
         "vmap_b": [1, 0, 0, 1, 2, -1, 0.5, 1, -1, 1, 1, 0],

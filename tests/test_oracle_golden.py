@@ -226,6 +226,22 @@ def test_grad_snapshots(golden):
     snap_close(want, [zo.reduce_sum(grads[0] * tangent)], tol)
 
 
+def test_attention_snapshot(golden):
+    """tests/snap/zpu.zig:298-329: a self-attention block with one weight
+    for q, k and v -- matmuls, q.k^T through a transposed operand, a scalar
+    division and a row softmax."""
+    inp = golden["inputs"]
+    x = np.array(inp["attn_x"], dtype=np.float64).reshape(4, 3)
+    w = np.array(inp["attn_w"], dtype=np.float64).reshape(3, 3)
+    q = zo.matmul(x, w)
+    scores = zo.binary("div", zo.matmul(q, np.ascontiguousarray(q.T)), np.float64(2.0))
+    _, weights = _log_softmax_rows(scores)
+    got = zo.matmul(weights, q)
+    want, tol, shape = snap(golden, "zpu/nn/attention")
+    assert list(got.shape) == shape
+    snap_close(want, got, tol)
+
+
 def test_adam_snapshots(golden):
     inp = golden["inputs"]
     p = np.array(inp["adam_params"], dtype=np.float64)
