@@ -254,10 +254,13 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
 int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void *const *host_outs,
                           void *stream);
 int zpucuda_plan_output(const zpucuda_plan *plan, int i, zpucuda_value *value);
-/* Index errors of the plan's take / scatter_add launches (zpu's
- * IndexOutOfRange, ops.zig:1735-1741) since the last check: waits for the
- * stream (bounded) and returns ZPUCUDA_ERR_INDEX_OUT_OF_RANGE once for them,
- * else ZPUCUDA_OK.  zpucuda_plan_run_host checks by itself. */
+/* Device-side errors of the plan's launches since the last check: waits for
+ * the stream (bounded), then returns ZPUCUDA_ERR_TIMEOUT once when a fused
+ * reduction's bounded wait for its input copies ran out (that result is
+ * NaN), else ZPUCUDA_ERR_INDEX_OUT_OF_RANGE once for a take / scatter_add
+ * index out of range (zpu's IndexOutOfRange, ops.zig:1735-1741), else
+ * ZPUCUDA_OK; both flags are cleared.  zpucuda_plan_run_host checks by
+ * itself. */
 int zpucuda_plan_check(zpucuda_plan *plan, void *stream);
 int zpucuda_plan_num_steps(const zpucuda_plan *plan);   /* jit.Plan.numSteps */
 int zpucuda_plan_num_kernels(const zpucuda_plan *plan); /* launches per run */
@@ -335,7 +338,11 @@ int zpucuda_nccl_destroy(int64_t timeout_ms);
  *  loss: copies the last loss (f32) to dst (host or device) on `stream`.
  *  check: synchronous; ZPUCUDA_ERR_INDEX_OUT_OF_RANGE when a label of an
  *    earlier step was outside [0, d_out) (nn.oneHot's error; that row's
- *    one-hot row was zero), and clears the flag.
+ *    one-hot row was zero), and clears the flag; ZPUCUDA_ERR_TIMEOUT when a
+ *    peer's dW2 tiles did not arrive within the exchange's bounded wait
+ *    (that step's W2 update then used the previous step's gradient shard:
+ *    the parameters are stale and the run should be restarted from a saved
+ *    state), and clears that flag too.
  *  steps: Adam steps taken. */
 typedef struct zpucuda_mlp zpucuda_mlp;
 enum { ZPUCUDA_MLP_PARAM = 0, ZPUCUDA_MLP_GRAD = 1, ZPUCUDA_MLP_ADAM_M = 2, ZPUCUDA_MLP_ADAM_V = 3 };
@@ -375,6 +382,17 @@ int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h);
  * (side stream; -1 where a point was not reached, e.g. on one rank). */
 int zpucuda_mlp_trace(zpucuda_mlp *h, int on);
 int zpucuda_mlp_trace_read(zpucuda_mlp *h, float *ms, int n);
+/* Diagnostics, no counterpart in the reference: runs the owner-side step of
+ * the peer-memory dW2 exchange -- wait until every flag d_flags[0 .. world)
+ * holds at least `epoch`, then d_out[i] = sum over s in rank order of
+ * d_inbox[s * n + i] -- on caller buffers (n a multiple of 4, d_inbox and
+ * d_out 16-byte aligned).  The wait polls at most spin_limit times, about
+ * 256 ns apart; when it runs out the kernel sets *d_err to 1, writes nothing
+ * and returns, which is what zpucuda_mlp_check then reports as
+ * ZPUCUDA_ERR_TIMEOUT.  Lets a test make that bounded wait run out without a
+ * second GPU. */
+int zpucuda_debug_peer_reduce(const float *d_inbox, int world, int64_t n, float *d_out, const uint64_t *d_flags,
+                              uint64_t epoch, uint32_t spin_limit, uint32_t *d_err, void *stream);
 
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot

@@ -191,6 +191,52 @@ def matmul(a, b, a_depth=0, b_depth=0):
     return out
 
 
+def promote(a, b):
+    """DType.promote (src/zpu/dtype.zig:89-104) on numpy dtypes: floats win,
+    the wider float wins; mixed signedness takes the wider integer (the
+    second on a tie), otherwise the wider (the first on a tie)."""
+    a, b = np.dtype(a), np.dtype(b)
+    if a == b:
+        return a
+    fa, fb = a.kind == "f", b.kind == "f"
+    if fa and not fb:
+        return a
+    if fb and not fa:
+        return b
+    if fa and fb:
+        return a if a.itemsize >= b.itemsize else b
+    sa, sb = a.kind == "i", b.kind == "i"
+    if sa != sb:
+        return a if a.itemsize > b.itemsize else b
+    return a if a.itemsize >= b.itemsize else b
+
+
+def gemm_convert(a, b):
+    """ops.matmul of two row-major [.., m, k] @ [.., k, n] arrays whose types
+    are not both f32 or both f64 (same leading batch shape):
+     - same-type integers: ops.gemmTyped's loop (src/zpu/ops.zig:1016-1049),
+       the element type's wrapping sums (reduceStep, ops.zig:685-688);
+     - otherwise ops.gemmF64 (ops.zig:1284-1333): the output, of type
+       promote(a, b), starts at 0 and for p = 0 .. k-1 in order becomes
+       fromF64(toF64(out) + toF64(a[.., i, p]) * toF64(b[.., p, j])), the
+       product and the sum in f64 with no fused multiply-add.
+    A bool result (bool @ bool) is zpu's DTypeMismatch."""
+    a, b = np.asarray(a), np.asarray(b)
+    out_dt = promote(a.dtype, b.dtype)
+    if out_dt == np.bool_:
+        raise ValueError("DTypeMismatch")
+    k = a.shape[-1]
+    if a.dtype == b.dtype and a.dtype.kind in "iu":
+        prod = np.matmul(a.astype(np.int64), b.astype(np.int64))  # wraps modulo 2^64
+        return prod.astype(out_dt)  # and modulo 2^bits
+    af, bf = to_f64(a), to_f64(b)
+    acc = np.zeros(a.shape[:-1] + (b.shape[-1],), dtype=out_dt)
+    for p in range(k):
+        step = acc.astype(np.float64) + af[..., :, p:p + 1] * bf[..., p:p + 1, :]
+        acc = from_f64(step, out_dt)
+    return acc
+
+
 # --------------------------------------------------------------- elementwise/sum
 def unary(prim, x):
     L = lib()

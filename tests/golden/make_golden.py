@@ -2,7 +2,7 @@
 
 Run once, in a container that has the reference mounted:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the zpu checkout>
 
 It reads the reference's own snapshot files (snapshots/zpu/**.snap, written by
 `zig build test -Dupdate-snapshots`) and pairs each with the inputs that
@@ -220,4 +220,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the zpu checkout>")
+    main(sys.argv[1])

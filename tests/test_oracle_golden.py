@@ -264,6 +264,35 @@ def test_known_answer_matmuls(golden):
         assert np.allclose(got.ravel(), case["want"], rtol=case["tol"], atol=0), case["name"]
 
 
+def test_known_answer_matmuls_in_other_types(golden):
+    """The same known answers (src/zpu/tests.zig:145-171, small integers)
+    through the oracle's restatement of ops.gemmF64 and of the integer
+    gemmTyped loop: every element type pair whose promotion is not bool."""
+    types = [np.float64, np.float32, np.float16, np.int64, np.int32, np.int16, np.uint8]
+    for case in golden["known_answers"]:
+        a_shape, b_shape = case["a_shape"], case["b_shape"]
+        if len(a_shape) != 2 or len(b_shape) != 2:
+            continue
+        for ta in types:
+            for tb in types:
+                if ta == tb and ta in (np.float32, np.float64):
+                    continue
+                a = np.array(case["a"]).reshape(a_shape).astype(ta)
+                b = np.array(case["b"]).reshape(b_shape).astype(tb)
+                got = zo.gemm_convert(a, b)
+                assert got.dtype == zo.promote(ta, tb)
+                want = np.array(case["want"], dtype=np.float64)
+                if got.dtype == np.uint8:
+                    want = np.minimum(want, 255.0)  # zpu clamps (mixed) or wraps (u8 @ u8)
+                    if ta == tb:
+                        want = np.array(case["want"], dtype=np.int64) % 256
+                assert np.array_equal(got.ravel().astype(np.float64), want), (case["name"], ta, tb)
+    assert zo.promote(np.uint8, np.int8) == np.int8 and zo.promote(np.int8, np.uint8) == np.uint8
+    assert zo.promote(np.int16, np.uint8) == np.int16 and zo.promote(np.float16, np.int64) == np.float16
+    with pytest.raises(ValueError):
+        zo.gemm_convert(np.ones((2, 2), np.bool_), np.ones((2, 2), np.bool_))
+
+
 def test_gemm_vs_naive_kernel_shapes(golden):
     """kernels.zig:512-543."""
     for m, k, n in golden["gemm_shapes"]:

@@ -6,12 +6,16 @@ latency-critical loop where cudaMalloc's implicit synchronisation is not
 allowed.  zpucuda_chain_tanh_sq_affine_sum_noalloc serves them with a static
 scratch array inside the library.  This file checks, through the C ABI, that
 two calls in a row give the existing entry point's result (the lowered jit
-plan of the same chain) within the suite's sum tolerance.  It is named to run
-last, and passes both alone in a fresh process and after the other tests.
+plan of the same chain): the same kernel on the same grid, so the two agree
+bit for bit, and both lie within the suite's sum tolerance of the f64 sum.
+It is named to run last, and passes both alone in a fresh process and after
+the other tests.
 """
-import ctypes as C
+import os
+import struct
+import subprocess
+import sys
 
-import numpy as np
 import pytest
 
 from oracle import zpu_oracle as zo
@@ -41,12 +45,40 @@ def test_no_alloc_matches_plan_twice_in_a_row():
     tol = 1e-6 * zo.abssum_f64(t)
     assert abs(want - s64) <= tol
     stream = zc.stream_of()
+    bits = lambda v: struct.pack("<f", v)
     for call in range(2):
         out = torch.full((), float("nan"), dtype=torch.float32, device="cuda")
         zc.check(L.zpucuda_chain_tanh_sq_affine_sum_noalloc(x.data_ptr(), n, a.data_ptr(), b.data_ptr(),
                                                             out.data_ptr(), stream))
         got = float(out.cpu())
-        assert abs(got - want) <= tol, (call, got, want)
+        assert bits(got) == bits(want), (call, got, want)
+        assert abs(got - s64) <= tol
+
+
+_OVERSIZE = r"""
+import torch, zpu_b200 as zc
+zc.check(zc.lib().zpucuda_init(0))
+L = zc.lib()
+x = torch.zeros(1 << 20, dtype=torch.float32, device="cuda")
+s = torch.zeros((), dtype=torch.float32, device="cuda")
+st = L.zpucuda_chain_tanh_sq_affine_sum_noalloc(x.data_ptr(), x.numel(), s.data_ptr(), s.data_ptr(),
+                                                s.data_ptr(), zc.stream_of())
+print(zc._capi.STATUS[st])
+print(L.zpucuda_last_error().decode())
+"""
+
+
+def test_no_alloc_rejects_a_grid_beyond_its_scratch():
+    # 16 blocks per SM on 148 SMs needs 2368 block partials; the static
+    # scratch holds 2048, so the call must refuse instead of overrunning it
+    env = dict(os.environ, ZPUCUDA_REGION_BPS="16")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _OVERSIZE], env=env, cwd=root, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.strip().splitlines()
+    assert lines[-2] == "NotSupported", r.stdout
+    assert "block partials" in lines[-1] and "2048" in lines[-1], r.stdout
 
 
 def test_no_alloc_rejects_bad_arguments():

@@ -81,7 +81,7 @@ def tensor_desc(t, batch_depth=0):
     """zpucuda_tensor for a torch tensor view (strides in elements)."""
     d = Tensor()
     d.data = t.data_ptr()
-    d.dtype = dtype_code(t) if t.is_floating_point() and t.dtype != _torch().float16 else storage_code(t)
+    d.dtype = storage_code(t)
     d.rank = t.dim()
     for i in range(t.dim()):
         d.dims[i] = t.shape[i]
@@ -116,19 +116,23 @@ def tensor_copy(src, out, stream=None):
     return out
 
 
-def matmul_shape(a, b, a_depth=0, b_depth=0):
+def matmul_shape(a, b, a_depth=0, b_depth=0, with_dtype=False):
+    """Output shape and vmap depth of ops.matmul (and its zpu DType code,
+    DType.promote of the operands, when with_dtype)."""
     out = Tensor()
     check(lib().zpucuda_matmul_shape(C.byref(tensor_desc(a, a_depth)), C.byref(tensor_desc(b, b_depth)),
                                      C.byref(out)))
-    return tuple(out.dims[i] for i in range(out.rank)), out.batch_depth
+    shape = tuple(out.dims[i] for i in range(out.rank))
+    return (shape, out.batch_depth, out.dtype) if with_dtype else (shape, out.batch_depth)
 
 
 def matmul(a, b, a_depth=0, b_depth=0, out=None, stream=None):
-    """ops.matmul on device tensors (NumPy semantics, vmap depth)."""
+    """ops.matmul on device tensors (NumPy semantics, vmap depth); any of
+    zpu's element types, the result of type DType.promote(a, b)."""
     torch = _torch()
-    shape, depth = matmul_shape(a, b, a_depth, b_depth)
+    shape, depth, code = matmul_shape(a, b, a_depth, b_depth, with_dtype=True)
     if out is None:
-        out = torch.empty(shape, dtype=a.dtype, device=a.device)
+        out = torch.empty(shape, dtype=torch_dtype(code), device=a.device)
     da, db, dc = tensor_desc(a, a_depth), tensor_desc(b, b_depth), tensor_desc(out, depth)
     check(lib().zpucuda_matmul(C.byref(da), C.byref(db), C.byref(dc), stream_of(stream)))
     return out

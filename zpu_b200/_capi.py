@@ -140,6 +140,7 @@ SIGNATURES = {
     "zpucuda_mlp_exchange_mode": (I32, [P]),
     "zpucuda_mlp_trace": (I32, [P, I32]),
     "zpucuda_mlp_trace_read": (I32, [P, P, I32]),
+    "zpucuda_debug_peer_reduce": (I32, [P, I32, I64, P, P, U64, C.c_uint32, P, P]),
 }
 
 

@@ -74,5 +74,14 @@ int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t
 int gemm_f64_device(const double *A, const double *B, double *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                     int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                     cudaStream_t s);
+// DType.promote (src/zpu/dtype.zig:89-104) of two element types.
+int dtype_promote(int a, int b);
+// The products the tensor-core GEMMs do not take (mixed operand types, f16,
+// bool operands, same-type integers), with zpu's own arithmetic: ops.gemmF64
+// or the integer gemmTyped loop.  C is contiguous [m, n] per matrix of type
+// cdt = dtype_promote(adt, bdt).
+int gemm_convert_device(const void *A, int adt, const void *B, int bdt, void *C, int cdt, int64_t m, int64_t n,
+                        int64_t k, int64_t lda, int64_t ldb, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                        cudaStream_t s);
 
 }  // namespace zc

@@ -63,6 +63,7 @@ int expand(View &v, int axis) {
 }
 
 struct Plan {
+    int32_t out_dtype;  // DType.promote of the operands
     int64_t m, n, k;
     bool ta, tb;
     int64_t lda, ldb;
@@ -76,8 +77,11 @@ int plan_matmul(const zpucuda_tensor *ta_, const zpucuda_tensor *tb_, Plan *P) {
     if (!ta_ || !tb_ || !P) return ZPUCUDA_ERR_INVALID_ARGUMENT;
     if (ta_->rank == 0 || tb_->rank == 0) return ZPUCUDA_ERR_SHAPE_MISMATCH;
     if (ta_->rank > ZPUCUDA_MAX_RANK || tb_->rank > ZPUCUDA_MAX_RANK) return ZPUCUDA_ERR_RANK_TOO_LARGE;
-    if (ta_->dtype != tb_->dtype) return ZPUCUDA_ERR_NOT_SUPPORTED;  // zpu's gemmF64 mixed path
-    if (ta_->dtype != ZPUCUDA_F32 && ta_->dtype != ZPUCUDA_F64) return ZPUCUDA_ERR_NOT_SUPPORTED;
+    if (ta_->dtype < 0 || ta_->dtype > ZPUCUDA_BOOL || tb_->dtype < 0 || tb_->dtype > ZPUCUDA_BOOL)
+        return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    // binaryOutDType(.mul, a, b) (ops.zig:275-285): a bool result is an error
+    P->out_dtype = dtype_promote(ta_->dtype, tb_->dtype);
+    if (P->out_dtype == ZPUCUDA_BOOL) return ZPUCUDA_ERR_DTYPE_MISMATCH;
     View a = view_of(ta_), b = view_of(tb_);
     const int depth = std::max(a.depth, b.depth);
     int st;
@@ -165,8 +169,11 @@ int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tens
     if (out->rank != P.out_rank) return ZPUCUDA_ERR_SHAPE_MISMATCH;
     for (int i = 0; i < P.out_rank; i++)
         if (out->dims[i] != P.out_dims[i]) return ZPUCUDA_ERR_SHAPE_MISMATCH;
-    if (out->dtype != a->dtype) return ZPUCUDA_ERR_DTYPE_MISMATCH;
+    if (out->dtype != P.out_dtype) return ZPUCUDA_ERR_DTYPE_MISMATCH;
     // the output is contiguous: batch after batch of [m, n]
+    if (a->dtype != b->dtype || (a->dtype != ZPUCUDA_F32 && a->dtype != ZPUCUDA_F64))
+        return gemm_convert_device(a->data, a->dtype, b->data, b->dtype, out->data, out->dtype, P.m, P.n, P.k, P.lda,
+                                   P.ldb, P.ta, P.tb, P.batch, P.m * P.n, s);
     if (a->dtype == ZPUCUDA_F32)
         return gemm_f32_device((const float *)a->data, (const float *)b->data, (float *)out->data, P.m, P.n, P.k,
                                P.lda, P.ldb, P.n, P.ta, P.tb, P.batch, P.m * P.n, s);
@@ -183,7 +190,7 @@ int matmul_device_epi(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_
     int st = plan_matmul(a, b, &P);
     if (st) return st;
     if (!out || !out->data || !a->data || !b->data) return ZPUCUDA_ERR_INVALID_ARGUMENT;
-    if (a->dtype != ZPUCUDA_F32 || out->dtype != ZPUCUDA_F32 || batch_count(P.batch) != 1)
+    if (a->dtype != ZPUCUDA_F32 || b->dtype != ZPUCUDA_F32 || out->dtype != ZPUCUDA_F32 || batch_count(P.batch) != 1)
         return ZPUCUDA_ERR_NOT_SUPPORTED;
     if (out->rank != P.out_rank) return ZPUCUDA_ERR_SHAPE_MISMATCH;
     for (int i = 0; i < P.out_rank; i++)
@@ -206,7 +213,7 @@ int zpucuda_matmul_shape(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucu
     void *keep = out->data;
     memset(out, 0, sizeof *out);
     out->data = keep;
-    out->dtype = a->dtype;
+    out->dtype = P.out_dtype;
     out->rank = P.out_rank;
     out->batch_depth = P.out_depth;
     int64_t q = 1;

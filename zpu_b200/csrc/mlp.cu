@@ -294,15 +294,17 @@ __global__ void xfer_signal_kernel(const __grid_constant__ XferFlags f, int worl
 }
 
 // out[i] = sum over s of inbox[s * n + i], s in rank order, once every rank's
-// flag shows `epoch`; a wait that runs out sets *err and writes nothing.
+// flag shows `epoch`; a wait that runs out (spin_limit polls ~256 ns apart)
+// sets *err and writes nothing.
 __global__ void __launch_bounds__(256) xfer_reduce_kernel(const float4 *__restrict__ inbox, int world, int64_t n4,
                                                           float4 *__restrict__ out,
                                                           const unsigned long long *flags,
-                                                          unsigned long long epoch, unsigned int *err) {
+                                                          unsigned long long epoch, unsigned int *err,
+                                                          uint32_t spin_limit) {
     __shared__ int ready;
     if (threadIdx.x == 0) {
         int ok = 0;
-        for (uint32_t it = 0; it < kXferSpin && !ok; it++) {
+        for (uint32_t it = 0; it < spin_limit && !ok; it++) {
             ok = 1;
             for (int r = 0; r < world; r++) {
                 unsigned long long v;
@@ -642,7 +644,7 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
             if (blocks > (int64_t)num_sms() * 4) blocks = (int64_t)num_sms() * 4;
             xfer_reduce_kernel<<<(unsigned)blocks, 256, 0, side>>>(
                 (const float4 *)xfer_inbox(h, rank), world, n4, (float4 *)(h->grads + h->off[2] + rank * w2_shard),
-                (const unsigned long long *)h->xfer, h->epoch, xfer_error(h));
+                (const unsigned long long *)h->xfer, h->epoch, xfer_error(h), kXferSpin);
             ZC_LAUNCHED("xfer_reduce_kernel");
         } else if (shard) {
             ZC_TRY(nccl_reduce_scatter_sum_f32(h->grads + h->off[2], nA / world, side));
@@ -940,8 +942,31 @@ extern "C" int zpucuda_mlp_check(zpucuda_mlp *h) {
     }
     if (h->xfer) {
         ZC_CUDA(cudaMemcpy(&e, xfer_error(h), sizeof e, cudaMemcpyDeviceToHost));
-        if (e) return set_error(ZPUCUDA_ERR_TIMEOUT, "a peer's dW2 tiles did not arrive in time");
+        if (e) {
+            ZC_CUDA(cudaMemset(xfer_error(h), 0, sizeof e));
+            return set_error(ZPUCUDA_ERR_TIMEOUT,
+                             "a peer's dW2 tiles did not arrive in time (that step's W2 update used a stale gradient shard)");
+        }
     }
+    return ZPUCUDA_OK;
+}
+
+extern "C" int zpucuda_debug_peer_reduce(const float *d_inbox, int world, int64_t n, float *d_out,
+                                         const uint64_t *d_flags, uint64_t epoch, uint32_t spin_limit,
+                                         uint32_t *d_err, void *stream) {
+    if (!d_inbox || !d_out || !d_flags || !d_err || world < 1 || world > kMaxPeers || n < 0 || n % 4 ||
+        ((uintptr_t)d_inbox & 15u) || ((uintptr_t)d_out & 15u) || spin_limit == 0)
+        return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT,
+                         "zpucuda_debug_peer_reduce: NULL pointer, world outside [1, 8], n not a multiple of 4, "
+                         "unaligned buffer or zero spin limit");
+    const int64_t n4 = n / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > (int64_t)num_sms() * 4) blocks = (int64_t)num_sms() * 4;
+    xfer_reduce_kernel<<<(unsigned)blocks, 256, 0, resolve_stream(stream)>>>(
+        (const float4 *)d_inbox, world, n4, (float4 *)d_out, (const unsigned long long *)d_flags,
+        (unsigned long long)epoch, d_err, spin_limit);
+    ZC_LAUNCHED("xfer_reduce_kernel");
     return ZPUCUDA_OK;
 }
 

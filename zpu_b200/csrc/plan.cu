@@ -659,7 +659,6 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             o.shape = a.shape;
         } else if (st.prim == PRIM_MATMUL && st.n_inputs == 2) {
             const Value &b = vals[st.ins[1]];
-            if (a.dtype != b.dtype) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed-dtype matmul");
             zpucuda_tensor ta = {}, tb = {}, tc = {};
             ta.dtype = a.dtype;
             ta.rank = a.shape.rank;
@@ -675,6 +674,11 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             for (int i = tb.rank - 1; i >= 0; i--) { tb.strides[i] = st_; st_ *= tb.dims[i]; }
             int r = zpucuda_matmul_shape(&ta, &tb, &tc);
             if (r) return lower_fail(plan, r, "matmul shape");
+            // mixed operand types run zpu's gemmF64 loop; a plan carries its
+            // result when that is a float value (DType.promote: floats win)
+            if (tc.dtype != ZPUCUDA_F32 && tc.dtype != ZPUCUDA_F64)
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "matmul with a non-float result in a plan");
+            o.dtype = tc.dtype;
             o.shape.rank = tc.rank;
             for (int i = 0; i < tc.rank; i++) o.shape.dims[i] = tc.dims[i];
             o.depth = tc.batch_depth;
@@ -971,7 +975,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 auto it = users.find(id);
                 return !out_index.count(id) && it != users.end() && it->second.size() == 1 && it->second[0] == step;
             };
-            if (a.dtype == ZPUCUDA_F32 && mo.shape.rank == 2 && a.shape.rank <= 2 && b.shape.rank <= 2 &&
+            if (a.dtype == ZPUCUDA_F32 && b.dtype == ZPUCUDA_F32 && mo.shape.rank == 2 && a.shape.rank <= 2 && b.shape.rank <= 2 &&
                 s + 1 < n_steps && only_user(st0.out, s + 1)) {
                 const zpucuda_step &ad = steps[s + 1];
                 const uint64_t other = ad.n_inputs == 2 ? (ad.ins[0] == st0.out ? ad.ins[1] : ad.ins[0]) : 0;
@@ -996,7 +1000,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
             char buf[160];
             snprintf(buf, sizeof buf, "  kernel %zu: gemm %s (%%%llu = matmul(%%%llu, %%%llu))\n", plan->launches.size(),
-                     a.dtype == ZPUCUDA_F64 ? "f64 dmma" : "f32 3xtf32", (unsigned long long)st0.out,
+                     a.dtype != b.dtype ? "mixed-type (gemmF64 loop)" : a.dtype == ZPUCUDA_F64 ? "f64 dmma" : "f32 3xtf32",
+                     (unsigned long long)st0.out,
                      (unsigned long long)st0.ins[0], (unsigned long long)st0.ins[1]);
             L.text = buf;
             if (fused) L.text.insert(L.text.size() - 1, fused == 2 ? " + bias + tanh epilogue" : " + bias epilogue");
@@ -1355,15 +1360,29 @@ int zpucuda_plan_run(zpucuda_plan *plan, const void *const *args, void *const *o
     return ZPUCUDA_OK;
 }
 
-// The plan's take / scatter_add index-error word, read and cleared (the
-// stream has drained): IndexOutOfRange once when set.
-static int take_index_error(zpucuda_plan *plan) {
-    if (!plan->err) return ZPUCUDA_OK;
-    unsigned int e = 0;
-    ZC_CUDA(cudaMemcpy(&e, plan->err, sizeof e, cudaMemcpyDeviceToHost));
-    if (!e) return ZPUCUDA_OK;
-    ZC_CUDA(cudaMemset(plan->err, 0, sizeof e));
-    return set_error(ZPUCUDA_ERR_INDEX_OUT_OF_RANGE, "a take / scatter_add index was out of range (ops.take)");
+// The plan's device error words, read and cleared once the stream has
+// drained: the take / scatter_add index-error word (IndexOutOfRange), and the
+// error word of every full-reduction workspace, which a region kernel sets
+// when one of its bounded waits runs out (its sum is then NaN): Timeout.
+static int plan_device_errors(zpucuda_plan *plan) {
+    bool timed_out = false;
+    for (void *w : plan->workspaces) {
+        unsigned int e = 0;
+        ZC_CUDA(cudaMemcpy(&e, (unsigned int *)w + 1, sizeof e, cudaMemcpyDeviceToHost));
+        if (e) {
+            ZC_CUDA(cudaMemset((unsigned int *)w + 1, 0, sizeof e));
+            timed_out = true;
+        }
+    }
+    unsigned int idx = 0;
+    if (plan->err) {
+        ZC_CUDA(cudaMemcpy(&idx, plan->err, sizeof idx, cudaMemcpyDeviceToHost));
+        if (idx) ZC_CUDA(cudaMemset(plan->err, 0, sizeof idx));
+    }
+    if (timed_out)
+        return set_error(ZPUCUDA_ERR_TIMEOUT, "a fused reduction's bounded wait for its input copies ran out (its result is NaN)");
+    if (idx) return set_error(ZPUCUDA_ERR_INDEX_OUT_OF_RANGE, "a take / scatter_add index was out of range (ops.take)");
+    return ZPUCUDA_OK;
 }
 
 static size_t value_bytes(const zpucuda_value &v) {
@@ -1400,7 +1419,7 @@ int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void
     // bounded wait on this stream
     for (int64_t spins = 0;; spins++) {
         cudaError_t e = cudaStreamQuery(s);
-        if (e == cudaSuccess) return take_index_error(plan);
+        if (e == cudaSuccess) return plan_device_errors(plan);
         if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
         if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_plan_run_host: stream did not drain");
         if (spins > 1000) usleep(10);
@@ -1409,11 +1428,11 @@ int zpucuda_plan_run_host(zpucuda_plan *plan, const void *const *host_args, void
 
 int zpucuda_plan_check(zpucuda_plan *plan, void *stream) {
     ZC_CHECK(plan, ZPUCUDA_ERR_INVALID_ARGUMENT);
-    if (!plan->err) return ZPUCUDA_OK;
+    if (!plan->err && plan->workspaces.empty()) return ZPUCUDA_OK;
     cudaStream_t s = resolve_stream(stream);
     for (int64_t spins = 0;; spins++) {
         cudaError_t e = cudaStreamQuery(s);
-        if (e == cudaSuccess) return take_index_error(plan);
+        if (e == cudaSuccess) return plan_device_errors(plan);
         if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
         if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_plan_check: stream did not drain");
         if (spins > 1000) usleep(10);

@@ -509,9 +509,10 @@ __global__ void __launch_bounds__(kBulkThreads) fused_sum_bulk_kernel(const __gr
     }
     if (failed) {
         // drain the copies this block still has in flight (bounded), then
-        // report: the error word, and NaN through this block's partial
+        // report: the error word, and NaN through this block's partial.  The
+        // drain starts at tile j itself: its copy is the one that stalled.
         if (threadIdx.x == 0) {
-            for (int64_t q = j + 1; q < mine && q < j + kBulkStages; q++)
+            for (int64_t q = j; q < mine && q < j + kBulkStages; q++)
                 mbar_wait(&full[q % kBulkStages], (uint32_t)((q / kBulkStages) & 1));
             if (io.error) atomicOr(io.error, 1u);
         }
