@@ -291,6 +291,103 @@ MLP_FLOPS = 2 * MLP_BATCH * (784 * 4096 + 4096 * 4096 + 4096 * 10) * 2 + 2 * MLP
 MLP_PARAMS = 784 * 4096 + 4096 + 4096 * 4096 + 4096 + 4096 * 10 + 10
 
 
+PARITY_DIMS, PARITY_BATCH, PARITY_STEPS = (64, 96, 80, 10), 512, 3
+
+
+def mlp_parity(rank, world, dev):
+    """The data-parallel step's parity, outside the timed region: every rank
+    trains the 64->96->80->10 net for 3 steps on its 1/N of a 512-row batch
+    from the same initial parameters, once with dW2 exchanged over peer
+    memory by its GEMM and once with every gradient through NCCL's
+    reduce-scatter.  The ranks' parameters must be bit-identical (an
+    all-reduce of their bits, max against min) and rank 0's must match a
+    one-GPU full-batch run (value_and_grad + Adam on rank 0's GPU) within
+    1e-5 relative Frobenius per parameter, the loss within 1e-5 relative."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from zpu_b200 import mlp as zm
+    from oracle import zpu_oracle as zo
+    dims, B, steps = PARITY_DIMS, PARITY_BATCH, PARITY_STEPS
+    X = zo.uniform_range(0x5EED0800, B * dims[0], 0.0, 1.0).reshape(B, dims[0])
+    y = zo.randint(0x5EED0801, B, 0, dims[3])
+    init = zo.mlp_init(dims)
+    per = B // world
+    xs = torch.from_numpy(np.ascontiguousarray(X[rank * per:(rank + 1) * per])).to(dev)
+    ys = torch.from_numpy(np.ascontiguousarray(y[rank * per:(rank + 1) * per])).to(dev)
+    want = want_loss = None
+    if rank == 0:
+        m1 = zm.MLP(*dims, max_batch=B)
+        m1.set_params(init)
+        xd, yd = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
+        for _ in range(steps):
+            m1.value_and_grad(xd, yd)
+            m1.adam_step()
+        want, want_loss = m1.params(), m1.loss()
+        m1.close()
+    out = {"net": "%d->%d->%d->%d" % dims, "global_batch": B, "adam_steps": steps,
+           "tolerance": "ranks bit-identical; rel. Frobenius <= 1e-5 per parameter and loss vs one GPU"}
+    saved = os.environ.get("ZPUCUDA_MLP_PEER_EXCHANGE")
+    try:
+        for mode in ("1", "0"):
+            os.environ["ZPUCUDA_MLP_PEER_EXCHANGE"] = mode
+            m = zm.MLP(*dims, max_batch=per)
+            m.set_params(init)
+            for _ in range(steps):
+                m.train_step(xs, ys, global_batch=B)
+            got, loss, ex = m.params(), m.loss(), m.exchange_mode()
+            m.close()
+            bits = torch.from_numpy(np.concatenate([g.ravel() for g in got]).view(np.int32)).to(dev)
+            hi, lo = bits.clone(), bits.clone()
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            entry = {"exchange": "peer memory (dW2 stored by its GEMM)" if ex == 1 else "NCCL reduce-scatter",
+                     "ranks_bit_identical": bool(torch.equal(hi, lo))}
+            if rank == 0:
+                rel = max(float(np.linalg.norm(g.astype(np.float64) - w) / np.linalg.norm(w.astype(np.float64)))
+                          for g, w in zip(got, want))
+                lrel = abs(loss - want_loss) / abs(want_loss)
+                entry.update({"max_rel_fro_vs_1gpu": rel, "loss": loss, "loss_1gpu": want_loss,
+                              "loss_rel_diff": lrel,
+                              "within": entry["ranks_bit_identical"] and rel <= 1e-5 and lrel <= 1e-5})
+            out["peer_exchange" if mode == "1" else "nccl"] = entry
+    finally:
+        if saved is None:
+            os.environ.pop("ZPUCUDA_MLP_PEER_EXCHANGE", None)
+        else:
+            os.environ["ZPUCUDA_MLP_PEER_EXCHANGE"] = saved
+    return out
+
+
+def mlp_drift(dev, adam_steps, loss_at_n):
+    """How far the loss after `adam_steps` Adam steps moves when only the
+    summation order changes: the full 784->4096->4096->10 step on one GPU over
+    the whole batch, with the rows in order and with the rows permuted (the
+    same mean loss and gradients in exact arithmetic), against the loss the
+    N-GPU run reached after as many steps."""
+    import torch
+    import zpu_b200 as zc
+    from zpu_b200 import mlp as zm
+    xs = zc.rng_uniform(0x5EED0006, MLP_BATCH * 784, 0.0, 1.0, device=dev).view(MLP_BATCH, 784)
+    ys = zc.rng_randint(0x5EED0007, MLP_BATCH, 0, 10, device=dev)
+    perm = torch.randperm(MLP_BATCH, generator=torch.Generator().manual_seed(1234)).to(dev)
+    losses = {}
+    for name, (x, y) in (("rows_in_order", (xs, ys)), ("rows_permuted", (xs[perm].contiguous(), ys[perm].contiguous()))):
+        m = zm.MLP(*MLP_DIMS, max_batch=MLP_BATCH)
+        m.init_xavier()
+        for _ in range(adam_steps):
+            m.value_and_grad(x, y)
+            m.adam_step()
+        losses[name] = m.loss()
+        m.close()
+    a, b = losses["rows_in_order"], losses["rows_permuted"]
+    del xs, ys
+    torch.cuda.empty_cache()
+    return {"adam_steps": adam_steps, "loss_1gpu_rows_in_order": a, "loss_1gpu_rows_permuted": b,
+            "rel_diff_permuted_vs_in_order": abs(a - b) / abs(a), "loss_at_n_gpus": loss_at_n,
+            "rel_diff_n_gpus_vs_1gpu": abs(loss_at_n - a) / abs(a)}
+
+
 def mlp_config(rank, world, steps, warmup, dev):
     """The data-parallel MLP train step (784->4096->4096->10, tanh, softmax
     cross-entropy, global batch 8192, Adam lr 1e-3): each rank takes 8192/N
@@ -368,15 +465,19 @@ def mlp_config(rank, world, steps, warmup, dev):
     torch.cuda.synchronize()
     e_ms = e2.elapsed_time(e3) / steps
     loss1 = float(lh[0])
+    adam_steps = m.steps()
     if world > 1:
         t = torch.tensor([ms, e_ms], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, e_ms = float(t[0]), float(t[1])
     m.close()
-    if world > 1:
-        zm.nccl_destroy()
     del x, y
     torch.cuda.empty_cache()
+    parity = mlp_parity(rank, world, dev) if world > 1 else None
+    drift = mlp_drift(dev, adam_steps, loss1) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+        zm.nccl_destroy()
     tflops = MLP_FLOPS / (ms / 1e3) / 1e12
     return {"metric": "MLP train steps/s (global batch 8192)", "steps_per_s": 1e3 / ms, "ms_per_step": ms,
             "n_gpus": world, "batch_per_gpu": bl, "gemm_tflops_whole_job": tflops,
@@ -385,7 +486,8 @@ def mlp_config(rank, world, steps, warmup, dev):
             "kernel_launches_per_step": launches / steps, "loss_after_warmup": loss0, "loss_last": loss1,
             "e2e": {"steps_per_s": 1e3 / e_ms, "ms_per_step": e_ms, "h2d_bytes_per_step": bl * (784 * 4 + 8),
                     "d2h_bytes_per_step": 4},
-            "scaling": "strong (global batch fixed)", "dtype": "f32 (3xTF32 GEMMs)"}
+            "scaling": "strong (global batch fixed)", "dtype": "f32 (3xTF32 GEMMs)",
+            "parity": parity, "drift": drift}
 
 
 def run_ours(args):

@@ -108,6 +108,52 @@ size_t zpucuda_buf_bytes(const zpucuda_buf *b);                  /* Buffer.byteL
 int zpucuda_buf_upload(zpucuda_buf *b, size_t off_bytes, const void *host, size_t nbytes);
 int zpucuda_buf_download(const zpucuda_buf *b, size_t off_bytes, void *host, size_t nbytes);
 
+/* ------------------------------------------------------------ residency */
+/* A zpu Buffer whose bytes also live in HBM keeps two copies: the host one
+ * its accessors read and write in place (Buffer.mem and Tensor's data /
+ * readF64 / writeF64, src/zpu/buffer.zig:14-24, src/zpu/tensor.zig:263-302)
+ * and the zpucuda_buf.  The residency state says which copy is current, so
+ * that a chain of device ops (matmul -> jit plan -> matmul) moves no bytes
+ * over PCIe until the host reads a result:
+ *   DEVICE: only the HBM copy is current (a device op wrote it last);
+ *   HOST:   only the host copy is current (host code wrote it last);
+ *   BOTH:   the two agree.
+ * A buffer starts DEVICE.  attach_host: the host copy of b->bytes bytes
+ * (stays owned by the caller) and the state to start in.  mark_device_dirty:
+ * after a device op wrote the buffer.  mark_host_dirty: after host code wrote
+ * the host copy.  host_sync: makes the host copy current before a host read
+ * (a device-to-host copy when the state is DEVICE, none otherwise; waits,
+ * bounded); device_sync: makes the HBM copy current before a device op
+ * reads it (a host-to-device copy on `stream` when the state is HOST, none
+ * otherwise).  Both leave BOTH.  transfer_stats: bytes these calls and
+ * zpucuda_buf_upload / _download copied since the process started. */
+enum { ZPUCUDA_RES_DEVICE = 1, ZPUCUDA_RES_HOST = 2, ZPUCUDA_RES_BOTH = 3 };
+int zpucuda_buf_attach_host(zpucuda_buf *b, void *host, int state);
+int zpucuda_buf_residency(const zpucuda_buf *b, int *state);
+int zpucuda_buf_mark_device_dirty(zpucuda_buf *b);
+int zpucuda_buf_mark_host_dirty(zpucuda_buf *b);
+int zpucuda_buf_host_sync(zpucuda_buf *b, void *stream);
+int zpucuda_buf_device_sync(zpucuda_buf *b, void *stream);
+int zpucuda_buf_transfer_stats(uint64_t *h2d_bytes, uint64_t *d2h_bytes);
+
+/* Scopes: zpu's Tracker / Scope (src/zpu/tensor.zig:537-664) for device
+ * buffers.  scope_begin installs the scope on the calling thread when no
+ * other scope is installed there (Tracker.begin; otherwise the new scope
+ * stays inert and buffers go to the installed one); every buffer the thread
+ * then creates (zpucuda_buf_alloc / _alloc_zeroed / _wrap) is adopted: the
+ * scope owns its creation reference.  scope_keep adds a reference so the
+ * buffer survives the scope (Tracker.keep); scope_forget hands the creation
+ * reference back to the caller (untrack); scope_end releases every adopted
+ * buffer still listed, uninstalls the scope and frees it (Scope.deinit).
+ * scope_count: buffers listed; scope_installed: 1 when installed. */
+typedef struct zpucuda_scope zpucuda_scope;
+int zpucuda_scope_begin(zpucuda_scope **out);
+int zpucuda_scope_end(zpucuda_scope *scope);
+zpucuda_buf *zpucuda_scope_keep(zpucuda_scope *scope, zpucuda_buf *b);
+int zpucuda_scope_forget(zpucuda_scope *scope, zpucuda_buf *b);
+int64_t zpucuda_scope_count(const zpucuda_scope *scope);
+int zpucuda_scope_installed(const zpucuda_scope *scope);
+
 /* ------------------------------------------------------------------ GEMM */
 /* C[b] = op(A[b]) @ op(B[b]) for b in 0..batch, row-major, written (not
  * accumulated) -- kernels.gemm / kernels.gemmBatch (src/zpu/kernels.zig:339,

@@ -16,6 +16,8 @@ AXIS_NONE = -2
 F64, F32 = 0, 1
 DT_I64 = 3  # zpu DType.i64: argmax / argmin results
 DT_BOOL = 8  # zpu DType.bool (one byte): predicates, any / all
+# residency states of a buffer (zpucuda_buf_residency)
+RES_DEVICE, RES_HOST, RES_BOTH = 1, 2, 3
 
 STATUS = {
     0: "ok", 1: "OutOfMemory", 2: "ShapeMismatch", 3: "DTypeMismatch", 4: "RankTooLarge",
@@ -97,6 +99,19 @@ SIGNATURES = {
     "zpucuda_buf_bytes": (S, [P]),
     "zpucuda_buf_upload": (I32, [P, S, P, S]),
     "zpucuda_buf_download": (I32, [P, S, P, S]),
+    "zpucuda_buf_attach_host": (I32, [P, P, I32]),
+    "zpucuda_buf_residency": (I32, [P, C.POINTER(I32)]),
+    "zpucuda_buf_mark_device_dirty": (I32, [P]),
+    "zpucuda_buf_mark_host_dirty": (I32, [P]),
+    "zpucuda_buf_host_sync": (I32, [P, P]),
+    "zpucuda_buf_device_sync": (I32, [P, P]),
+    "zpucuda_buf_transfer_stats": (I32, [C.POINTER(U64), C.POINTER(U64)]),
+    "zpucuda_scope_begin": (I32, [C.POINTER(P)]),
+    "zpucuda_scope_end": (I32, [P]),
+    "zpucuda_scope_keep": (P, [P, P]),
+    "zpucuda_scope_forget": (I32, [P, P]),
+    "zpucuda_scope_count": (I64, [P]),
+    "zpucuda_scope_installed": (I32, [P]),
     "zpucuda_gemm_f32": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I64, I64, I64, I64, P]),
     "zpucuda_gemm_f64": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I64, I64, I64, I64, P]),
     "zpucuda_matmul_shape": (I32, [C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]),

@@ -24,9 +24,18 @@ View view_of(const zpucuda_tensor *t) {
     View v;
     v.rank = t->rank;
     v.depth = t->batch_depth;
+    bool empty = false;
     for (int i = 0; i < ZPUCUDA_MAX_RANK; i++) {
         v.dims[i] = i < t->rank ? t->dims[i] : 0;
         v.strides[i] = i < t->rank ? t->strides[i] : 0;
+        if (i < t->rank && t->dims[i] == 0) empty = true;
+    }
+    if (empty) {  // no element is read: any strides will do, take the row-major ones
+        int64_t q = 1;
+        for (int i = t->rank - 1; i >= 0; i--) {
+            v.strides[i] = q;
+            q *= v.dims[i] > 1 ? v.dims[i] : 1;
+        }
     }
     return v;
 }
@@ -161,11 +170,19 @@ int plan_matmul(const zpucuda_tensor *ta_, const zpucuda_tensor *tb_, Plan *P) {
 
 }  // namespace
 
+static int64_t numel_of(const zpucuda_tensor *t) {
+    int64_t q = 1;
+    for (int i = 0; i < t->rank; i++) q *= t->dims[i];
+    return q;
+}
+
 int matmul_device(const zpucuda_tensor *a, const zpucuda_tensor *b, zpucuda_tensor *out, cudaStream_t s) {
     Plan P;
     int st = plan_matmul(a, b, &P);
     if (st) return st;
-    if (!out || !out->data || !a->data || !b->data) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    // empty tensors may carry a NULL data pointer (nothing is read or written)
+    if (!out || (!out->data && numel_of(out)) || (!a->data && numel_of(a)) || (!b->data && numel_of(b)))
+        return ZPUCUDA_ERR_INVALID_ARGUMENT;
     if (out->rank != P.out_rank) return ZPUCUDA_ERR_SHAPE_MISMATCH;
     for (int i = 0; i < P.out_rank; i++)
         if (out->dims[i] != P.out_dims[i]) return ZPUCUDA_ERR_SHAPE_MISMATCH;

@@ -7,6 +7,7 @@
 #include <chrono>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "common.cuh"
 
@@ -179,9 +180,30 @@ struct zpucuda_buf {
     size_t bytes;
     bool owned;
     int device;
+    // residency: the host copy zpu's accessors read (Buffer.mem) when one is
+    // attached, and which copies hold the current bytes
+    void *host = nullptr;
+    std::atomic<int> state{ZPUCUDA_RES_DEVICE};
+};
+
+// A lifetime domain for device buffers (zpu's Tracker / Scope,
+// src/zpu/tensor.zig:537-664): while a scope is installed on a thread, every
+// buffer that thread creates is adopted by it, and ending the scope drops
+// those creation references.
+struct zpucuda_scope {
+    std::vector<zpucuda_buf *> list;
+    bool installed = false;
 };
 
 namespace {
+thread_local zpucuda_scope *t_scope = nullptr;
+std::atomic<uint64_t> g_h2d_bytes{0}, g_d2h_bytes{0};
+
+// Tracker.adopt through track() (tensor.zig:599-606): the creation reference
+// goes to the thread's installed scope, if any.
+void track(zpucuda_buf *b) {
+    if (t_scope && t_scope->installed) t_scope->list.push_back(b);
+}
 // Host-side fault injection for the failure-path tests: with
 // ZPUCUDA_FAULT_ALLOC_AFTER=n the (n+1)-th and later allocations fail with
 // OutOfMemory before any CUDA call is made.
@@ -217,6 +239,7 @@ int alloc_impl(size_t nbytes, bool zero, zpucuda_buf **out) {
     b->bytes = nbytes;
     b->owned = true;
     b->device = current_device();
+    track(b);
     *out = b;
     return ZPUCUDA_OK;
 }
@@ -235,6 +258,7 @@ int zpucuda_buf_wrap(void *d_ptr, size_t nbytes, zpucuda_buf **out) {
     b->bytes = nbytes;
     b->owned = false;
     b->device = current_device();
+    track(b);
     *out = b;
     return ZPUCUDA_OK;
 }
@@ -262,6 +286,7 @@ int zpucuda_buf_upload(zpucuda_buf *b, size_t off, const void *host, size_t nbyt
     if (!nbytes) return ZPUCUDA_OK;
     cudaStream_t s = resolve_stream(nullptr);
     ZC_CUDA(cudaMemcpyAsync((char *)b->ptr + off, host, nbytes, cudaMemcpyHostToDevice, s));
+    g_h2d_bytes += nbytes;
     return zpucuda_sync(-1);
 }
 
@@ -271,7 +296,121 @@ int zpucuda_buf_download(const zpucuda_buf *b, size_t off, void *host, size_t nb
     if (!nbytes) return ZPUCUDA_OK;
     cudaStream_t s = resolve_stream(nullptr);
     ZC_CUDA(cudaMemcpyAsync(host, (const char *)b->ptr + off, nbytes, cudaMemcpyDeviceToHost, s));
+    g_d2h_bytes += nbytes;
     return zpucuda_sync(-1);
 }
+
+// ------------------------------------------------------------- residency
+
+int zpucuda_buf_attach_host(zpucuda_buf *b, void *host, int state) {
+    ZC_CHECK(b && (host || !b->bytes), ZPUCUDA_ERR_INVALID_ARGUMENT);
+    ZC_CHECK(state == ZPUCUDA_RES_DEVICE || state == ZPUCUDA_RES_HOST || state == ZPUCUDA_RES_BOTH,
+             ZPUCUDA_ERR_INVALID_ARGUMENT);
+    b->host = host;
+    b->state.store(state);
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_residency(const zpucuda_buf *b, int *state) {
+    ZC_CHECK(b && state, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    *state = b->state.load();
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_mark_device_dirty(zpucuda_buf *b) {
+    ZC_CHECK(b, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    b->state.store(ZPUCUDA_RES_DEVICE);
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_mark_host_dirty(zpucuda_buf *b) {
+    ZC_CHECK(b, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    if (!b->host) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "zpucuda_buf_mark_host_dirty: no host copy attached");
+    b->state.store(ZPUCUDA_RES_HOST);
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_host_sync(zpucuda_buf *b, void *stream) {
+    ZC_CHECK(b, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    if (!b->host) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "zpucuda_buf_host_sync: no host copy attached");
+    if (b->state.load() != ZPUCUDA_RES_DEVICE) return ZPUCUDA_OK;  // the host copy is current
+    cudaStream_t s = resolve_stream(stream);
+    if (b->bytes) ZC_CUDA(cudaMemcpyAsync(b->host, b->ptr, b->bytes, cudaMemcpyDeviceToHost, s));
+    g_d2h_bytes += b->bytes;
+    // bounded wait on that stream: the host reads the bytes right after
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "cudaStreamQuery");
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60))
+            return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_buf_host_sync: stream did not drain in time");
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    b->state.store(ZPUCUDA_RES_BOTH);
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_device_sync(zpucuda_buf *b, void *stream) {
+    ZC_CHECK(b, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    if (b->state.load() != ZPUCUDA_RES_HOST) return ZPUCUDA_OK;  // the device copy is current
+    cudaStream_t s = resolve_stream(stream);
+    if (b->bytes) ZC_CUDA(cudaMemcpyAsync(b->ptr, b->host, b->bytes, cudaMemcpyHostToDevice, s));
+    g_h2d_bytes += b->bytes;
+    b->state.store(ZPUCUDA_RES_BOTH);
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_buf_transfer_stats(uint64_t *h2d_bytes, uint64_t *d2h_bytes) {
+    ZC_CHECK(h2d_bytes && d2h_bytes, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    *h2d_bytes = g_h2d_bytes.load();
+    *d2h_bytes = g_d2h_bytes.load();
+    return ZPUCUDA_OK;
+}
+
+// ----------------------------------------------------------------- scopes
+
+int zpucuda_scope_begin(zpucuda_scope **out) {
+    ZC_CHECK(out, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    zpucuda_scope *sc = new zpucuda_scope;
+    if (!t_scope) {  // Tracker.begin: installs only when no other scope is active
+        t_scope = sc;
+        sc->installed = true;
+    }
+    *out = sc;
+    return ZPUCUDA_OK;
+}
+
+int zpucuda_scope_end(zpucuda_scope *sc) {
+    ZC_CHECK(sc, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    if (sc->installed) {
+        if (t_scope == sc) t_scope = nullptr;
+        for (zpucuda_buf *b : sc->list) zpucuda_buf_release(b);
+        sc->list.clear();
+        sc->installed = false;
+    }
+    delete sc;
+    return ZPUCUDA_OK;
+}
+
+zpucuda_buf *zpucuda_scope_keep(zpucuda_scope *sc, zpucuda_buf *b) {
+    (void)sc;
+    return zpucuda_buf_retain(b);
+}
+
+int zpucuda_scope_forget(zpucuda_scope *sc, zpucuda_buf *b) {
+    ZC_CHECK(sc && b, ZPUCUDA_ERR_INVALID_ARGUMENT);
+    for (size_t i = 0; i < sc->list.size(); i++)
+        if (sc->list[i] == b) {
+            sc->list[i] = sc->list.back();
+            sc->list.pop_back();
+            return ZPUCUDA_OK;
+        }
+    return ZPUCUDA_OK;
+}
+
+int64_t zpucuda_scope_count(const zpucuda_scope *sc) { return sc ? (int64_t)sc->list.size() : -1; }
+
+int zpucuda_scope_installed(const zpucuda_scope *sc) { return sc && sc->installed ? 1 : 0; }
 
 }  // extern "C"
