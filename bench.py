@@ -16,7 +16,6 @@ max over ranks of the CUDA-event time of exactly K steps.
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -53,18 +52,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def ncu_traffic(kernel_tag):
-    """dram bytes per launch from the committed ncu summary, when present."""
-    path = os.path.join(ROOT, "profiles", "region_tanh_sq_affine_sum_2e26.md")
+def ncu_traffic(workload):
+    """DRAM bytes per launch of the workload's kernel (dram__bytes_read.sum +
+    dram__bytes_write.sum from one ncu capture), kept in
+    profiles/traffic.json; None when no capture is recorded."""
     try:
-        with open(path) as f:
-            for line in f:
-                m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", line)
-                if m:
-                    return int(m.group(1))
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return int(json.load(f)[workload]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
 
 
 class Clocks:
@@ -206,6 +202,35 @@ def _time_events(fn, reps, warm=2):
     return e0.elapsed_time(e1) / reps
 
 
+def _time_graph(fn, calls=20, reps=5):
+    """Device time of one fn() call: `calls` calls captured in a CUDA graph,
+    replayed `reps` times between CUDA events (host launch cost excluded).
+    None when the calls cannot be captured."""
+    import torch
+    try:
+        fn()
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(calls):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * calls)
+        del g
+        return ms
+    except Exception:
+        torch.cuda.synchronize()
+        return None
+
+
 def _max_over_ranks(ms, world, dev):
     if world == 1:
         return ms
@@ -243,10 +268,16 @@ def gemm_configs(rank=0, world=1, dev="cuda"):
     B = zc.rng_uniform(0x5EED0002, n * n, -1.0, 1.0, device=dev).view(n, n)
     C = torch.empty(n, n, device=dev)
     _barrier(world)
-    ms = _max_over_ranks(_time_events(lambda: zc.matmul(A, B, out=C), 20), world, dev)
+    host_ms = _max_over_ranks(_time_events(lambda: zc.matmul(A, B, out=C), 20), world, dev)
+    # at ~10 us of device time per product, the Python call that launches it
+    # costs as much: the device time comes from a CUDA graph of 20 calls
+    g_ms = _time_graph(lambda: zc.matmul(A, B, out=C))
+    ms = _max_over_ranks(g_ms if g_ms is not None else host_ms, world, dev)
     t = 2 * n ** 3 / ms / 1e9
     out["config1_f32_gemm_1024"] = {"tflops_per_replica": t, "ms": ms, "frac_of_3xtf32_ceiling": t / (tf32 / 3),
                                     "ceiling_tflops": tf32 / 3, "ceiling_source": src,
+                                    "timing": "CUDA graph of 20 calls" if g_ms is not None else "host loop",
+                                    "host_loop_ms": host_ms, "tflops_host_loop": 2 * n ** 3 / host_ms / 1e9,
                                     "parallelism": "replicas (%d)" % world}
     bsz, n = 256, 512
     s = 1.0 / (512.0 ** 0.5)
@@ -280,6 +311,64 @@ def gemm_configs(rank=0, world=1, dev="cuda"):
     del A, B, C
     torch.cuda.empty_cache()
     return out
+
+
+def chain_sharded_config(rank, world, steps, dev):
+    """The jit chain sumAll(tanh(x*x)*a + b) on ONE 2^26-element input
+    range-sharded over the N GPUs: rank r reduces elements
+    [r 2^26 / N, (r+1) 2^26 / N) with the fused kernel, then one
+    1-element NCCL all-reduce sums the N partials (zpu's single reduction,
+    ops.sumAll, done as partial sums plus one exchange).  At 8 GPUs a shard
+    is 32 MiB and would stay in the 126 MB L2 between steps, so L2 is
+    flushed (a 256 MiB write) before every step, outside the timed span;
+    each step's span (kernel + all-reduce) is timed with CUDA events and the
+    spans summed, max over ranks.  The all-reduce alone is timed the same
+    way for its share."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import zpu_b200 as zc
+    n = N_ELEM // world
+    x = zc.rng_normal(SEED_X, N_ELEM, device=dev)[rank * n:(rank + 1) * n].contiguous()
+    torch.cuda.empty_cache()
+    steps_def = [("mul", [1, 1], 10, -2, 0), ("tanh", [10], 11, -2, 0), ("mul", [11, 2], 12, -2, 0),
+                 ("add", [12, 3], 13, -2, 0), ("sum", [13], 14, -2, 0)]
+    plan = zc.Plan([(1, zc.F32, (n,))], [(2, np.float32(A)), (3, np.float32(B))], steps_def, [14])
+    part = torch.empty((), dtype=torch.float32, device=dev)
+    flush = torch.empty(1 << 26, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        plan.run([x], [part])
+        if world > 1:
+            dist.all_reduce(part)
+
+    def timed(fn, k):
+        total = 0.0
+        for _ in range(k):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        return total / k
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(timed(step, steps), world, dev)
+    result = float(part.item())
+    ar_ms = _max_over_ranks(timed(lambda: dist.all_reduce(part), steps), world, dev) if world > 1 else 0.0
+    del flush
+    torch.cuda.empty_cache()
+    return {"metric": "fused-elementwise HBM GB/s, one 2^26 input range-sharded (whole job)",
+            "gbs": BYTES_PER_STEP / ms / 1e6, "ms_per_step": ms, "n_gpus": world,
+            "elements_per_gpu": n, "allreduce_ms": ar_ms, "allreduce_share": ar_ms / ms if world > 1 else 0.0,
+            "sum": result, "l2": "flushed before every step (a shard of %d MiB%s)" % (
+                n * 4 >> 20, " fits in L2" if n * 4 < 126 * 10 ** 6 else ""),
+            "scaling": "strong (one input, fixed size)"}
 
 
 MLP_DIMS = (784, 4096, 4096, 10)
@@ -591,7 +680,7 @@ def run_ours(args):
                    "parallelism": "replicas: each GPU runs the plan on its own 2^26 shard",
                    "kernel": "catalogue region tanh_sq_affine+sum (1 launch/step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": ncu_traffic("tanh_sq_affine"),
+                     "frac": achieved / peak, "traffic": ncu_traffic("tanh_sq_affine+sum 2^26 f32"),
                      "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": N_ELEM * 4, "d2h_bytes_per_step": 4,
                 "path": "zpucuda_plan_run_host (pinned host x -> HBM, fused kernel, scalar -> host)"},
@@ -600,6 +689,7 @@ def run_ours(args):
         "warmup_soak_steps": soak,
     }
     line["other_configs"] = gemm_configs(rank, world, dev)
+    line["other_configs"]["config2_chain_range_sharded"] = chain_sharded_config(rank, world, min(args.steps, 20), dev)
     line["other_configs"]["config4_mlp_train_step"] = mlp_config(rank, world, min(args.steps, 20), args.warmup, dev)
     if rank == 0 and world == 1:
         gbs, cores, sample, per = cpu_chain_baseline()
@@ -650,12 +740,112 @@ def _only_gemm(kind, steps, warmup):
     return {"ms": ms, "tflops": max(1, bsz) * 2 * n ** 3 / ms / 1e9, "n": n, "batch": max(1, bsz)}
 
 
+def _only_kernel(kind, steps, warmup):
+    """One of the library's other kernels alone, on inputs larger than L2, for
+    its ncu summary: returns its CUDA-event time per call and the algorithmic
+    bytes per call (reads + writes of the kernel's own data)."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    import zpu_b200 as zc
+    F = zc.F32
+    if kind in ("region_bytecode", "sum_sq_bulk"):
+        n = 1 << 26
+        x = zc.rng_normal(SEED_X, n)
+        if kind == "sum_sq_bulk":  # catalogue "sq+sum": the bulk-copy pipeline
+            plan = zc.Plan([(1, F, (n,))], [], [("mul", [1, 1], 10, -2, 0), ("sum", [10], 11, -2, 0)], [11])
+            out = [torch.empty((), device="cuda")]
+            nbytes = n * 4 + 4
+        else:  # outside the catalogue: the one-pass bytecode kernel
+            plan = zc.Plan([(1, F, (n,))], [], [("sin", [1], 10, -2, 0), ("mul", [1, 1], 11, -2, 0),
+                                                 ("add", [10, 11], 12, -2, 0)], [12])
+            out = [torch.empty(n, device="cuda")]
+            nbytes = n * 8
+        fn = lambda: plan.run([x], out)
+    elif kind == "cumsum":
+        r, c = 8192, 4096
+        x = zc.rng_normal(SEED_X, r * c).view(r, c)
+        plan = zc.Plan([(1, F, (r, c))], [], [("cumsum", [1], 10, 0, 0)], [10])
+        out = [torch.empty(r, c, device="cuda")]
+        fn = lambda: plan.run([x], out)
+        nbytes = r * c * 8
+    elif kind in ("take", "scatter_add"):
+        r, c, k = 16384, 1024, 16384
+        x = zc.rng_normal(SEED_X, r * c).view(r, c)
+        idx = zc.rng_randint(SEED_X + 1, k, 0, r)
+        if kind == "take":
+            plan = zc.Plan([(1, F, (r, c)), (2, zc.DT_I64, (k,))], [], [("take", [1, 2], 10, 0, 0)], [10])
+            out = [torch.empty(k, c, device="cuda")]
+            fn = lambda: plan.run([x, idx], out)
+            nbytes = k * c * 8 + k * 8
+        else:
+            upd = zc.rng_normal(SEED_X + 2, k * c).view(k, c)
+            plan = zc.Plan([(1, F, (r, c)), (2, zc.DT_I64, (k,)), (3, F, (k, c))], [],
+                           [("scatter_add", [1, 2, 3], 10, 0, 0)], [10])
+            out = [torch.empty(r, c, device="cuda")]
+            fn = lambda: plan.run([x, idx, upd], out)
+            nbytes = r * c * 8 + k * c * 4 + k * 8
+    elif kind == "rng_normal":
+        n = 1 << 26
+        buf = torch.empty(n, device="cuda")
+        fn = lambda: zc.rng_normal(SEED_X, n, out=buf)
+        nbytes = n * 4
+    elif kind == "peer_reduce":  # the owner-side sum of the dW2 exchange, 8 slots
+        world, n = 8, 1 << 23
+        inbox = zc.rng_normal(SEED_X, world * n)
+        flags = torch.ones(world, dtype=torch.int64, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        outv = torch.empty(n, device="cuda")
+        L = zc.lib()
+        fn = lambda: zc.check(L.zpucuda_debug_peer_reduce(inbox.data_ptr(), world, n, outv.data_ptr(),
+                                                          flags.data_ptr(), 1, 1 << 20, err.data_ptr(), zc.stream_of()))
+        nbytes = world * n * 4 + n * 4
+    elif kind == "gather_copy":  # a flipped (negative-stride) view made contiguous
+        r, c = 8192, 4096
+        x = zc.rng_normal(SEED_X, r * c).view(r, c)
+        d = zc.tensor_desc(x)
+        d.data = x.data_ptr() + (r - 1) * c * 4
+        d.strides[0] = -c
+        out = torch.empty(r, c, device="cuda")
+        fn = lambda: zc.tensor_copy(d, out)
+        nbytes = r * c * 8
+    elif kind == "gemm_fma_fallback":  # a row pitch the tensor maps cannot take
+        n, ld = 2048, 2049
+        a = zc.rng_uniform(SEED_X, n * ld, -1.0, 1.0).view(n, ld)[:, :n]
+        b = zc.rng_uniform(SEED_X + 1, n * ld, -1.0, 1.0).view(n, ld)[:, :n]
+        o = torch.empty(n, n, device="cuda")
+        fn = lambda: zc.matmul(a, b, out=o)
+        nbytes = None
+        flops = 2 * n ** 3
+    elif kind == "gemm_convert":  # f16 @ f32: zpu's gemmF64 loop
+        n = 1024
+        a = zc.rng_uniform(SEED_X, n * n, -1.0, 1.0).view(n, n).half()
+        b = zc.rng_uniform(SEED_X + 1, n * n, -1.0, 1.0).view(n, n)
+        o = torch.empty(n, n, device="cuda")
+        fn = lambda: zc.matmul(a, b, out=o)
+        nbytes = None
+        flops = 2 * n ** 3
+    else:
+        raise ValueError(kind)
+    ms = _time_events(fn, steps, warm=warmup)
+    res = {"ms": ms}
+    if nbytes:
+        res.update({"gbs": nbytes / ms / 1e6, "algorithmic_bytes": nbytes})
+    else:
+        res.update({"tflops": flops / ms / 1e9})
+    return res
+
+
+KERNEL_CASES = ("region_bytecode", "sum_sq_bulk", "cumsum", "take", "scatter_add", "rng_normal", "peer_reduce",
+                "gather_copy", "gemm_fma_fallback", "gemm_convert")
+
 ONLY_CASES = {
-    "chain": None, "mlp": None,
+    "chain": None, "mlp": None, "chain_sharded": None,
     "gemm_f32_1024": "f32_1024", "gemm_f32_4096": "f32_4096", "gemm_f32_8192": "f32_8192",
     "gemm_f32_batched": "f32_batched",
     "gemm_f64_4096": "f64_4096",
 }
+ONLY_CASES.update({k: None for k in KERNEL_CASES})
 
 
 def run_only(args):
@@ -667,12 +857,15 @@ def run_only(args):
     rank, local, world = dist_env()
     torch.cuda.set_device(local)
     zc.check(zc.lib().zpucuda_init(local))
-    if args.only == "mlp":  # the only case that runs under torchrun (data parallel)
+    if args.only in ("mlp", "chain_sharded"):  # the cases that run under torchrun (data parallel)
         if world > 1:
             import datetime
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                                  device_id=torch.device("cuda", local))
-        out = mlp_config(rank, world, args.steps, args.warmup, torch.device("cuda", local))
+        if args.only == "mlp":
+            out = mlp_config(rank, world, args.steps, args.warmup, torch.device("cuda", local))
+        else:
+            out = chain_sharded_config(rank, world, args.steps, torch.device("cuda", local))
         if world > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
@@ -686,6 +879,8 @@ def run_only(args):
         y = torch.empty((), dtype=torch.float32, device="cuda")
         ms = _time_events(lambda: plan.run([x], [y]), args.steps, warm=args.warmup)
         out = {"ms": ms, "gbs": BYTES_PER_STEP / ms / 1e6}
+    elif args.only in KERNEL_CASES:
+        out = _only_kernel(args.only, args.steps, args.warmup)
     else:
         out = _only_gemm(ONLY_CASES[args.only], args.steps, args.warmup)
     print(json.dumps({"only": args.only, **out}), flush=True)

@@ -261,6 +261,8 @@ struct Maps {
 };
 
 struct Params {
+    const float *A, *B;  // the operands as stored (the non-finite recompute reads them)
+    int64_t lda, ldb;
     int64_t M, N, K, ldc, stride_c;
     int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
     int32_t nmma;          // MMA width: N rounded up to 16, at most BN
@@ -275,6 +277,29 @@ struct Params {
 uint32_t make_idesc(bool ta, bool tb, int nmma) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((ta ? 1u : 0u) << 15) | ((tb ? 0u : 1u) << 16) |
            ((uint32_t)(nmma >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// zpu's own chain for one element (kernels.gemm, src/zpu/kernels.zig:369-400):
+// c = 0, then for p = k0 .. k1-1 in order c = fma(a[row,p], b[p,col], c) --
+// except for the nb % 8 columns past the last whole 8-lane vector of their
+// 128-column panel, where zpu adds a separate product (row[j] += a * b).
+// The tensor-core path hands an element here when its 3xTF32 result is not
+// finite: an infinite operand meets a zero low TF32 half of its partner
+// (inf * 0 = NaN in the hi x lo product), or the sum overflows.  zpu's chain
+// then gives the exact inf / NaN it gives on the CPU.
+template <bool TA, bool TB>
+__device__ __noinline__ float zpu_chain_element(const float *A, const float *B, int64_t lda, int64_t ldb, int64_t row,
+                                                int64_t col, int64_t N, int64_t k0, int64_t k1) {
+    const int64_t jb = col & ~(int64_t)127;
+    const int64_t nb = N - jb < 128 ? N - jb : 128;
+    const bool fused = col - jb < (nb & ~(int64_t)7);
+    float c = 0.0f;
+    for (int64_t p = k0; p < k1; p++) {
+        const float a = TA ? A[p * lda + row] : A[row * lda + p];
+        const float b = TB ? B[col * ldb + p] : B[p * ldb + col];
+        c = fused ? fmaf(a, b, c) : __fadd_rn(c, __fmul_rn(a, b));
+    }
+    return c;
 }
 
 // One result element through the epilogue (the element is at row, col of C).
@@ -491,6 +516,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float acc[32];
                 tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)cl, acc);
                 const int64_t col0 = (int64_t)n0 + cl;
+                // non-finite results: zpu's chain instead (over the whole K;
+                // split-K partials are left to the reduction, which does it)
+                if (P.splits == 1 && row < P.M) {
+                    bool bad = false;
+#pragma unroll
+                    for (int v = 0; v < 32; v++) bad |= !isfinite(acc[v]);
+                    if (bad) {  // through this lane's row of the (idle) staging area
+                        float *mine = stage + lane * 33;
+#pragma unroll
+                        for (int v = 0; v < 32; v++) mine[v] = acc[v];
+#pragma unroll 1
+                        for (int v = 0; v < 32; v++)
+                            if (!isfinite(mine[v]) && col0 + v < P.N)
+                                mine[v] = zpu_chain_element<TA, TB>(P.A + oa, P.B + ob, P.lda, P.ldb, row, col0 + v,
+                                                                    P.N, 0, P.K);
+#pragma unroll
+                        for (int v = 0; v < 32; v++) acc[v] = mine[v];
+                    }
+                }
                 if (!staged) {
                     float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
                     if (row < P.M) {
@@ -570,16 +614,25 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
 
 // Split-K: C = epilogue(sum over s of ws[(batch * splits + s)][m][n]), the
 // partials added in split order (deterministic).
+// A non-finite sum is recomputed with zpu's chain over the whole K (see
+// zpu_chain_element).
+template <bool TA, bool TB>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ ws, int splits, int64_t m,
                                                             int64_t n, int64_t batches, float *__restrict__ C,
                                                             int64_t ldc, int64_t stride_c,
-                                                            const __grid_constant__ Epilogue epi) {
+                                                            const __grid_constant__ Epilogue epi,
+                                                            const __grid_constant__ Params P) {
     const int64_t mn = m * n, total = batches * mn;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = i / mn, r = (i / n) % m, c = i % n;
         const float *p = ws + b * splits * mn + r * n + c;
         float acc = p[0];
         for (int sp = 1; sp < splits; sp++) acc = __fadd_rn(acc, p[sp * mn]);
+        if (!isfinite(acc)) {
+            int64_t oa, ob;
+            batch_offsets(P.bt, b, &oa, &ob);
+            acc = zpu_chain_element<TA, TB>(P.A + oa, P.B + ob, P.lda, P.ldb, r, c, n, 0, P.K);
+        }
         C[b * stride_c + r * ldc + c] = epi_apply(epi, acc, r, c);
     }
 }
@@ -767,6 +820,10 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
         if (tc) {
             Params P;
             memset(&P, 0, sizeof P);
+            P.A = A;
+            P.B = B;
+            P.lda = lda;
+            P.ldb = ldb;
             P.M = m;
             P.N = n;
             P.K = k;
@@ -806,8 +863,13 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
                     const int64_t total = batches * m * n;
                     int64_t blocks = (total + 255) / 256;
                     if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-                    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(ws, splits, m, n, batches, C, ldc, stride_c,
-                                                                          epi);
+#define ZC_RED(TA_, TB_) \
+    splitk_reduce_kernel<TA_, TB_><<<(unsigned)blocks, 256, 0, s>>>(ws, splits, m, n, batches, C, ldc, stride_c, epi, P)
+                    if (!ta && !tb) ZC_RED(false, false);
+                    else if (!ta && tb) ZC_RED(false, true);
+                    else if (ta && !tb) ZC_RED(true, false);
+                    else ZC_RED(true, true);
+#undef ZC_RED
                     cudaError_t e = cudaGetLastError();
                     if (e != cudaSuccess) st = cuda_fail(e, "splitk_reduce_kernel");
                     else count_launch();
