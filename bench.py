@@ -555,6 +555,16 @@ def mlp_config(rank, world, steps, warmup, dev):
     e_ms = e2.elapsed_time(e3) / steps
     loss1 = float(lh[0])
     adam_steps = m.steps()
+    # one more step with the phase trace on (outside every timed span): where
+    # the step's time goes on this rank, in ms from the step's start
+    m.trace(True)
+    m.train_step(x, y, global_batch=MLP_BATCH)
+    trace = m.trace_read()
+    m.trace(False)
+    names = ["start", "forward_gemms", "loss", "layer3_bwd_db2", "dW2_gemm", "g1_gemm", "db1_dW1_gemm",
+             "main_stream_end", "bucket_W2_summed", "bucket_W2_adam_gather", "bucket_W1_summed",
+             "bucket_W1_adam_gather"]
+    trace = {k: round(v, 4) for k, v in zip(names, trace)}
     if world > 1:
         t = torch.tensor([ms, e_ms], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -576,7 +586,7 @@ def mlp_config(rank, world, steps, warmup, dev):
             "e2e": {"steps_per_s": 1e3 / e_ms, "ms_per_step": e_ms, "h2d_bytes_per_step": bl * (784 * 4 + 8),
                     "d2h_bytes_per_step": 4},
             "scaling": "strong (global batch fixed)", "dtype": "f32 (3xTF32 GEMMs)",
-            "parity": parity, "drift": drift}
+            "parity": parity, "drift": drift, "phase_trace_rank0_ms": trace}
 
 
 def run_ours(args):

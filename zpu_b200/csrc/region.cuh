@@ -297,11 +297,30 @@ __device__ __forceinline__ void eval_group(const float4 (&v)[F::NIN > 0 ? F::NIN
     y23 = F::call2(hi);
 }
 
-// Register-loop kernel: each thread keeps kFusedUnroll 16-byte loads per
-// input in flight, evaluates them, and stores (element-wise) or sums them (a
-// full sum: the 32 values of one iteration in f32 pairs, then one f64 add).
+// Register-loop kernel.  Each block streams ONE contiguous range of the
+// input(s): whole chunks of kChunk4 float4 (32 KiB per input), the ranges as
+// equal as whole chunks allow, one resident wave of blocks.  In a chunk, warp
+// w reads its own 4 KiB with kFusedUnroll coalesced 512-byte loads per input,
+// all in flight at once, evaluates them and stores (element-wise) or sums them
+// (a full sum: the 32 values of one chunk in f32 pairs, then one f64 add).
+// Measured on the 2^26-element tanh chain: 5695 GB/s against 5237 for the
+// same loop over kFusedUnroll grid-strided streams 3 MB apart -- DRAM serves
+// a few thousand sequential streams better than eight interleaved ones -- and
+// software pipelining the loads (the next chunk's issued before this one is
+// evaluated) measured slower (80+ registers, 3 blocks per SM).
+constexpr int64_t kChunk4 = (int64_t)kFusedThreads * kFusedUnroll;
+
+// Full (non-scalar) inputs of a catalogued region.
+template <class F>
+constexpr int full_inputs() {
+    int c = 0;
+    for (int k = 0; k < F::NIN; k++)
+        if (!(F::SCALARS & (1u << k))) c++;
+    return c;
+}
+
 template <class F, bool SUM>
-__global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_constant__ RegionIO io, int64_t n) {
+__device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
     constexpr int NIN = F::NIN > 0 ? F::NIN : 1;
     float sv[NIN];
     f2_t sv2[NIN];
@@ -313,17 +332,64 @@ __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_c
         sv2[k] = splat2(sv[k]);
     }
     float4 *dst = (float4 *)io.out[0];
-    const int64_t n4 = n >> 2;
-    const int64_t G = (int64_t)gridDim.x * kFusedThreads;
+    if constexpr (!SUM) {
+        // element-wise: kFusedUnroll grid-strided streams, several waves of
+        // blocks (measured at 0.92 of the HBM peak writing the tanh chain's
+        // vector); the contiguous ranges below pay off for the sums
+        const int64_t n4 = n >> 2;
+        const int64_t G = (int64_t)gridDim.x * kFusedThreads;
+        int64_t b4 = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
+        for (; b4 + (kFusedUnroll - 1) * G < n4; b4 += kFusedUnroll * G) {
+            float4 v[kFusedUnroll][NIN];
+#pragma unroll
+            for (int u = 0; u < kFusedUnroll; u++)
+#pragma unroll
+                for (int k = 0; k < F::NIN; k++)
+                    if (!(F::SCALARS & (1u << k))) v[u][k] = __ldcs(src[k] + b4 + u * G);
+#pragma unroll
+            for (int u = 0; u < kFusedUnroll; u++) {
+                f2_t y01, y23;
+                eval_group<F>(v[u], sv2, y01, y23);
+                float4 o;
+                upk2(y01, o.x, o.y);
+                upk2(y23, o.z, o.w);
+                __stcs(dst + b4 + u * G, o);
+            }
+        }
+        for (; b4 < n4; b4 += G) {
+            float4 v[NIN];
+#pragma unroll
+            for (int k = 0; k < F::NIN; k++)
+                if (!(F::SCALARS & (1u << k))) v[k] = __ldcs(src[k] + b4);
+            f2_t y01, y23;
+            eval_group<F>(v, sv2, y01, y23);
+            float4 o;
+            upk2(y01, o.x, o.y);
+            upk2(y23, o.z, o.w);
+            __stcs(dst + b4, o);
+        }
+        const int64_t t = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
+        if (t < (n & 3)) {
+            const int64_t i = (n4 << 2) + t;
+            float e[NIN];
+#pragma unroll
+            for (int k = 0; k < F::NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : ((const float *)io.in[k])[i];
+            ((float *)io.out[0])[i] = F::call(e);
+        }
+        return;
+    }
+    const int64_t chunks = (n >> 2) / kChunk4;
+    const int64_t c0 = chunks * blockIdx.x / gridDim.x, c1 = chunks * (blockIdx.x + 1) / gridDim.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     double acc = 0.0;
-    int64_t base = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
-    for (; base + (kFusedUnroll - 1) * G < n4; base += kFusedUnroll * G) {
+    int64_t base = c0 * kChunk4 + w * (32 * kFusedUnroll) + lane;
+    for (int64_t c = c0; c < c1; c++, base += kChunk4) {
         float4 v[kFusedUnroll][NIN];
 #pragma unroll
         for (int u = 0; u < kFusedUnroll; u++)
 #pragma unroll
             for (int k = 0; k < F::NIN; k++)
-                if (!(F::SCALARS & (1u << k))) v[u][k] = __ldcs(src[k] + base + u * G);
+                if (!(F::SCALARS & (1u << k))) v[u][k] = __ldcs(src[k] + base + u * 32);
         f2_t s = 0ull;
 #pragma unroll
         for (int u = 0; u < kFusedUnroll; u++) {
@@ -335,7 +401,7 @@ __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_c
                 float4 o;
                 upk2(y01, o.x, o.y);
                 upk2(y23, o.z, o.w);
-                __stcs(dst + base + u * G, o);
+                __stcs(dst + base + u * 32, o);
             }
         }
         if (SUM) {
@@ -344,23 +410,10 @@ __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_c
             acc += (double)(s0 + s1);
         }
     }
-    for (; base < n4; base += G) {
-        float4 v[NIN];
-#pragma unroll
-        for (int k = 0; k < F::NIN; k++)
-            if (!(F::SCALARS & (1u << k))) v[k] = __ldcs(src[k] + base);
-        f2_t y01, y23;
-        eval_group<F>(v, sv2, y01, y23);
-        float s0, s1, s2, s3;
-        upk2(y01, s0, s1);
-        upk2(y23, s2, s3);
-        if (SUM) acc += (double)((s0 + s1) + (s2 + s3));
-        else __stcs(dst + base, make_float4(s0, s1, s2, s3));
-    }
-    // the n % 4 leftover elements
-    const int64_t t = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
-    if (t < (n & 3)) {
-        const int64_t i = (n4 << 2) + t;
+    // the elements past the last whole chunk (fewer than 4 * kChunk4 + 4),
+    // one at a time, grid-strided
+    for (int64_t i = chunks * kChunk4 * 4 + (int64_t)blockIdx.x * kFusedThreads + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * kFusedThreads) {
         float e[NIN];
 #pragma unroll
         for (int k = 0; k < F::NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : ((const float *)io.in[k])[i];
@@ -372,6 +425,28 @@ __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_c
         const double b = block_sum<kFusedThreads>(acc);
         finish_full_sum<kFusedThreads>(b, io, false);
     }
+}
+
+// A one-input sum fits 32 registers without spilling, so it runs 8 blocks of
+// 256 per SM (measured on the tanh chain: 5695 GB/s at 8 blocks per SM, 5237
+// at 6); other regions keep the compiler's own register choice.
+template <class F, bool SUM>
+constexpr bool kTightSum = SUM && full_inputs<F>() <= 1;
+
+template <class F, bool SUM>
+__global__ void __launch_bounds__(kFusedThreads, 8) fused_f32_tight_kernel(const __grid_constant__ RegionIO io, int64_t n) {
+    fused_f32_body<F, SUM>(io, n);
+}
+template <class F, bool SUM>
+__global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_constant__ RegionIO io, int64_t n) {
+    fused_f32_body<F, SUM>(io, n);
+}
+
+// The register-loop kernel launch_fused_f32 uses for F.
+template <class F, bool SUM>
+constexpr auto fused_kernel_of() {
+    if constexpr (kTightSum<F, SUM>) return fused_f32_tight_kernel<F, SUM>;
+    else return fused_f32_kernel<F, SUM>;
 }
 
 // --------------------------------------- full reductions: bulk-copy pipeline
@@ -542,14 +617,16 @@ int bulk_blocks_per_sm();
 // blocks per SM against 4940 at 12; element-wise regions run best at 12).
 int fused_sum_blocks_per_sm(int occupancy);
 
-// The grid launch_fused_f32 uses for the register-loop kernel of F.
+// The grid launch_fused_f32 uses for the register-loop kernel of F: a sum
+// runs one resident wave (the kernel's own blocks per SM), each block one
+// range; element-wise regions run fused_blocks_per_sm() blocks per SM.
 template <class F, bool SUM>
 int fused_grid() {
     int per_sm = fused_blocks_per_sm();
     if (SUM) {
         static const int occ = [] {
             int nb = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fused_f32_kernel<F, SUM>, kFusedThreads, 0) !=
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fused_kernel_of<F, SUM>(), kFusedThreads, 0) !=
                 cudaSuccess)
                 nb = 0;
             return nb;
@@ -585,7 +662,7 @@ int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s)
         ZC_LAUNCHED("fused region kernel (bulk pipeline)");
         return ZPUCUDA_OK;
     }
-    auto k = fused_f32_kernel<F, SUM>;
+    auto k = fused_kernel_of<F, SUM>();
     const int grid = fused_grid<F, SUM>();
     k<<<grid, kFusedThreads, 0, s>>>(io, p.numel);
     ZC_LAUNCHED("fused region kernel");
