@@ -297,18 +297,18 @@ __device__ __forceinline__ void eval_group(const float4 (&v)[F::NIN > 0 ? F::NIN
     y23 = F::call2(hi);
 }
 
-// Register-loop kernel.  Each block streams ONE contiguous range of the
-// input(s): whole chunks of kChunk4 float4 (32 KiB per input), the ranges as
-// equal as whole chunks allow, one resident wave of blocks.  In a chunk, warp
-// w reads its own 4 KiB with kFusedUnroll coalesced 512-byte loads per input,
-// all in flight at once, evaluates them and stores (element-wise) or sums them
-// (a full sum: the 32 values of one chunk in f32 pairs, then one f64 add).
-// Measured on the 2^26-element tanh chain: 5695 GB/s against 5237 for the
-// same loop over kFusedUnroll grid-strided streams 3 MB apart -- DRAM serves
-// a few thousand sequential streams better than eight interleaved ones -- and
-// software pipelining the loads (the next chunk's issued before this one is
-// evaluated) measured slower (80+ registers, 3 blocks per SM).
-constexpr int64_t kChunk4 = (int64_t)kFusedThreads * kFusedUnroll;
+// Register-loop kernel.  For a full sum each block streams ONE contiguous
+// range of the input(s): whole chunks of THREADS * kFusedUnroll float4, the
+// ranges as equal as whole chunks allow, one resident wave of blocks.  In a
+// chunk, warp w reads its own 4 KiB with kFusedUnroll coalesced 512-byte
+// loads per input, all in flight at once, and sums their values (the 32 of
+// one chunk in f32 pairs, then one f64 add).  Measured on the 2^26-element
+// tanh chain: 5695 GB/s against 5237 for the same loop over kFusedUnroll
+// grid-strided streams 3 MB apart (DRAM serves a few hundred long sequential
+// streams better than eight interleaved ones); under sustained load 1024-
+// thread blocks (2 per SM, 128 KiB chunks) 5235 against 5040 for 256-thread
+// ones; software pipelining the loads (the next chunk's issued before this
+// one is evaluated) measured slower (80+ registers, 3 blocks per SM).
 
 // Full (non-scalar) inputs of a catalogued region.
 template <class F>
@@ -319,8 +319,9 @@ constexpr int full_inputs() {
     return c;
 }
 
-template <class F, bool SUM>
+template <class F, bool SUM, int THREADS>
 __device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
+    constexpr int64_t kChunk4 = (int64_t)THREADS * kFusedUnroll;
     constexpr int NIN = F::NIN > 0 ? F::NIN : 1;
     float sv[NIN];
     f2_t sv2[NIN];
@@ -337,8 +338,8 @@ __device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
         // blocks (measured at 0.92 of the HBM peak writing the tanh chain's
         // vector); the contiguous ranges below pay off for the sums
         const int64_t n4 = n >> 2;
-        const int64_t G = (int64_t)gridDim.x * kFusedThreads;
-        int64_t b4 = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
+        const int64_t G = (int64_t)gridDim.x * THREADS;
+        int64_t b4 = (int64_t)blockIdx.x * THREADS + threadIdx.x;
         for (; b4 + (kFusedUnroll - 1) * G < n4; b4 += kFusedUnroll * G) {
             float4 v[kFusedUnroll][NIN];
 #pragma unroll
@@ -368,7 +369,7 @@ __device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
             upk2(y23, o.z, o.w);
             __stcs(dst + b4, o);
         }
-        const int64_t t = (int64_t)blockIdx.x * kFusedThreads + threadIdx.x;
+        const int64_t t = (int64_t)blockIdx.x * THREADS + threadIdx.x;
         if (t < (n & 3)) {
             const int64_t i = (n4 << 2) + t;
             float e[NIN];
@@ -412,8 +413,8 @@ __device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
     }
     // the elements past the last whole chunk (fewer than 4 * kChunk4 + 4),
     // one at a time, grid-strided
-    for (int64_t i = chunks * kChunk4 * 4 + (int64_t)blockIdx.x * kFusedThreads + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * kFusedThreads) {
+    for (int64_t i = chunks * kChunk4 * 4 + (int64_t)blockIdx.x * THREADS + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * THREADS) {
         float e[NIN];
 #pragma unroll
         for (int k = 0; k < F::NIN; k++) e[k] = (F::SCALARS & (1u << k)) ? sv[k] : ((const float *)io.in[k])[i];
@@ -422,24 +423,31 @@ __device__ __forceinline__ void fused_f32_body(const RegionIO &io, int64_t n) {
         else ((float *)io.out[0])[i] = y;
     }
     if (SUM) {
-        const double b = block_sum<kFusedThreads>(acc);
-        finish_full_sum<kFusedThreads>(b, io, false);
+        const double b = block_sum<THREADS>(acc);
+        finish_full_sum<THREADS>(b, io, false);
     }
 }
 
-// A one-input sum fits 32 registers without spilling, so it runs 8 blocks of
-// 256 per SM (measured on the tanh chain: 5695 GB/s at 8 blocks per SM, 5237
-// at 6); other regions keep the compiler's own register choice.
+// A one-input sum fits 32 registers without spilling, so it runs 2 blocks of
+// 1024 threads per SM (64 warps); other regions keep 256-thread blocks and
+// the compiler's own register choice.
 template <class F, bool SUM>
 constexpr bool kTightSum = SUM && full_inputs<F>() <= 1;
+constexpr int kTightThreads = 1024;
 
 template <class F, bool SUM>
-__global__ void __launch_bounds__(kFusedThreads, 8) fused_f32_tight_kernel(const __grid_constant__ RegionIO io, int64_t n) {
-    fused_f32_body<F, SUM>(io, n);
+__global__ void __launch_bounds__(kTightThreads, 2) fused_f32_tight_kernel(const __grid_constant__ RegionIO io, int64_t n) {
+    fused_f32_body<F, SUM, kTightThreads>(io, n);
 }
 template <class F, bool SUM>
 __global__ void __launch_bounds__(kFusedThreads) fused_f32_kernel(const __grid_constant__ RegionIO io, int64_t n) {
-    fused_f32_body<F, SUM>(io, n);
+    fused_f32_body<F, SUM, kFusedThreads>(io, n);
+}
+
+// Threads per block of F's register-loop kernel.
+template <class F, bool SUM>
+constexpr int fused_threads() {
+    return kTightSum<F, SUM> ? kTightThreads : kFusedThreads;
 }
 
 // The register-loop kernel launch_fused_f32 uses for F.
@@ -626,7 +634,7 @@ int fused_grid() {
     if (SUM) {
         static const int occ = [] {
             int nb = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fused_kernel_of<F, SUM>(), kFusedThreads, 0) !=
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fused_kernel_of<F, SUM>(), fused_threads<F, SUM>(), 0) !=
                 cudaSuccess)
                 nb = 0;
             return nb;
@@ -664,7 +672,7 @@ int launch_fused_f32(const RegionProgram &p, const RegionIO &io, cudaStream_t s)
     }
     auto k = fused_kernel_of<F, SUM>();
     const int grid = fused_grid<F, SUM>();
-    k<<<grid, kFusedThreads, 0, s>>>(io, p.numel);
+    k<<<grid, fused_threads<F, SUM>(), 0, s>>>(io, p.numel);
     ZC_LAUNCHED("fused region kernel");
     return ZPUCUDA_OK;
 }
