@@ -15,6 +15,7 @@
 //   * cudaMemcpyAsync for a contiguous view of the same type (clone).
 // HBM-bound: 1 read + 1 write per element.
 #include <cuda_fp16.h>
+#include <type_traits>
 
 #include <string>
 
@@ -104,6 +105,41 @@ __global__ void __launch_bounds__(kCopyThreads) copy_gather_kernel(const __grid_
             }
         }
         dst[i] = convert<S, D>(src[off]);
+    }
+}
+
+// Rows of a view (its last axis at least kRowMin long): each row's start
+// comes from one index walk over the leading axes, then its elements stream
+// with the last axis's stride -- coalesced for a unit (or -1) stride, 16-byte
+// loads when every row starts 16-byte aligned and the stride is 1.
+constexpr int64_t kRowMin = 64;
+
+template <class S, class D, bool VEC>
+__global__ void __launch_bounds__(kCopyThreads) copy_rows_kernel(const __grid_constant__ View v, D *dst, int64_t rows,
+                                                                 int64_t C) {
+    const S *src = (const S *)v.data;
+    const int64_t sc = v.strides[v.rank - 1];
+    constexpr int VS = 16 / sizeof(S);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        int64_t rem = r, off = 0;
+        for (int a = v.rank - 2; a >= 0; a--) {
+            const int64_t d = v.dims[a];
+            const int64_t q = rem / d;
+            off += (rem - q * d) * v.strides[a];
+            rem = q;
+        }
+        const S *srow = src + off;
+        D *drow = dst + r * C;
+        if (VEC) {
+            for (int64_t c = (int64_t)threadIdx.x * VS; c < C; c += (int64_t)kCopyThreads * VS) {
+                const uint4 x = __ldcs((const uint4 *)(srow + c));
+                const S *e = reinterpret_cast<const S *>(&x);
+#pragma unroll
+                for (int k = 0; k < VS; k++) drow[c + k] = convert<S, D>(e[k]);
+            }
+        } else {
+            for (int64_t c = threadIdx.x; c < C; c += kCopyThreads) drow[c] = convert<S, D>(srow[c * sc]);
+        }
     }
 }
 
@@ -234,6 +270,17 @@ int launch_copy(const View &v, void *dst, int64_t n, bool contig, cudaStream_t s
             return ZPUCUDA_OK;
         }
     }
+    if (!contig && r >= 1 && v.dims[r - 1] >= kRowMin) {
+        const int64_t C = v.dims[r - 1], rows = n / C;
+        constexpr int64_t VS = 16 / sizeof(S);
+        bool vec = v.strides[r - 1] == 1 && (uintptr_t)v.data % 16 == 0 && C % VS == 0;
+        for (int a = 0; a < r - 1; a++) vec = vec && (v.dims[a] == 1 || v.strides[a] % VS == 0);
+        int64_t g = rows < (int64_t)sms * 16 ? rows : (int64_t)sms * 16;
+        if (vec) copy_rows_kernel<S, D, true><<<(int)g, kCopyThreads, 0, s>>>(v, (D *)dst, rows, C);
+        else copy_rows_kernel<S, D, false><<<(int)g, kCopyThreads, 0, s>>>(v, (D *)dst, rows, C);
+        ZC_LAUNCHED("tensor copy (rows)");
+        return ZPUCUDA_OK;
+    }
     int64_t g = (n + kCopyThreads - 1) / kCopyThreads;
     if (g > (int64_t)sms * 16) g = (int64_t)sms * 16;
     if (contig) copy_gather_kernel<S, D, true><<<(int)g, kCopyThreads, 0, s>>>(v, (D *)dst, n);
@@ -310,6 +357,68 @@ __global__ void __launch_bounds__(kCopyThreads) take_kernel(const T *x, const I 
     }
 }
 
+// take with long rows (inner >= kRowMin): one block per output row (o, t),
+// the index resolved once, the row copied with coalesced (16-byte when
+// aligned) accesses.
+template <class T, class I, bool VEC>
+__global__ void __launch_bounds__(kCopyThreads) take_rows_kernel(const T *x, const I *indices, T *out, int64_t outer,
+                                                                 int64_t sdim, int64_t inner, int64_t k,
+                                                                 unsigned int *err) {
+    constexpr int VS = 16 / sizeof(T);
+    const int64_t rows = outer * k;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const int64_t t = row % k, o = row / k;
+        const int64_t ix = resolve_index<I>(indices[t], sdim);
+        T *orow = out + row * inner;
+        if (ix < 0) {
+            if (threadIdx.x == 0) atomicOr(err, 1u);
+            for (int64_t c = threadIdx.x; c < inner; c += kCopyThreads) orow[c] = from_f64<T>(0.0);
+            continue;
+        }
+        const T *xrow = x + (o * sdim + ix) * inner;
+        if (VEC) {
+            for (int64_t c = (int64_t)threadIdx.x * VS; c < inner; c += (int64_t)kCopyThreads * VS)
+                __stcs((uint4 *)(orow + c), __ldcs((const uint4 *)(xrow + c)));
+        } else {
+            for (int64_t c = threadIdx.x; c < inner; c += kCopyThreads) orow[c] = convert<T, T>(xrow[c]);
+        }
+    }
+}
+
+// ops.scatterAdd's indices, resolved once (zpu's rule; -1 and the error word
+// for one out of range).
+template <class I>
+__global__ void __launch_bounds__(kCopyThreads) resolve_kernel(const I *indices, int64_t k, int64_t sdim, int64_t *ix,
+                                                               unsigned int *err) {
+    for (int64_t t = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; t < k; t += (int64_t)gridDim.x * kCopyThreads) {
+        const int64_t r = resolve_index<I>(indices[t], sdim);
+        if (r < 0) atomicOr(err, 1u);
+        ix[t] = r;
+    }
+}
+
+// scatter_add with the target rows split into G groups (G a power of two):
+// thread (g, o, i) owns the output elements (o, r, i) with r % G == g and
+// walks all k updates in order, adding those that land on its rows -- each
+// output element still gets its updates in zpu's order, one thread per
+// element, and G threads share a column.
+template <class T>
+__global__ void __launch_bounds__(kCopyThreads) scatter_add_grouped_kernel(const int64_t *ix, const T *updates, T *out,
+                                                                           int64_t outer, int64_t sdim, int64_t inner,
+                                                                           int64_t k, int64_t G) {
+    const int64_t cols = outer * inner, total = cols * G;
+    for (int64_t id = (int64_t)blockIdx.x * kCopyThreads + threadIdx.x; id < total;
+         id += (int64_t)gridDim.x * kCopyThreads) {
+        const int64_t i = id % inner, rest = id / inner, o = rest % outer, g = rest / outer;
+        for (int64_t t = 0; t < k; t++) {
+            const int64_t r = __ldg(ix + t);
+            if (r < 0 || (r & (G - 1)) != g) continue;
+            T *d = out + (o * sdim + r) * inner + i;
+            *d = from_f64<T>(to_f64<T>(*d) + to_f64<T>(updates[(o * k + t) * inner + i]));
+        }
+    }
+}
+
 template <class T, class I>
 __global__ void __launch_bounds__(kCopyThreads) scatter_add_kernel(const I *indices, const T *updates, T *out,
                                                                    int64_t outer, int64_t sdim, int64_t inner, int64_t k,
@@ -364,12 +473,37 @@ int copy_view_from(const View &v, const View &w, int dst_dtype, int64_t n, cudaS
     return ZPUCUDA_OK;
 }
 
+template <class T, class I>
+int take_rows(const T *x, const void *indices, T *out, int64_t outer, int64_t sdim, int64_t inner, int64_t k,
+              unsigned int *err, cudaStream_t s) {
+    constexpr int64_t VS = 16 / sizeof(T);
+    // a plain copy of the bits for every type but i64 (zpu's round trip
+    // through f64), when rows start 16-byte aligned
+    const bool vec = !std::is_same<T, int64_t>::value;
+    const bool aligned = vec && inner % VS == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)out % 16 == 0;
+    int64_t g = outer * k;
+    if (g > (int64_t)num_sms() * 16) g = (int64_t)num_sms() * 16;
+    if (aligned) take_rows_kernel<T, I, true><<<(int)g, kCopyThreads, 0, s>>>(x, (const I *)indices, out, outer, sdim, inner, k, err);
+    else take_rows_kernel<T, I, false><<<(int)g, kCopyThreads, 0, s>>>(x, (const I *)indices, out, outer, sdim, inner, k, err);
+    ZC_LAUNCHED("take_rows_kernel");
+    return ZPUCUDA_OK;
+}
+
 template <class T>
 int take_typed(const void *x, int idx_dtype, const void *indices, void *out, int64_t outer, int64_t sdim,
                int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
     const int g = grid_for(outer * k * inner);
     const T *xx = (const T *)x;
     T *oo = (T *)out;
+    if (inner >= kRowMin) {
+        switch (idx_dtype) {
+        case ZPUCUDA_I64: return take_rows<T, int64_t>(xx, indices, oo, outer, sdim, inner, k, err, s);
+        case ZPUCUDA_I32: return take_rows<T, int32_t>(xx, indices, oo, outer, sdim, inner, k, err, s);
+        case ZPUCUDA_F32: return take_rows<T, float>(xx, indices, oo, outer, sdim, inner, k, err, s);
+        case ZPUCUDA_F64: return take_rows<T, double>(xx, indices, oo, outer, sdim, inner, k, err, s);
+        default: return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "take: index dtype");
+        }
+    }
     switch (idx_dtype) {
     case ZPUCUDA_I64: take_kernel<T, int64_t><<<g, kCopyThreads, 0, s>>>(xx, (const int64_t *)indices, oo, outer, sdim, inner, k, err); break;
     case ZPUCUDA_I32: take_kernel<T, int32_t><<<g, kCopyThreads, 0, s>>>(xx, (const int32_t *)indices, oo, outer, sdim, inner, k, err); break;
@@ -381,12 +515,44 @@ int take_typed(const void *x, int idx_dtype, const void *indices, void *out, int
     return ZPUCUDA_OK;
 }
 
+// Groups of target rows for the grouped scatter: enough threads to fill the
+// GPU (about 2^17), a power of two no larger than the rows, 1 when the
+// columns alone fill it.
+int64_t scatter_groups(int64_t cols, int64_t sdim) {
+    int64_t G = 1;
+    while (G * 2 <= sdim && cols * G * 2 <= (int64_t)1 << 17) G *= 2;
+    return G;
+}
+
 template <class T>
 int scatter_typed(int idx_dtype, const void *indices, const void *updates, void *out, int64_t outer, int64_t sdim,
                   int64_t inner, int64_t k, unsigned int *err, cudaStream_t s) {
     const int g = grid_for(outer * inner);
     const T *uu = (const T *)updates;
     T *oo = (T *)out;
+    const int64_t G = scatter_groups(outer * inner, sdim);
+    if (G > 1) {
+        int64_t *ix = nullptr;
+        ZC_CUDA(cudaMallocAsync((void **)&ix, (size_t)k * sizeof(int64_t), s));
+        const int gr = grid_for(k);
+        switch (idx_dtype) {
+        case ZPUCUDA_I64: resolve_kernel<int64_t><<<gr, kCopyThreads, 0, s>>>((const int64_t *)indices, k, sdim, ix, err); break;
+        case ZPUCUDA_I32: resolve_kernel<int32_t><<<gr, kCopyThreads, 0, s>>>((const int32_t *)indices, k, sdim, ix, err); break;
+        case ZPUCUDA_F32: resolve_kernel<float><<<gr, kCopyThreads, 0, s>>>((const float *)indices, k, sdim, ix, err); break;
+        case ZPUCUDA_F64: resolve_kernel<double><<<gr, kCopyThreads, 0, s>>>((const double *)indices, k, sdim, ix, err); break;
+        default:
+            cudaFreeAsync(ix, s);
+            return set_error(ZPUCUDA_ERR_NOT_SUPPORTED, "scatter_add: index dtype");
+        }
+        ZC_LAUNCHED("resolve_kernel");
+        scatter_add_grouped_kernel<T><<<grid_for(outer * inner * G), kCopyThreads, 0, s>>>(ix, uu, oo, outer, sdim, inner,
+                                                                                           k, G);
+        cudaError_t e = cudaGetLastError();
+        cudaFreeAsync(ix, s);
+        if (e != cudaSuccess) return cuda_fail(e, "scatter_add_grouped_kernel");
+        count_launch();
+        return ZPUCUDA_OK;
+    }
     switch (idx_dtype) {
     case ZPUCUDA_I64: scatter_add_kernel<T, int64_t><<<g, kCopyThreads, 0, s>>>((const int64_t *)indices, uu, oo, outer, sdim, inner, k, err); break;
     case ZPUCUDA_I32: scatter_add_kernel<T, int32_t><<<g, kCopyThreads, 0, s>>>((const int32_t *)indices, uu, oo, outer, sdim, inner, k, err); break;
