@@ -404,18 +404,37 @@ def mlp_parity(rank, world, dev):
     per = B // world
     xs = torch.from_numpy(np.ascontiguousarray(X[rank * per:(rank + 1) * per])).to(dev)
     ys = torch.from_numpy(np.ascontiguousarray(y[rank * per:(rank + 1) * per])).to(dev)
-    want = want_loss = None
+    want = want_loss = split = split_loss = None
     if rank == 0:
+        xd, yd = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
         m1 = zm.MLP(*dims, max_batch=B)
         m1.set_params(init)
-        xd, yd = torch.from_numpy(X).to(dev), torch.from_numpy(y).to(dev)
         for _ in range(steps):
             m1.value_and_grad(xd, yd)
             m1.adam_step()
         want, want_loss = m1.params(), m1.loss()
+        # the same N-way split of every sum on this one GPU: value_and_grad
+        # on each rank's rows, gradients and losses added in rank order in
+        # f32, one Adam step
+        m2 = zm.MLP(*dims, max_batch=B)
+        m2.set_params(init)
+        for _ in range(steps):
+            gsum = lsum = None
+            for r in range(world):
+                m2.value_and_grad(xd[r * per:(r + 1) * per].contiguous(), yd[r * per:(r + 1) * per].contiguous(),
+                                  global_batch=B)
+                g, l = m2.grads(), np.float32(m2.loss())
+                gsum = g if gsum is None else [a + b for a, b in zip(gsum, g)]
+                lsum = l if lsum is None else np.float32(lsum + l)
+            m2._write(zm.GRAD, gsum)
+            m2.adam_step()
+        split, split_loss = m2.params(), float(lsum)
         m1.close()
+        m2.close()
     out = {"net": "%d->%d->%d->%d" % dims, "global_batch": B, "adam_steps": steps,
-           "tolerance": "ranks bit-identical; rel. Frobenius <= 1e-5 per parameter and loss vs one GPU"}
+           "tolerance": "ranks bit-identical; rel. Frobenius <= 1e-5 per parameter and loss vs one GPU",
+           "split_emulation": "one GPU, value_and_grad on each rank's rows, sums in rank order (NCCL's ring "
+                              "order differs from rank order beyond 2 ranks)"}
     saved = os.environ.get("ZPUCUDA_MLP_PEER_EXCHANGE")
     try:
         for mode in ("1", "0"):
@@ -436,8 +455,13 @@ def mlp_parity(rank, world, dev):
                 rel = max(float(np.linalg.norm(g.astype(np.float64) - w) / np.linalg.norm(w.astype(np.float64)))
                           for g, w in zip(got, want))
                 lrel = abs(loss - want_loss) / abs(want_loss)
+                same = all(np.array_equal(g, w) for g, w in zip(got, split)) and loss == split_loss
+                srel = max(float(np.linalg.norm(g.astype(np.float64) - w) / np.linalg.norm(w.astype(np.float64)))
+                           for g, w in zip(got, split))
                 entry.update({"max_rel_fro_vs_1gpu": rel, "loss": loss, "loss_1gpu": want_loss,
                               "loss_rel_diff": lrel,
+                              "bit_identical_to_1gpu_split_emulation": same,
+                              "max_rel_fro_vs_1gpu_split_emulation": srel,
                               "within": entry["ranks_bit_identical"] and rel <= 1e-5 and lrel <= 1e-5})
             out["peer_exchange" if mode == "1" else "nccl"] = entry
     finally:

@@ -5,8 +5,10 @@ Each rank is a child process bound to its own GPU; the 128-byte NCCL id
 travels through a gloo process group.  Run once with dW2 exchanged over peer
 memory by its GEMM and once with NCCL alone.  After two train steps on halves of
 the batch (gradients summed over NCCL in the library's two buckets) every
-rank's parameters must equal each other bit for bit and match a one-GPU
-full-batch run within 1e-5 (the halves' partial sums re-associate).
+rank's parameters must equal each other bit for bit, match a one-GPU
+full-batch run within 1e-5 (the halves' partial sums re-associate), and
+equal bit for bit a one-GPU run of the same split (each half's gradients
+added in f32 in rank order before Adam).
 """
 import os
 import socket
@@ -103,6 +105,26 @@ def test_two_gpu_train_steps_match_one_gpu(tmp_path, peer, last_ar):
         assert np.array_equal(a, b), i
         assert np.linalg.norm(a - want[i]) <= 1e-5 * np.linalg.norm(want[i]), i
     assert abs(float(r0["loss"]) - m.loss()) <= 1e-5 * abs(m.loss())
+    # exactly the arithmetic of the split: one GPU, value_and_grad on each
+    # rank's half (loss averaged over the global batch), gradients and losses
+    # added in f32 in rank order, then Adam -- bit for bit the 2-GPU result
+    per = B // 2
+    e = zm.MLP(*DIMS, max_batch=B)
+    e.set_params(zo.mlp_init(DIMS))
+    for _ in range(STEPS):
+        gsum = lsum = None
+        for r in range(2):
+            e.value_and_grad(xd[r * per:(r + 1) * per].contiguous(), yd[r * per:(r + 1) * per].contiguous(),
+                             global_batch=B)
+            g, l = e.grads(), np.float32(e.loss())
+            gsum = g if gsum is None else [a + b for a, b in zip(gsum, g)]
+            lsum = l if lsum is None else np.float32(lsum + l)
+        e._write(zm.GRAD, gsum)
+        e.adam_step()
+    split = e.params()
+    for i in range(6):
+        assert np.array_equal(r0["arr_%d" % i], split[i]), i
+    assert np.float32(r0["loss"]) == lsum
 
 
 JOIN_SCRIPT = textwrap.dedent("""
