@@ -521,39 +521,58 @@ ZO_EXPORT float zo_jit_chain_tanh_sq_affine_sum(const float *x, size_t n, float 
 /* Adam: src/zpu/optim.zig:149-265, std.math.pow restated                    */
 /* ------------------------------------------------------------------------ */
 
-/* Zig's std.math.pow follows Go's math.Pow: the integer part of y by
- * repeated squaring on the frexp mantissa with a separately tracked binary
- * exponent, the fractional part (if any) through exp(yf*log(x)), then ldexp.
- * Restated here for finite x > 0 and finite y (all Adam needs). */
+/* Zig's std.math.pow(f64), which scalar.zig:151-153 calls, restated branch
+ * for branch (it follows Go's math.Pow): the special values of x and y, a
+ * half power as sqrt, then the integer part of |y| by repeated squaring of
+ * frexp(x)'s mantissa with a separately tracked binary exponent, the
+ * fractional part (if any) through exp(yf*log(x)), and one ldexp. */
+static int odd_integer(double x) {
+    if (fabs(x) >= 9007199254740992.0) return 0; /* 2^53 */
+    double ip;
+    double fp = modf(x, &ip);
+    return fp == 0.0 && (((long long)ip) & 1) == 1;
+}
 static double go_pow(double x, double y) {
-    if (y == 0.0 || x == 1.0) return 1.0;
-    if (y == 1.0) return x;
-    if (x != x || y != y) return NAN;
-    if (x <= 0.0 || isinf(x) || isinf(y)) return pow(x, y);
+    for (int pass = 0; pass < 2; pass++) {
+        if (y == 0.0 || x == 1.0) return 1.0;
+        if (x != x || y != y) return NAN;
+        if (y == 1.0) return x;
+        if (x == 0.0) {
+            if (y < 0.0) return odd_integer(y) ? copysign(INFINITY, x) : INFINITY;
+            return odd_integer(y) ? x : 0.0;
+        }
+        if (isinf(y)) {
+            if (x == -1.0) return 1.0;
+            return ((fabs(x) < 1.0) == (y > 0.0)) ? 0.0 : INFINITY;
+        }
+        if (!isinf(x)) break;
+        if (x > 0.0) return y < 0.0 ? 0.0 : INFINITY;
+        x = 1.0 / x; /* pow(-inf, y) = pow(-0, -y) */
+        y = -y;
+    }
     if (y == 0.5) return sqrt(x);
     if (y == -0.5) return 1.0 / sqrt(x);
-    double ay = fabs(y);
     double yi;
-    double yf = modf(ay, &yi);
-    if (yi >= 9.223372036854775808e18) return pow(x, y);
+    double yf = modf(fabs(y), &yi);
+    if (yf != 0.0 && x < 0.0) return NAN;
+    if (yi >= 9.223372036854775808e18) return exp(y * log(x));
     double a1 = 1.0;
-    long ae = 0;
+    int ae = 0;
     if (yf != 0.0) {
         if (yf > 0.5) { yf -= 1.0; yi += 1.0; }
         a1 = exp(yf * log(x));
     }
-    int xe_i;
-    double x1 = frexp(x, &xe_i);
-    long xe = xe_i;
-    for (int64_t i = (int64_t)yi; i != 0; i >>= 1) {
-        if (xe < -(1L << 12) || (1L << 12) < xe) { ae += xe; break; }
+    int xe;
+    double x1 = frexp(x, &xe);
+    for (long long i = (long long)yi; i != 0; i >>= 1) {
+        if (xe < -(1 << 12) || (1 << 12) < xe) { ae += xe; break; }
         if (i & 1) { a1 *= x1; ae += xe; }
         x1 *= x1;
         xe <<= 1;
         if (x1 < 0.5) { x1 += x1; xe--; }
     }
     if (y < 0) { a1 = 1.0 / a1; ae = -ae; }
-    return ldexp(a1, (int)ae);
+    return ldexp(a1, ae);
 }
 ZO_EXPORT double zo_pow(double x, double y) { return go_pow(x, y); }
 

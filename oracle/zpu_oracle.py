@@ -379,7 +379,8 @@ def reduce_bool(x, kind, axis=AXIS_NONE, keepdims=False, depth=0):
 def cumsum(x, axis, reverse=False, depth=0):
     """ops.cumsum (src/zpu/ops.zig:2032-2060): along ops.realAxis (a
     non-negative axis counts from the first payload axis, no AXIS_NONE), a
-    running f64 sum, each prefix rounded to x's type; `reverse` from the end."""
+    running f64 sum, each prefix written into x's type as writeF64 writes it
+    (rounded for floats, scalar.fromF64 for i64); `reverse` from the end."""
     x = np.asarray(x)
     ax = axis + depth if axis >= 0 else axis + x.ndim
     if ax < 0 or ax >= x.ndim:
@@ -394,7 +395,7 @@ def cumsum(x, axis, reverse=False, depth=0):
         out[..., d] = acc
     if reverse:
         out = out[..., ::-1]
-    return np.moveaxis(out, -1, ax).astype(x.dtype)
+    return from_f64(np.moveaxis(out, -1, ax), x.dtype)  # writeF64
 
 
 # zpu DType order (src/zpu/dtype.zig:4-13) as numpy types
@@ -429,6 +430,73 @@ def from_f64(v, dt):
         out[top] = info.max
         return out
     return t.astype(dt)
+
+
+# ------------------------------------------------------------ i64 values
+I64_INT_BINARY = ("add", "sub", "mul", "mod_op", "maximum", "minimum")
+I64_INT_UNARY = ("abs", "sign", "relu")
+
+
+def binary_i64(prim, a, b):
+    """scalar.binary(i64, p, a, b) (src/zpu/scalar.zig:285-302) for two i64
+    operands whose result type is i64: + - * on the integers (two's-complement
+    wrap where zpu's own would overflow), mod with a zero divisor giving a and
+    @mod's sign of the divisor otherwise, max / min; every other prim is the
+    f64 computation of the operands read as f64, written back by fromF64."""
+    a, b = np.broadcast_arrays(np.asarray(a, dtype=np.int64), np.asarray(b, dtype=np.int64))
+    if prim in I64_INT_BINARY:
+        with np.errstate(over="ignore"):
+            if prim == "add":
+                return a + b
+            if prim == "sub":
+                return a - b
+            if prim == "mul":
+                return a * b
+            if prim == "maximum":
+                return np.maximum(a, b)
+            if prim == "minimum":
+                return np.minimum(a, b)
+        safe = np.where((b == 0) | (b == -1), 1, b)
+        return np.where(b == 0, a, np.where(b == -1, 0, np.mod(a, safe)))
+    return from_f64(binary(prim, to_f64(a), to_f64(b)), np.int64)
+
+
+def unary_i64(prim, x):
+    """scalar.unary(i64, p, x) (src/zpu/scalar.zig:262-283): relu, abs and
+    sign on the integer; the rest through f64 and fromF64."""
+    x = np.asarray(x, dtype=np.int64)
+    if prim == "abs":
+        with np.errstate(over="ignore"):
+            return np.where(x < 0, -x, x)
+    if prim == "sign":
+        return np.sign(x).astype(np.int64)
+    if prim == "relu":
+        return np.where(x > 0, x, 0).astype(np.int64)
+    return from_f64(unary(prim, to_f64(x)), np.int64)
+
+
+def where_i64(cond, a, b):
+    """ops.where with two i64 branches (src/zpu/ops.zig:572-590): both read
+    as f64, the chosen one written back into an i64 by fromF64."""
+    return from_f64(np.where(to_f64(cond) != 0, to_f64(a), to_f64(b)), np.int64)
+
+
+def reduce_i64(x, prim, axis=AXIS_NONE, keepdims=False, depth=0):
+    """ops.reduceOp of an i64 tensor (src/zpu/ops.zig:662-700, 820-869): sum
+    and prod wrap in the integer type (+%, *%), max / min on the integers;
+    an empty reduction gives the identity zpu writes through fromF64 (0, 1,
+    minInt for -inf, maxInt for +inf)."""
+    x = np.asarray(x, dtype=np.int64)
+    axes = reduced_axes(x.ndim, axis, depth)
+    with np.errstate(over="ignore"):
+        if prim == "sum":
+            return np.sum(x, axis=axes, keepdims=bool(keepdims), dtype=np.int64)
+        if prim == "prod_op":
+            return np.prod(x, axis=axes, keepdims=bool(keepdims), dtype=np.int64)
+    info = np.iinfo(np.int64)
+    if prim == "max_reduce":
+        return np.max(x, axis=axes, keepdims=bool(keepdims), initial=info.min)
+    return np.min(x, axis=axes, keepdims=bool(keepdims), initial=info.max)
 
 
 def tensor_copy(x, dt):

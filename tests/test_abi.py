@@ -123,7 +123,11 @@ def test_lowering_types_i64_operands_as_zpu_promotes(capi):
     """argmax / argmin give i64 (ops.zig:931-934); an i64 operand against a
     float gives the float type; i64 operands alone give i64, f32 for the
     float-only prims and div, bool for predicates (DType.promote,
-    dtype.zig:89-104; unaryOutDType / binaryOutDType, ops.zig:268-285)."""
+    dtype.zig:89-104; unaryOutDType / binaryOutDType, ops.zig:268-285); sum /
+    prod / max / min of i64 give i64 (reduceOutDType, ops.zig:813-818).  The
+    region holding them runs on 64-bit words: + - * max min mod abs sign relu
+    of two i64 values on the integers, the rest through f64 (i2f / f2i), f32
+    results of an i64 operand rounded once (r32)."""
     import zpu_b200 as zc
     F, I, B = zc.F32, zc.DT_I64, zc.DT_BOOL
     args = [(1, F, (8, 10)), (2, I, (8,)), (3, F, (8,))]
@@ -134,14 +138,24 @@ def test_lowering_types_i64_operands_as_zpu_promotes(capi):
     shp = (8,)
     assert p.outputs == [(I, shp), (B, shp), (F, shp), (B, shp), (I, shp), (I, shp), (F, shp), (F, shp), (I, shp)]
     d = p.describe()
-    assert "bytecode" in d and "to_i64" in d and "catalogue" not in d, d
+    assert "bytecode" in d and "catalogue" not in d, d
+    for word in ("w64", "iadd(", "isign(", "f2i(", "i2f(", "r32("):
+        assert word in d, (word, d)
     w = zc.Plan(args + [(4, B, (8,))], [], [("argmax", [1], 10, 1, 0), ("where", [4, 2, 10], 11, -2, 0),
                                             ("where", [4, 2, 3], 12, -2, 0)], [10, 11, 12])
     assert w.outputs == [(I, shp), (I, shp), (F, shp)]
-    for bad in [("pow", [10, 2], 11, -2, 0), ("sum", [10], 11, -2, 0), ("where", [2, 10, 10], 11, -2, 0),
-                ("where", [3, 10, 2], 11, -2, 0)]:
+    # (a reduction's plan needs a device workspace: its typing is checked in
+    # the GPU tests)
+    for step, want in [(("pow", [10, 2], 11, -2, 0), (I, shp)), (("where", [2, 10, 10], 11, -2, 0), (I, shp)),
+                       (("where", [3, 10, 2], 11, -2, 0), (I, shp)), (("cumsum", [2], 11, 0, 0), (I, shp))]:
+        # the argmax result is an output too: a plan made without a GPU
+        # cannot allocate an intermediate
+        q = zc.Plan(args, [], [("argmax", [1], 10, 1, 0), step], [10, 11])
+        assert q.outputs[1] == want, step
+    assert "zpow(" in zc.Plan(args, [], [("argmax", [1], 10, 1, 0), ("pow", [10, 2], 11, -2, 0)], [10, 11]).describe()
+    for bad in [("add", [10, 4], 11, -2, 0), ("sum", [4], 11, -2, 0)]:  # i64 + bool; a sum of bools
         with pytest.raises(zc.ZpuCudaError) as e:
-            zc.Plan(args, [], [("argmax", [1], 10, 1, 0), bad], [11])
+            zc.Plan(args + [(4, B, (8,))], [], [("argmax", [1], 10, 1, 0), bad], [10, 11])
         assert e.value.name == "NotSupported", bad
 
 

@@ -601,8 +601,7 @@ def test_i64_operands_follow_zpus_promotion(zc):
     """eq(argmax(logits, 1), labels) -- a classifier's hits -- and i64
     values against floats: argmax's i64 result feeds the next region as an
     input read as zpu reads it (readAtF64), each result typed by
-    DType.promote / binaryOutDType (dtype.zig:89-104, ops.zig:275-285);
-    pow of two i64 values stays outside the lowering."""
+    DType.promote / binaryOutDType (dtype.zig:89-104, ops.zig:275-285)."""
     logits = zo.uniform_range(71, 64 * 10, -3.0, 3.0).reshape(64, 10).astype(np.float32)
     lab = (np.arange(64, dtype=np.int64) * 7) % 10
     scale = zo.uniform_range(72, 64, -2.0, 2.0).astype(np.float32)
@@ -625,15 +624,13 @@ def test_i64_operands_follow_zpus_promotion(zc):
                 [("eq", [1, 2], 10, -2, 0), ("lt", [1, 2], 11, -2, 0)], [10, 11])
     e, l = [o.cpu().numpy() for o in q.run([torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()])]
     assert e.tolist() == [False, True, False, True] and l.tolist() == [False, False, True, False]
-    with pytest.raises(zc.ZpuCudaError) as err:  # pow of two i64 values: zpu's exact integer pow
-        zc.Plan([(1, zc.DT_I64, (4,)), (2, zc.DT_I64, (4,))], [], [("pow", [1, 2], 10, -2, 0)], [10])
-    assert err.value.status == 9
 
 
 def test_i64_arithmetic_is_zpus_f64_compute_and_write_back(zc):
-    """Steps of i64 values alone: each element computed from the operands
-    read as f64 and written back as zpu writes an i64 (0 for NaN, clamp,
-    truncate; scalar.zig:7-27) -- recip(2) is 0 before it is multiplied;
+    """Steps of i64 values alone outside scalar.binary's integer set: each
+    element computed from the operands read as f64 and written back as zpu
+    writes an i64 (0 for NaN, clamp, truncate; scalar.zig:7-27) -- recip(2)
+    is 0 before it is multiplied;
     div and the float-only prims give f32 (ops.zig:268-285); where takes
     the promoted type of its branches."""
     a = np.array([7, -7, 2 ** 40 + 3, -(2 ** 52) + 1, 0, 9], dtype=np.int64)
@@ -668,6 +665,127 @@ def test_i64_arithmetic_is_zpus_f64_compute_and_write_back(zc):
     w1, w2 = [o.cpu().numpy() for o in q.run([torch.from_numpy(v).cuda() for v in (a, b, c, x)])]
     assert w1.dtype == np.int64 and np.array_equal(w1, np.where(c, a, b))
     assert w2.dtype == np.float32 and np.array_equal(w2, np.where(c, zo.from_f64(af, np.float32), x))
+
+
+def _i64_run(zc, args, steps, outs, arrays):
+    p = zc.Plan(args, [], steps, outs)
+    return p, [o.cpu().numpy() for o in p.run([torch.from_numpy(v).cuda() for v in arrays])]
+
+
+def test_i64_steps_run_on_the_integers(zc):
+    """scalar.binary / scalar.unary of two i64 values (scalar.zig:262-302):
+    + - * wrap in two's complement, mod with a zero divisor gives a and
+    otherwise the divisor's sign, max / min / abs / sign / relu on the
+    integers -- exact beyond 2^53, where an f64 computation would round;
+    neg and the rest go through f64 and fromF64 (neg(minInt) clamps)."""
+    big = 2 ** 62
+    a = np.array([big + 5, -big - 7, 2 ** 53 + 1, -3, 0, 9, 7, -(2 ** 63), 2 ** 63 - 1, 12345678901234567,
+                  -12345678901234567, 2 ** 53 + 3], dtype=np.int64)
+    b = np.array([3, -big, 1, 4, -1, -9, 0, 5, -1, 99991, 99991, -(2 ** 53) - 1], dtype=np.int64)
+    names = ["add", "sub", "mul", "mod_op", "maximum", "minimum"]
+    steps = [(nm, [1, 2], 10 + k, -2, 0) for k, nm in enumerate(names)]
+    unames = ["abs", "sign", "relu", "neg", "square"]
+    steps += [(nm, [1], 20 + k, -2, 0) for k, nm in enumerate(unames)]
+    outs = [10 + k for k in range(len(names))] + [20 + k for k in range(len(unames))]
+    p, got = _i64_run(zc, [(1, zc.DT_I64, a.shape), (2, zc.DT_I64, b.shape)], steps, outs, (a, b))
+    assert "w64" in p.describe() and "iadd(" in p.describe()
+    for k, nm in enumerate(names):
+        want = zo.binary_i64(nm, a, b)
+        assert got[k].dtype == np.int64 and np.array_equal(got[k], want), (nm, got[k], want)
+    for k, nm in enumerate(unames):
+        want = zo.unary_i64(nm, a)
+        assert np.array_equal(got[len(names) + k], want), (nm, got[len(names) + k], want)
+    # the integer result is not the f64 one: 2^53 + 1 + 1 and a wrapped sum
+    assert got[0][2] == 2 ** 53 + 2 and got[0][0] == zo.binary_i64("add", a[:1], b[:1])[0]
+    assert got[1][8] == np.int64(-(2 ** 63)) and got[3][2] == 0 and got[3][6] == 7
+
+
+def test_i64_pow_is_zigs_pow_written_back(zc):
+    """pow of two i64 values: std.math.pow(f64) on the operands read as f64
+    (scalar.zig:151-153), written back by fromF64 -- the repeated-squaring
+    product with its separate binary exponent, so odd powers above 2^53 have
+    zpu's bits, negative exponents truncate to 0 (or +-1), 0^-k is +inf and
+    clamps to maxInt."""
+    x = np.array([-3, 2, 7, 10, -2, 3, 0, 1, 5, 2, -1, 0, 11, 2, -7, 3], dtype=np.int64)
+    y = np.array([3, 10, 19, 18, 63, -1, 0, 40, 27, 62, -5, -3, 17, 64, 21, 39], dtype=np.int64)
+    p, (got, f) = _i64_run(zc, [(1, zc.DT_I64, x.shape), (2, zc.DT_I64, y.shape), (3, zc.F32, x.shape)],
+                           [("pow", [1, 2], 10, -2, 0), ("pow", [1, 3], 11, -2, 0)], [10, 11],
+                           (x, y, y.astype(np.float32) * 0.25))
+    assert "zpow(" in p.describe()
+    want = zo.binary_i64("pow", x, y)
+    assert got.dtype == np.int64 and np.array_equal(got, want), (got, want)
+    assert got[0] == -27 and got[1] == 1024 and got[11] == 2 ** 63 - 1 and got[10] == -1
+    # an i64 base against an f32 exponent: the f32 type, std.math.pow in f64
+    # rounded once (binaryKernelF64, ops.zig:245-253)
+    wantf = zo.from_f64(zo.binary("pow", x.astype(np.float64), (y.astype(np.float32) * 0.25).astype(np.float64)),
+                        np.float32)
+    assert f.dtype == np.float32
+    fin = np.isfinite(wantf)
+    assert np.array_equal(np.isnan(f), np.isnan(wantf))
+    assert ulp_diff_f32(f[fin], wantf[fin]).max() <= 1
+
+
+def test_i64_reductions_wrap_in_the_integer_type(zc):
+    """sum / prod / max / min of i64 values stay i64 (reduceOutDType,
+    ops.zig:813-818) and run on the integers: +% and *% wrap (reduceStep,
+    ops.zig:686-700), so the result is exact where an f64 sum would round;
+    every axis form, keepdims, and the empty reduction's identities written
+    through fromF64 (0, 1, minInt, maxInt; ops.zig:822-838)."""
+    rng = np.random.default_rng(7)
+    x = rng.integers(-(2 ** 62), 2 ** 62, size=(6, 7, 5), dtype=np.int64)
+    s = rng.integers(-9, 10, size=(6, 7, 5), dtype=np.int64)
+    args = [(1, zc.DT_I64, x.shape), (2, zc.DT_I64, s.shape)]
+    cases = [(prim, axis, keep) for prim in ("sum", "prod_op", "max_reduce", "min_reduce")
+             for axis, keep in ((-2, 0), (0, 0), (1, 1), (-1, 0))]
+    for prim, axis, keep in cases:
+        for arr in (x, s):
+            p, (got,) = _i64_run(zc, [(1, zc.DT_I64, arr.shape)], [(prim, [1], 10, axis, keep)], [10], (arr,))
+            want = zo.reduce_i64(arr, prim, axis, bool(keep))
+            assert got.dtype == np.int64 and got.shape == np.shape(want), (prim, axis, got.shape)
+            assert np.array_equal(got, want), (prim, axis, keep)
+    p = zc.Plan(args, [], [("sum", [1], 10, -2, 0)], [10])
+    assert "red=isum" in p.describe()
+    # fused: sum(a * b + a) of i64 values, one region on 64-bit words
+    p, (got,) = _i64_run(zc, args, [("mul", [1, 2], 10, -2, 0), ("add", [10, 1], 11, -2, 0),
+                                    ("sum", [11], 12, 1, 0)], [12], (x, s))
+    assert p.num_kernels() == 1
+    want = zo.reduce_i64(zo.binary_i64("add", zo.binary_i64("mul", x, s), x), "sum", 1)
+    assert np.array_equal(got, want)
+    # empty reductions: the identities as zpu writes them into an i64
+    e = np.zeros((0, 4), dtype=np.int64)
+    for prim, ident in (("sum", 0), ("prod_op", 1), ("max_reduce", -(2 ** 63)), ("min_reduce", 2 ** 63 - 1)):
+        _, (got,) = _i64_run(zc, [(1, zc.DT_I64, e.shape)], [(prim, [1], 10, -2, 0)], [10], (e,))
+        assert got.dtype == np.int64 and int(got) == ident, prim
+        _, (got,) = _i64_run(zc, [(1, zc.DT_I64, e.shape)], [(prim, [1], 10, 0, 0)], [10], (e,))
+        assert got.tolist() == [ident] * 4, prim
+
+
+def test_i64_cumsum_and_where_as_zpu_writes_them(zc):
+    """cumsum of i64 (ops.cumsum, ops.zig:2032-2057): an f64 running sum,
+    each prefix written by fromF64 -- it rounds above 2^53 as zpu's does;
+    where of two i64 branches reads and writes through f64 (ops.zig:572-590),
+    argmax feeding i64 arithmetic in the next region."""
+    x = np.array([[2 ** 53, 1, 1, 1, -5], [3, -(2 ** 62), -(2 ** 62), -(2 ** 62), 7]], dtype=np.int64)
+    for axis, flags in ((1, 0), (0, 0), (1, REVERSE), (-1, 0)):
+        _, (got,) = _i64_run(zc, [(1, zc.DT_I64, x.shape)], [("cumsum", [1], 10, axis, flags)], [10], (x,))
+        want = zo.cumsum(x, axis, reverse=bool(flags))
+        assert got.dtype == np.int64 and np.array_equal(got, want), (axis, flags, got, want)
+    assert zo.cumsum(x, 1)[0, 1] == 2 ** 53  # 2^53 + 1 rounds in the f64 accumulator
+    c = np.array([True, False, True, False, True])
+    a = np.array([2 ** 53 + 1, 4, -(2 ** 63), 2 ** 63 - 1, 6], dtype=np.int64)
+    b = np.array([1, 2 ** 60 + 1, 3, 5, -1], dtype=np.int64)
+    _, (w,) = _i64_run(zc, [(1, zc.DT_BOOL, c.shape), (2, zc.DT_I64, a.shape), (3, zc.DT_I64, b.shape)],
+                       [("where", [1, 2, 3], 10, -2, 0)], [10], (c, a, b))
+    assert np.array_equal(w, zo.where_i64(c, a, b))
+    logits = zo.uniform_range(91, 16 * 9, -1.0, 1.0).reshape(16, 9).astype(np.float32)
+    off = np.arange(16, dtype=np.int64) * (2 ** 55 + 3)
+    p, (am, r) = _i64_run(zc, [(1, zc.F32, logits.shape), (2, zc.DT_I64, off.shape)],
+                          [("argmax", [1], 10, 1, 0), ("add", [10, 2], 11, -2, 0), ("mul", [11, 11], 12, -2, 0),
+                           ("max_reduce", [12], 13, -2, 0)], [10, 13], (logits, off))
+    want_am = zo.arg_reduce(logits, 1, want_max=True)
+    assert np.array_equal(am, want_am)
+    t = zo.binary_i64("add", want_am, off)
+    assert int(r) == int(zo.reduce_i64(zo.binary_i64("mul", t, t), "max_reduce"))
 
 
 REVERSE = 32  # prims.Attrs.REVERSE

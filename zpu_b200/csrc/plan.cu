@@ -352,19 +352,18 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         const bool takes_bool = pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim) ||
                                 st.prim == PRIM_WHERE;
         // i64 values (argmax / argmin results, i64 arguments) enter
-        // element-wise steps, typed as zpu types them (DType.promote,
-        // dtype.zig:89-104: floats win; unaryOutDType / binaryOutDType,
-        // ops.zig:268-285): against a float the float type; of i64 values
-        // alone an i64, except the float-only prims and div (f32) and the
-        // predicates (bool).  Every element is computed from its operands
-        // read as f64; an i64 result is written back as zpu writes it.
+        // element-wise steps and reductions, typed as zpu types them
+        // (DType.promote, dtype.zig:89-104: floats win; unaryOutDType /
+        // binaryOutDType, ops.zig:268-285; reduceOutDType, ops.zig:813-818):
+        // against a float the float type; of i64 values alone an i64, except
+        // the float-only prims and div (f32) and the predicates (bool); sum /
+        // prod / max / min of i64 values an i64.
         for (int k = 0; k < st.n_inputs && (region_unary(st.prim) || region_binary(st.prim) ||
                                             region_reduce(st.prim) || st.prim == PRIM_WHERE);
              k++) {
             const int dt = vals[st.ins[k]].dtype;
-            const bool ok = float_dtype(dt) || (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0)) ||
-                            (dt == ZPUCUDA_I64 && (region_binary(st.prim) || region_unary(st.prim) ||
-                                                   (st.prim == PRIM_WHERE && k > 0)));
+            const bool ok = float_dtype(dt) || dt == ZPUCUDA_I64 ||
+                            (dt == ZPUCUDA_BOOL && takes_bool && !(st.prim == PRIM_WHERE && k > 0));
             if (!ok) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "prim " + prim_name(st.prim) + " on a value of dtype " + std::to_string(dt));
         }
         if (pred_unary(st.prim) || pred_binary(st.prim) || bool_reduce(st.prim)) o.dtype = ZPUCUDA_BOOL;
@@ -379,14 +378,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 (math_binary(st.prim) && a.dtype != b.dtype && !int_and_float))
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in an element-wise step");
             if (math_binary(st.prim) && int_and_float) o.dtype = float_dtype(a.dtype) ? a.dtype : b.dtype;
-            if (math_binary(st.prim) && a.dtype == ZPUCUDA_I64 && b.dtype == ZPUCUDA_I64) {
-                // pow of two integers: zpu's pow multiplies exactly for an
-                // integral exponent; the device's f64 pow may land an ulp
-                // below an integer, which the i64 write would truncate
-                if (st.prim == PRIM_POW)
-                    return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "pow of two i64 values");
+            if (math_binary(st.prim) && a.dtype == ZPUCUDA_I64 && b.dtype == ZPUCUDA_I64)
                 o.dtype = (float_only(st.prim) || st.prim == PRIM_DIV) ? ZPUCUDA_F32 : ZPUCUDA_I64;
-            }
             if (a.depth != b.depth && a.shape.rank && b.shape.rank)
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "vmap depth mismatch in an element-wise step");
             o.depth = std::max(a.depth, b.depth);
@@ -394,12 +387,11 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         } else if (st.prim == PRIM_WHERE && st.n_inputs == 3) {
             // where(cond, a, b): a / b broadcast, then with cond; the type
             // DType.promote(a, b) (ops.zig:572-576): i64 when both are i64,
-            // else the float one
+            // else the float one; the condition is any value's v != 0
             const Value &x = vals[st.ins[1]], &y = vals[st.ins[2]];
             const bool xi = x.dtype == ZPUCUDA_I64, yi = y.dtype == ZPUCUDA_I64;
             const int odt = (xi && yi) ? ZPUCUDA_I64 : xi ? y.dtype : x.dtype;
-            if ((!xi && !yi && x.dtype != y.dtype) ||
-                !carriers_agree(carrier_of(a.dtype), odt == ZPUCUDA_I64 ? ZPUCUDA_F64 : odt))
+            if ((!xi && !yi && x.dtype != y.dtype) || !carriers_agree(carrier_of(a.dtype), carrier_of(odt)))
                 return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "mixed dtypes in where");
             Shape xy;
             if (!broadcast(x.shape, y.shape, &xy) || !broadcast(xy, a.shape, &o.shape))
@@ -653,7 +645,10 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             }
         } else if (st.prim == PRIM_CUMSUM && st.n_inputs == 1) {
             // ops.realAxis (src/zpu/ops.zig:1466-1471): vmap-aware, no AXIS_NONE
-            if (!float_dtype(a.dtype)) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "cumsum of a non-float value");
+            // f64 accumulator, each prefix written as the element type
+            // (ops.cumsum, ops.zig:2032-2057): floats and i64
+            if (!float_dtype(a.dtype) && a.dtype != ZPUCUDA_I64)
+                return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "cumsum of a bool or narrow integer value");
             const int ax = st.axis >= 0 ? st.axis + a.depth : st.axis + a.shape.rank;
             if (ax < 0 || ax >= a.shape.rank) return lower_fail(plan, ZPUCUDA_ERR_INVALID_AXIS, "cumsum axis");
             o.shape = a.shape;
@@ -1028,7 +1023,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             if (L.mc.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
             char buf[160];
             snprintf(buf, sizeof buf, "  kernel %zu: cumsum %s axis %d%s (%%%llu = cumsum(%%%llu))\n",
-                     plan->launches.size(), a.dtype == ZPUCUDA_F64 ? "f64" : "f32", ax, L.reverse ? " reverse" : "",
+                     plan->launches.size(), a.dtype == ZPUCUDA_F64 ? "f64" : a.dtype == ZPUCUDA_I64 ? "i64" : "f32", ax, L.reverse ? " reverse" : "",
                      (unsigned long long)st0.out, (unsigned long long)st0.ins[0]);
             L.text = buf;
             plan->launches.push_back(L);
@@ -1048,14 +1043,10 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         int e = s;
         // first pass: which steps join
         // the float type a step computes in: its output's, else its inputs'
+        // (i64 and bool values need no float type: they join any region)
         auto step_carrier = [&](const zpucuda_step &st) {
-            // an i64 result, and a predicate of i64 values, are computed in
-            // f64 registers as zpu computes them: exact below 2^53
-            if (vals[st.out].dtype == ZPUCUDA_I64 && !region_reduce(st.prim)) return (int)ZPUCUDA_F64;
             int c = carrier_of(vals[st.out].dtype);
             for (int k = 0; k < st.n_inputs && c < 0; k++) c = carrier_of(vals[st.ins[k]].dtype);
-            for (int k = 0; k < st.n_inputs && c < 0; k++)
-                if (vals[st.ins[k]].dtype == ZPUCUDA_I64) c = ZPUCUDA_F64;
             return c;
         };
         for (; e < n_steps; e++) {
@@ -1081,16 +1072,18 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             }
             break;
         }
-        if (rdtype < 0) {
-            // no float value: bools ride as f32; i64 operands (predicates of
-            // two i64 values) are compared in f64, exact below 2^53
-            bool any_i64 = false;
-            for (int m : member)
-                for (int k = 0; k < steps[m].n_inputs; k++) any_i64 |= vals[steps[m].ins[k]].dtype == ZPUCUDA_I64;
-            rdtype = any_i64 ? ZPUCUDA_F64 : ZPUCUDA_F32;
+        // an i64 value anywhere in the region (an operand, a step's result,
+        // the reduced value): 64-bit registers (RegionProgram::words64)
+        bool words64 = false;
+        for (int m : member) {
+            for (int k = 0; k < steps[m].n_inputs; k++) words64 |= vals[steps[m].ins[k]].dtype == ZPUCUDA_I64;
+            if (!region_reduce(steps[m].prim)) words64 |= vals[steps[m].out].dtype == ZPUCUDA_I64;
         }
+        // no float value: bools ride as f32, i64 regions store no float
+        if (rdtype < 0) rdtype = words64 ? ZPUCUDA_F64 : ZPUCUDA_F32;
         if (member.empty()) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "step " + std::to_string(s) + " cannot start a region");
         P.dtype = rdtype;
+        P.words64 = words64 ? 1 : 0;
         P.rank = rshape.rank;
         for (int i = 0; i < rshape.rank; i++) P.dims[i] = rshape.dims[i];
         P.numel = rshape.numel();
@@ -1108,7 +1101,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             }
         if ((int)loads.size() > RP_MAX_IN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region has too many inputs");
         P.n_in = (int)loads.size();
-        std::string sig = std::string(rdtype == ZPUCUDA_F64 ? "f64" : "f32") + ";";
+        std::string sig = std::string(rdtype == ZPUCUDA_F64 ? "f64" : "f32") + (words64 ? "w64" : "") + ";";
         std::string kinds;
         for (int k = 0; k < P.n_in; k++) {
             Value &iv = vals[loads[k]];
@@ -1167,6 +1160,57 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
         bool has_red = false;
         int red_prim = -1, red_axis = ZPUCUDA_AXIS_NONE, red_depth = 0;
         uint64_t red_in = 0, red_out_id = 0;
+        // one instruction into a fresh register; -1 when the region is full
+        auto push = [&](uint8_t op, int na, int a, int b, int c, uint8_t flag, const std::string &name) -> int {
+            if (nreg >= RP_MAX_REG || n_insn >= RP_MAX_INSN) return -1;
+            P.insn[n_insn++] = Insn{op, (uint8_t)nreg, (uint8_t)a, (uint8_t)b, (uint8_t)(na > 2 ? c : flag)};
+            char buf[96];
+            if (na > 2) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d,r%d)", nreg, name.c_str(), a, b, c);
+            else if (na > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, name.c_str(), a, b);
+            else snprintf(buf, sizeof buf, ";r%d=%s(r%d)", nreg, name.c_str(), a);
+            sig += buf;
+            return nreg++;
+        };
+        // 64-bit words: the register holding i64 value `id` as an f64
+        // (readAtF64), converted once at its first numeric use
+        std::map<uint64_t, int> num_reg;
+        auto num = [&](uint64_t id) -> int {
+            if (vals[id].dtype != ZPUCUDA_I64) return reg[id];
+            auto it = num_reg.find(id);
+            if (it != num_reg.end()) return it->second;
+            const int r = push(OPC_I2F, 1, reg[id], 0, 0, 0, "i2f");
+            if (r >= 0) num_reg[id] = r;
+            return r;
+        };
+        // scalar.binary / scalar.unary's integer operations on two i64
+        // values (scalar.zig:262-302); the rest go through f64
+        auto int_op = [](int prim) -> int {
+            switch (prim) {
+            case 35: return OPC_IADD;
+            case 36: return OPC_ISUB;
+            case 37: return OPC_IMUL;
+            case 44: return OPC_IMOD;
+            case 40: return OPC_IMAX;
+            case 41: return OPC_IMIN;
+            case 1: return OPC_IABS;
+            case 31: return OPC_ISIGN;
+            case 26: return OPC_IRELU;
+            default: return -1;
+            }
+        };
+        auto int_name = [](int op) -> const char * {
+            switch (op) {
+            case OPC_IADD: return "iadd";
+            case OPC_ISUB: return "isub";
+            case OPC_IMUL: return "imul";
+            case OPC_IMOD: return "imod";
+            case OPC_IMAX: return "imax";
+            case OPC_IMIN: return "imin";
+            case OPC_IABS: return "iabs";
+            case OPC_ISIGN: return "isign";
+            default: return "irelu";
+            }
+        };
         for (int m : member) {
             const zpucuda_step &st = steps[m];
             if (region_reduce(st.prim)) {
@@ -1178,23 +1222,53 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                 red_out_id = st.out;
                 continue;
             }
-            if (nreg >= RP_MAX_REG || n_insn >= RP_MAX_INSN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
-            Insn in{(uint8_t)st.prim, (uint8_t)nreg, (uint8_t)reg[st.ins[0]], (uint8_t)(st.n_inputs > 1 ? reg[st.ins[1]] : 0),
-                    (uint8_t)(st.n_inputs > 2 ? reg[st.ins[2]] : 0)};
-            P.insn[n_insn++] = in;
-            char buf[80];
-            if (st.n_inputs > 2)
-                snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b, in.c);
-            else if (st.n_inputs > 1) snprintf(buf, sizeof buf, ";r%d=%s(r%d,r%d)", nreg, prim_name(st.prim).c_str(), in.a, in.b);
-            else snprintf(buf, sizeof buf, ";r%d=%s(r%d)", nreg, prim_name(st.prim).c_str(), in.a);
-            sig += buf;
-            if (vals[st.out].dtype == ZPUCUDA_I64) {
-                if (n_insn >= RP_MAX_INSN) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
-                P.insn[n_insn++] = Insn{OPC_TO_I64, (uint8_t)nreg, (uint8_t)nreg, 0, 0};
-                snprintf(buf, sizeof buf, ";r%d=to_i64(r%d)", nreg, nreg);
-                sig += buf;
+            const int n = st.n_inputs;
+            int r = -1;
+            if (!words64) {
+                r = push((uint8_t)st.prim, n, reg[st.ins[0]], n > 1 ? reg[st.ins[1]] : 0, n > 2 ? reg[st.ins[2]] : 0, 0,
+                         prim_name(st.prim));
+            } else {
+                const int odt = vals[st.out].dtype;
+                bool all_i = true, any_i = false;
+                for (int k = (st.prim == PRIM_WHERE ? 1 : 0); k < n; k++) {
+                    const bool ik = vals[st.ins[k]].dtype == ZPUCUDA_I64;
+                    all_i &= ik;
+                    any_i |= ik;
+                }
+                const int iop = int_op(st.prim);
+                if (odt == ZPUCUDA_I64 && all_i && iop >= 0) {
+                    r = push((uint8_t)iop, n, reg[st.ins[0]], n > 1 ? reg[st.ins[1]] : 0, 0, 0, int_name(iop));
+                } else {
+                    // the step in f64 on f64 operands (where: ops.zig:572-590
+                    // reads and writes through f64 too), or as an f32 region
+                    // computes it when it is an f32 step of f32 / bool values;
+                    // an f32 result of an i64 operand rounds once from f64
+                    const bool f32_step = odt == ZPUCUDA_F32 && !any_i && st.prim != PRIM_WHERE;
+                    int ops[3] = {0, 0, 0};
+                    bool bad = false;
+                    for (int k = 0; k < n; k++) bad |= (ops[k] = num(st.ins[k])) < 0;
+                    if (!bad) {
+                        if (st.prim == PRIM_POW && all_i) r = push(OPC_ZPOW, 2, ops[0], ops[1], 0, 0, "zpow");
+                        else r = push((uint8_t)st.prim, n, ops[0], ops[1], ops[2], f32_step ? kInsnF32 : 0,
+                                      prim_name(st.prim) + (f32_step ? ".f32" : ""));
+                    }
+                    if (r >= 0 && odt == ZPUCUDA_I64) r = push(OPC_F2I, 1, r, 0, 0, 0, "f2i");
+                    else if (r >= 0 && odt == ZPUCUDA_F32 && any_i) r = push(OPC_R32, 1, r, 0, 0, 0, "r32");
+                }
             }
-            reg[st.out] = nreg++;
+            if (r < 0) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
+            reg[st.out] = r;
+        }
+        // the reduced value: i64 sum / prod / max / min on the integers,
+        // anything else (argmax / argmin / any / all of i64 values) on f64
+        int red_reg = -1, red_kind_int = 0;
+        if (has_red) {
+            const bool int_red = vals[red_in].dtype == ZPUCUDA_I64 &&
+                                 (red_prim == PRIM_SUM || red_prim == PRIM_PROD || red_prim == PRIM_MAX_REDUCE ||
+                                  red_prim == PRIM_MIN_REDUCE);
+            red_kind_int = int_red;
+            red_reg = int_red ? reg[red_in] : num(red_in);
+            if (red_reg < 0) return lower_fail(plan, ZPUCUDA_ERR_NOT_SUPPORTED, "region too long");
         }
         (void)next_reg_after_loads;
         P.n_insn = n_insn;
@@ -1220,7 +1294,8 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
                      : red_prim == PRIM_MAX_REDUCE ? RED_MAX : red_prim == PRIM_MIN_REDUCE ? RED_MIN
                      : red_prim == PRIM_ARGMAX ? RED_ARGMAX : red_prim == PRIM_ARGMIN ? RED_ARGMIN
                      : red_prim == PRIM_ANY ? RED_ANY : RED_ALL;
-            P.reduce_reg = reg[red_in];
+            if (red_kind_int) P.reduce += RED_ISUM - RED_SUM;  // the same kind on i64 words
+            P.reduce_reg = red_reg;
             // the folded axes [r0, r1] split the region into [outer, red_len, inner]
             int r0 = 0, r1 = -1;
             reduced_axes(rshape, red_depth, red_axis, &r0, &r1);
@@ -1247,7 +1322,7 @@ int zpucuda_plan_create(const zpucuda_value *args, int n_args, const zpucuda_blo
             L.red = materialise(red_out_id);
             if (L.red.index < 0) return lower_fail(plan, ZPUCUDA_ERR_OUT_OF_MEMORY, "intermediate allocation");
             char buf[64];
-            snprintf(buf, sizeof buf, ";out=r%d;red=%s%s", P.reduce_reg,
+            snprintf(buf, sizeof buf, ";out=r%d;red=%s%s%s", P.reduce_reg, red_kind_int ? "i" : "",
                      red_prim == PRIM_SUM ? "sum" : red_prim == PRIM_PROD ? "prod" : red_prim == PRIM_MAX_REDUCE ? "max"
                      : red_prim == PRIM_MIN_REDUCE ? "min" : red_prim == PRIM_ARGMAX ? "argmax"
                      : red_prim == PRIM_ARGMIN ? "argmin" : red_prim == PRIM_ANY ? "any" : "all",

@@ -6,6 +6,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <type_traits>
+
 #include "region.cuh"
 #include "regions_gen.cuh"
 
@@ -174,35 +176,29 @@ template <> __device__ __forceinline__ double bin<double>(int op, double a, doub
 
 // ------------------------------------------------------- bytecode kernel
 
-template <class T>
-__device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io, int k, int64_t i) {
-    int64_t off;
+// Element offset of region element i in input k.
+__device__ __forceinline__ int64_t in_offset(const RegionProgram &p, int k, int64_t i) {
     switch (p.in_kind[k]) {
-    case IN_FULL: off = i; break;
-    case IN_SCALAR: off = 0; break;
-    case IN_ROW: off = i % p.in_numel[k]; break;
+    case IN_FULL: return i;
+    case IN_SCALAR: return 0;
+    case IN_ROW: return i % p.in_numel[k];
     default: {
-        int64_t rem = i;
-        off = 0;
+        int64_t rem = i, off = 0;
         for (int d = p.rank - 1; d >= 0; d--) {
             const int64_t idx = rem % p.dims[d];
             rem /= p.dims[d];
             off += idx * p.in_strides[k][d];
         }
+        return off;
     }
     }
-    if (p.in_bool[k]) return ((const uint8_t *)io.in[k])[off] ? (T)1 : (T)0;
-    if (p.in_i64[k]) return (T)__ll2double_rn(((const long long *)io.in[k])[off]);
-    return ((const T *)io.in[k])[off];
 }
 
-// scalar.fromF64 to i64 followed by toF64 (src/zpu/scalar.zig:7-27).
 template <class T>
-__device__ __forceinline__ T to_i64_value(T v) {
-    if (isnan(v)) return (T)0;
-    const T lim = (T)9223372036854775808.0;  // 2^63
-    v = v < -lim ? -lim : (v > lim ? lim : v);
-    return trunc(v);
+__device__ __forceinline__ T load_in(const RegionProgram &p, const RegionIO &io, int k, int64_t i) {
+    const int64_t off = in_offset(p, k, i);
+    if (p.in_bool[k]) return ((const uint8_t *)io.in[k])[off] ? (T)1 : (T)0;
+    return ((const T *)io.in[k])[off];
 }
 
 template <class T>
@@ -210,11 +206,162 @@ __device__ __forceinline__ void eval(const RegionProgram &p, const RegionIO &io,
     for (int k = 0; k < p.n_insn; k++) {
         const Insn in = p.insn[k];
         if (in.op == OPC_LOAD) r[in.dst] = load_in<T>(p, io, in.a, i);
-        else if (in.op == OPC_TO_I64) r[in.dst] = to_i64_value<T>(r[in.a]);
         else if (in.op == 55) r[in.dst] = r[in.a] != (T)0 ? r[in.b] : r[in.c];  // where: ops.zig:572-590
         else if (in.op < 35 || in.op == 54) r[in.dst] = un<T>(in.op, r[in.a]);
         else r[in.dst] = bin<T>(in.op, r[in.a], r[in.b]);
     }
+}
+
+// ------------------------------------------------ 64-bit-word regions
+
+__device__ __forceinline__ long long ibits(double r) { return __double_as_longlong(r); }
+__device__ __forceinline__ double iword(long long v) { return __longlong_as_double(v); }
+// scalar.fromF64(i64, v) (scalar.zig:17-27): 0 for NaN, else clamped to
+// [minInt, maxInt] and truncated toward zero (cvt.rzi saturates, so 2^63,
+// maxInt as an f64, gives maxInt)
+__device__ __forceinline__ long long f64_to_i64(double v) { return isnan(v) ? 0 : __double2ll_rz(v); }
+
+// std.math.pow(f64, x, y), which zpu's pow calls (scalar.zig:151-153),
+// branch for branch: the special values, a half power as sqrt, then the
+// integer part of |y| by repeated squaring of frexp(x)'s mantissa with the
+// binary exponent kept apart, a fractional part through exp(yf * log(x)),
+// and one ldexp.  With integer operands (zpu's pow of two i64 values) every
+// step is an IEEE multiply or an exact scaling, so the bits are zpu's.
+__device__ bool odd_integer(double x) {
+    if (fabs(x) >= 9007199254740992.0) return false;  // 2^53: every such f64 is even
+    double ip;
+    const double fp = modf(x, &ip);
+    return fp == 0.0 && (((long long)ip) & 1) == 1;
+}
+__device__ double zig_pow(double x, double y) {
+    for (int pass = 0; pass < 2; pass++) {
+        if (y == 0.0 || x == 1.0) return 1.0;
+        if (isnan(x) || isnan(y)) return nan("");
+        if (y == 1.0) return x;
+        if (x == 0.0) {
+            if (y < 0.0) return odd_integer(y) ? copysign(INFINITY, x) : INFINITY;
+            return odd_integer(y) ? x : 0.0;
+        }
+        if (isinf(y)) {
+            if (x == -1.0) return 1.0;
+            return ((fabs(x) < 1.0) == (y > 0.0)) ? 0.0 : INFINITY;
+        }
+        if (!isinf(x)) break;
+        if (x > 0.0) return y < 0.0 ? 0.0 : INFINITY;
+        x = 1.0 / x;  // pow(-inf, y) = pow(-0, -y): one more pass
+        y = -y;
+    }
+    if (y == 0.5) return sqrt(x);
+    if (y == -0.5) return 1.0 / sqrt(x);
+    double yi;
+    double yf = modf(fabs(y), &yi);
+    if (yf != 0.0 && x < 0.0) return nan("");
+    if (yi >= 9223372036854775808.0) return exp(y * log(x));  // 2^63
+    double a1 = 1.0;
+    int ae = 0;
+    if (yf != 0.0) {
+        if (yf > 0.5) {
+            yf -= 1.0;
+            yi += 1.0;
+        }
+        a1 = exp(yf * log(x));
+    }
+    int xe;
+    double x1 = frexp(x, &xe);
+    for (long long i = (long long)yi; i != 0; i >>= 1) {
+        if (xe < -(1 << 12) || (1 << 12) < xe) {  // far past the range: ldexp saturates
+            ae += xe;
+            break;
+        }
+        if (i & 1) {
+            a1 *= x1;
+            ae += xe;
+        }
+        x1 *= x1;
+        xe <<= 1;
+        if (x1 < 0.5) {
+            x1 += x1;
+            xe -= 1;
+        }
+    }
+    if (y < 0.0) {
+        a1 = 1.0 / a1;
+        ae = -ae;
+    }
+    return ldexp(a1, ae);
+}
+
+// scalar.binary / scalar.unary of two i64 values (scalar.zig:262-302):
+// + - * on the integers (two's-complement wrap where zpu's would overflow),
+// mod with a zero divisor giving a, @mod's sign of the divisor otherwise.
+__device__ __forceinline__ long long int_binary(int op, long long a, long long b) {
+    const unsigned long long ua = (unsigned long long)a, ub = (unsigned long long)b;
+    switch (op) {
+    case OPC_IADD: return (long long)(ua + ub);
+    case OPC_ISUB: return (long long)(ua - ub);
+    case OPC_IMUL: return (long long)(ua * ub);
+    case OPC_IMOD: {
+        if (b == 0) return a;
+        if (b == -1) return 0;
+        long long r = a % b;
+        if (r != 0 && ((r < 0) != (b < 0))) r += b;
+        return r;
+    }
+    case OPC_IMAX: return a > b ? a : b;
+    default: return a < b ? a : b;  // OPC_IMIN
+    }
+}
+__device__ __forceinline__ long long int_unary(int op, long long x) {
+    switch (op) {
+    case OPC_IABS: return x < 0 ? (long long)(0ull - (unsigned long long)x) : x;
+    case OPC_ISIGN: return x > 0 ? 1 : (x < 0 ? -1 : 0);
+    default: return x > 0 ? x : 0;  // OPC_IRELU
+    }
+}
+
+template <class T>
+__device__ __forceinline__ double load_w(const RegionProgram &p, const RegionIO &io, int k, int64_t i) {
+    const int64_t off = in_offset(p, k, i);
+    if (p.in_bool[k]) return ((const uint8_t *)io.in[k])[off] ? 1.0 : 0.0;
+    if (p.in_i64[k]) return iword(((const long long *)io.in[k])[off]);
+    return (double)((const T *)io.in[k])[off];
+}
+
+template <class T>
+__device__ __forceinline__ void eval_w(const RegionProgram &p, const RegionIO &io, int64_t i, double *r) {
+    for (int k = 0; k < p.n_insn; k++) {
+        const Insn in = p.insn[k];
+        double v;
+        switch (in.op) {
+        case OPC_LOAD: v = load_w<T>(p, io, in.a, i); break;
+        case OPC_I2F: v = __ll2double_rn(ibits(r[in.a])); break;
+        case OPC_F2I: v = iword(f64_to_i64(r[in.a])); break;
+        case OPC_R32: v = (double)__double2float_rn(r[in.a]); break;
+        case OPC_ZPOW: v = zig_pow(r[in.a], r[in.b]); break;
+        case OPC_IADD: case OPC_ISUB: case OPC_IMUL: case OPC_IMOD: case OPC_IMAX: case OPC_IMIN:
+            v = iword(int_binary(in.op, ibits(r[in.a]), ibits(r[in.b])));
+            break;
+        case OPC_IABS: case OPC_ISIGN: case OPC_IRELU: v = iword(int_unary(in.op, ibits(r[in.a]))); break;
+        case 55: v = r[in.a] != 0.0 ? r[in.b] : r[in.c]; break;
+        default: {
+            const bool u = in.op < 35 || in.op == 54;
+            if (in.c == kInsnF32)
+                v = u ? (double)unary_f32(in.op, (float)r[in.a]) : (double)binary_f32(in.op, (float)r[in.a], (float)r[in.b]);
+            else
+                v = u ? unary_f64(in.op, r[in.a]) : binary_f64(in.op, r[in.a], r[in.b]);
+        }
+        }
+        r[in.dst] = v;
+    }
+}
+
+// One element through either evaluator: R is the register type (T, or the
+// 64-bit word of a words64 region).
+template <class T, bool W>
+__device__ __forceinline__ void eval_any(const RegionProgram &p, const RegionIO &io, int64_t i,
+                                         typename std::conditional<W, double, T>::type *r) {
+    if constexpr (W) eval_w<T>(p, io, i, r);
+    else eval<T>(p, io, i, r);
 }
 
 __device__ __forceinline__ double red_identity(int red) {
@@ -223,6 +370,11 @@ __device__ __forceinline__ double red_identity(int red) {
     case RED_MAX: return -INFINITY;
     case RED_MIN: return INFINITY;
     case RED_ALL: return 1.0;
+    // i64 identities as bits (an empty i64 max / min is zpu's -inf / +inf
+    // written into an i64: minInt / maxInt); RED_ISUM's 0 is the word 0.0
+    case RED_IPROD: return iword(1);
+    case RED_IMAX: return iword((long long)0x8000000000000000ull);
+    case RED_IMIN: return iword(0x7fffffffffffffffll);
     default: return 0.0;
     }
 }
@@ -236,6 +388,11 @@ __device__ __forceinline__ double red_combine(int red, double acc, double v) {
     // first, ops.zig:845-853)
     case RED_ANY: return (acc != 0.0 || v != 0.0) ? 1.0 : 0.0;
     case RED_ALL: return (acc != 0.0 && v != 0.0) ? 1.0 : 0.0;
+    // i64 words: the order of a wrapping sum / product does not change it
+    case RED_ISUM: return iword((long long)((unsigned long long)ibits(acc) + (unsigned long long)ibits(v)));
+    case RED_IPROD: return iword((long long)((unsigned long long)ibits(acc) * (unsigned long long)ibits(v)));
+    case RED_IMAX: return ibits(v) > ibits(acc) ? v : acc;
+    case RED_IMIN: return ibits(v) < ibits(acc) ? v : acc;
     default: return acc + v;
     }
 }
@@ -247,18 +404,21 @@ __device__ __forceinline__ double warp_reduce(int red, double v) {
 
 constexpr int kInterpThreads = 256;
 
-template <class T>
-__device__ __forceinline__ void store_outputs(const RegionProgram &p, const RegionIO &io, int64_t i, const T *r) {
+// R: the register type (T, or double in a words64 region, where an i64
+// output's register holds its bits and a float one an exact T value).
+template <class T, class R>
+__device__ __forceinline__ void store_outputs(const RegionProgram &p, const RegionIO &io, int64_t i, const R *r) {
     for (int o = 0; o < p.n_out; o++) {
-        if (p.out_bool[o]) ((uint8_t *)io.out[o])[i] = r[p.out_reg[o]] != (T)0;
-        else if (p.out_i64[o]) ((long long *)io.out[o])[i] = __double2ll_rz((double)to_i64_value<T>(r[p.out_reg[o]]));
-        else ((T *)io.out[o])[i] = r[p.out_reg[o]];
+        if (p.out_bool[o]) ((uint8_t *)io.out[o])[i] = r[p.out_reg[o]] != (R)0;
+        else if (p.out_i64[o]) ((long long *)io.out[o])[i] = __double_as_longlong((double)r[p.out_reg[o]]);
+        else ((T *)io.out[o])[i] = (T)r[p.out_reg[o]];
     }
 }
 // The reduced value at output index `i`: any / all store a bool byte.
 template <class T>
 __device__ __forceinline__ void store_red(const RegionProgram &p, const RegionIO &io, int64_t i, double v) {
     if (p.reduce == RED_ANY || p.reduce == RED_ALL) ((uint8_t *)io.red_out)[i] = v != 0.0;
+    else if (red_is_int(p.reduce)) ((long long *)io.red_out)[i] = ibits(v);
     else ((T *)io.red_out)[i] = (T)v;
 }
 
@@ -268,21 +428,21 @@ __device__ __forceinline__ void store_red(const RegionProgram &p, const RegionIO
 // thread per output element walks the reduced axis in order (the row-order
 // walk of ops.reduceKernel, src/zpu/ops.zig:746-752), threads of a warp on
 // consecutive inner indices so every step of the walk is one coalesced load.
-template <class T, int MODE>
+template <class T, int MODE, bool W>
 __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_constant__ RegionProgram p,
                                                                 const __grid_constant__ RegionIO io) {
-    T r[RP_MAX_REG];
+    typename std::conditional<W, double, T>::type r[RP_MAX_REG];
     if (MODE == 0) {
         for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
              i += (int64_t)gridDim.x * kInterpThreads) {
-            eval<T>(p, io, i, r);
+            eval_any<T, W>(p, io, i, r);
             store_outputs<T>(p, io, i, r);
         }
     } else if (MODE == 1) {
         double acc = red_identity(p.reduce);
         for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
              i += (int64_t)gridDim.x * kInterpThreads) {
-            eval<T>(p, io, i, r);
+            eval_any<T, W>(p, io, i, r);
             store_outputs<T>(p, io, i, r);
             acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
         }
@@ -313,7 +473,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
             double acc = red_identity(p.reduce);
             for (int64_t k = 0; k < p.red_len; k++) {
                 const int64_t i = (a * p.red_len + k) * p.inner + c;
-                eval<T>(p, io, i, r);
+                eval_any<T, W>(p, io, i, r);
                 store_outputs<T>(p, io, i, r);
                 acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
             }
@@ -326,7 +486,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_kernel(const __grid_con
             double acc = red_identity(p.reduce);
             for (int64_t j = lane; j < p.inner; j += 32) {
                 const int64_t i = row * p.inner + j;
-                eval<T>(p, io, i, r);
+                eval_any<T, W>(p, io, i, r);
                 store_outputs<T>(p, io, i, r);
                 acc = red_combine(p.reduce, acc, (double)r[p.reduce_reg]);
             }
@@ -391,17 +551,17 @@ __device__ __forceinline__ ArgAcc arg_warp(ArgAcc a, bool want_max) {
 
 // MODE as interp_kernel (1: all axes, 2: trailing axes, one warp per row,
 // 3: an inner axis, one thread per output); the output is i64.
-template <class T, int MODE>
+template <class T, int MODE, bool W>
 __global__ void __launch_bounds__(kInterpThreads) interp_arg_kernel(const __grid_constant__ RegionProgram p,
                                                                     const __grid_constant__ RegionIO io) {
-    T r[RP_MAX_REG];
+    typename std::conditional<W, double, T>::type r[RP_MAX_REG];
     const bool want_max = p.reduce == RED_ARGMAX;
     int64_t *out = (int64_t *)io.red_out;
     if (MODE == 1) {
         ArgAcc acc = arg_empty();
         for (int64_t i = (int64_t)blockIdx.x * kInterpThreads + threadIdx.x; i < p.numel;
              i += (int64_t)gridDim.x * kInterpThreads) {
-            eval<T>(p, io, i, r);
+            eval_any<T, W>(p, io, i, r);
             store_outputs<T>(p, io, i, r);
             arg_take(acc, (double)r[p.reduce_reg], i, want_max);
         }
@@ -438,7 +598,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_arg_kernel(const __grid
             ArgAcc acc = arg_empty();
             for (int64_t k = 0; k < p.red_len; k++) {
                 const int64_t i = (a * p.red_len + k) * p.inner + c;
-                eval<T>(p, io, i, r);
+                eval_any<T, W>(p, io, i, r);
                 store_outputs<T>(p, io, i, r);
                 arg_take(acc, (double)r[p.reduce_reg], k, want_max);
             }
@@ -451,7 +611,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_arg_kernel(const __grid
             ArgAcc acc = arg_empty();
             for (int64_t j = lane; j < p.inner; j += 32) {
                 const int64_t i = row * p.inner + j;
-                eval<T>(p, io, i, r);
+                eval_any<T, W>(p, io, i, r);
                 store_outputs<T>(p, io, i, r);
                 arg_take(acc, (double)r[p.reduce_reg], j, want_max);
             }
@@ -461,7 +621,7 @@ __global__ void __launch_bounds__(kInterpThreads) interp_arg_kernel(const __grid
     }
 }
 
-template <class T>
+template <class T, bool W>
 int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
     const int sms = num_sms();
     const bool arg = p.reduce == RED_ARGMAX || p.reduce == RED_ARGMIN;
@@ -469,26 +629,26 @@ int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
         if (p.numel == 0) return ZPUCUDA_OK;
         int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
         if (g > sms * 8) g = sms * 8;
-        interp_kernel<T, 0><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        interp_kernel<T, 0, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else if (p.reduce_all) {
         int64_t g = (p.numel + kInterpThreads - 1) / kInterpThreads;
         if (g > sms * 8) g = sms * 8;
         if (g < 1) g = 1;
-        if (arg) interp_arg_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
-        else interp_kernel<T, 1><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 1, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 1, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else if (p.reduce_mid) {
         const int64_t n_out = p.outer * p.inner;
         if (n_out == 0) return ZPUCUDA_OK;
         int64_t g = (n_out + kInterpThreads - 1) / kInterpThreads;
         if (g > sms * 8) g = sms * 8;
-        if (arg) interp_arg_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
-        else interp_kernel<T, 3><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 3, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 3, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     } else {
         if (p.outer == 0) return ZPUCUDA_OK;
         int64_t g = (p.outer + (kInterpThreads / 32) - 1) / (kInterpThreads / 32);
         if (g > sms * 8) g = sms * 8;
-        if (arg) interp_arg_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
-        else interp_kernel<T, 2><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        if (arg) interp_arg_kernel<T, 2, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
+        else interp_kernel<T, 2, W><<<(int)g, kInterpThreads, 0, s>>>(p, io);
     }
     ZC_LAUNCHED("region bytecode kernel");
     return ZPUCUDA_OK;
@@ -500,6 +660,15 @@ int launch_interp(const RegionProgram &p, const RegionIO &io, cudaStream_t s) {
 // accumulator, so every prefix has zpu's bits; threads of a warp take
 // consecutive inner indices (coalesced when inner >= 32; for the last axis
 // each thread streams its own row, sequential sectors through L1).
+// readF64 / writeF64 of one element (an i64 reads as the nearest f64 and
+// writes as scalar.fromF64 does)
+__device__ __forceinline__ double cum_read(float v) { return (double)v; }
+__device__ __forceinline__ double cum_read(double v) { return v; }
+__device__ __forceinline__ double cum_read(long long v) { return __ll2double_rn(v); }
+__device__ __forceinline__ void cum_write(float *y, double a) { *y = (float)a; }
+__device__ __forceinline__ void cum_write(double *y, double a) { *y = a; }
+__device__ __forceinline__ void cum_write(long long *y, double a) { *y = f64_to_i64(a); }
+
 template <class T>
 __global__ void __launch_bounds__(256) cumsum_kernel(const T *__restrict__ x, T *__restrict__ y, int64_t outer,
                                                      int64_t dim, int64_t inner, int reverse) {
@@ -510,8 +679,8 @@ __global__ void __launch_bounds__(256) cumsum_kernel(const T *__restrict__ x, T 
         double acc = 0.0;
         for (int64_t d = 0; d < dim; d++) {
             const int64_t idx = base + (reverse ? dim - 1 - d : d) * inner;
-            acc += (double)x[idx];
-            y[idx] = (T)acc;
+            acc += cum_read(x[idx]);
+            cum_write(y + idx, acc);
         }
     }
 }
@@ -524,6 +693,8 @@ int cumsum_launch(int dtype, const void *x, void *y, int64_t outer, int64_t dim,
     if (g > (int64_t)num_sms() * 16) g = (int64_t)num_sms() * 16;
     if (dtype == ZPUCUDA_F64)
         cumsum_kernel<double><<<(int)g, 256, 0, s>>>((const double *)x, (double *)y, outer, dim, inner, reverse);
+    else if (dtype == ZPUCUDA_I64)
+        cumsum_kernel<long long><<<(int)g, 256, 0, s>>>((const long long *)x, (long long *)y, outer, dim, inner, reverse);
     else
         cumsum_kernel<float><<<(int)g, 256, 0, s>>>((const float *)x, (float *)y, outer, dim, inner, reverse);
     ZC_LAUNCHED("cumsum_kernel");
@@ -541,8 +712,9 @@ int region_launch(const RegionProgram &p, const CatalogueEntry *cat, const Regio
             if (!aligned16(io.out[o])) ok = false;
         if (ok) return cat->launch(p, io, s);
     }
-    if (p.dtype == ZPUCUDA_F32) return launch_interp<float>(p, io, s);
-    return launch_interp<double>(p, io, s);
+    if (p.words64) return p.dtype == ZPUCUDA_F32 ? launch_interp<float, true>(p, io, s) : launch_interp<double, true>(p, io, s);
+    if (p.dtype == ZPUCUDA_F32) return launch_interp<float, false>(p, io, s);
+    return launch_interp<double, false>(p, io, s);
 }
 
 }  // namespace zc

@@ -26,19 +26,35 @@ constexpr int RP_MAX_RANK = 8;
 enum : int8_t { IN_FULL = 0, IN_SCALAR = 1, IN_ROW = 2, IN_GENERAL = 3 };
 enum : int32_t {
     RED_NONE = 0, RED_SUM = 1, RED_PROD = 2, RED_MAX = 3, RED_MIN = 4, RED_ARGMAX = 5, RED_ARGMIN = 6,
-    RED_ANY = 7, RED_ALL = 8  // bool results (ops.reduceBoolKernel)
+    RED_ANY = 7, RED_ALL = 8,  // bool results (ops.reduceBoolKernel)
+    // i64 reductions in the integer type (ops.reduceStep, ops.zig:686-700):
+    // wrapping sum / product, max / min; the register holds i64 bits
+    RED_ISUM = 9, RED_IPROD = 10, RED_IMAX = 11, RED_IMIN = 12
 };
+inline __host__ __device__ bool red_is_int(int r) { return r >= RED_ISUM && r <= RED_IMIN; }
 enum : uint8_t {
+    // Only in 64-bit-word regions (RegionProgram::words64), where an i64
+    // value's register holds its two's-complement bits and every other
+    // value's register an f64 number:
+    OPC_I2F = 230,   // i64 bits -> f64 (readAtF64: @floatFromInt, round to nearest)
+    OPC_F2I = 231,   // f64 -> i64 bits (scalar.fromF64: 0 for NaN, clamp, truncate)
+    OPC_R32 = 232,   // f64 -> the nearest f32 (writeF64 into an f32 tensor)
+    // scalar.binary / scalar.unary of i64 values (scalar.zig:262-302): the
+    // integer operations zpu performs on the integers themselves
+    OPC_IADD = 233, OPC_ISUB = 234, OPC_IMUL = 235, OPC_IMOD = 236, OPC_IMAX = 237, OPC_IMIN = 238,
+    OPC_IABS = 239, OPC_ISIGN = 240, OPC_IRELU = 241,
+    // std.math.pow(f64) step for step (zpu's pow of two i64 values)
+    OPC_ZPOW = 242,
     OPC_LOAD = 250,
-    // after a step with an i64 result: the register takes the value zpu
-    // writes and reads back (writeF64 to i64, readAtF64): 0 for NaN, else
-    // clamped to [-2^63, 2^63] and truncated toward zero
-    OPC_TO_I64 = 251,
 };
+// Insn.c of a prim op in a 64-bit-word region: 1 = the step's type is f32 and
+// all its operands are f32 / bool, so it computes as an f32 region does and
+// the result (exact in f64) is widened back.
+constexpr uint8_t kInsnF32 = 1;
 
 struct Insn {
-    uint8_t op;  // prims.Prim code, or OPC_LOAD
-    uint8_t dst, a, b, c;  // c: the third operand of `where`
+    uint8_t op;  // prims.Prim code, or OPC_*
+    uint8_t dst, a, b, c;  // c: the third operand of `where`, else the kInsnF32 flag
 };
 
 // One lowered region.  Loads come first (r0..r(n_in-1)), then one register
@@ -68,12 +84,14 @@ struct RegionProgram {
     // outputs store (v != 0) as a byte.
     uint8_t in_bool[RP_MAX_IN];
     uint8_t out_bool[RP_MAX_OUT];
-    // i64 inputs (argmax / argmin results, i64 arguments) load as int64 and
-    // convert to the region's float type, as zpu reads them (readAtF64):
-    // exact below 2^24 in an f32 region, below 2^53 in an f64 one.
+    // A region that holds an i64 value (an argmax / argmin result, an i64
+    // argument, a step of i64 values) runs on 64-bit registers: i64 values
+    // as their bits (loaded, computed and stored as integers), the rest as
+    // f64 numbers; f32 steps keep f32 arithmetic (kInsnF32) and f32 results
+    // computed in f64 round to f32 (OPC_R32).  `dtype` is then the storage
+    // type of the region's float inputs and outputs.
+    int32_t words64;
     uint8_t in_i64[RP_MAX_IN];
-    // i64 outputs store the register (already an i64 value, OPC_TO_I64) as
-    // int64; 2^63 saturates to maxInt(i64)
     uint8_t out_i64[RP_MAX_OUT];
 };
 
