@@ -2,6 +2,11 @@
 
 Tolerance: relative Frobenius error <= 1e-5 against zpu's f32 FMA-chain
 gemm (the north star's bound for f32).
+
+Every test runs twice: with the lo halves of the TF32 split made in shared
+memory by the kernel's converter warps (ZPUCUDA_GEMM_PRESPLIT=0) and made
+by a split pass in HBM and loaded beside the operands (=1); by default the
+library picks per problem.
 """
 import os
 
@@ -15,6 +20,17 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 TOL = 1e-5
+
+
+@pytest.fixture(scope="module", params=["0", "1"], ids=["lo-in-smem", "lo-presplit"], autouse=True)
+def lo_mode(request):
+    old = os.environ.get("ZPUCUDA_GEMM_PRESPLIT")
+    os.environ["ZPUCUDA_GEMM_PRESPLIT"] = request.param
+    yield request.param
+    if old is None:
+        del os.environ["ZPUCUDA_GEMM_PRESPLIT"]
+    else:
+        os.environ["ZPUCUDA_GEMM_PRESPLIT"] = old
 
 
 @pytest.fixture(scope="module")
@@ -47,6 +63,41 @@ def test_layouts_and_edges(zc, ta, tb, m, k, n):
     got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
     check_no_device_error(zc)
     assert rel_fro(got, want) <= TOL, (m, k, n, ta, tb, rel_fro(got, want))
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_lo_in_hbm_and_in_shared_memory_give_the_same_bits(zc, ta, tb):
+    """The two sources of the lo halves feed the tensor core identical
+    operands in the same order, so the products agree bit for bit (split-K,
+    a broadcast batch and the FMA-chain shapes included)."""
+    keep = os.environ["ZPUCUDA_GEMM_PRESPLIT"]
+    try:
+        _same_bits_both_ways(zc, ta, tb)
+    finally:
+        os.environ["ZPUCUDA_GEMM_PRESPLIT"] = keep
+
+
+def _same_bits_both_ways(zc, ta, tb):
+    rng = np.random.default_rng(11)
+    cases = [(512, 1024, 640), (256, 8192, 16), (129, 100, 136)]
+    for m, k, n in cases:
+        a = rng.standard_normal((m, k)).astype(np.float32)
+        b = rng.standard_normal((k, n)).astype(np.float32)
+        A = dev(a.T.copy()) if ta else dev(a)
+        B = dev(b.T.copy()) if tb else dev(b)
+        outs = []
+        for mode in ("0", "1"):
+            os.environ["ZPUCUDA_GEMM_PRESPLIT"] = mode
+            outs.append(zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy())
+        check_no_device_error(zc)
+        assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32)), (m, k, n, ta, tb)
+    A3 = dev(rng.standard_normal((6, 96, 160)).astype(np.float32))
+    B1 = dev(rng.standard_normal((160, 72)).astype(np.float32))
+    outs = []
+    for mode in ("0", "1"):
+        os.environ["ZPUCUDA_GEMM_PRESPLIT"] = mode
+        outs.append(zc.matmul(A3, B1, a_depth=1).cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
 
 
 def test_kernel_test_shapes_take_the_fma_path(zc, golden):

@@ -21,6 +21,22 @@ torch = pytest.importorskip("torch")
 TOL = 1e-4
 
 
+@pytest.fixture(scope="module", params=[None, "1"], ids=["lo-by-rule", "lo-presplit"], autouse=True)
+def lo_mode(request):
+    """Each test runs with the library's own choice of where the GEMMs' TF32
+    lo halves come from, and with every product forced onto lo halves made
+    in HBM (split passes and the epilogues' lo outputs, handed on from the
+    product that writes an operand to the ones that read it)."""
+    import os
+    old = os.environ.pop("ZPUCUDA_GEMM_PRESPLIT", None)
+    if request.param is not None:
+        os.environ["ZPUCUDA_GEMM_PRESPLIT"] = request.param
+    yield request.param
+    os.environ.pop("ZPUCUDA_GEMM_PRESPLIT", None)
+    if old is not None:
+        os.environ["ZPUCUDA_GEMM_PRESPLIT"] = old
+
+
 @pytest.fixture(scope="module")
 def zc():
     import zpu_b200

@@ -61,6 +61,10 @@ struct Epilogue {
     float *peer[kMaxPeers] = {};
     int64_t rows_per_owner = 0;
     int32_t src = 0, world = 0;
+    // Not EPI_SCATTER: when set, the lo half of the TF32 split of every
+    // stored value is also written here (same row pitch as C), for a later
+    // GEMM that takes this result as an operand (gemm_f32_device_lo).
+    float *lo_out = nullptr;
 };
 
 // op(A)[m,k] @ op(B)[k,n] -> C[m,n] (ldc), per batch; trans flags as in
@@ -68,6 +72,17 @@ struct Epilogue {
 int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                         int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                         const Epilogue &epi, cudaStream_t s);
+// The same with the lo halves of the operands' TF32 split supplied (nullptr:
+// none): a_lo / b_lo hold lo(x) at x's own offsets (split_lo_device, or an
+// Epilogue::lo_out).  Used only where gemm_f32_presplit() holds.
+int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                       int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                       const Epilogue &epi, const float *a_lo, const float *b_lo, cudaStream_t s);
+// Whether an m x n product (batches matrices, one A and one B matrix) reads
+// the lo halves from HBM rather than making them in shared memory.
+bool gemm_f32_presplit(int64_t m, int64_t n, int64_t batches);
+// lo halves of n contiguous floats (16-byte aligned x and lo).
+int split_lo_device(const float *x, float *lo, int64_t n, cudaStream_t s);
 int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                     int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                     cudaStream_t s);

@@ -54,6 +54,7 @@
 // matrices) run a plain FMA-chain kernel instead.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -81,17 +82,22 @@ constexpr uint32_t SUM_COL = 256;  // the running sum starts at TMEM column 256
 //             (the tensor core waits for each fold, ~4% of the time); 2 raw
 //             stages.  Half the shared-memory traffic per flop for A, hence
 //             ~14% faster where the tile count fills the SMs.
-template <int BN_>
+//   PRE:      the lo halves come from HBM (split_lo_kernel wrote them once per
+//             operand), so a stage holds A, B, A lo and B lo, loaded by the
+//             TMA together; no converter work and no lo slots: 3 stages of
+//             64 KiB (BN = 128) or 2 of 96 KiB (BN = 256).
+template <int BN_, bool PRE_ = false>
 struct Tile {
     static constexpr int BN = BN_;
     static constexpr int NBUF = BN_ == 128 ? 2 : 1;
     static constexpr int KC_BLOCKS = BN_ == 128 ? 4 : 8;  // K-slices per accumulation chunk
-    static constexpr int RAW = BN_ == 128 ? 4 : 2;        // stages of raw A/B tiles (the hi operands)
-    static constexpr int LO = 2;                          // slots of lo tiles
+    static constexpr int RAW = PRE_ ? (BN_ == 128 ? 3 : 2) : (BN_ == 128 ? 4 : 2);  // stages
+    static constexpr int LO = PRE_ ? 0 : 2;               // slots of lo tiles made in shared memory
     static constexpr uint32_t B_BYTES = BN_ * BK * 4;
-    static constexpr uint32_t RAW_BYTES = A_BYTES + B_BYTES;  // one stage (and one lo slot)
+    static constexpr uint32_t RAW_BYTES = A_BYTES + B_BYTES;  // A + B of one K slice
+    static constexpr uint32_t STAGE_BYTES = PRE_ ? 2 * RAW_BYTES : RAW_BYTES;
     static constexpr int CONV_ITERS = (RAW_BYTES / 16 + NWORK * 32 - 1) / (NWORK * 32);
-    static constexpr size_t SMEM_BYTES = (size_t)(RAW + LO) * RAW_BYTES + 1024;  // + alignment slack
+    static constexpr size_t SMEM_BYTES = (size_t)RAW * STAGE_BYTES + (size_t)LO * RAW_BYTES + 1024;  // + alignment slack
     static constexpr int FOLD_COLS = BN_ / 2;  // columns per folding thread
     static_assert(NBUF * BN_ <= (int)SUM_COL && SUM_COL + BN_ <= TMEM_COLS, "TMEM columns");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
@@ -232,6 +238,39 @@ __device__ __forceinline__ uint4 lo4(const uint4 &x) {
     return out;
 }
 
+__device__ __forceinline__ float lo1(float x) {
+    const uint4 v = lo4(make_uint4(__float_as_uint(x), 0u, 0u, 0u));
+    return __uint_as_float(v.x);
+}
+
+// The lo halves of an operand stored as (inner, rows, nmats) with row pitch
+// ld and matrix pitch mat, written at the same offsets of `lo`: one
+// HBM-bound pass per operand, so the GEMM's tensor map for lo has the
+// operand's own geometry and the GEMM makes no lo in shared memory.
+__global__ void __launch_bounds__(256) split_lo_kernel(const float *__restrict__ x, float *__restrict__ lo,
+                                                       int64_t inner, int64_t rows, int64_t nmats, int64_t ld,
+                                                       int64_t mat) {
+    const int64_t stride = (int64_t)gridDim.x * 256;
+    if (ld == inner && (nmats == 1 || mat == rows * ld)) {  // one contiguous range
+        const int64_t n = inner * rows * nmats, n4 = n >> 2;
+        for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < n4; t += stride)
+            __stcs((uint4 *)lo + t, lo4(__ldcs((const uint4 *)x + t)));
+        for (int64_t t = (n4 << 2) + (int64_t)blockIdx.x * 256 + threadIdx.x; t < n; t += stride) lo[t] = lo1(x[t]);
+        return;
+    }
+    const int64_t v4 = (inner + 3) >> 2;  // 16-byte groups per row; the last may be partial
+    const int64_t total = v4 * rows * nmats;
+    for (int64_t t = (int64_t)blockIdx.x * 256 + threadIdx.x; t < total; t += stride) {
+        const int64_t g = t % v4, rz = t / v4;
+        const int64_t off = (rz / rows) * mat + (rz % rows) * ld + g * 4;  // ld, mat: multiples of 4
+        if (g * 4 + 4 <= inner) {
+            __stcs((uint4 *)(lo + off), lo4(__ldcs((const uint4 *)(x + off))));
+        } else {
+            for (int64_t i = g * 4; i < inner; i++) lo[off + i - g * 4] = lo1(x[off + i - g * 4]);
+        }
+    }
+}
+
 // Folds accumulation chunk q (TMEM buffer q % NBUF) into the running sum at
 // SUM_COL with round-to-nearest f32 adds; this warp's 32 lanes, columns
 // half * FOLD_COLS .. + FOLD_COLS - 1 (those inside the MMA width).
@@ -258,6 +297,7 @@ __device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q,
 
 struct Maps {
     CUtensorMap a, b;
+    CUtensorMap alo, blo;  // the lo halves (PRE kernels only)
 };
 
 struct Params {
@@ -343,15 +383,16 @@ __device__ __forceinline__ void epi_apply32(const Epilogue &e, float (&acc)[32],
     }
 }
 
-template <bool TA, bool TB, int BN_>
+template <bool TA, bool TB, int BN_, bool PRE>
 __global__ void __launch_bounds__(THREADS, 1)
     tf32x3_gemm_kernel(const __grid_constant__ Maps maps, float *__restrict__ C, const __grid_constant__ Params P) {
-    using T = Tile<BN_>;
+    using T = Tile<BN_, PRE>;
     constexpr int BN = BN_, RAW = T::RAW, LO = T::LO, NBUF = T::NBUF, KC_BLOCKS = T::KC_BLOCKS;
-    constexpr uint32_t B_BYTES = T::B_BYTES, RAW_BYTES = T::RAW_BYTES;
+    constexpr uint32_t B_BYTES = T::B_BYTES, RAW_BYTES = T::RAW_BYTES, STAGE_BYTES = T::STAGE_BYTES;
+    constexpr int NLO = LO > 0 ? LO : 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[LO], lofree[LO], tfull[NBUF], tfree[NBUF];
+    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[NLO], lofree[NLO], tfull[NBUF], tfree[NBUF];
     __shared__ uint32_t tmem_base;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -370,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mb_init(&full[s], 1);
             mb_init(&empty[s], 1);
         }
-        for (int l = 0; l < LO; l++) {
+        for (int l = 0; l < NLO; l++) {
             mb_init(&conv[l], NWORK);
             mb_init(&lofree[l], 1);
         }
@@ -390,48 +431,58 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = tmem_base;
 
-    // raw stage s: A then B (the hi operands as loaded); lo slot l: A then B
-    auto raw_a = [&](int s) { return smem + (size_t)s * RAW_BYTES; };
-    auto raw_b = [&](int s) { return smem + (size_t)s * RAW_BYTES + A_BYTES; };
-    auto lo_a = [&](int l) { return smem + (size_t)RAW * RAW_BYTES + (size_t)l * RAW_BYTES; };
-    auto lo_b = [&](int l) { return smem + (size_t)RAW * RAW_BYTES + (size_t)l * RAW_BYTES + A_BYTES; };
+    // stage s: A then B (the hi operands as loaded), for PRE then A lo and
+    // B lo; lo slot l (converted in shared memory): A then B.  For PRE the
+    // lo tiles are indexed by stage.
+    auto raw_a = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
+    auto raw_b = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
+    auto lo_a = [&](int l) {
+        return PRE ? smem + (size_t)l * STAGE_BYTES + RAW_BYTES : smem + (size_t)RAW * STAGE_BYTES + (size_t)l * RAW_BYTES;
+    };
+    auto lo_b = [&](int l) { return lo_a(l) + A_BYTES; };
 
     if (warp == 0) {
         if (lane == 0) {
             for (int j = 0; j < KT; j++) {
                 const int s = j % RAW;
                 if (j >= RAW && !mb_wait(&empty[s], ((j / RAW) - 1) & 1)) break;
-                mb_expect_tx(&full[s], A_BYTES + B_BYTES);
+                mb_expect_tx(&full[s], STAGE_BYTES);
                 const int k0 = (kb0 + j) * BK;
-                if (!TA) tma_load_3d(raw_a(s), &maps.a, k0, m0, za, &full[s]);
-                else
-                    for (int c = 0; c < BM / 32; c++) tma_load_3d(raw_a(s) + c * 4096, &maps.a, m0 + 32 * c, k0, za, &full[s]);
-                if (TB) tma_load_3d(raw_b(s), &maps.b, k0, n0, zb, &full[s]);
-                else
-                    for (int c = 0; c < BN / 32; c++) tma_load_3d(raw_b(s) + c * 4096, &maps.b, n0 + 32 * c, k0, zb, &full[s]);
+#pragma unroll
+                for (int h = 0; h < (PRE ? 2 : 1); h++) {  // hi, then (PRE) lo
+                    uint8_t *da = h ? lo_a(s) : raw_a(s), *db = h ? lo_b(s) : raw_b(s);
+                    const CUtensorMap *ma = h ? &maps.alo : &maps.a, *mb = h ? &maps.blo : &maps.b;
+                    if (!TA) tma_load_3d(da, ma, k0, m0, za, &full[s]);
+                    else
+                        for (int c = 0; c < BM / 32; c++) tma_load_3d(da + c * 4096, ma, m0 + 32 * c, k0, za, &full[s]);
+                    if (TB) tma_load_3d(db, mb, k0, n0, zb, &full[s]);
+                    else
+                        for (int c = 0; c < BN / 32; c++) tma_load_3d(db + c * 4096, mb, n0 + 32 * c, k0, zb, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t ID = P.idesc;
             for (int j = 0; j < KT; j++) {
-                const int s = j % RAW, l = j % LO, q = j / KC_BLOCKS, buf = q % NBUF;
+                const int s = j % RAW, l = j % NLO, q = j / KC_BLOCKS, buf = q % NBUF;
                 const bool first = (j % KC_BLOCKS) == 0;
                 const bool last = (j % KC_BLOCKS) == KC_BLOCKS - 1 || j == KT - 1;
                 if (first && q >= NBUF && !mb_wait(&tfree[buf], ((q / NBUF) - 1) & 1)) break;
-                if (!mb_wait(&conv[l], (j / LO) & 1)) break;
+                if (PRE ? !mb_wait(&full[s], (j / RAW) & 1) : !mb_wait(&conv[l], (j / NLO) & 1)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t d = tmem + (uint32_t)(buf * BN);
+                const int lt = PRE ? s : l;  // where this slice's lo tiles are
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; kk++) {
-                    const uint64_t ah = op_desc<!TA>(raw_a(s), kk), al = op_desc<!TA>(lo_a(l), kk);
-                    const uint64_t bh = op_desc<TB>(raw_b(s), kk), bl = op_desc<TB>(lo_b(l), kk);
+                    const uint64_t ah = op_desc<!TA>(raw_a(s), kk), al = op_desc<!TA>(lo_a(lt), kk);
+                    const uint64_t bh = op_desc<TB>(raw_b(s), kk), bl = op_desc<TB>(lo_b(lt), kk);
                     mma_tf32(d, ah, bh, ID, (first && kk == 0) ? 0u : 1u);
                     mma_tf32(d, ah, bl, ID, 1u);
                     mma_tf32(d, al, bh, ID, 1u);
                 }
                 mma_commit(&empty[s]);
-                mma_commit(&lofree[l]);
+                if (!PRE) mma_commit(&lofree[l]);
                 if (last) mma_commit(&tfull[buf]);
             }
         }
@@ -463,10 +514,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             atomicOr(&g_gemm_error, 1u);
             return false;
         };
-        for (int j = 0; j < KT && ok; j++) {
-            const int s = j % RAW, l = j % LO;
+        for (int j = 0; j < (PRE ? 0 : KT) && ok; j++) {  // PRE: nothing to convert
+            const int s = j % RAW, l = j % NLO;
             if (!wait(&full[s], (j / RAW) & 1)) ok = false;
-            else if (j >= LO && !wait(&lofree[l], ((j / LO) - 1) & 1)) ok = false;
+            else if (j >= NLO && !wait(&lofree[l], ((j / NLO) - 1) & 1)) ok = false;
             if (!ok) break;
             const uint4 *src = (const uint4 *)raw_a(s);  // A then B, contiguous
             uint4 *dst = (uint4 *)lo_a(l);
@@ -537,6 +588,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 if (!staged) {
                     float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
+                    float *lrow = P.epi.lo_out ? P.epi.lo_out + row * P.ldc : nullptr;  // one matrix, no split
                     if (row < P.M) {
                         if (col0 + 32 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
                             epi_apply32(P.epi, acc, row, col0);
@@ -544,10 +596,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                             for (int v = 0; v < 8; v++)
                                 *(float4 *)(crow + col0 + 4 * v) =
                                     make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                            if (lrow && ((((uintptr_t)(lrow + col0)) & 15) == 0)) {
+#pragma unroll
+                                for (int v = 0; v < 8; v++)
+                                    *(uint4 *)(lrow + col0 + 4 * v) =
+                                        lo4(make_uint4(__float_as_uint(acc[4 * v]), __float_as_uint(acc[4 * v + 1]),
+                                                       __float_as_uint(acc[4 * v + 2]), __float_as_uint(acc[4 * v + 3])));
+                            } else if (lrow) {
+#pragma unroll
+                                for (int v = 0; v < 32; v++) lrow[col0 + v] = lo1(acc[v]);
+                            }
                         } else {
 #pragma unroll
                             for (int v = 0; v < 32; v++)
-                                if (col0 + v < P.N) crow[col0 + v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                                if (col0 + v < P.N) {
+                                    const float y = epi_apply(P.epi, acc[v], row, col0 + v);
+                                    crow[col0 + v] = y;
+                                    if (lrow) lrow[col0 + v] = lo1(y);
+                                }
                         }
                     }
                     continue;
@@ -607,7 +673,11 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
         for (int kk = 0; kk < kmax; kk++) acc = fmaf(sa[ty][kk], sb[kk][tx], acc);
         __syncthreads();
     }
-    if (row < M && col < N) C[row * ldc + col] = epi_apply(epi, acc, row, col);
+    if (row < M && col < N) {
+        const float y = epi_apply(epi, acc, row, col);
+        C[row * ldc + col] = y;
+        if (epi.lo_out) epi.lo_out[row * ldc + col] = lo1(y);
+    }
 }
 
 // ------------------------------------------------------------- host side
@@ -633,7 +703,9 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
             batch_offsets(P.bt, b, &oa, &ob);
             acc = zpu_chain_element<TA, TB>(P.A + oa, P.B + ob, P.lda, P.ldb, r, c, n, 0, P.K);
         }
-        C[b * stride_c + r * ldc + c] = epi_apply(epi, acc, r, c);
+        const float y = epi_apply(epi, acc, r, c);
+        C[b * stride_c + r * ldc + c] = y;
+        if (epi.lo_out) epi.lo_out[r * ldc + c] = lo1(y);  // one matrix (lo_out is refused for batches)
     }
 }
 
@@ -730,17 +802,18 @@ int64_t max_offset(const GemmBatch &bt, const int64_t *s) {
     return o;
 }
 
-template <bool TA, bool TB, int BN_>
+template <bool TA, bool TB, int BN_, bool PRE>
 int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
-    auto k = tf32x3_gemm_kernel<TA, TB, BN_>;
+    using T = Tile<BN_, PRE>;
+    auto k = tf32x3_gemm_kernel<TA, TB, BN_, PRE>;
     static bool attr[64] = {false};
     const int dev = current_device();
     if (dev < 0 || dev >= 64 || !attr[dev]) {
-        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile<BN_>::SMEM_BYTES));
+        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T::SMEM_BYTES));
         if (dev >= 0 && dev < 64) attr[dev] = true;
     }
     dim3 grid((unsigned)((P.N + BN_ - 1) / BN_), (unsigned)((P.M + BM - 1) / BM), (unsigned)(batches * P.splits));
-    k<<<grid, THREADS, Tile<BN_>::SMEM_BYTES, s>>>(maps, C, P);
+    k<<<grid, THREADS, T::SMEM_BYTES, s>>>(maps, C, P);
     ZC_LAUNCHED("tf32x3_gemm_kernel");
     return ZPUCUDA_OK;
 }
@@ -757,12 +830,50 @@ int choose_bn(int64_t m, int64_t n, int64_t batches) {
     return 1.75 * (double)w256 < (double)w128 ? 256 : 128;
 }
 
-template <int BN_>
+template <int BN_, bool PRE>
 int dispatch_tf32x3(bool ta, bool tb, const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
-    if (!ta && !tb) return launch_tf32x3<false, false, BN_>(maps, C, P, batches, s);
-    if (!ta && tb) return launch_tf32x3<false, true, BN_>(maps, C, P, batches, s);
-    if (ta && !tb) return launch_tf32x3<true, false, BN_>(maps, C, P, batches, s);
-    return launch_tf32x3<true, true, BN_>(maps, C, P, batches, s);
+    if (!ta && !tb) return launch_tf32x3<false, false, BN_, PRE>(maps, C, P, batches, s);
+    if (!ta && tb) return launch_tf32x3<false, true, BN_, PRE>(maps, C, P, batches, s);
+    if (ta && !tb) return launch_tf32x3<true, false, BN_, PRE>(maps, C, P, batches, s);
+    return launch_tf32x3<true, true, BN_, PRE>(maps, C, P, batches, s);
+}
+
+// The lo halves of one operand into stream-ordered scratch from `pool`
+// (nullptr when that fails): the operand as (inner, rows, nmats).
+float *split_operand(cudaMemPool_t pool, const float *x, int64_t inner, int64_t rows, int64_t nmats, int64_t ld,
+                     int64_t mat, cudaStream_t s) {
+    const int64_t extent = (nmats - 1) * mat + (rows - 1) * ld + inner;  // elements the map can reach
+    float *lo = nullptr;
+    if (!pool || cudaMallocFromPoolAsync((void **)&lo, (size_t)extent * sizeof(float), pool, s) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    const int64_t n4 = (inner + 3) / 4 * rows * nmats;
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+    split_lo_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, s>>>(x, lo, inner, rows, nmats, ld, mat);
+    if (cudaGetLastError() != cudaSuccess) {
+        cudaFreeAsync(lo, s);
+        return nullptr;
+    }
+    count_launch();
+    return lo;
+}
+
+// Whether the lo halves come from a split pass (PRE kernels) rather than
+// from the converter warps.  The PRE kernel runs ~1.25x faster (measured:
+// 8192^3 4.9 against 6.2 ms, 4096^3 0.66 against 0.87 ms), but the pass
+// moves 8 bytes per operand element through HBM (read x, write lo), so it
+// pays where each operand element takes part in many products: the pass's
+// time 8 (na m + nb n) k / HBM below a fifth of the product's
+// 2 m n k batches / (~180 TFLOP/s), i.e. na m + nb n < 0.0018 m n batches
+// (4096^3 and the MLP's products yes; 1024^3 and 256 x 512^3 no: measured
+// 51 -> 44 and 135 -> 117 TFLOP/s with the pass).  ZPUCUDA_GEMM_PRESPLIT=0
+// or 1 forces the choice (read at every call).
+bool use_presplit(int64_t m, int64_t n, int64_t batches, int64_t na, int64_t nb) {
+    const char *e = getenv("ZPUCUDA_GEMM_PRESPLIT");
+    if (e && (e[0] == '0' || e[0] == '1') && e[1] == 0) return e[0] == '1';
+    return (double)(na * m + nb * n) < 0.0018 * (double)m * (double)n * (double)batches;
 }
 
 }  // namespace
@@ -773,12 +884,32 @@ int gemm_f32_device(const float *A, const float *B, float *C, int64_t m, int64_t
     return gemm_f32_device_epi(A, B, C, m, n, k, lda, ldb, ldc, ta, tb, bt, stride_c, Epilogue{}, s);
 }
 
+bool gemm_f32_presplit(int64_t m, int64_t n, int64_t batches) { return use_presplit(m, n, batches, 1, 1); }
+
+int split_lo_device(const float *x, float *lo, int64_t n, cudaStream_t s) {
+    if (n <= 0) return ZPUCUDA_OK;
+    if (!x || !lo || ((uintptr_t)x & 15) || ((uintptr_t)lo & 15)) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    int64_t blocks = (n / 4 + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+    split_lo_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, s>>>(x, lo, n, 1, 1, n, 0);
+    ZC_LAUNCHED("split_lo_kernel");
+    return ZPUCUDA_OK;
+}
+
 int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
                         int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
                         const Epilogue &epi, cudaStream_t s) {
+    return gemm_f32_device_lo(A, B, C, m, n, k, lda, ldb, ldc, ta, tb, bt, stride_c, epi, nullptr, nullptr, s);
+}
+
+int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda,
+                       int64_t ldb, int64_t ldc, bool ta, bool tb, const GemmBatch &bt, int64_t stride_c,
+                       const Epilogue &epi, const float *a_lo, const float *b_lo, cudaStream_t s) {
     const int64_t batches = batch_count(bt);
     if (m == 0 || n == 0 || batches == 0) return ZPUCUDA_OK;
     if (!C || ldc < n) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if (epi.lo_out && (batches != 1 || epi.mode == EPI_SCATTER)) return ZPUCUDA_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)a_lo & 15) || ((uintptr_t)b_lo & 15)) return ZPUCUDA_ERR_INVALID_ARGUMENT;
     if (epi.mode != EPI_STORE) {  // the epilogue inputs belong to one matrix
         if (batches != 1 || epi.mode < 0 || epi.mode > EPI_SCATTER) return ZPUCUDA_ERR_INVALID_ARGUMENT;
         if (epi.mode == EPI_SCATTER) {
@@ -795,6 +926,7 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
     if (k == 0) {  // kernels.zig:346-349: an empty contraction writes zeros
         for (int64_t b = 0; b < batches; b++)
             ZC_CUDA(cudaMemset2DAsync(C + b * stride_c, ldc * sizeof(float), 0, n * sizeof(float), m, s));
+        if (epi.lo_out) ZC_CUDA(cudaMemset2DAsync(epi.lo_out, ldc * sizeof(float), 0, n * sizeof(float), m, s));
         return ZPUCUDA_OK;
     }
     if (!A || !B) return ZPUCUDA_ERR_INVALID_ARGUMENT;
@@ -856,8 +988,25 @@ int gemm_f32_device_epi(const float *A, const float *B, float *C, int64_t m, int
                 P.stride_c = m * n;
                 P.epi = Epilogue{};
             }
-            int st = bn == 256 ? dispatch_tf32x3<256>(ta, tb, maps, splits > 1 ? ws : C, P, batches, s)
-                               : dispatch_tf32x3<128>(ta, tb, maps, splits > 1 ? ws : C, P, batches, s);
+            // lo halves from a split pass: scratch with each operand's own
+            // geometry, the same tensor maps on another base
+            // (or the caller's, when it supplies them)
+            float *alo = nullptr, *blo = nullptr;  // scratch made here
+            bool pre = use_presplit(m, n, batches, na, nb);
+            if (pre) {
+                cudaMemPool_t lpool = splitk_pool();
+                if (!a_lo) a_lo = alo = split_operand(lpool, A, a_inner, a_rows, na, lda, mat_a, s);
+                if (a_lo && !b_lo) b_lo = blo = split_operand(lpool, B, b_inner, b_rows, nb, ldb, mat_b, s);
+                pre = a_lo && b_lo && make_map(&maps.alo, a_lo, a_inner, a_rows, lda, na, mat_a, ta ? 32 : BM, !ta) &&
+                      make_map(&maps.blo, b_lo, b_inner, b_rows, ldb, nb, mat_b, tb ? bn : 32, tb);
+            }
+            float *cout = splits > 1 ? ws : C;
+            int st = pre ? (bn == 256 ? dispatch_tf32x3<256, true>(ta, tb, maps, cout, P, batches, s)
+                                      : dispatch_tf32x3<128, true>(ta, tb, maps, cout, P, batches, s))
+                         : (bn == 256 ? dispatch_tf32x3<256, false>(ta, tb, maps, cout, P, batches, s)
+                                      : dispatch_tf32x3<128, false>(ta, tb, maps, cout, P, batches, s));
+            if (alo) cudaFreeAsync(alo, s);
+            if (blo) cudaFreeAsync(blo, s);
             if (splits > 1) {
                 if (st == ZPUCUDA_OK) {
                     const int64_t total = batches * m * n;

@@ -352,6 +352,10 @@ struct zpucuda_mlp {
     int64_t total = 0;  // floats per array (multiple of kAlign)
     float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr;
     float *a1 = nullptr, *a2 = nullptr, *ga2 = nullptr, *ga1 = nullptr, *logits = nullptr, *gl = nullptr;
+    // lo halves of the TF32 split of the big products' operands, made once
+    // per step (x, W1, W2 by a split pass; a1, ga2, ga1 by the epilogue that
+    // writes them) and read by every product that takes them
+    float *x_lo = nullptr, *w1_lo = nullptr, *w2_lo = nullptr, *a1_lo = nullptr, *ga2_lo = nullptr, *ga1_lo = nullptr;
     float *col_partials[3] = {nullptr, nullptr, nullptr};
     float *xent_partials = nullptr;
     unsigned int *counters = nullptr;  // colsum tickets x3 groups, xent ticket, label error
@@ -388,7 +392,7 @@ namespace {
 void free_mlp(zpucuda_mlp *h) {
     float *bufs[] = {h->params, h->grads, h->m,   h->v,           h->a1,          h->a2,          h->ga2,
                      h->ga1,    h->logits, h->gl, h->col_partials[0], h->col_partials[1], h->col_partials[2],
-                     h->xent_partials};
+                     h->xent_partials, h->x_lo, h->w1_lo, h->w2_lo, h->a1_lo, h->ga2_lo, h->ga1_lo};
     for (float *b : bufs)
         if (b) cudaFree(b);
     for (int r = 0; r < kMaxPeers; r++)
@@ -425,10 +429,17 @@ int colsum(zpucuda_mlp *h, int which, const float *X, int64_t rows, int64_t n, i
 }
 
 int gemm(const float *A, const float *B, float *C, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-         int64_t ldc, bool ta, bool tb, const Epilogue &e, cudaStream_t s) {
+         int64_t ldc, bool ta, bool tb, const Epilogue &e, cudaStream_t s, const float *a_lo = nullptr,
+         const float *b_lo = nullptr) {
     GemmBatch one;
     memset(&one, 0, sizeof one);
-    return gemm_f32_device_epi(A, B, C, m, n, k, lda, ldb, ldc, ta, tb, one, 0, e, s);
+    return gemm_f32_device_lo(A, B, C, m, n, k, lda, ldb, ldc, ta, tb, one, 0, e, a_lo, b_lo, s);
+}
+
+// e with its lo halves written to `lo` when `want` (a later product reads them)
+Epilogue with_lo(Epilogue e, bool want, float *lo) {
+    e.lo_out = want ? lo : nullptr;
+    return e;
 }
 
 Epilogue epi(int32_t mode, const float *bias, const float *aux = nullptr, int64_t ldaux = 0) {
@@ -576,10 +587,35 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     const int world = ar ? nccl_world(&rank) : 1;
     if (ar && adam && world > 1 && h->peer_state == 0) ZC_TRY(peer_setup(h, world, rank, h->comm_stream));
 
+    // The big products that read the lo halves of their operands from HBM
+    // (gemm_f32_presplit): each such operand's lo is made once, here by a
+    // split pass (x and the weights) or by the epilogue of the product that
+    // writes it (a1, ga2, ga1), and handed to every product that reads it.
+    const bool p_f1 = gemm_f32_presplit(B, d1, 1), p_f2 = gemm_f32_presplit(B, d2, 1);
+    const bool p_w2 = gemm_f32_presplit(d1, d2, 1), p_g1 = gemm_f32_presplit(B, d1, 1);
+    const bool p_w1 = gemm_f32_presplit(d0, d1, 1);
+    const bool x_al = ((uintptr_t)x & 15) == 0;
+    const float *x_lo = nullptr, *w1_lo = nullptr, *w2_lo = nullptr;
+    if ((p_f1 || p_w1) && x_al) {
+        ZC_TRY(split_lo_device(x, h->x_lo, B * d0, s));
+        x_lo = h->x_lo;
+    }
+    if (p_f1) {
+        ZC_TRY(split_lo_device(W1, h->w1_lo, d0 * d1, s));
+        w1_lo = h->w1_lo;
+    }
+    if (p_f2 || p_g1) {
+        ZC_TRY(split_lo_device(W2, h->w2_lo, d1 * d2, s));
+        w2_lo = h->w2_lo;
+    }
+    const bool a1_lo = p_f2 || p_w2, ga2_lo = p_w2 || p_g1, ga1_lo = p_w1;
+
     // forward: dense -> tanh -> dense -> tanh -> dense
     ZC_TRY(tmark(h, 0, s));
-    ZC_TRY(gemm(x, W1, h->a1, B, d1, d0, d0, d1, d1, false, false, epi(EPI_BIAS_TANH, b1), s));
-    ZC_TRY(gemm(h->a1, W2, h->a2, B, d2, d1, d1, d2, d2, false, false, epi(EPI_BIAS_TANH, b2), s));
+    ZC_TRY(gemm(x, W1, h->a1, B, d1, d0, d0, d1, d1, false, false, with_lo(epi(EPI_BIAS_TANH, b1), a1_lo, h->a1_lo),
+                s, x_lo, w1_lo));
+    ZC_TRY(gemm(h->a1, W2, h->a2, B, d2, d1, d1, d2, d2, false, false, epi(EPI_BIAS_TANH, b2), s,
+                a1_lo ? h->a1_lo : nullptr, w2_lo));
     ZC_TRY(gemm(h->a2, W3, h->logits, B, d3p, d2, d2, d3p, d3p, false, false, epi(EPI_BIAS, b3), s));
     ZC_TRY(tmark(h, 1, s));
 
@@ -600,7 +636,8 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     // layer 3: dW3 = a2^T gl, db3 = colsum(gl), g_a2 = (gl W3^T) * (1 - a2^2)
     ZC_TRY(gemm(h->a2, h->gl, gW3, d2, d3p, B, d2, d3p, d3p, true, false, Epilogue{}, s));
     ZC_TRY(colsum(h, 2, h->gl, B, d3p, d3p, gb3, s));
-    ZC_TRY(gemm(h->gl, W3, h->ga2, B, d2, d3p, d3p, d3p, d2, false, true, epi(EPI_TANH_GRAD, nullptr, h->a2, d2), s));
+    ZC_TRY(gemm(h->gl, W3, h->ga2, B, d2, d3p, d3p, d3p, d2, false, true,
+                with_lo(epi(EPI_TANH_GRAD, nullptr, h->a2, d2), ga2_lo, h->ga2_lo), s));
     // layer 2
     ZC_TRY(colsum(h, 1, h->ga2, B, d2, d2, gb2, s));
     ZC_TRY(tmark(h, 3, s));
@@ -615,7 +652,8 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         se.rows_per_owner = d1 / world;
         se.src = rank;
         se.world = world;
-        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, se, s));
+        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, se, s, a1_lo ? h->a1_lo : nullptr,
+                    ga2_lo ? h->ga2_lo : nullptr));
         XferFlags f;
         memset(&f, 0, sizeof f);
         for (int r = 0; r < world; r++) f.flag[r] = (unsigned long long *)h->peer_base[r];
@@ -623,7 +661,8 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         xfer_signal_kernel<<<1, 1, 0, s>>>(f, world, rank, h->epoch);
         ZC_LAUNCHED("xfer_signal_kernel");
     } else {
-        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s));
+        ZC_TRY(gemm(h->a1, h->ga2, gW2, d1, d2, B, d1, d2, d2, true, false, Epilogue{}, s, a1_lo ? h->a1_lo : nullptr,
+                    ga2_lo ? h->ga2_lo : nullptr));
     }
     ZC_TRY(tmark(h, 4, s));
     cudaStream_t side = h->comm_stream;
@@ -654,7 +693,9 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         }
         ZC_TRY(tmark(h, 8, side));
     }
-    ZC_TRY(gemm(h->ga2, W2, h->ga1, B, d1, d2, d2, d2, d1, false, true, epi(EPI_TANH_GRAD, nullptr, h->a1, d1), s));
+    ZC_TRY(gemm(h->ga2, W2, h->ga1, B, d1, d2, d2, d2, d1, false, true,
+                with_lo(epi(EPI_TANH_GRAD, nullptr, h->a1, d1), ga1_lo, h->ga1_lo), s, ga2_lo ? h->ga2_lo : nullptr,
+                w2_lo));
     ZC_TRY(tmark(h, 5, s));
     AdamConsts ac;
     if (adam) {  // every later kernel on s leaves W2, b2, W3, b3 alone
@@ -675,7 +716,8 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
     }
     // layer 1
     ZC_TRY(colsum(h, 0, h->ga1, B, d1, d1, gb1, s));
-    ZC_TRY(gemm(x, h->ga1, gW1, d0, d1, B, d0, d1, d1, true, false, Epilogue{}, s));
+    ZC_TRY(gemm(x, h->ga1, gW1, d0, d1, B, d0, d1, d1, true, false, Epilogue{}, s, x_lo,
+                ga1_lo ? h->ga1_lo : nullptr));
     ZC_TRY(tmark(h, 6, s));
     if (ar || adam) {
         ZC_CUDA(cudaEventRecord(h->ev_b, s));
@@ -807,6 +849,12 @@ extern "C" int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int6
     if (!st) st = alloc_f32(&h->gl, max_batch * h->d3p);
     for (int i = 0; i < 3 && !st; i++) st = alloc_f32(&h->col_partials[i], R * widths[i]);
     if (!st) st = alloc_f32(&h->xent_partials, (max_batch + kXentThreads - 1) / kXentThreads);
+    if (!st) st = alloc_f32(&h->x_lo, max_batch * d_in);
+    if (!st) st = alloc_f32(&h->w1_lo, d_in * d_h1);
+    if (!st) st = alloc_f32(&h->w2_lo, d_h1 * d_h2);
+    if (!st) st = alloc_f32(&h->a1_lo, max_batch * d_h1);
+    if (!st) st = alloc_f32(&h->ga2_lo, max_batch * d_h2);
+    if (!st) st = alloc_f32(&h->ga1_lo, max_batch * d_h1);
     if (!st && cudaMalloc((void **)&h->counters, (size_t)n_counters * sizeof(unsigned int)) != cudaSuccess) {
         cudaGetLastError();
         st = set_error(ZPUCUDA_ERR_OUT_OF_MEMORY, "cudaMalloc (mlp counters)");
