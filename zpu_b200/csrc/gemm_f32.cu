@@ -16,16 +16,19 @@
 // chunks into a running sum (a third TMEM region) with round-to-nearest f32
 // adds while the tensor core fills the other buffer.
 //
-// Shared-memory bandwidth is what limits this kernel: per 32-wide K slice
-// the TMA writes 32 KiB, making lo reads 32 and writes 32, and the three
-// MMAs read 96 (measured: the pipeline without making lo ran 1.7x faster;
-// ncu shows the LSU and tensor-core shared-memory pipes together near
-// saturation).  So every warp that is not the producer or the MMA issuer
-// converts, raw tiles have a deeper ring than lo tiles, and the hi tiles are
-// never rewritten.  (Feeding A from TMEM instead -- tcgen05.mma with a TMEM A
-// operand, hi and lo written by tcgen05.st -- cuts the traffic to 128 KiB but
-// measured slower: that pipeline peaked at 180 TFLOP/s even without
-// conversion, against 220 for this one.)
+// Where lo comes from is the kernel's main limit.  Made in shared memory,
+// per 32-wide K slice the TMA writes 32 KiB, making lo reads 32 and writes
+// 32, and the three MMAs read 96; so every warp that is not the producer or
+// the MMA issuer converts, raw tiles have a deeper ring than lo tiles, and
+// the hi tiles are never rewritten.  (Feeding A from TMEM instead --
+// tcgen05.mma with a TMEM A operand, hi and lo written by tcgen05.st -- cuts
+// the traffic to 128 KiB but measured slower: that pipeline peaked at 180
+// TFLOP/s even without conversion, against 220 for this one.)  Where every
+// operand element takes part in many products, a split pass writes lo into
+// HBM once per operand (split_lo_kernel, or a producing GEMM's epilogue) and
+// the PRE form of the kernel TMA-loads the lo tiles beside the hi ones: no
+// conversion at all (8192^3: 223 against 178 TFLOP/s, the pass included).
+// Both forms give the same bits.
 //
 // One CTA computes a 128 x BN tile (BN = 128 or 256, chosen per problem by
 // how the tiles fill the SMs; the Tile struct has the differences) with 16
@@ -37,7 +40,7 @@
 //               the tcgen05.commits;
 //   warps 2-15  write lo of each landed stage into one of LO lo slots at the
 //               same (swizzled) position, so hi and lo tiles share their
-//               descriptor layout;
+//               descriptor layout (idle in the PRE form);
 //   warps 8-15  also fold each finished chunk (tcgen05.ld / tcgen05.st
 //               32x32b) whenever they wait, then store the tile; warp w owns
 //               TMEM lanes 32 (w % 4) .. +31 and columns BN/2 ((w - 8) / 4)
