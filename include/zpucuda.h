@@ -351,8 +351,9 @@ int zpucuda_nccl_destroy(int64_t timeout_ms);
  * labels) (src/zpu/nn.zig:123-134,190-194), its gradients as
  * zpu.valueAndGrad computes them (src/zpu/transforms.zig:87-148,
  * src/zpu/autodiff.zig:51,323-330,451-454,480-487), and Adam.step with f32
- * moments (src/zpu/optim.zig:149-259), lowered to 16 kernels per step
- * (2 of them, the Adam updates, on a side stream).
+ * moments (src/zpu/optim.zig:149-259), lowered to 14 kernels per step
+ * (2 of them, the Adam updates, on a side stream), plus one split pass per
+ * large operand (x, W1, W2) where the products read presplit lo halves.
  * Parameters are numbered in the reference's argument order: 0 W1 [d_in,d_h1],
  * 1 b1 [d_h1], 2 W2 [d_h1,d_h2], 3 b2 [d_h2], 4 W3 [d_h2,d_out], 5 b3 [d_out],
  * row-major as the reference stores them; the handle owns the parameters,

@@ -201,6 +201,30 @@ def test_split_k_shapes(zc, ta, tb, m, k, n):
     assert np.array_equal(got, again)  # deterministic
 
 
+@pytest.mark.parametrize("splits", ["2", "3", "5", "8"])
+@pytest.mark.parametrize("bn", ["128", "256"])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, True)])
+def test_split_k_cluster_counts(zc, monkeypatch, splits, bn, ta, tb):
+    """Split counts forced to 2..8 (the CTAs of a tile form one cluster and
+    add their partials through distributed shared memory): ragged rows and
+    columns, rows of a tile shared unevenly among the splits (128 / 3, / 5),
+    both tile widths; deterministic from call to call."""
+    monkeypatch.setenv("ZPUCUDA_GEMM_SPLITS", splits)
+    monkeypatch.setenv("ZPUCUDA_GEMM_BN", bn)
+    rng = np.random.default_rng(int(splits) * 10 + int(bn))
+    for m, k, n in ((200, 2048, 10), (131, 1000, 300)):
+        a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        want = zo.gemm(a, b)
+        A = dev(a.T.copy()) if ta else dev(a)
+        B = dev(b.T.copy()) if tb else dev(b)
+        got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+        check_no_device_error(zc)
+        assert rel_fro(got, want) <= TOL, (m, k, n, rel_fro(got, want))
+        again = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+        assert np.array_equal(got, again)
+
+
 def test_split_k_batched(zc):
     rng = np.random.default_rng(11)
     a = rng.uniform(-1, 1, (3, 128, 4096)).astype(np.float32)

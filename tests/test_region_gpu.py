@@ -1144,6 +1144,29 @@ def test_matmul_bias_tanh_fuse_into_the_gemm_epilogue(zc):
             assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)
 
 
+def test_split_k_gemm_epilogues(zc):
+    """A product with one output tile and a long K runs split-K (the tile's
+    CTAs add their partials in a cluster): the bias + tanh and the bias
+    epilogues are applied after that sum."""
+    rng = np.random.default_rng(93)
+    x = rng.standard_normal((64, 4096)).astype(np.float32) * 0.05
+    w = rng.standard_normal((4096, 36)).astype(np.float32) * 0.05
+    b = rng.standard_normal(36).astype(np.float32)
+    F = zc.F32
+    args = [(1, F, (64, 4096)), (2, F, (4096, 36)), (3, F, (36,))]
+    mm = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0), ("tanh", [11], 12, -2, 0)]
+    ref_h = x.astype(np.float64) @ w.astype(np.float64) + b
+    for outs in ([12], [11, 12]):
+        p = zc.Plan(args, [], mm, outs)
+        got = dict(zip(outs, [o.cpu().numpy().astype(np.float64)
+                              for o in p.run([torch.from_numpy(v).cuda() for v in (x, w, b)])]))
+        torch.cuda.synchronize()
+        zc.check(zc.lib().zpucuda_check_device())
+        assert np.max(np.abs(got[12] - np.tanh(ref_h))) <= 2e-5
+        if 11 in got:
+            assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)
+
+
 def test_data_movement_snapshots_on_device(zc, golden):
     """The reference's shape/{pad,take,concat,stack} snapshots as plan steps."""
     x = torch.tensor(golden["inputs"]["spread12"], dtype=torch.float64, device="cuda").reshape(3, 4)

@@ -102,7 +102,11 @@ struct Tile {
     static constexpr int CONV_ITERS = (RAW_BYTES / 16 + NWORK * 32 - 1) / (NWORK * 32);
     static constexpr size_t SMEM_BYTES = (size_t)RAW * STAGE_BYTES + (size_t)LO * RAW_BYTES + 1024;  // + alignment slack
     static constexpr int FOLD_COLS = BN_ / 2;  // columns per folding thread
+    // split-K: the CTA's partial tile in its own shared memory, rows padded
+    // by 4 floats (a warp's float4 stores then take the minimum 4 wavefronts)
+    static constexpr int XPITCH = BN_ + 4;
     static_assert(NBUF * BN_ <= (int)SUM_COL && SUM_COL + BN_ <= TMEM_COLS, "TMEM columns");
+    static_assert((size_t)BM * XPITCH * 4 + 1024 <= SMEM_BYTES, "split-K partial fits the pipeline buffers");
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 constexpr uint32_t kGemmSpin = 1u << 24;
@@ -138,6 +142,31 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
             "r"(su32(dst)),
         "l"(map), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
         : "memory");
+}
+
+// Thread-block cluster barrier (every thread of every CTA of the cluster).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The address of this CTA's shared-memory location `a` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(a)
+                 : "memory");
+    return v;
 }
 
 // Shared-memory matrix descriptor (sm_100, version 1).  layout: 2 = 128-byte
@@ -310,7 +339,7 @@ struct Params {
     int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
     int32_t nmma;          // MMA width: N rounded up to 16, at most BN
     uint32_t idesc;
-    int32_t splits;        // K split across this many CTAs (blockIdx.z = batch * splits + split)
+    int32_t splits;        // K split across a cluster of this many CTAs (blockIdx.z = batch * splits + split)
     int32_t kb_per_split;  // 32-wide K slices per split
     Epilogue epi;
     GemmBatch bt;
@@ -384,6 +413,64 @@ __device__ __forceinline__ void epi_apply32(const Epilogue &e, float (&acc)[32],
 #pragma unroll
         for (int v = 0; v < 32; v++) acc[v] = __fadd_rn(acc[v], __ldg(b + v));
     }
+}
+
+// Split-K inside a cluster: the `splits` CTAs of one output tile are one
+// thread-block cluster, each holding its raw partial tile in its own shared
+// memory.  CTA `rank` sums rows [128 rank / splits, 128 (rank + 1) / splits)
+// of the tile over all partials, read through distributed shared memory and
+// added in split order (deterministic, the same order for every element),
+// recomputes non-finite sums with zpu's chain, applies the epilogue and
+// stores.  No scratch in HBM and no second kernel.
+template <bool TA, bool TB, int BN_>
+__device__ __noinline__ void splitk_cluster_reduce(const uint8_t *smem, float *C, const Params &P, int64_t oa,
+                                                   int64_t ob, int64_t bz, int m0, int n0) {
+    constexpr int XPITCH = Tile<BN_>::XPITCH, C4 = BN_ / 4;
+    cluster_sync_all();  // every CTA's partial is in place
+    const int S = P.splits;
+    const int rank = (int)cluster_rank();
+    const int r0 = BM * rank / S, r1 = BM * (rank + 1) / S;
+    uint32_t rb[8];
+#pragma unroll
+    for (int sp = 0; sp < 8; sp++) rb[sp] = sp < S ? cluster_map(su32(smem), (uint32_t)sp) : 0u;
+    float *cm = C + bz * P.stride_c;
+    for (int i = threadIdx.x; i < (r1 - r0) * C4; i += THREADS) {
+        const int rl = r0 + i / C4, c = (i % C4) * 4;
+        const int64_t row = (int64_t)m0 + rl, col0 = (int64_t)n0 + c;
+        if (row >= P.M || col0 >= P.N) continue;
+        const uint32_t off = (uint32_t)((rl * XPITCH + c) * 4);
+        float4 a = ld_cluster4(rb[0] + off);
+        for (int sp = 1; sp < S; sp++) {
+            const float4 b = ld_cluster4(rb[sp] + off);
+            a.x = __fadd_rn(a.x, b.x);
+            a.y = __fadd_rn(a.y, b.y);
+            a.z = __fadd_rn(a.z, b.z);
+            a.w = __fadd_rn(a.w, b.w);
+        }
+        float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            if (col0 + e >= P.N) break;
+            if (!isfinite(v[e]))
+                v[e] = zpu_chain_element<TA, TB>(P.A + oa, P.B + ob, P.lda, P.ldb, row, col0 + e, P.N, 0, P.K);
+            v[e] = epi_apply(P.epi, v[e], row, col0 + e);
+        }
+        float *crow = cm + row * P.ldc;
+        if (col0 + 4 <= P.N && (((uintptr_t)(crow + col0)) & 15) == 0) {
+            *(float4 *)(crow + col0) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (col0 + e < P.N) crow[col0 + e] = v[e];
+        }
+        if (P.epi.lo_out) {
+            float *lrow = P.epi.lo_out + row * P.ldc;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (col0 + e < P.N) lrow[col0 + e] = lo1(v[e]);
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while another still reads its partial
 }
 
 template <bool TA, bool TB, int BN_, bool PRE>
@@ -570,9 +657,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float acc[32];
                 tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)cl, acc);
                 const int64_t col0 = (int64_t)n0 + cl;
-                // non-finite results: zpu's chain instead (over the whole K;
-                // split-K partials are left to the reduction, which does it)
-                if (P.splits == 1 && row < P.M) {
+                if (P.splits > 1) {  // split-K: the raw partial into this CTA's shared memory
+                    float *xr = (float *)smem + (size_t)(q4 * 32 + lane) * T::XPITCH + cl;
+#pragma unroll
+                    for (int v = 0; v < 8; v++)
+                        *(float4 *)(xr + 4 * v) = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                    continue;
+                }
+                // non-finite results: zpu's chain instead (over the whole K)
+                if (row < P.M) {
                     bool bad = false;
 #pragma unroll
                     for (int v = 0; v < 32; v++) bad |= !isfinite(acc[v]);
@@ -644,6 +737,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     }
+    if (P.splits > 1) splitk_cluster_reduce<TA, TB, BN_>(smem, C, P, oa, ob, bz, m0, n0);
 }
 
 // ------------------------------------------------ plain FMA-chain fallback
@@ -685,35 +779,9 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
 
 // ------------------------------------------------------------- host side
 
-// Split-K: C = epilogue(sum over s of ws[(batch * splits + s)][m][n]), the
-// partials added in split order (deterministic).
-// A non-finite sum is recomputed with zpu's chain over the whole K (see
-// zpu_chain_element).
-template <bool TA, bool TB>
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ ws, int splits, int64_t m,
-                                                            int64_t n, int64_t batches, float *__restrict__ C,
-                                                            int64_t ldc, int64_t stride_c,
-                                                            const __grid_constant__ Epilogue epi,
-                                                            const __grid_constant__ Params P) {
-    const int64_t mn = m * n, total = batches * mn;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b = i / mn, r = (i / n) % m, c = i % n;
-        const float *p = ws + b * splits * mn + r * n + c;
-        float acc = p[0];
-        for (int sp = 1; sp < splits; sp++) acc = __fadd_rn(acc, p[sp * mn]);
-        if (!isfinite(acc)) {
-            int64_t oa, ob;
-            batch_offsets(P.bt, b, &oa, &ob);
-            acc = zpu_chain_element<TA, TB>(P.A + oa, P.B + ob, P.lda, P.ldb, r, c, n, 0, P.K);
-        }
-        const float y = epi_apply(epi, acc, r, c);
-        C[b * stride_c + r * ldc + c] = y;
-        if (epi.lo_out) epi.lo_out[r * ldc + c] = lo1(y);  // one matrix (lo_out is refused for batches)
-    }
-}
-
-// Stream-ordered scratch for split-K partials: one memory pool per device
-// that keeps what it has allocated (no release at synchronisation).
+// Stream-ordered scratch for the lo halves of presplit operands: one memory
+// pool per device that keeps what it has allocated (no release at
+// synchronisation).
 cudaMemPool_t splitk_pool() {
     static std::mutex mu;
     static cudaMemPool_t pools[64] = {nullptr};
@@ -740,13 +808,23 @@ cudaMemPool_t splitk_pool() {
 
 // K splits for a problem of `tiles` output tiles and KT K slices: enough CTAs
 // to cover the SMs when the tiles alone fill less than half of them, with at
-// least two accumulation chunks per split.
+// least two accumulation chunks per split; at most kMaxSplits (one
+// portable-size cluster per tile).  ZPUCUDA_GEMM_SPLITS=<n> forces the
+// split count (read at every call; still capped at kMaxSplits and KT).
+constexpr int kMaxSplits = 8;
 int choose_splits(int64_t tiles, int64_t KT, int kc) {
-    const int64_t sms = num_sms();
-    if (tiles * 2 > sms) return 1;
-    int64_t sp = sms / tiles;
-    if (sp > KT / (2 * kc)) sp = KT / (2 * kc);
-    if (sp > 16) sp = 16;
+    int64_t sp;
+    const char *e = getenv("ZPUCUDA_GEMM_SPLITS");
+    if (e && atoi(e) >= 1) {
+        sp = atoi(e);
+    } else {
+        const int64_t sms = num_sms();
+        if (tiles * 2 > sms) return 1;
+        sp = sms / tiles;
+        if (sp > KT / (2 * kc)) sp = KT / (2 * kc);
+    }
+    if (sp > kMaxSplits) sp = kMaxSplits;
+    if (sp > KT) sp = KT;
     return sp < 1 ? 1 : (int)sp;
 }
 
@@ -816,21 +894,44 @@ int launch_tf32x3(const Maps &maps, float *C, const Params &P, int64_t batches, 
         if (dev >= 0 && dev < 64) attr[dev] = true;
     }
     dim3 grid((unsigned)((P.N + BN_ - 1) / BN_), (unsigned)((P.M + BM - 1) / BM), (unsigned)(batches * P.splits));
-    k<<<grid, THREADS, T::SMEM_BYTES, s>>>(maps, C, P);
-    ZC_LAUNCHED("tf32x3_gemm_kernel");
+    if (P.splits == 1) {
+        k<<<grid, THREADS, T::SMEM_BYTES, s>>>(maps, C, P);
+        ZC_LAUNCHED("tf32x3_gemm_kernel");
+        return ZPUCUDA_OK;
+    }
+    // split-K: the splits of one tile form a cluster along z
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = T::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = (unsigned)P.splits;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    ZC_CUDA(cudaLaunchKernelEx(&cfg, k, maps, C, P));
+    count_launch();
     return ZPUCUDA_OK;
 }
 
-// Tile width for an m x n x batches problem: the 256-wide tile does a
-// 128 x 256 tile in ~1.75x the time of a 128 x 128 one; pick the width whose
-// whole waves of tiles over the SMs take less time.
+// Tile width for an m x n x batches problem: a 128 x 256 tile takes ~1.6x
+// the time of a 128 x 128 one (measured 1.5-1.7 over 4096^3, the batched
+// 256 x 512^3 and the MLP's products, with and without the presplit lo);
+// pick the width whose whole waves of tiles over the SMs take less time.
+// ZPUCUDA_GEMM_BN=128 or 256 forces the width (read at every call).
 int choose_bn(int64_t m, int64_t n, int64_t batches) {
+    const char *e = getenv("ZPUCUDA_GEMM_BN");
+    if (e && (atoi(e) == 128 || atoi(e) == 256)) return atoi(e);
     if (n <= 128) return 128;
     const int64_t sms = num_sms();
     const int64_t rows = (m + BM - 1) / BM;
     const int64_t w128 = (rows * ((n + 127) / 128) * batches + sms - 1) / sms;
     const int64_t w256 = (rows * ((n + 255) / 256) * batches + sms - 1) / sms;
-    return 1.75 * (double)w256 < (double)w128 ? 256 : 128;
+    return 1.6 * (double)w256 < (double)w128 ? 256 : 128;
 }
 
 template <int BN_, bool PRE>
@@ -974,23 +1075,8 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
             const int64_t tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn) * batches;
             int splits = choose_splits(tiles, KT, bn == 256 ? Tile<256>::KC_BLOCKS : Tile<128>::KC_BLOCKS);
             if (batches * splits > 65535 || epi.mode == EPI_SCATTER) splits = 1;  // the tile store is the scatter
-            float *ws = nullptr;
-            cudaMemPool_t pool = splits > 1 ? splitk_pool() : nullptr;
-            if (splits > 1 &&
-                (!pool || cudaMallocFromPoolAsync((void **)&ws, (size_t)(splits * batches * m * n) * sizeof(float),
-                                                  pool, s) != cudaSuccess)) {
-                cudaGetLastError();
-                splits = 1;  // no scratch: one CTA per tile over the whole K
-                ws = nullptr;
-            }
-            P.splits = splits;
             P.kb_per_split = (int32_t)((KT + splits - 1) / splits);
-            if (splits > 1) {  // every split writes raw partial sums into ws
-                P.splits = splits = (int)((KT + P.kb_per_split - 1) / P.kb_per_split);
-                P.ldc = n;
-                P.stride_c = m * n;
-                P.epi = Epilogue{};
-            }
+            P.splits = (int32_t)((KT + P.kb_per_split - 1) / P.kb_per_split);  // every split has a K slice
             // lo halves from a split pass: scratch with each operand's own
             // geometry, the same tensor maps on another base
             // (or the caller's, when it supplies them)
@@ -1003,31 +1089,12 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
                 pre = a_lo && b_lo && make_map(&maps.alo, a_lo, a_inner, a_rows, lda, na, mat_a, ta ? 32 : BM, !ta) &&
                       make_map(&maps.blo, b_lo, b_inner, b_rows, ldb, nb, mat_b, tb ? bn : 32, tb);
             }
-            float *cout = splits > 1 ? ws : C;
-            int st = pre ? (bn == 256 ? dispatch_tf32x3<256, true>(ta, tb, maps, cout, P, batches, s)
-                                      : dispatch_tf32x3<128, true>(ta, tb, maps, cout, P, batches, s))
-                         : (bn == 256 ? dispatch_tf32x3<256, false>(ta, tb, maps, cout, P, batches, s)
-                                      : dispatch_tf32x3<128, false>(ta, tb, maps, cout, P, batches, s));
+            int st = pre ? (bn == 256 ? dispatch_tf32x3<256, true>(ta, tb, maps, C, P, batches, s)
+                                      : dispatch_tf32x3<128, true>(ta, tb, maps, C, P, batches, s))
+                         : (bn == 256 ? dispatch_tf32x3<256, false>(ta, tb, maps, C, P, batches, s)
+                                      : dispatch_tf32x3<128, false>(ta, tb, maps, C, P, batches, s));
             if (alo) cudaFreeAsync(alo, s);
             if (blo) cudaFreeAsync(blo, s);
-            if (splits > 1) {
-                if (st == ZPUCUDA_OK) {
-                    const int64_t total = batches * m * n;
-                    int64_t blocks = (total + 255) / 256;
-                    if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-#define ZC_RED(TA_, TB_) \
-    splitk_reduce_kernel<TA_, TB_><<<(unsigned)blocks, 256, 0, s>>>(ws, splits, m, n, batches, C, ldc, stride_c, epi, P)
-                    if (!ta && !tb) ZC_RED(false, false);
-                    else if (!ta && tb) ZC_RED(false, true);
-                    else if (ta && !tb) ZC_RED(true, false);
-                    else ZC_RED(true, true);
-#undef ZC_RED
-                    cudaError_t e = cudaGetLastError();
-                    if (e != cudaSuccess) st = cuda_fail(e, "splitk_reduce_kernel");
-                    else count_launch();
-                }
-                cudaFreeAsync(ws, s);
-            }
             return st;
         }
     }

@@ -6,8 +6,10 @@
 // src/zpu/ops.zig:998-1010), the reverse sweep's rules for matmul, tanh, sum
 // and the broadcast bias (src/zpu/autodiff.zig:51,323-330,451-454,480-487),
 // then Adam.step with f32 moment state (src/zpu/optim.zig:183-259).
-// Here the same arithmetic is lowered to 16 kernel launches over buffers that
-// stay in HBM (the two 16-column products run split-K with a reduce each):
+// Here the same arithmetic is lowered to 14 kernel launches (plus the split
+// passes of the presplit lo halves, below) over buffers that stay in HBM (the
+// two 16-column products run split-K, the CTAs of a tile adding their
+// partials inside one cluster):
 //   forward   3 GEMMs; bias + tanh run in the first two GEMMs' epilogues,
 //             the bias of the logits in the third's;
 //   loss      one kernel per 256 rows: log-softmax, the picked NLL, the loss
