@@ -144,29 +144,31 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// Thread-block cluster barrier (every thread of every CTA of the cluster).
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
-// The address of this CTA's shared-memory location `a` in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t cluster_map(uint32_t a, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-    return r;
+// The generic address of this CTA's shared-memory object `p` in CTA `rank`
+// of the cluster (plain loads through it read that CTA's shared memory).
+__device__ __forceinline__ const void *cluster_map_generic(const void *p, uint32_t rank) {
+    uint64_t r;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"((uint64_t)p), "r"(rank));
+    return (const void *)r;
 }
-__device__ __forceinline__ float4 ld_cluster4(uint32_t a) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(a)
+
+// TMA store of a 32 x 32 f32 box (128-byte swizzled in shared memory) at
+// (x, y, z) of `map`; out-of-range rows and columns are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+                 "r"(su32(src)), "r"(x), "r"(y), "r"(z)
                  : "memory");
-    return v;
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Until at most N of this thread's committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
 // Shared-memory matrix descriptor (sm_100, version 1).  layout: 2 = 128-byte
@@ -330,6 +332,7 @@ __device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q,
 struct Maps {
     CUtensorMap a, b;
     CUtensorMap alo, blo;  // the lo halves (PRE kernels only)
+    CUtensorMap c, clo;    // C and the epilogue's lo output, for the TMA tile store
 };
 
 struct Params {
@@ -341,6 +344,7 @@ struct Params {
     uint32_t idesc;
     int32_t splits;        // K split across a cluster of this many CTAs (blockIdx.z = batch * splits + split)
     int32_t kb_per_split;  // 32-wide K slices per split
+    int32_t tma_store;     // the tile leaves through maps.c (and maps.clo when epi.lo_out)
     Epilogue epi;
     GemmBatch bt;
 };
@@ -421,33 +425,55 @@ __device__ __forceinline__ void epi_apply32(const Epilogue &e, float (&acc)[32],
 // of the tile over all partials, read through distributed shared memory and
 // added in split order (deterministic, the same order for every element),
 // recomputes non-finite sums with zpu's chain, applies the epilogue and
-// stores.  No scratch in HBM and no second kernel.
+// stores.  No scratch in HBM and no second kernel.  Each thread first loads
+// and adds all its elements (KR float4 per partial, loads of a partial in
+// flight together), then tells the cluster it is done reading, and stores
+// while the other CTAs finish; it waits for them only before it exits (its
+// own partial must stay until every CTA has read it).  The caller has
+// arrived on the cluster barrier once its partial was in place.
 template <bool TA, bool TB, int BN_>
-__device__ __noinline__ void splitk_cluster_reduce(const uint8_t *smem, float *C, const Params &P, int64_t oa,
+__device__ __forceinline__ void splitk_cluster_reduce(const uint8_t *smem, float *C, const Params &P, int64_t oa,
                                                    int64_t ob, int64_t bz, int m0, int n0) {
     constexpr int XPITCH = Tile<BN_>::XPITCH, C4 = BN_ / 4;
-    cluster_sync_all();  // every CTA's partial is in place
+    constexpr int KR = (BM * C4 / 2 + THREADS - 1) / THREADS;  // float4 per thread at 2 splits (the most)
+    static_assert(KR % 4 == 0, "loads go in groups of four");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // every partial is in place
     const int S = P.splits;
     const int rank = (int)cluster_rank();
-    const int r0 = BM * rank / S, r1 = BM * (rank + 1) / S;
-    uint32_t rb[8];
+    const int r0 = BM * rank / S, r1 = BM * (rank + 1) / S, n4 = (r1 - r0) * C4;
+    float4 acc[KR];
+    for (int sp = 0; sp < S; sp++) {
+        const float *part = (const float *)cluster_map_generic(smem, (uint32_t)sp);
 #pragma unroll
-    for (int sp = 0; sp < 8; sp++) rb[sp] = sp < S ? cluster_map(su32(smem), (uint32_t)sp) : 0u;
-    float *cm = C + bz * P.stride_c;
-    for (int i = threadIdx.x; i < (r1 - r0) * C4; i += THREADS) {
-        const int rl = r0 + i / C4, c = (i % C4) * 4;
-        const int64_t row = (int64_t)m0 + rl, col0 = (int64_t)n0 + c;
-        if (row >= P.M || col0 >= P.N) continue;
-        const uint32_t off = (uint32_t)((rl * XPITCH + c) * 4);
-        float4 a = ld_cluster4(rb[0] + off);
-        for (int sp = 1; sp < S; sp++) {
-            const float4 b = ld_cluster4(rb[sp] + off);
-            a.x = __fadd_rn(a.x, b.x);
-            a.y = __fadd_rn(a.y, b.y);
-            a.z = __fadd_rn(a.z, b.z);
-            a.w = __fadd_rn(a.w, b.w);
+        for (int g = 0; g < KR; g += 4) {  // four loads in flight, then their adds
+            float4 b[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = (int)threadIdx.x + (g + u) * THREADS;
+                if (i < n4) b[u] = *(const float4 *)(part + (r0 + i / C4) * XPITCH + (i % C4) * 4);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (sp == 0) {
+                    acc[g + u] = b[u];
+                } else {
+                    acc[g + u].x = __fadd_rn(acc[g + u].x, b[u].x);
+                    acc[g + u].y = __fadd_rn(acc[g + u].y, b[u].y);
+                    acc[g + u].z = __fadd_rn(acc[g + u].z, b[u].z);
+                    acc[g + u].w = __fadd_rn(acc[g + u].w, b[u].w);
+                }
+            }
         }
-        float v[4] = {a.x, a.y, a.z, a.w};
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");  // done reading the partials
+    float *cm = C + bz * P.stride_c;
+#pragma unroll
+    for (int u = 0; u < KR; u++) {
+        const int i = (int)threadIdx.x + u * THREADS;
+        if (i >= n4) break;
+        const int64_t row = (int64_t)m0 + r0 + i / C4, col0 = (int64_t)n0 + (i % C4) * 4;
+        if (row >= P.M || col0 >= P.N) continue;
+        float v[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             if (col0 + e >= P.N) break;
@@ -470,7 +496,7 @@ __device__ __noinline__ void splitk_cluster_reduce(const uint8_t *smem, float *C
                 if (col0 + e < P.N) lrow[col0 + e] = lo1(v[e]);
         }
     }
-    cluster_sync_all();  // no CTA leaves while another still reads its partial
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // no CTA leaves while another still reads
 }
 
 template <bool TA, bool TB, int BN_, bool PRE>
@@ -496,6 +522,35 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int KT = min((int)((P.K + BK - 1) / BK) - kb0, P.kb_per_split);
     const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
 
+    // stage s: A then B (the hi operands as loaded), for PRE then A lo and
+    // B lo; lo slot l (converted in shared memory): A then B.  For PRE the
+    // lo tiles are indexed by stage.
+    auto raw_a = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
+    auto raw_b = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
+    auto lo_a = [&](int l) {
+        return PRE ? smem + (size_t)l * STAGE_BYTES + RAW_BYTES : smem + (size_t)RAW * STAGE_BYTES + (size_t)l * RAW_BYTES;
+    };
+    auto lo_b = [&](int l) { return lo_a(l) + A_BYTES; };
+
+    // TMA loads of K slice j into stage j % RAW (A, B; for PRE also A lo, B lo)
+    auto issue = [&](int j) {
+        const int s = j % RAW;
+        mb_expect_tx(&full[s], STAGE_BYTES);
+        const int k0 = (kb0 + j) * BK;
+#pragma unroll
+        for (int h = 0; h < (PRE ? 2 : 1); h++) {  // hi, then (PRE) lo
+            uint8_t *da = h ? lo_a(s) : raw_a(s), *db = h ? lo_b(s) : raw_b(s);
+            const CUtensorMap *ma = h ? &maps.alo : &maps.a, *mb = h ? &maps.blo : &maps.b;
+            if (!TA) tma_load_3d(da, ma, k0, m0, za, &full[s]);
+            else
+                for (int c = 0; c < BM / 32; c++) tma_load_3d(da + c * 4096, ma, m0 + 32 * c, k0, za, &full[s]);
+            if (TB) tma_load_3d(db, mb, k0, n0, zb, &full[s]);
+            else
+                for (int c = 0; c < BN / 32; c++) tma_load_3d(db + c * 4096, mb, n0 + 32 * c, k0, zb, &full[s]);
+        }
+    };
+    const int first_loads = KT < RAW ? KT : RAW;
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < RAW; s++) {
             mb_init(&full[s], 1);
@@ -510,6 +565,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mb_init(&tfree[b], NFOLD);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int j = 0; j < first_loads; j++) issue(j);  // these load while TMEM is allocated
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
@@ -521,34 +577,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = tmem_base;
 
-    // stage s: A then B (the hi operands as loaded), for PRE then A lo and
-    // B lo; lo slot l (converted in shared memory): A then B.  For PRE the
-    // lo tiles are indexed by stage.
-    auto raw_a = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
-    auto raw_b = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
-    auto lo_a = [&](int l) {
-        return PRE ? smem + (size_t)l * STAGE_BYTES + RAW_BYTES : smem + (size_t)RAW * STAGE_BYTES + (size_t)l * RAW_BYTES;
-    };
-    auto lo_b = [&](int l) { return lo_a(l) + A_BYTES; };
-
     if (warp == 0) {
         if (lane == 0) {
-            for (int j = 0; j < KT; j++) {
-                const int s = j % RAW;
-                if (j >= RAW && !mb_wait(&empty[s], ((j / RAW) - 1) & 1)) break;
-                mb_expect_tx(&full[s], STAGE_BYTES);
-                const int k0 = (kb0 + j) * BK;
-#pragma unroll
-                for (int h = 0; h < (PRE ? 2 : 1); h++) {  // hi, then (PRE) lo
-                    uint8_t *da = h ? lo_a(s) : raw_a(s), *db = h ? lo_b(s) : raw_b(s);
-                    const CUtensorMap *ma = h ? &maps.alo : &maps.a, *mb = h ? &maps.blo : &maps.b;
-                    if (!TA) tma_load_3d(da, ma, k0, m0, za, &full[s]);
-                    else
-                        for (int c = 0; c < BM / 32; c++) tma_load_3d(da + c * 4096, ma, m0 + 32 * c, k0, za, &full[s]);
-                    if (TB) tma_load_3d(db, mb, k0, n0, zb, &full[s]);
-                    else
-                        for (int c = 0; c < BN / 32; c++) tma_load_3d(db + c * 4096, mb, n0 + 32 * c, k0, zb, &full[s]);
-                }
+            for (int j = first_loads; j < KT; j++) {  // j >= RAW: wait for the stage's last MMAs
+                if (!mb_wait(&empty[j % RAW], ((j / RAW) - 1) & 1)) break;
+                issue(j);
             }
         }
     } else if (warp == 1) {
@@ -647,7 +680,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t row = (int64_t)m0 + q4 * 32 + lane;
             const bool staged = P.epi.mode == EPI_SCATTER;
             const int64_t row0 = (int64_t)m0 + q4 * 32;
-            float *stage = (float *)(smem + (size_t)(warp - 8) * (32 * 33 * sizeof(float)));
+            // per-warp staging area in the (idle) pipeline buffers: 32 rows of
+            // SPITCH floats (pitch 33 for the scatter's column reads)
+            constexpr int SPITCH = 36;
+            float *stage = (float *)(smem + (size_t)(warp - 8) * (32 * SPITCH * sizeof(float)));
+            // TMA store boxes: per warp two C boxes then two lo boxes (4 KiB
+            // each, 1024-byte aligned), after the staging areas
+            float *tbuf = (float *)(smem + 40960 + (size_t)(warp - 8) * 16384);
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll 1
@@ -683,35 +722,118 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
                 if (!staged) {
-                    float *crow = C + (int64_t)blockIdx.z * P.stride_c + row * P.ldc;  // (batch, split) slab
-                    float *lrow = P.epi.lo_out ? P.epi.lo_out + row * P.ldc : nullptr;  // one matrix, no split
-                    if (row < P.M) {
-                        if (col0 + 32 <= P.N && ((((uintptr_t)(crow + col0)) & 15) == 0)) {
-                            epi_apply32(P.epi, acc, row, col0);
+                    // the epilogue on this lane's row in registers; then the
+                    // warp's 32 x 32 piece is turned around in shared memory so
+                    // that each store instruction writes 128 contiguous bytes
+                    // of four rows (a lane-per-row store touches 32 lines)
+                    const int c4 = (lane & 7) * 4;
+                    const int64_t col = col0 + c4;
+                    if (P.epi.mode == EPI_TANH_GRAD) {
+                        // y of the warp's 32 x 32 piece, read the same coalesced
+                        // way into the staging area, then each lane takes its row
+                        __syncwarp();
 #pragma unroll
-                            for (int v = 0; v < 8; v++)
-                                *(float4 *)(crow + col0 + 4 * v) =
-                                    make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-                            if (lrow && ((((uintptr_t)(lrow + col0)) & 15) == 0)) {
-#pragma unroll
-                                for (int v = 0; v < 8; v++)
-                                    *(uint4 *)(lrow + col0 + 4 * v) =
-                                        lo4(make_uint4(__float_as_uint(acc[4 * v]), __float_as_uint(acc[4 * v + 1]),
-                                                       __float_as_uint(acc[4 * v + 2]), __float_as_uint(acc[4 * v + 3])));
-                            } else if (lrow) {
-#pragma unroll
-                                for (int v = 0; v < 32; v++) lrow[col0 + v] = lo1(acc[v]);
+                        for (int it = 0; it < 8; it++) {
+                            const int r = it * 4 + (lane >> 3);
+                            const int64_t rr = row0 + r;
+                            float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                            if (rr < P.M && col < P.N) {
+                                const float *yp = P.epi.aux + rr * P.epi.ldaux + col;
+                                if (col + 4 <= P.N && ((((uintptr_t)yp) & 15) == 0)) {
+                                    y = __ldg((const float4 *)yp);
+                                } else {
+                                    y.x = yp[0];
+                                    if (col + 1 < P.N) y.y = yp[1];
+                                    if (col + 2 < P.N) y.z = yp[2];
+                                    if (col + 3 < P.N) y.w = yp[3];
+                                }
                             }
+                            *(float4 *)(stage + r * SPITCH + c4) = y;
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int v = 0; v < 8; v++) {
+                            const float4 y = *(const float4 *)(stage + lane * SPITCH + 4 * v);
+                            acc[4 * v] = __fmul_rn(acc[4 * v], __fsub_rn(1.0f, __fmul_rn(y.x, y.x)));
+                            acc[4 * v + 1] = __fmul_rn(acc[4 * v + 1], __fsub_rn(1.0f, __fmul_rn(y.y, y.y)));
+                            acc[4 * v + 2] = __fmul_rn(acc[4 * v + 2], __fsub_rn(1.0f, __fmul_rn(y.z, y.z)));
+                            acc[4 * v + 3] = __fmul_rn(acc[4 * v + 3], __fsub_rn(1.0f, __fmul_rn(y.w, y.w)));
+                        }
+                    } else if (row < P.M) {
+                        if (col0 + 32 <= P.N) {
+                            epi_apply32(P.epi, acc, row, col0);
                         } else {
 #pragma unroll
                             for (int v = 0; v < 32; v++)
-                                if (col0 + v < P.N) {
-                                    const float y = epi_apply(P.epi, acc[v], row, col0 + v);
-                                    crow[col0 + v] = y;
-                                    if (lrow) lrow[col0 + v] = lo1(y);
+                                if (col0 + v < P.N) acc[v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                        }
+                    }
+                    __syncwarp();
+                    if (P.tma_store) {
+                        // this lane's row into a 128-byte swizzled 32 x 32 box
+                        // (16-byte chunk v of row r at chunk v ^ (r % 8): the
+                        // warp's writes take the minimum 4 wavefronts), then
+                        // one lane hands the box to the TMA; two buffers per
+                        // warp, so the next piece is staged while this one leaves
+                        if (c >= 2 && lane == 0) bulk_wait_read<1>();
+                        __syncwarp();
+                        float *bc = tbuf + (c & 1) * 1024, *bl = bc + 2048;
+#pragma unroll
+                        for (int v = 0; v < 8; v++)
+                            *(float4 *)(bc + lane * 32 + ((v ^ (lane & 7)) * 4)) =
+                                make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                        if (P.epi.lo_out) {
+#pragma unroll
+                            for (int v = 0; v < 8; v++)
+                                *(uint4 *)(bl + lane * 32 + ((v ^ (lane & 7)) * 4)) =
+                                    lo4(make_uint4(__float_as_uint(acc[4 * v]), __float_as_uint(acc[4 * v + 1]),
+                                                   __float_as_uint(acc[4 * v + 2]), __float_as_uint(acc[4 * v + 3])));
+                        }
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_3d(&maps.c, bc, (int)col0, (int)row0, (int)blockIdx.z);
+                            if (P.epi.lo_out) tma_store_3d(&maps.clo, bl, (int)col0, (int)row0, 0);
+                            bulk_commit();
+                        }
+                        continue;
+                    }
+#pragma unroll
+                    for (int v = 0; v < 8; v++)
+                        *(float4 *)(stage + lane * SPITCH + 4 * v) =
+                            make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                    __syncwarp();
+                    float *cm = C + (int64_t)blockIdx.z * P.stride_c;
+#pragma unroll
+                    for (int it = 0; it < 8; it++) {
+                        const int r = it * 4 + (lane >> 3);
+                        const int64_t rr = row0 + r;
+                        if (rr >= P.M || col >= P.N) continue;
+                        const float4 y = *(const float4 *)(stage + r * SPITCH + c4);
+                        float *cp = cm + rr * P.ldc + col;
+                        float *lp = P.epi.lo_out ? P.epi.lo_out + rr * P.ldc + col : nullptr;  // one matrix
+                        if (col + 4 <= P.N && ((((uintptr_t)cp) & 15) == 0)) {
+                            *(float4 *)cp = y;
+                            if (lp && ((((uintptr_t)lp) & 15) == 0)) {
+                                *(uint4 *)lp = lo4(make_uint4(__float_as_uint(y.x), __float_as_uint(y.y),
+                                                              __float_as_uint(y.z), __float_as_uint(y.w)));
+                            } else if (lp) {
+                                lp[0] = lo1(y.x);
+                                lp[1] = lo1(y.y);
+                                lp[2] = lo1(y.z);
+                                lp[3] = lo1(y.w);
+                            }
+                        } else {
+                            const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+                            for (int e = 0; e < 4; e++)
+                                if (col + e < P.N) {
+                                    cp[e] = yv[e];
+                                    if (lp) lp[e] = lo1(yv[e]);
                                 }
                         }
                     }
+                    __syncwarp();
                     continue;
                 }
 #pragma unroll
@@ -729,10 +851,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 __syncwarp();
             }
+            if (P.tma_store && lane == 0) bulk_wait_read<0>();  // the boxes have left shared memory
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
+    // split-K: this CTA's partial is in place (the release orders the
+    // folders' shared-memory stores before the other CTAs read them)
+    if (P.splits > 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
@@ -974,6 +1100,14 @@ float *split_operand(cudaMemPool_t pool, const float *x, int64_t inner, int64_t 
 // (4096^3 and the MLP's products yes; 1024^3 and 256 x 512^3 no: measured
 // 51 -> 44 and 135 -> 117 TFLOP/s with the pass).  ZPUCUDA_GEMM_PRESPLIT=0
 // or 1 forces the choice (read at every call).
+// Whether result tiles leave through TMA stores (default) rather than the
+// folding warps' own stores; ZPUCUDA_GEMM_TMA_STORE=0 turns them off (read
+// at every call).
+bool use_tma_store() {
+    const char *e = getenv("ZPUCUDA_GEMM_TMA_STORE");
+    return !(e && e[0] == '0' && e[1] == 0);
+}
+
 bool use_presplit(int64_t m, int64_t n, int64_t batches, int64_t na, int64_t nb) {
     const char *e = getenv("ZPUCUDA_GEMM_PRESPLIT");
     if (e && (e[0] == '0' || e[0] == '1') && e[1] == 0) return e[0] == '1';
@@ -1077,6 +1211,15 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
             if (batches * splits > 65535 || epi.mode == EPI_SCATTER) splits = 1;  // the tile store is the scatter
             P.kb_per_split = (int32_t)((KT + splits - 1) / splits);
             P.splits = (int32_t)((KT + P.kb_per_split - 1) / P.kb_per_split);  // every split has a K slice
+            // the tile leaves through the TMA where C (and the lo output) can
+            // be described by a tensor map: 16-byte base, pitches multiples
+            // of 4 floats
+            if (P.splits == 1 && epi.mode != EPI_SCATTER && use_tma_store() && ((uintptr_t)C & 15) == 0 &&
+                ldc % 4 == 0 && (batches == 1 || stride_c % 4 == 0) &&
+                make_map(&maps.c, C, n, m, ldc, batches, stride_c, 32, true) &&
+                (!epi.lo_out || (((uintptr_t)epi.lo_out & 15) == 0 &&
+                                 make_map(&maps.clo, epi.lo_out, n, m, ldc, 1, 0, 32, true))))
+                P.tma_store = 1;
             // lo halves from a split pass: scratch with each operand's own
             // geometry, the same tensor maps on another base
             // (or the caller's, when it supplies them)
