@@ -225,6 +225,53 @@ def test_split_k_cluster_counts(zc, monkeypatch, splits, bn, ta, tb):
         assert np.array_equal(got, again)
 
 
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+def test_persistent_form_matches(zc, monkeypatch, ta, tb):
+    """The persistent form (one CTA per SM walking its tiles, the next tile's
+    loads and MMAs overlapping this tile's last fold and its store) gives
+    the bits of the one-tile-per-CTA kernel: ragged rows and columns, a
+    batch, fewer tiles than SMs and many tiles per SM, K up to the form's 64
+    slices; both agree with zpu's chain."""
+    monkeypatch.setenv("ZPUCUDA_GEMM_BN", "256")
+    monkeypatch.setenv("ZPUCUDA_GEMM_PRESPLIT", "0")
+    rng = np.random.default_rng(7 + 2 * ta + tb)
+    for bs, m, k, n in ((1, 200, 300, 520), (40, 130, 96, 300), (300, 128, 64, 256), (3, 256, 2048, 512)):
+        a = rng.uniform(-1, 1, (bs, m, k)).astype(np.float32)
+        b = rng.uniform(-1, 1, (bs, k, n)).astype(np.float32)
+        A = dev(np.swapaxes(a, 1, 2).copy()) if ta else dev(a)
+        B = dev(np.swapaxes(b, 1, 2).copy()) if tb else dev(b)
+        if bs == 1:
+            A, B = A[0], B[0]
+        monkeypatch.setenv("ZPUCUDA_GEMM_PERSISTENT", "1")
+        got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+        check_no_device_error(zc)
+        monkeypatch.setenv("ZPUCUDA_GEMM_PERSISTENT", "0")
+        want = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+        assert np.array_equal(got, want), (bs, m, k, n)
+        got = got.reshape(bs, m, n)
+        for i in sorted({0, bs // 2, bs - 1}):
+            assert rel_fro(got[i], zo.gemm(a[i], b[i])) <= TOL, (bs, m, k, n, i)
+
+
+def test_persistent_form_infinities(zc, monkeypatch):
+    """zpu's infinities and NaNs (the non-finite recompute) in the persistent form."""
+    monkeypatch.setenv("ZPUCUDA_GEMM_BN", "256")
+    monkeypatch.setenv("ZPUCUDA_GEMM_PRESPLIT", "0")
+    monkeypatch.setenv("ZPUCUDA_GEMM_PERSISTENT", "1")
+    rng = np.random.default_rng(17)
+    a = (rng.integers(-8, 9, (300, 160)) / 8.0).astype(np.float32)
+    b = (rng.integers(-8, 9, (160, 600)) / 8.0).astype(np.float32)
+    a[3, 5] = np.inf
+    a[250, 9] = -np.inf
+    a[11, 2] = np.nan
+    b[4, 517] = np.inf
+    want = zo.gemm(a, b)
+    got = zc.gemm(dev(a), dev(b)).cpu().numpy()
+    check_no_device_error(zc)
+    _exact_nonfinite(got, want)
+
+
 def test_split_k_batched(zc):
     rng = np.random.default_rng(11)
     a = rng.uniform(-1, 1, (3, 128, 4096)).astype(np.float32)

@@ -1167,6 +1167,34 @@ def test_split_k_gemm_epilogues(zc):
             assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)
 
 
+def test_persistent_gemm_epilogues(zc, monkeypatch):
+    """The bias + tanh and bias epilogues in the persistent GEMM form (one CTA
+    per SM walking its tiles) give the one-tile-per-CTA kernel's bits."""
+    monkeypatch.setenv("ZPUCUDA_GEMM_BN", "256")
+    monkeypatch.setenv("ZPUCUDA_GEMM_PRESPLIT", "0")
+    rng = np.random.default_rng(95)
+    x = rng.standard_normal((700, 96)).astype(np.float32)
+    w = rng.standard_normal((96, 600)).astype(np.float32) * 0.1
+    b = rng.standard_normal(600).astype(np.float32)
+    F = zc.F32
+    args = [(1, F, (700, 96)), (2, F, (96, 600)), (3, F, (600,))]
+    mm = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0), ("tanh", [11], 12, -2, 0)]
+    ins = [torch.from_numpy(v).cuda() for v in (x, w, b)]
+    for outs in ([12], [11, 12]):
+        res = []
+        for mode in ("1", "0"):
+            monkeypatch.setenv("ZPUCUDA_GEMM_PERSISTENT", mode)
+            p = zc.Plan(args, [], mm, outs)
+            res.append([o.cpu().numpy() for o in p.run(ins)])
+            torch.cuda.synchronize()
+            zc.check(zc.lib().zpucuda_check_device())
+        for g, w_ in zip(*res):
+            assert np.array_equal(g, w_)
+    h = x.astype(np.float64) @ w.astype(np.float64) + b
+    assert np.max(np.abs(res[0][-1] - np.tanh(h))) <= 2e-5
+    assert np.linalg.norm(res[0][0] - h) <= 1e-5 * np.linalg.norm(h)
+
+
 def test_data_movement_snapshots_on_device(zc, golden):
     """The reference's shape/{pad,take,concat,stack} snapshots as plan steps."""
     x = torch.tensor(golden["inputs"]["spread12"], dtype=torch.float64, device="cuda").reshape(3, 4)

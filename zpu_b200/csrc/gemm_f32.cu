@@ -309,15 +309,16 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float *__restrict__
 // SUM_COL with round-to-nearest f32 adds; this warp's 32 lanes, columns
 // half * FOLD_COLS .. + FOLD_COLS - 1 (those inside the MMA width).
 template <int BN_>
-__device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q, int half, int nmma) {
+__device__ __forceinline__ void fold_chunk(uint32_t tmem, uint32_t lanes, int q, int half, int nmma, int buf = -1) {
     using T = Tile<BN_>;
+    if (buf < 0) buf = q % T::NBUF;
     asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll
     for (int c = 0; c < T::FOLD_COLS / 32; c++) {
         const int col = half * T::FOLD_COLS + c * 32;
         if (col >= nmma) continue;
         float v[32];
-        tmem_ld32(tmem + lanes + (uint32_t)((q % T::NBUF) * BN_ + col), v);
+        tmem_ld32(tmem + lanes + (uint32_t)(buf * BN_ + col), v);
         if (q > 0) {
             float sum[32];
             tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)col, sum);
@@ -345,6 +346,7 @@ struct Params {
     int32_t splits;        // K split across a cluster of this many CTAs (blockIdx.z = batch * splits + split)
     int32_t kb_per_split;  // 32-wide K slices per split
     int32_t tma_store;     // the tile leaves through maps.c (and maps.clo when epi.lo_out)
+    int64_t batches;       // matrices of the flattened batch
     Epilogue epi;
     GemmBatch bt;
 };
@@ -866,6 +868,277 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (P.splits > 1) splitk_cluster_reduce<TA, TB, BN_>(smem, C, P, oa, ob, bz, m0, n0);
 }
 
+// ------------------------------------------------ persistent form
+//
+// For many output tiles over a short K (the vmapped 256 x 512^3 batch: 2048
+// tiles of 16 K slices), a CTA's fixed costs -- barrier set-up and TMEM
+// allocation, the first loads, the last fold and the tile store, ~8 of ~34
+// us per tile -- leave the tensor core idle.  Here one CTA per SM walks the
+// tiles blockIdx.x, blockIdx.x + gridDim.x, ...: the producer runs on into
+// the next tile's K slices, the MMAs of the next tile start as soon as the
+// last chunk of this one is folded, and the folding warps store a finished
+// tile (TMA, one 32 x 32 box buffer per warp after the pipeline's buffers)
+// while the next tile accumulates.  Stage, lo-slot and chunk phases run on
+// across tiles (slice counter g, chunk counter).  Same chunks, folds and
+// order per element as tf32x3_gemm_kernel: identical results.  128 x 256
+// tiles, lo halves made in shared memory, epilogues without HBM inputs
+// (store, bias, bias + tanh), no split-K.
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(THREADS, 1)
+    tf32x3_gemm_persistent_kernel(const __grid_constant__ Maps maps, float *__restrict__ C,
+                                  const __grid_constant__ Params P) {
+    using T = Tile<256, false>;
+    constexpr int BN = 256, RAW = T::RAW, NLO = T::LO, NBUF = T::NBUF, KC_BLOCKS = T::KC_BLOCKS;
+    constexpr uint32_t RAW_BYTES = T::RAW_BYTES, STAGE_BYTES = T::STAGE_BYTES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv[NLO], lofree[NLO], tfull[NBUF], tfree[NBUF];
+    __shared__ uint32_t tmem_base;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t ncols = (P.N + BN - 1) / BN, nrows = (P.M + BM - 1) / BM;
+    const int64_t total = ncols * nrows * P.batches;
+    const int ntiles = (int)((total - (int64_t)blockIdx.x + gridDim.x - 1) / gridDim.x);
+    const int KT = (int)((P.K + BK - 1) / BK);
+    const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
+    struct Co {
+        int m0, n0, za, zb;
+        int64_t bz, oa, ob;
+    };
+    auto coords = [&](int it) {  // this CTA's tile `it`: columns fastest, then rows, then matrices
+        Co c;
+        const int64_t t = (int64_t)blockIdx.x + (int64_t)it * gridDim.x, r = t / ncols;
+        c.n0 = (int)((t % ncols) * BN);
+        c.m0 = (int)((r % nrows) * BM);
+        c.bz = r / nrows;
+        batch_offsets(P.bt, c.bz, &c.oa, &c.ob);
+        c.za = (int)(P.mat_a ? c.oa / P.mat_a : 0);
+        c.zb = (int)(P.mat_b ? c.ob / P.mat_b : 0);
+        return c;
+    };
+    auto raw_a = [&](int s) { return smem + (size_t)s * STAGE_BYTES; };
+    auto raw_b = [&](int s) { return smem + (size_t)s * STAGE_BYTES + A_BYTES; };
+    auto lo_a = [&](int l) { return smem + (size_t)RAW * STAGE_BYTES + (size_t)l * RAW_BYTES; };
+    auto lo_b = [&](int l) { return lo_a(l) + A_BYTES; };
+    // K slice j of tile c into stage g % RAW (g: the slice's place in this CTA's sequence)
+    auto issue = [&](int g, int j, const Co &c) {
+        const int s = g % RAW;
+        mb_expect_tx(&full[s], STAGE_BYTES);
+        const int k0 = j * BK;
+        if (!TA) tma_load_3d(raw_a(s), &maps.a, k0, c.m0, c.za, &full[s]);
+        else
+            for (int q = 0; q < BM / 32; q++) tma_load_3d(raw_a(s) + q * 4096, &maps.a, c.m0 + 32 * q, k0, c.za, &full[s]);
+        if (TB) tma_load_3d(raw_b(s), &maps.b, k0, c.n0, c.zb, &full[s]);
+        else
+            for (int q = 0; q < BN / 32; q++) tma_load_3d(raw_b(s) + q * 4096, &maps.b, c.n0 + 32 * q, k0, c.zb, &full[s]);
+    };
+    const int first_loads = KT < RAW ? KT : RAW;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < RAW; s++) {
+            mb_init(&full[s], 1);
+            mb_init(&empty[s], 1);
+        }
+        for (int l = 0; l < NLO; l++) {
+            mb_init(&conv[l], NWORK);
+            mb_init(&lofree[l], 1);
+        }
+        for (int b = 0; b < NBUF; b++) {
+            mb_init(&tfull[b], 1);
+            mb_init(&tfree[b], NFOLD);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const Co c0 = coords(0);
+        for (int j = 0; j < first_loads; j++) issue(j, j, c0);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int it = 0, g = 0; it < ntiles && ok; it++) {
+                const Co c = coords(it);
+                for (int j = 0; j < KT; j++, g++) {
+                    if (g < first_loads) continue;  // issued before the TMEM allocation
+                    if (!mb_wait(&empty[g % RAW], ((g / RAW) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    issue(g, j, c);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t ID = P.idesc;
+            bool ok = true;
+            for (int it = 0, g = 0, qg = 0; it < ntiles && ok; it++) {
+                for (int j = 0; j < KT; j++, g++) {
+                    const int s = g % RAW, l = g % NLO, buf = qg % NBUF;
+                    const bool first = (j % KC_BLOCKS) == 0;
+                    const bool last = (j % KC_BLOCKS) == KC_BLOCKS - 1 || j == KT - 1;
+                    if ((first && qg >= NBUF && !mb_wait(&tfree[buf], ((qg / NBUF) - 1) & 1)) ||
+                        !mb_wait(&conv[l], (g / NLO) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint32_t d = tmem + (uint32_t)(buf * BN);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; kk++) {
+                        const uint64_t ah = op_desc<!TA>(raw_a(s), kk), al = op_desc<!TA>(lo_a(l), kk);
+                        const uint64_t bh = op_desc<TB>(raw_b(s), kk), bl = op_desc<TB>(lo_b(l), kk);
+                        mma_tf32(d, ah, bh, ID, (first && kk == 0) ? 0u : 1u);
+                        mma_tf32(d, ah, bl, ID, 1u);
+                        mma_tf32(d, al, bh, ID, 1u);
+                    }
+                    mma_commit(&empty[s]);
+                    mma_commit(&lofree[l]);
+                    if (last) {
+                        mma_commit(&tfull[buf]);
+                        qg++;
+                    }
+                }
+            }
+        }
+    } else {
+        const int wt = threadIdx.x - 64;
+        const bool folder = warp >= 8;
+        const int q4 = warp & 3, half = (warp - 8) >> 2;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        const int total_q = ntiles * NQ;
+        int folded = 0;
+        bool ok = true;
+        // this warp's 32 x 32 box buffer, after the stages and lo slots
+        float *tb = (float *)(smem + (size_t)RAW * STAGE_BYTES + (size_t)NLO * RAW_BYTES +
+                              (size_t)(warp >= 8 ? warp - 8 : 0) * 4096);
+        // the finished tile `it`: running sum -> epilogue -> TMA store, one
+        // 32-column piece of this warp's rows at a time
+        auto store_tile = [&](int it) {
+            const Co c = coords(it);
+            const int64_t row = (int64_t)c.m0 + q4 * 32 + lane;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll 1
+            for (int pc = 0; pc < T::FOLD_COLS / 32; pc++) {
+                const int cl = half * T::FOLD_COLS + pc * 32;
+                if (cl >= P.nmma) break;
+                if (lane == 0) bulk_wait_read<0>();  // the box buffer has left shared memory
+                __syncwarp();
+                float acc[32];
+                tmem_ld32(tmem + lanes + SUM_COL + (uint32_t)cl, acc);
+                const int64_t col0 = (int64_t)c.n0 + cl;
+                if (row < P.M) {
+                    bool bad = false;
+#pragma unroll
+                    for (int v = 0; v < 32; v++) bad |= !isfinite(acc[v]);
+                    if (bad) {  // zpu's chain for the non-finite elements, through this lane's row of the buffer
+                        float *mine = tb + lane * 32;
+#pragma unroll
+                        for (int v = 0; v < 32; v++) mine[v] = acc[v];
+#pragma unroll 1
+                        for (int v = 0; v < 32; v++)
+                            if (!isfinite(mine[v]) && col0 + v < P.N)
+                                mine[v] = zpu_chain_element<TA, TB>(P.A + c.oa, P.B + c.ob, P.lda, P.ldb, row,
+                                                                    col0 + v, P.N, 0, P.K);
+#pragma unroll
+                        for (int v = 0; v < 32; v++) acc[v] = mine[v];
+                    }
+                    if (col0 + 32 <= P.N) {
+                        epi_apply32(P.epi, acc, row, col0);
+                    } else {
+#pragma unroll
+                        for (int v = 0; v < 32; v++)
+                            if (col0 + v < P.N) acc[v] = epi_apply(P.epi, acc[v], row, col0 + v);
+                    }
+                }
+                __syncwarp();
+#pragma unroll
+                for (int v = 0; v < 8; v++)
+                    *(float4 *)(tb + lane * 32 + ((v ^ (lane & 7)) * 4)) =
+                        make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&maps.c, tb, (int)col0, c.m0 + q4 * 32, (int)c.bz);
+                    bulk_commit();
+                }
+            }
+        };
+        // fold chunk `folded` (its tile's first chunk starts the running
+        // sum); a tile's last chunk is followed by the tile's store
+        auto fold_next = [&]() {
+            fold_chunk<BN>(tmem, lanes, folded % NQ, half, P.nmma, folded % NBUF);
+            mb_arrive(&tfree[folded % NBUF]);
+            folded++;
+            if (folded % NQ == 0) store_tile(folded / NQ - 1);
+        };
+        auto try_folds = [&]() {
+            while (folded < total_q && __all_sync(0xffffffffu, mb_test(&tfull[folded % NBUF], (folded / NBUF) & 1)))
+                fold_next();
+        };
+        auto wait = [&](uint64_t *bar, uint32_t parity) {
+            if (!folder) return mb_wait(bar, parity);
+            for (uint32_t i = 0; i < kGemmSpin; i++) {
+                if (__all_sync(0xffffffffu, mb_try(bar, parity))) return true;
+                try_folds();
+            }
+            atomicOr(&g_gemm_error, 1u);
+            return false;
+        };
+        for (int it = 0, g = 0; it < ntiles && ok; it++) {
+            for (int j = 0; j < KT; j++, g++) {
+                const int s = g % RAW, l = g % NLO;
+                if (!wait(&full[s], (g / RAW) & 1) || (g >= NLO && !wait(&lofree[l], ((g / NLO) - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                const uint4 *src = (const uint4 *)raw_a(s);  // A then B, contiguous
+                uint4 *dst = (uint4 *)lo_a(l);
+                uint4 x[T::CONV_ITERS];
+#pragma unroll
+                for (int u = 0; u < T::CONV_ITERS; u++) {
+                    const int i = wt + u * NWORK * 32;
+                    if (i < (int)(RAW_BYTES / 16)) x[u] = src[i];
+                }
+#pragma unroll
+                for (int u = 0; u < T::CONV_ITERS; u++) {
+                    const int i = wt + u * NWORK * 32;
+                    if (i < (int)(RAW_BYTES / 16)) dst[i] = lo4(x[u]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mb_arrive(&conv[l]);
+                if (folder) try_folds();
+            }
+        }
+        if (folder) {
+            while (ok && folded < total_q) {
+                if (!mb_wait(&tfull[folded % NBUF], (folded / NBUF) & 1)) {
+                    ok = false;
+                    break;
+                }
+                __syncwarp();
+                fold_next();
+            }
+            if (lane == 0) bulk_wait_read<0>();
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
 // ------------------------------------------------ plain FMA-chain fallback
 //
 // For shapes the tensor maps cannot take: each output element is the FMA
@@ -1060,6 +1333,40 @@ int choose_bn(int64_t m, int64_t n, int64_t batches) {
     return 1.6 * (double)w256 < (double)w128 ? 256 : 128;
 }
 
+// The persistent form: one CTA per SM (at most one per tile), each walking
+// its tiles; 32 KiB more shared memory for the store boxes.
+constexpr size_t kPersSmem = Tile<256, false>::SMEM_BYTES + 8 * 4096;
+static_assert(kPersSmem <= 227 * 1024, "persistent form's shared memory");
+
+template <bool TA, bool TB>
+int launch_persistent(const Maps &maps, float *C, const Params &P, int64_t tiles, cudaStream_t s) {
+    auto k = tf32x3_gemm_persistent_kernel<TA, TB>;
+    static bool attr[64] = {false};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64 || !attr[dev]) {
+        ZC_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPersSmem));
+        if (dev >= 0 && dev < 64) attr[dev] = true;
+    }
+    const int64_t ctas = tiles < num_sms() ? tiles : num_sms();
+    k<<<(unsigned)ctas, THREADS, kPersSmem, s>>>(maps, C, P);
+    ZC_LAUNCHED("tf32x3_gemm_persistent_kernel");
+    return ZPUCUDA_OK;
+}
+
+// Whether a 128 x 256 product without presplit lo runs in the persistent
+// form: at least two tiles per SM over a short K (where a tile's fixed
+// costs weigh), a TMA tile store, an epilogue without HBM inputs.
+// ZPUCUDA_GEMM_PERSISTENT=0 or 1 forces the choice among the products the
+// form can take (read at every call).
+bool use_persistent(const Params &P, int64_t tiles, int64_t KT) {
+    if (!P.tma_store || P.splits != 1 || P.epi.lo_out ||
+        !(P.epi.mode == EPI_STORE || P.epi.mode == EPI_BIAS || P.epi.mode == EPI_BIAS_TANH))
+        return false;
+    const char *e = getenv("ZPUCUDA_GEMM_PERSISTENT");
+    if (e && (e[0] == '0' || e[0] == '1') && e[1] == 0) return e[0] == '1';
+    return tiles >= 2 * (int64_t)num_sms() && KT <= 64;
+}
+
 template <int BN_, bool PRE>
 int dispatch_tf32x3(bool ta, bool tb, const Maps &maps, float *C, const Params &P, int64_t batches, cudaStream_t s) {
     if (!ta && !tb) return launch_tf32x3<false, false, BN_, PRE>(maps, C, P, batches, s);
@@ -1232,10 +1539,20 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
                 pre = a_lo && b_lo && make_map(&maps.alo, a_lo, a_inner, a_rows, lda, na, mat_a, ta ? 32 : BM, !ta) &&
                       make_map(&maps.blo, b_lo, b_inner, b_rows, ldb, nb, mat_b, tb ? bn : 32, tb);
             }
-            int st = pre ? (bn == 256 ? dispatch_tf32x3<256, true>(ta, tb, maps, C, P, batches, s)
-                                      : dispatch_tf32x3<128, true>(ta, tb, maps, C, P, batches, s))
-                         : (bn == 256 ? dispatch_tf32x3<256, false>(ta, tb, maps, C, P, batches, s)
-                                      : dispatch_tf32x3<128, false>(ta, tb, maps, C, P, batches, s));
+            P.batches = batches;
+            int st;
+            if (!pre && bn == 256 && use_persistent(P, tiles, KT)) {
+                if (!ta && !tb) st = launch_persistent<false, false>(maps, C, P, tiles, s);
+                else if (!ta && tb) st = launch_persistent<false, true>(maps, C, P, tiles, s);
+                else if (ta && !tb) st = launch_persistent<true, false>(maps, C, P, tiles, s);
+                else st = launch_persistent<true, true>(maps, C, P, tiles, s);
+            } else if (pre) {
+                st = bn == 256 ? dispatch_tf32x3<256, true>(ta, tb, maps, C, P, batches, s)
+                               : dispatch_tf32x3<128, true>(ta, tb, maps, C, P, batches, s);
+            } else {
+                st = bn == 256 ? dispatch_tf32x3<256, false>(ta, tb, maps, C, P, batches, s)
+                               : dispatch_tf32x3<128, false>(ta, tb, maps, C, P, batches, s);
+            }
             if (alo) cudaFreeAsync(alo, s);
             if (blo) cudaFreeAsync(blo, s);
             return st;
