@@ -410,6 +410,14 @@ int zpucuda_mlp_adam_step(zpucuda_mlp *h, void *stream);
 int zpucuda_mlp_train_step(zpucuda_mlp *h, const float *d_x, const int64_t *d_labels, int64_t batch,
                            int64_t global_batch, void *stream);
 int zpucuda_mlp_loss(const zpucuda_mlp *h, float *dst, void *stream);
+/* A data-parallel train step returns (its stream's work ends) once W1 and b1
+ * are whole; the all-gather of the larger bucket [W2 .. b3] runs on into the
+ * next step, which waits for it only before it reads W2.  Every call that
+ * touches the arrays (read, write, array, the next step) waits for it
+ * itself; zpucuda_mlp_join makes `stream` wait for it, for callers that time
+ * a sequence of steps or read the parameters by pointer.  No counterpart in
+ * the reference (one CPU, no exchange). */
+int zpucuda_mlp_join(zpucuda_mlp *h, void *stream);
 int zpucuda_mlp_check(zpucuda_mlp *h);
 int64_t zpucuda_mlp_steps(const zpucuda_mlp *h);
 /* 1 when train_step exchanges dW2 over peer memory (its GEMM stores each
@@ -422,11 +430,12 @@ int zpucuda_mlp_exchange_mode(const zpucuda_mlp *h);
 /* Phase trace of the step (diagnostics): with tracing on, each
  * value_and_grad / train_step records timing events at its phase boundaries;
  * zpucuda_mlp_trace_read waits (bounded) for the last traced step and writes
- * up to 12 times in ms from its start: [0] start, [1] forward GEMMs, [2]
+ * up to 13 times in ms from its start: [0] start, [1] forward GEMMs, [2]
  * loss, [3] layer-3 backward + db2, [4] dW2 GEMM, [5] g1 GEMM, [6] db1 + dW1
- * GEMM, [7] end (main stream); [8] bucket [W2 ..] summed, [9] its Adam and
- * all-gather, [10] bucket [W1, b1] summed, [11] its Adam and all-gather
- * (side stream; -1 where a point was not reached, e.g. on one rank). */
+ * GEMM, [7] end (main stream); [8] bucket [W2 ..] summed, [9] its Adam,
+ * [10] bucket [W1, b1] summed, [11] its Adam and all-gather, [12] the
+ * all-gather of bucket [W2 ..] (side stream; -1 where a point was not
+ * reached, e.g. on one rank). */
 int zpucuda_mlp_trace(zpucuda_mlp *h, int on);
 int zpucuda_mlp_trace_read(zpucuda_mlp *h, float *ms, int n);
 /* Diagnostics, no counterpart in the reference: runs the owner-side step of

@@ -256,7 +256,7 @@ def test_phase_trace_orders_the_step(zc):
     t = b.trace_read()
     assert t[0] == 0.0
     assert all(t[i] > 0 for i in range(1, 8)) and all(t[i] <= t[i + 1] for i in range(0, 7)), t
-    assert t[8] == -1.0
+    assert t[8] == -1.0 and t[12] == -1.0  # no exchange, no deferred all-gather
     assert 0 < t[9] <= t[11] <= t[7] and t[10] <= t[11], t
     for x, y in zip(a.params(), b.params()):
         assert np.array_equal(x, y)

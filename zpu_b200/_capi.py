@@ -150,6 +150,7 @@ SIGNATURES = {
     "zpucuda_mlp_adam_step": (I32, [P, P]),
     "zpucuda_mlp_train_step": (I32, [P, P, P, I64, I64, P]),
     "zpucuda_mlp_loss": (I32, [P, P, P]),
+    "zpucuda_mlp_join": (I32, [P, P]),
     "zpucuda_mlp_check": (I32, [P]),
     "zpucuda_mlp_steps": (I64, [P]),
     "zpucuda_mlp_exchange_mode": (I32, [P]),

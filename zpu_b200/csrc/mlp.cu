@@ -341,8 +341,9 @@ using namespace zc;
 // Phase boundaries the trace records, in this order: main stream -- start,
 // forward GEMMs, loss, layer-3 backward + db2, dW2 GEMM, g1 GEMM, db1 + dW1
 // GEMM, end (side stream joined); side stream -- bucket [W2 ..] summed,
-// its Adam + all-gather, bucket [W1, b1] summed, its Adam + all-gather.
-constexpr int kTracePoints = 12;
+// its Adam, bucket [W1, b1] summed, its Adam + all-gather, the all-gather of
+// bucket [W2 ..] (which the next step joins before it reads W2).
+constexpr int kTracePoints = 13;
 
 struct zpucuda_mlp {
     int device = -1;
@@ -365,7 +366,11 @@ struct zpucuda_mlp {
     int64_t t = 0;  // Adam steps taken
     double lr = 1e-3, beta1 = 0.9, beta2 = 0.999, eps = 1e-8;
     cudaStream_t comm_stream = nullptr;
-    cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_w2 = nullptr, ev_done = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr, ev_w2 = nullptr, ev_done = nullptr, ev_w1 = nullptr;
+    // a data-parallel step leaves the all-gather of bucket [W2 ..] running on
+    // the side stream (ev_done); the next call that touches the arrays waits
+    // for it on its own stream (join_exchange)
+    bool w2_pending = false;
     // dW2 exchange over peer memory (data parallel): one allocation per rank,
     // [flags | inbox], opened on every peer through CUDA IPC
     int peer_state = 0;  // 0 not set up, 1 in use, -1 not available
@@ -405,6 +410,7 @@ void free_mlp(zpucuda_mlp *h) {
     if (h->ev_b) cudaEventDestroy(h->ev_b);
     if (h->ev_w2) cudaEventDestroy(h->ev_w2);
     if (h->ev_done) cudaEventDestroy(h->ev_done);
+    if (h->ev_w1) cudaEventDestroy(h->ev_w1);
     for (cudaEvent_t e : h->tev)
         if (e) cudaEventDestroy(e);
     if (h->comm_stream) cudaStreamDestroy(h->comm_stream);
@@ -576,6 +582,13 @@ inline int tmark(zpucuda_mlp *h, int i, cudaStream_t st) {
     return ZPUCUDA_OK;
 }
 
+// Makes stream st wait for the all-gather of bucket [W2 ..] that the last
+// data-parallel step left running on the side stream.
+int join_exchange(const zpucuda_mlp *h, cudaStream_t st) {
+    if (h->w2_pending) ZC_CUDA(cudaStreamWaitEvent(st, h->ev_done, 0));
+    return ZPUCUDA_OK;
+}
+
 int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_t B, int64_t global_b, bool ar,
                    bool adam, cudaStream_t s) {
     const int64_t d0 = h->d[0], d1 = h->d[1], d2 = h->d[2], d3 = h->d[3], d3p = h->d3p;
@@ -606,16 +619,20 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         ZC_TRY(split_lo_device(W1, h->w1_lo, d0 * d1, s));
         w1_lo = h->w1_lo;
     }
-    if (p_f2 || p_g1) {
-        ZC_TRY(split_lo_device(W2, h->w2_lo, d1 * d2, s));
-        w2_lo = h->w2_lo;
-    }
     const bool a1_lo = p_f2 || p_w2, ga2_lo = p_w2 || p_g1, ga1_lo = p_w1;
 
     // forward: dense -> tanh -> dense -> tanh -> dense
     ZC_TRY(tmark(h, 0, s));
     ZC_TRY(gemm(x, W1, h->a1, B, d1, d0, d0, d1, d1, false, false, with_lo(epi(EPI_BIAS_TANH, b1), a1_lo, h->a1_lo),
                 s, x_lo, w1_lo));
+    // W2 .. b3 from here on: the last step's all-gather of them ran beside
+    // the split passes and the first product
+    ZC_TRY(join_exchange(h, s));
+    h->w2_pending = false;
+    if (p_f2 || p_g1) {
+        ZC_TRY(split_lo_device(W2, h->w2_lo, d1 * d2, s));
+        w2_lo = h->w2_lo;
+    }
     ZC_TRY(gemm(h->a1, W2, h->a2, B, d2, d1, d1, d2, d2, false, false, epi(EPI_BIAS_TANH, b2), s,
                 a1_lo ? h->a1_lo : nullptr, w2_lo));
     ZC_TRY(gemm(h->a2, W3, h->logits, B, d3p, d2, d2, d3p, d3p, false, false, epi(EPI_BIAS, b3), s));
@@ -704,13 +721,11 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
         ac = adam_consts(h);
         ZC_CUDA(cudaEventRecord(h->ev_w2, s));
         ZC_CUDA(cudaStreamWaitEvent(side, h->ev_w2, 0));
-        if (fused) {  // Adam on this rank's dW2 rows, gather W2; b2, W3, b3 everywhere
+        if (fused) {  // Adam on this rank's dW2 rows; b2, W3, b3 everywhere (W2 gathered last)
             ZC_TRY(adam_range(h, ac, h->off[2] + rank * w2_shard, w2_shard, side));
-            ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], w2_shard, side));
             ZC_TRY(adam_range(h, ac, h->off[3], nA3, side));
-        } else if (shard) {
+        } else if (shard) {  // Adam on this rank's shard of the bucket (gathered last)
             ZC_TRY(adam_range(h, ac, h->off[2] + rank * (nA / world), nA / world, side));
-            ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], nA / world, side));
         } else {
             ZC_TRY(adam_range(h, ac, h->off[2], nA, side));
         }
@@ -735,8 +750,21 @@ int value_and_grad(zpucuda_mlp *h, const float *x, const int64_t *labels, int64_
             if (adam) ZC_TRY(adam_range(h, ac, 0, nB, side));
         }
         ZC_TRY(tmark(h, 11, side));
-        ZC_CUDA(cudaEventRecord(h->ev_done, side));
-        ZC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
+        if (adam && (fused || shard)) {
+            // the step ends once W1 is whole; the gather of bucket [W2 ..]
+            // (the larger one) follows on the side stream and overlaps the
+            // next step's split passes and first product (join_exchange)
+            ZC_CUDA(cudaEventRecord(h->ev_w1, side));
+            ZC_CUDA(cudaStreamWaitEvent(s, h->ev_w1, 0));
+            if (fused) ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], w2_shard, side));
+            else ZC_TRY(nccl_all_gather_f32(h->params + h->off[2], nA / world, side));
+            ZC_TRY(tmark(h, 12, side));
+            ZC_CUDA(cudaEventRecord(h->ev_done, side));
+            h->w2_pending = true;
+        } else {
+            ZC_CUDA(cudaEventRecord(h->ev_done, side));
+            ZC_CUDA(cudaStreamWaitEvent(s, h->ev_done, 0));
+        }
     }
     ZC_TRY(tmark(h, 7, s));
     return ZPUCUDA_OK;
@@ -871,7 +899,8 @@ extern "C" int zpucuda_mlp_create(int64_t d_in, int64_t d_h1, int64_t d_h2, int6
                                  cudaEventCreateWithFlags(&h->ev_a, cudaEventDisableTiming),
                                  cudaEventCreateWithFlags(&h->ev_b, cudaEventDisableTiming),
                                  cudaEventCreateWithFlags(&h->ev_w2, cudaEventDisableTiming),
-                                 cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming)};
+                                 cudaEventCreateWithFlags(&h->ev_done, cudaEventDisableTiming),
+                                 cudaEventCreateWithFlags(&h->ev_w1, cudaEventDisableTiming)};
         for (cudaError_t x : e)
             if (x != cudaSuccess && !st) st = cuda_fail(x, "mlp_create setup");
     }
@@ -915,6 +944,7 @@ extern "C" int zpucuda_mlp_write(zpucuda_mlp *h, int what, int i, const float *s
         return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_write: bad handle, array or index");
     if (numel != h->rows[i] * h->cols[i]) return set_error(ZPUCUDA_ERR_SHAPE_MISMATCH, "mlp_write: element count");
     float *dst = array_of(h, what) + h->off[i];
+    ZC_TRY(join_exchange(h, resolve_stream(stream)));
     ZC_CUDA(cudaMemcpy2DAsync(dst, (size_t)h->ld[i] * 4, src, (size_t)h->cols[i] * 4, (size_t)h->cols[i] * 4,
                               (size_t)h->rows[i], cudaMemcpyDefault, resolve_stream(stream)));
     return ZPUCUDA_OK;
@@ -925,6 +955,7 @@ extern "C" int zpucuda_mlp_read(const zpucuda_mlp *h, int what, int i, float *ds
         return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_read: bad handle, array or index");
     if (numel != h->rows[i] * h->cols[i]) return set_error(ZPUCUDA_ERR_SHAPE_MISMATCH, "mlp_read: element count");
     const float *src = array_of(h, what) + h->off[i];
+    ZC_TRY(join_exchange(h, resolve_stream(stream)));
     ZC_CUDA(cudaMemcpy2DAsync(dst, (size_t)h->cols[i] * 4, src, (size_t)h->ld[i] * 4, (size_t)h->cols[i] * 4,
                               (size_t)h->rows[i], cudaMemcpyDefault, resolve_stream(stream)));
     return ZPUCUDA_OK;
@@ -932,6 +963,7 @@ extern "C" int zpucuda_mlp_read(const zpucuda_mlp *h, int what, int i, float *ds
 
 extern "C" int zpucuda_mlp_array(const zpucuda_mlp *h, int what, float **d_ptr, int64_t *n) {
     if (!h || !d_ptr || !n || !array_of(h, what)) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_array");
+    if (h->w2_pending) ZC_CUDA(cudaEventSynchronize(h->ev_done));  // the arrays are whole when this returns
     *d_ptr = array_of(h, what);
     *n = h->total;
     return ZPUCUDA_OK;
@@ -959,12 +991,14 @@ extern "C" int zpucuda_mlp_allreduce_grads(zpucuda_mlp *h, void *stream) {
     if (!h) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_allreduce_grads: NULL handle");
     if (nccl_world(nullptr) == 1) return ZPUCUDA_OK;
     std::lock_guard<std::mutex> lk(h->mu);
+    ZC_TRY(join_exchange(h, resolve_stream(stream)));
     return nccl_allreduce_sum_f32(h->grads, h->total + 1, resolve_stream(stream));
 }
 
 extern "C" int zpucuda_mlp_adam_step(zpucuda_mlp *h, void *stream) {
     if (!h) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_adam_step: NULL handle");
     std::lock_guard<std::mutex> lk(h->mu);
+    ZC_TRY(join_exchange(h, resolve_stream(stream)));
     return adam_step(h, resolve_stream(stream));
 }
 
@@ -974,6 +1008,12 @@ extern "C" int zpucuda_mlp_train_step(zpucuda_mlp *h, const float *d_x, const in
     std::lock_guard<std::mutex> lk(h->mu);
     cudaStream_t s = resolve_stream(stream);
     return value_and_grad(h, d_x, d_labels, batch, global_batch, nccl_world(nullptr) > 1, true, s);
+}
+
+extern "C" int zpucuda_mlp_join(zpucuda_mlp *h, void *stream) {
+    if (!h) return set_error(ZPUCUDA_ERR_INVALID_ARGUMENT, "mlp_join: NULL handle");
+    std::lock_guard<std::mutex> lk(h->mu);
+    return join_exchange(h, resolve_stream(stream));
 }
 
 extern "C" int zpucuda_mlp_loss(const zpucuda_mlp *h, float *dst, void *stream) {
@@ -1038,9 +1078,11 @@ extern "C" int zpucuda_mlp_trace_read(zpucuda_mlp *h, float *ms, int n) {
     ZC_CHECK(h && ms && n >= 0, ZPUCUDA_ERR_INVALID_ARGUMENT);
     std::lock_guard<std::mutex> g(h->mu);
     ZC_CHECK(h->tev[0], ZPUCUDA_ERR_NOT_SUPPORTED);
-    // bounded wait for the traced step's last point
+    // bounded wait for the traced step's last points (the main stream's end
+    // and the all-gather it left on the side stream)
     for (int64_t spins = 0;; spins++) {
-        const cudaError_t e = cudaEventQuery(h->tev[7]);
+        cudaError_t e = cudaEventQuery(h->tev[7]);
+        if (e == cudaSuccess && h->w2_pending) e = cudaEventQuery(h->ev_done);
         if (e == cudaSuccess) break;
         if (e != cudaErrorNotReady) return cuda_fail(e, "cudaEventQuery");
         if (spins > 60LL * 1000 * 100) return set_error(ZPUCUDA_ERR_TIMEOUT, "zpucuda_mlp_trace_read: step did not end");

@@ -153,6 +153,11 @@ class MLP:
         xp, lp, B, G = self._args(x, labels, global_batch)
         check(lib().zpucuda_mlp_train_step(self._h, xp, lp, B, G, _stream(stream)))
 
+    def join(self, stream=None):
+        """Makes `stream` wait for the exchange a data-parallel step leaves
+        running (the all-gather of W2 .. b3): call it before timing ends."""
+        check(lib().zpucuda_mlp_join(self._h, _stream(stream)))
+
     def loss_to(self, dst_ptr, stream=None):
         check(lib().zpucuda_mlp_loss(self._h, dst_ptr, _stream(stream)))
 
@@ -175,8 +180,8 @@ class MLP:
     def trace_read(self):
         """Times (ms from the step's start) of the last traced step's phase
         boundaries, in zpucuda_mlp_trace_read's order (-1: not reached)."""
-        buf = (C.c_float * 12)()
-        check(lib().zpucuda_mlp_trace_read(self._h, buf, 12))
+        buf = (C.c_float * 13)()
+        check(lib().zpucuda_mlp_trace_read(self._h, buf, 13))
         return [float(v) for v in buf]
 
     def exchange_mode(self):
