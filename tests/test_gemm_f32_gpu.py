@@ -254,6 +254,24 @@ def test_persistent_form_matches(zc, monkeypatch, ta, tb):
             assert rel_fro(got[i], zo.gemm(a[i], b[i])) <= TOL, (bs, m, k, n, i)
 
 
+@pytest.mark.parametrize("group", ["1", "3", "16"])
+def test_raster_groups_cover_every_tile(zc, monkeypatch, group):
+    """Grouped tile order (CTAs sweep `group` row tiles column by column):
+    every tile computed once, ragged last group, the same bits as blockIdx
+    order."""
+    rng = np.random.default_rng(int(group))
+    a = rng.uniform(-1, 1, (1000, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (96, 1100)).astype(np.float32)
+    A, B = dev(a), dev(b)
+    monkeypatch.setenv("ZPUCUDA_GEMM_RASTER", "0")
+    want = zc.gemm(A, B).cpu().numpy()
+    monkeypatch.setenv("ZPUCUDA_GEMM_RASTER", group)
+    got = zc.gemm(A, B).cpu().numpy()
+    check_no_device_error(zc)
+    assert np.array_equal(got, want)
+    assert rel_fro(got, zo.gemm(a, b)) <= TOL
+
+
 def test_persistent_form_infinities(zc, monkeypatch):
     """zpu's infinities and NaNs (the non-finite recompute) in the persistent form."""
     monkeypatch.setenv("ZPUCUDA_GEMM_BN", "256")

@@ -342,6 +342,7 @@ struct Params {
     int64_t M, N, K, ldc, stride_c;
     int64_t mat_a, mat_b;  // elements between the matrices the tensor maps index
     int32_t nmma;          // MMA width: N rounded up to 16, at most BN
+    int32_t group;         // row tiles per raster group (0: blockIdx order)
     uint32_t idesc;
     int32_t splits;        // K split across a cluster of this many CTAs (blockIdx.z = batch * splits + split)
     int32_t kb_per_split;  // 32-wide K slices per split
@@ -519,7 +520,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t bz = blockIdx.z / (unsigned)P.splits;
     batch_offsets(P.bt, bz, &oa, &ob);
     const int za = (int)(P.mat_a ? oa / P.mat_a : 0), zb = (int)(P.mat_b ? ob / P.mat_b : 0);
-    const int m0 = (int)blockIdx.y * BM, n0 = (int)blockIdx.x * BN;
+    // tile origin: with P.group > 0 the CTAs (launched x fastest) sweep
+    // groups of P.group row tiles column by column, so the A and B panels a
+    // wave of CTAs reads at once overlap in L2
+    int mt = (int)blockIdx.y, nt = (int)blockIdx.x;
+    if (P.group > 0) {
+        const int gx = (int)gridDim.x, lin = (int)blockIdx.y * gx + (int)blockIdx.x;
+        const int first = lin / (P.group * gx) * P.group;
+        const int rows = min((int)gridDim.y - first, P.group), r = lin % (P.group * gx);
+        mt = first + r % rows;
+        nt = r / rows;
+    }
+    const int m0 = mt * BM, n0 = nt * BN;
     const int kb0 = split * P.kb_per_split;  // this CTA's first K slice
     const int KT = min((int)((P.K + BK - 1) / BK) - kb0, P.kb_per_split);
     const int NQ = (KT + KC_BLOCKS - 1) / KC_BLOCKS;
@@ -1407,6 +1419,18 @@ float *split_operand(cudaMemPool_t pool, const float *x, int64_t inner, int64_t 
 // (4096^3 and the MLP's products yes; 1024^3 and 256 x 512^3 no: measured
 // 51 -> 44 and 135 -> 117 TFLOP/s with the pass).  ZPUCUDA_GEMM_PRESPLIT=0
 // or 1 forces the choice (read at every call).
+// Row tiles per raster group for an rows x cols tile grid: groups of 16
+// where the grid has more than 32 rows and columns of tiles (at 8192^3 a
+// wave of 148 CTAs in row-major order reads every B column panel, 512 MB
+// with the lo halves, so B comes from HBM again in every wave), else
+// blockIdx order.  ZPUCUDA_GEMM_RASTER=<g> forces g (0: off; read at every
+// call).
+int raster_group(int64_t rows, int64_t cols) {
+    const char *e = getenv("ZPUCUDA_GEMM_RASTER");
+    if (e && e[0] >= '0' && e[0] <= '9') return atoi(e);
+    return rows > 32 && cols > 32 ? 16 : 0;
+}
+
 // Whether result tiles leave through TMA stores (default) rather than the
 // folding warps' own stores; ZPUCUDA_GEMM_TMA_STORE=0 turns them off (read
 // at every call).
@@ -1540,6 +1564,7 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
                       make_map(&maps.blo, b_lo, b_inner, b_rows, ldb, nb, mat_b, tb ? bn : 32, tb);
             }
             P.batches = batches;
+            P.group = raster_group((m + BM - 1) / BM, (n + bn - 1) / bn);
             int st;
             if (!pre && bn == 256 && use_persistent(P, tiles, KT)) {
                 if (!ta && !tb) st = launch_persistent<false, false>(maps, C, P, tiles, s);
