@@ -53,7 +53,10 @@ def check_no_device_error(zc):
 @pytest.mark.parametrize("tb", [False, True])
 @pytest.mark.parametrize("m,k,n", [(128, 32, 128), (256, 64, 256), (129, 100, 136), (300, 516, 260),
                                    (1, 8, 4), (513, 33, 1000)])
-def test_layouts_and_edges(zc, ta, tb, m, k, n):
+def test_layouts_and_edges(zc, monkeypatch, ta, tb, m, k, n):
+    # the tensor-core path also for the short contractions (k <= 32), which
+    # otherwise run zpu's chain on CUDA cores (test_short_contractions_exact)
+    monkeypatch.setenv("ZPUCUDA_GEMM_SMALLK", "0")
     rng = np.random.default_rng(m * 7 + k * 3 + n)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
@@ -288,6 +291,33 @@ def test_persistent_form_infinities(zc, monkeypatch):
     got = zc.gemm(dev(a), dev(b)).cpu().numpy()
     check_no_device_error(zc)
     _exact_nonfinite(got, want)
+
+
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (300, 16, 4096), (77, 7, 133), (257, 32, 263), (64, 5, 8)])
+def test_short_contractions_exact(zc, ta, tb, m, k, n):
+    """k <= 32: zpu's own chain on CUDA cores, bit for bit the oracle's
+    kernels.gemm (FMA order and the scalar tail of each 128-column panel:
+    n = 133 and 263 leave 5 and 7 tail columns)."""
+    rng = np.random.default_rng(m * 31 + k * 7 + n)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    A = dev(a.T.copy()) if ta else dev(a)
+    B = dev(b.T.copy()) if tb else dev(b)
+    got = zc.gemm(A, B, trans_a=ta, trans_b=tb).cpu().numpy()
+    check_no_device_error(zc)
+    assert np.array_equal(got, zo.gemm(a, b)), (m, k, n, ta, tb)
+
+
+def test_short_contractions_batched_exact(zc):
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((5, 70, 12)).astype(np.float32)
+    b = rng.standard_normal((5, 12, 300)).astype(np.float32)
+    got = zc.gemm(dev(a), dev(b)).cpu().numpy()
+    check_no_device_error(zc)
+    for i in range(5):
+        assert np.array_equal(got[i], zo.gemm(a[i], b[i])), i
 
 
 def test_split_k_batched(zc):

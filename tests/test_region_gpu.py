@@ -1167,6 +1167,28 @@ def test_split_k_gemm_epilogues(zc):
             assert np.linalg.norm(got[11] - ref_h) <= 1e-5 * np.linalg.norm(ref_h)
 
 
+def test_short_contraction_epilogues(zc):
+    """matmul (k = 16) -> add(row bias) -> tanh as one short-contraction
+    launch: zpu's chain for the product, then the bias and tanh epilogue."""
+    rng = np.random.default_rng(97)
+    x = rng.standard_normal((300, 16)).astype(np.float32)
+    w = rng.standard_normal((16, 77)).astype(np.float32) * 0.3
+    b = rng.standard_normal(77).astype(np.float32)
+    F = zc.F32
+    args = [(1, F, (300, 16)), (2, F, (16, 77)), (3, F, (77,))]
+    mm = [("matmul", [1, 2], 10, -2, 0), ("add", [10, 3], 11, -2, 0), ("tanh", [11], 12, -2, 0)]
+    ins = [torch.from_numpy(v).cuda() for v in (x, w, b)]
+    want11 = (zo.gemm(x, w) + b).astype(np.float32)  # f32 add after zpu's chain
+    p = zc.Plan(args, [], mm[:2], [11])  # bias epilogue
+    assert p.num_kernels() == 1, p.describe()
+    (got11,) = [o.cpu().numpy() for o in p.run(ins)]
+    assert np.array_equal(got11, want11)
+    p = zc.Plan(args, [], mm, [12])  # bias + tanh epilogue
+    assert p.num_kernels() == 1, p.describe()
+    (got12,) = [o.cpu().numpy() for o in p.run(ins)]
+    assert np.max(np.abs(got12.astype(np.float64) - np.tanh(want11.astype(np.float64)))) <= 2e-7
+
+
 def test_persistent_gemm_epilogues(zc, monkeypatch):
     """The bias + tanh and bias epilogues in the persistent GEMM form (one CTA
     per SM walking its tiles) give the one-tile-per-CTA kernel's bits."""

@@ -1188,6 +1188,92 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
     }
 }
 
+// ------------------------------------------------ short contractions
+//
+// Products with k <= kSmallK (the MLP's g2 = gl W3^T has k = 16) are bound by
+// writing the result (and reading the epilogue's inputs), not by flops: one
+// K slice per tensor-core tile would leave every CTA in its set-up and store.
+// Here CUDA cores compute zpu's own chain per element -- kernels.gemm's FMA
+// order and its scalar tail (the columns past the last whole 8-lane vector of
+// a 128-column panel take c + a*b), src/zpu/kernels.zig:369-400 -- so the
+// bits are zpu's.  A 32 x 128 tile per 256-thread block, A rows and B columns
+// of the tile in shared memory, 4 rows x 4 consecutive columns per thread,
+// float4 stores.
+constexpr int kSmallK = 32;
+
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(256) smallk_gemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
+                                                          float *__restrict__ C, int64_t M, int64_t N, int k,
+                                                          int64_t lda, int64_t ldb, int64_t ldc,
+                                                          const __grid_constant__ GemmBatch bt, int64_t stride_c,
+                                                          const __grid_constant__ Epilogue epi) {
+    __shared__ float sa[32][kSmallK + 1];
+    __shared__ __align__(16) float sb[kSmallK][128];
+    int64_t oa, ob;
+    batch_offsets(bt, blockIdx.z, &oa, &ob);
+    A += oa;
+    B += ob;
+    C += (int64_t)blockIdx.z * stride_c;
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 128;
+    for (int i = threadIdx.x; i < 32 * kSmallK; i += 256) {  // A tile, zero past the edges
+        const int r = TA ? i % 32 : i / kSmallK, p = TA ? i / 32 : i % kSmallK;
+        const int64_t row = r0 + r;
+        sa[r][p] = (row < M && p < k) ? (TA ? A[(int64_t)p * lda + row] : A[row * lda + p]) : 0.0f;
+    }
+    for (int i = threadIdx.x; i < kSmallK * 128; i += 256) {  // B tile
+        const int p = TB ? i % kSmallK : i / 128, c = TB ? i / kSmallK : i % 128;
+        const int64_t col = c0 + c;
+        sb[p][c] = (p < k && col < N) ? (TB ? B[col * ldb + p] : B[(int64_t)p * ldb + col]) : 0.0f;
+    }
+    __syncthreads();
+    const int cg = (threadIdx.x & 31) * 4, rg = (threadIdx.x >> 5) * 4;
+    // the panel's vector-covered columns (c0 starts a 128-column panel)
+    const int64_t nv = ((N - c0 < 128 ? N - c0 : 128) / 8) * 8;
+    bool fused[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) fused[j] = cg + j < nv;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    for (int p = 0; p < k; p++) {
+        const float4 b4 = *(const float4 *)&sb[p][cg];
+        const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float a = sa[rg + i][p];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                acc[i][j] = fused[j] ? fmaf(a, bv[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(a, bv[j]));
+        }
+    }
+    const int64_t col = c0 + cg;
+    if (col >= N) return;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int64_t row = r0 + rg + i;
+        if (row >= M) break;
+        float y[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) y[j] = col + j < N ? epi_apply(epi, acc[i][j], row, col + j) : 0.0f;
+        float *cp = C + row * ldc + col;
+        float *lp = epi.lo_out ? epi.lo_out + row * ldc + col : nullptr;
+        if (col + 4 <= N && ((((uintptr_t)cp) & 15) == 0)) {
+            *(float4 *)cp = make_float4(y[0], y[1], y[2], y[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (col + j < N) cp[j] = y[j];
+        }
+        if (lp) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (col + j < N) lp[j] = lo1(y[j]);
+        }
+    }
+}
+
 // ------------------------------------------------------------- host side
 
 // Stream-ordered scratch for the lo halves of presplit operands: one memory
@@ -1431,6 +1517,13 @@ int raster_group(int64_t rows, int64_t cols) {
     return rows > 32 && cols > 32 ? 16 : 0;
 }
 
+// Whether contractions of k <= kSmallK run on CUDA cores (default);
+// ZPUCUDA_GEMM_SMALLK=0 sends them to the tensor cores (read at every call).
+bool use_smallk() {
+    const char *e = getenv("ZPUCUDA_GEMM_SMALLK");
+    return !(e && e[0] == '0' && e[1] == 0);
+}
+
 // Whether result tiles leave through TMA stores (default) rather than the
 // folding warps' own stores; ZPUCUDA_GEMM_TMA_STORE=0 turns them off (read
 // at every call).
@@ -1501,6 +1594,20 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
     if (!A || !B) return ZPUCUDA_ERR_INVALID_ARGUMENT;
     if ((!ta && lda < k) || (ta && lda < m) || (!tb && ldb < n) || (tb && ldb < k)) return ZPUCUDA_ERR_INVALID_SHAPE;
     if (batches > 65535 || (m + BM - 1) / BM > 65535) return ZPUCUDA_ERR_NOT_SUPPORTED;
+
+    // a short contraction: zpu's chain on CUDA cores (bound by the result's bytes)
+    if (k <= kSmallK && epi.mode != EPI_SCATTER && (m + 31) / 32 <= 65535 && use_smallk()) {
+        dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 31) / 32), (unsigned)batches);
+#define ZC_SK(TA_, TB_) \
+    smallk_gemm_kernel<TA_, TB_><<<grid, 256, 0, s>>>(A, B, C, m, n, (int)k, lda, ldb, ldc, bt, stride_c, epi)
+        if (!ta && !tb) ZC_SK(false, false);
+        else if (!ta && tb) ZC_SK(false, true);
+        else if (ta && !tb) ZC_SK(true, false);
+        else ZC_SK(true, true);
+#undef ZC_SK
+        ZC_LAUNCHED("smallk_gemm_kernel");
+        return ZPUCUDA_OK;
+    }
 
     // the tensor-core path needs what a TMA tensor map can describe
     int64_t mat_a = 0, mat_b = 0;
