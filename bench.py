@@ -853,6 +853,20 @@ def _only_kernel(kind, steps, warmup):
         fn = lambda: zc.matmul(a, b, out=o)
         nbytes = None
         flops = 2 * n ** 3
+    elif kind == "gemm_smallk":  # a short contraction (k = 16, like the MLP's g2): zpu's chain, CUDA cores
+        m, n, k = 8192, 4096, 16
+        a = zc.rng_uniform(SEED_X, m * k, -1.0, 1.0).view(m, k)
+        b = zc.rng_uniform(SEED_X + 1, n * k, -1.0, 1.0).view(n, k)
+        o = torch.empty(m, n, device="cuda")
+        fn = lambda: zc.gemm(a, b, out=o, trans_b=True)
+        nbytes = m * n * 4 + (m + n) * k * 4
+    elif kind in ("transpose_f16", "transpose_u8"):  # toContiguous of a transposed view, 256 MiB (> L2)
+        dt = torch.float16 if kind == "transpose_f16" else torch.uint8
+        r, c = (16384, 8192) if dt == torch.float16 else (16384, 16384)
+        x = (zc.rng_uniform(SEED_X, r * c, 0.0, 100.0).view(r, c)).to(dt)
+        out = torch.empty(c, r, dtype=dt, device="cuda")
+        fn = lambda: zc.tensor_copy(x.transpose(0, 1), out)
+        nbytes = 2 * r * c * x.element_size()
     elif kind == "gemm_convert":  # f16 @ f32: zpu's gemmF64 loop
         n = 1024
         a = zc.rng_uniform(SEED_X, n * n, -1.0, 1.0).view(n, n).half()
@@ -873,7 +887,7 @@ def _only_kernel(kind, steps, warmup):
 
 
 KERNEL_CASES = ("region_bytecode", "sum_sq_bulk", "cumsum", "take", "scatter_add", "rng_normal", "peer_reduce",
-                "gather_copy", "gemm_fma_fallback", "gemm_convert")
+                "gather_copy", "gemm_fma_fallback", "gemm_convert", "gemm_smallk", "transpose_f16", "transpose_u8")
 
 ONLY_CASES = {
     "chain": None, "mlp": None, "chain_sharded": None,

@@ -93,12 +93,12 @@ def spread_values(k, n):
 @pytest.mark.parametrize("src", range(9), ids=NAMES)
 def test_transposed_aligned_views(zc, src, dst):
     """16-byte aligned views (every dim a multiple of 16 elements, ragged
-    64-tiles) take the 16-byte transpose for every element size; a
+    64- and 128-tiles) take the 16-byte transpose for every element size; a
     one-element offset with an odd ld takes the 1-element kernel; a flipped
     column axis (negative ld) and a broadcast batch axis (stride 0) cover the
     addressing of both."""
     cases = []
-    for shape in [(144, 80), (3, 48, 32), (272, 256), (2, 2, 16, 32)]:
+    for shape in [(144, 80), (3, 48, 32), (272, 256), (2, 2, 16, 32), (400, 272)]:
         x = spread_values(src, int(np.prod(shape))).reshape(shape)
         cases.append((torch.from_numpy(x).cuda().transpose(-1, -2), np.swapaxes(x, -1, -2)))
     x = spread_values(src, 67 * 131).reshape(67, 131)  # offset 1 element, ld 131

@@ -1196,10 +1196,11 @@ __global__ void __launch_bounds__(256) fma_gemm_kernel(const float *__restrict__
 // Here CUDA cores compute zpu's own chain per element -- kernels.gemm's FMA
 // order and its scalar tail (the columns past the last whole 8-lane vector of
 // a 128-column panel take c + a*b), src/zpu/kernels.zig:369-400 -- so the
-// bits are zpu's.  A 32 x 128 tile per 256-thread block, A rows and B columns
-// of the tile in shared memory, 4 rows x 4 consecutive columns per thread,
-// float4 stores.
+// bits are zpu's.  A block takes 128 columns and kSmallRowTiles tiles of 32
+// rows: the B columns staged once in shared memory, each A tile in turn,
+// 4 rows x 4 consecutive columns per thread, float4 stores.
 constexpr int kSmallK = 32;
+constexpr int kSmallRowTiles = 4;  // 32-row tiles per block (the B tile staged once)
 
 template <bool TA, bool TB>
 __global__ void __launch_bounds__(256) smallk_gemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
@@ -1214,62 +1215,100 @@ __global__ void __launch_bounds__(256) smallk_gemm_kernel(const float *__restric
     A += oa;
     B += ob;
     C += (int64_t)blockIdx.z * stride_c;
-    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 128;
-    for (int i = threadIdx.x; i < 32 * kSmallK; i += 256) {  // A tile, zero past the edges
-        const int r = TA ? i % 32 : i / kSmallK, p = TA ? i / 32 : i % kSmallK;
-        const int64_t row = r0 + r;
-        sa[r][p] = (row < M && p < k) ? (TA ? A[(int64_t)p * lda + row] : A[row * lda + p]) : 0.0f;
-    }
-    for (int i = threadIdx.x; i < kSmallK * 128; i += 256) {  // B tile
-        const int p = TB ? i % kSmallK : i / 128, c = TB ? i / kSmallK : i % 128;
+    const int64_t c0 = (int64_t)blockIdx.x * 128;
+    // tiles zero past the matrix edges (slices p >= k are never read); a
+    // thread's loads first, then its shared-memory stores, so the loads are
+    // in flight together.  The B tile is staged once for kSmallRowTiles A tiles.
+    constexpr int UA = 32 * kSmallK / 256, UB = kSmallK * 128 / 256;
+    float vb[UB];
+#pragma unroll
+    for (int u = 0; u < UB; u++) {  // consecutive threads take consecutive columns
+        const int i = (int)threadIdx.x + u * 256, p = i / 128, c = i % 128;
         const int64_t col = c0 + c;
-        sb[p][c] = (p < k && col < N) ? (TB ? B[col * ldb + p] : B[(int64_t)p * ldb + col]) : 0.0f;
+        vb[u] = (p < k && col < N) ? (TB ? B[col * ldb + p] : B[(int64_t)p * ldb + col]) : 0.0f;
     }
-    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < UB; u++) {
+        const int i = (int)threadIdx.x + u * 256;
+        sb[i / 128][i % 128] = vb[u];
+    }
     const int cg = (threadIdx.x & 31) * 4, rg = (threadIdx.x >> 5) * 4;
     // the panel's vector-covered columns (c0 starts a 128-column panel)
     const int64_t nv = ((N - c0 < 128 ? N - c0 : 128) / 8) * 8;
     bool fused[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) fused[j] = cg + j < nv;
-    float acc[4][4];
+    const int64_t col = c0 + cg;
+    for (int rt = 0; rt < kSmallRowTiles; rt++) {
+        const int64_t r0 = ((int64_t)blockIdx.y * kSmallRowTiles + rt) * 32;
+        if (r0 >= M) break;  // uniform over the block
+        float va[UA];
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+        for (int u = 0; u < UA; u++) {
+            const int i = (int)threadIdx.x + u * 256;
+            const int r = TA ? i % 32 : i / kSmallK, p = TA ? i / 32 : i % kSmallK;
+            const int64_t row = r0 + r;
+            va[u] = (row < M && p < k) ? (TA ? A[(int64_t)p * lda + row] : A[row * lda + p]) : 0.0f;
+        }
+        __syncthreads();  // the last tile's readers are done with sa
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    for (int p = 0; p < k; p++) {
-        const float4 b4 = *(const float4 *)&sb[p][cg];
-        const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+        for (int u = 0; u < UA; u++) {
+            const int i = (int)threadIdx.x + u * 256;
+            sa[TA ? i % 32 : i / kSmallK][TA ? i / 32 : i % kSmallK] = va[u];
+        }
+        __syncthreads();
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        if (fused[3]) {  // all four columns vector-covered (the common case): plain FMA chains
+            for (int p = 0; p < k; p++) {
+                const float4 b4 = *(const float4 *)&sb[p][cg];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float a = sa[rg + i][p];
+                    acc[i][0] = fmaf(a, b4.x, acc[i][0]);
+                    acc[i][1] = fmaf(a, b4.y, acc[i][1]);
+                    acc[i][2] = fmaf(a, b4.z, acc[i][2]);
+                    acc[i][3] = fmaf(a, b4.w, acc[i][3]);
+                }
+            }
+        } else {
+            for (int p = 0; p < k; p++) {
+                const float4 b4 = *(const float4 *)&sb[p][cg];
+                const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float a = sa[rg + i][p];
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        acc[i][j] = fused[j] ? fmaf(a, bv[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(a, bv[j]));
+                }
+            }
+        }
+        if (col >= N) continue;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const float a = sa[rg + i][p];
+            const int64_t row = r0 + rg + i;
+            if (row >= M) break;
+            float y[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                acc[i][j] = fused[j] ? fmaf(a, bv[j], acc[i][j]) : __fadd_rn(acc[i][j], __fmul_rn(a, bv[j]));
-        }
-    }
-    const int64_t col = c0 + cg;
-    if (col >= N) return;
+            for (int j = 0; j < 4; j++) y[j] = col + j < N ? epi_apply(epi, acc[i][j], row, col + j) : 0.0f;
+            float *cp = C + row * ldc + col;
+            float *lp = epi.lo_out ? epi.lo_out + row * ldc + col : nullptr;
+            if (col + 4 <= N && ((((uintptr_t)cp) & 15) == 0)) {
+                *(float4 *)cp = make_float4(y[0], y[1], y[2], y[3]);
+            } else {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int64_t row = r0 + rg + i;
-        if (row >= M) break;
-        float y[4];
+                for (int j = 0; j < 4; j++)
+                    if (col + j < N) cp[j] = y[j];
+            }
+            if (lp) {
 #pragma unroll
-        for (int j = 0; j < 4; j++) y[j] = col + j < N ? epi_apply(epi, acc[i][j], row, col + j) : 0.0f;
-        float *cp = C + row * ldc + col;
-        float *lp = epi.lo_out ? epi.lo_out + row * ldc + col : nullptr;
-        if (col + 4 <= N && ((((uintptr_t)cp) & 15) == 0)) {
-            *(float4 *)cp = make_float4(y[0], y[1], y[2], y[3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (col + j < N) cp[j] = y[j];
-        }
-        if (lp) {
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (col + j < N) lp[j] = lo1(y[j]);
+                for (int j = 0; j < 4; j++)
+                    if (col + j < N) lp[j] = lo1(y[j]);
+            }
         }
     }
 }
@@ -1597,7 +1636,8 @@ int gemm_f32_device_lo(const float *A, const float *B, float *C, int64_t m, int6
 
     // a short contraction: zpu's chain on CUDA cores (bound by the result's bytes)
     if (k <= kSmallK && epi.mode != EPI_SCATTER && (m + 31) / 32 <= 65535 && use_smallk()) {
-        dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 31) / 32), (unsigned)batches);
+        dim3 grid((unsigned)((n + 127) / 128), (unsigned)((m + 32 * kSmallRowTiles - 1) / (32 * kSmallRowTiles)),
+                  (unsigned)batches);
 #define ZC_SK(TA_, TB_) \
     smallk_gemm_kernel<TA_, TB_><<<grid, 256, 0, s>>>(A, B, C, m, n, (int)k, lda, ldb, ldc, bt, stride_c, epi)
         if (!ta && !tb) ZC_SK(false, false);

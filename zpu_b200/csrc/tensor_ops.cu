@@ -8,10 +8,9 @@
 //   * a plain gather, one thread per output element (coalesced writes; reads
 //     coalesced when the view's last axis has unit stride);
 //   * a tiled transpose for views whose unit-stride axis is the second to
-//     last (the swapLastTwo views of the matmul VJP): 64 x 64 tiles through
-//     shared memory so reads and writes both coalesce, with 16-byte global
-//     accesses when the view is 16-byte aligned (f32 at the speed of a
-//     plain copy);
+//     last (the swapLastTwo views of the matmul VJP): tiles through shared
+//     memory so reads and writes both coalesce, with 16-byte global accesses
+//     when the view is 16-byte aligned (f32 at the speed of a plain copy);
 //   * cudaMemcpyAsync for a contiguous view of the same type (clone).
 // HBM-bound: 1 read + 1 write per element.
 #include <cuda_fp16.h>
@@ -187,26 +186,33 @@ __global__ void __launch_bounds__(256) copy_transpose_kernel(const __grid_consta
 // The same transpose with 16-byte global accesses, for views that are
 // 16-byte aligned: base pointers, ld, the batch strides and R multiples of
 // VS = 16 / sizeof(S) elements, C a multiple of VD = 16 / sizeof(D).  On the
-// load side 64 / VS lanes read one column (VS rows each), on the store side
-// 64 / VD lanes write one row (VD columns each); shared accesses stay one
-// element wide (pitch 65).
+// load side T / VS lanes read one column (VS rows each), on the store side
+// T / VD lanes write one row (VD columns each); shared accesses stay one
+// element wide (pitch T + 1).  T = 64 for 4- and 8-byte sources, 128 for 1-
+// and 2-byte ones (a block then still moves 16-64 KiB: 64 x 64 tiles of
+// 2-byte elements left f16 at 0.58 and the byte types at 0.47 of HBM).
+template <class S>
+constexpr int transpose_tile() { return sizeof(S) <= 2 ? 128 : 64; }
+
 template <class S, class D>
 __global__ void __launch_bounds__(256) copy_transpose16_kernel(const __grid_constant__ View v, D *dst, int64_t R,
                                                                      int64_t C, int64_t ld, int64_t b0) {
+    constexpr int T = transpose_tile<S>();
     constexpr int VS = 16 / sizeof(S), VD = 16 / sizeof(D);
-    constexpr int LS = kTile / VS, LD = kTile / VD;  // lanes per column / per row
+    constexpr int LS = T / VS, LD = T / VD;  // lanes per column / per row
     static_assert(VS * sizeof(S) == 16 && VD * sizeof(D) == 16, "element size divides 16");
+    static_assert(256 % LS == 0 && 256 % LD == 0, "whole columns / rows per pass");
     struct alignas(16) VecS { S e[VS]; };
     struct alignas(16) VecD { D e[VD]; };
-    __shared__ S tile[kTile][kTile + 1];  // [column][row]
-    const int64_t r0 = (int64_t)blockIdx.y * kTile, c0 = (int64_t)blockIdx.x * kTile;
-    const int rr = (int)min((int64_t)kTile, R - r0), cc = (int)min((int64_t)kTile, C - c0);
+    __shared__ S tile[T][T + 1];  // [column][row]
+    const int64_t r0 = (int64_t)blockIdx.y * T, c0 = (int64_t)blockIdx.x * T;
+    const int rr = (int)min((int64_t)T, R - r0), cc = (int)min((int64_t)T, C - c0);
     const int t = threadIdx.x;
     const int64_t b = b0 + blockIdx.z;
     const S *s = (const S *)v.data + batch_offset(v, b) + c0 * ld + r0;
     const int ql = VS * (t % LS), wl = t / LS;
 #pragma unroll
-    for (int j = 0; j < kTile; j += 256 / LS) {
+    for (int j = 0; j < T; j += 256 / LS) {
         const int c = wl + j;
         if (c < cc && ql < rr) {
             const VecS x = *(const VecS *)(s + (int64_t)c * ld + ql);
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(256) copy_transpose16_kernel(const __grid_cons
     D *d = dst + (b * R + r0) * C + c0;
     const int qs = VD * (t % LD), ws = t / LD;
 #pragma unroll
-    for (int j = 0; j < kTile; j += 256 / LD) {
+    for (int j = 0; j < T; j += 256 / LD) {
         const int r = ws + j;
         if (r < rr && qs < cc) {
             VecD y;
@@ -254,7 +260,8 @@ int launch_copy(const View &v, void *dst, int64_t n, bool contig, cudaStream_t s
             nb *= v.dims[a];
             aligned16 = aligned16 && v.strides[a] % VS == 0;
         }
-        const int64_t gx = (C + kTile - 1) / kTile, gy = (R + kTile - 1) / kTile;
+        const int64_t T = aligned16 ? transpose_tile<S>() : kTile;
+        const int64_t gx = (C + T - 1) / T, gy = (R + T - 1) / T;
         if (gy <= 65535 && gx <= 0x7fffffff) {
             // one launch per 65535 batches (the grid's z limit)
             for (int64_t b0 = 0; b0 < nb; b0 += 65535) {
