@@ -204,7 +204,7 @@ def test_split_k_shapes(zc, ta, tb, m, k, n):
     assert np.array_equal(got, again)  # deterministic
 
 
-@pytest.mark.parametrize("splits", ["2", "3", "5", "8"])
+@pytest.mark.parametrize("splits", ["2", "3", "4", "5", "8"])
 @pytest.mark.parametrize("bn", ["128", "256"])
 @pytest.mark.parametrize("ta,tb", [(False, False), (True, True)])
 def test_split_k_cluster_counts(zc, monkeypatch, splits, bn, ta, tb):
