@@ -42,9 +42,10 @@
 //               same (swizzled) position, so hi and lo tiles share their
 //               descriptor layout (idle in the PRE form);
 //   warps 8-15  also fold each finished chunk (tcgen05.ld / tcgen05.st
-//               32x32b) whenever they wait, then store the tile; warp w owns
-//               TMEM lanes 32 (w % 4) .. +31 and columns BN/2 ((w - 8) / 4)
-//               .. + BN/2 - 1.
+//               32x32b) whenever they wait, then store the tile (32 x 32
+//               boxes through TMA stores where C has a tensor map); warp w
+//               owns TMEM lanes 32 (w % 4) .. +31 and columns BN/2
+//               ((w - 8) / 4) .. + BN/2 - 1.
 // TMEM columns: chunk accumulators below 256, running sum from 256.
 // K-major operands use the 128-byte swizzle; MN-major ones (the matmul VJP's
 // swapLastTwo views, read in place) use the 128-byte swizzle with 32-byte
@@ -52,9 +53,13 @@
 // Every mbarrier wait is bounded: a wait that runs out sets an error word
 // (zpucuda_check_device) and its warp stops; TMEM is freed before exit.
 //
-// Shapes the tensor maps cannot describe (row pitch not a multiple of 4
-// elements, base not 16-byte aligned, batch offsets that are not whole
-// matrices) run a plain FMA-chain kernel instead.
+// Few output tiles split K over a thread-block cluster whose CTAs add their
+// partials through distributed shared memory; many tiles over a short K run
+// a persistent form (tf32x3_gemm_persistent_kernel); contractions of k <= 32
+// run zpu's own chain on CUDA cores (smallk_gemm_kernel).  Shapes the tensor
+// maps cannot describe (row pitch not a multiple of 4 elements, base not
+// 16-byte aligned, batch offsets that are not whole matrices) run a plain
+// FMA-chain kernel instead.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
