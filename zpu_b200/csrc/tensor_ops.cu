@@ -235,6 +235,147 @@ __global__ void __launch_bounds__(256) copy_transpose16_kernel(const __grid_cons
     }
 }
 
+// One-byte elements in and out (u8, i8, bool): moving each byte through
+// shared memory on its own leaves the 128 x 128 transpose bound by the SM
+// (75 %).  Here a thread loads four columns' 4-byte runs (rows 4q .. 4q+3),
+// transposes the 4 x 4 bytes in registers (__byte_perm) and stores four
+// words, one per row, into a word tile [row][column quad]; the store side
+// reads 16-byte runs of a row.  Word w of row r sits at w ^ ((r >> 2) & 31)
+// (the lanes of a warp, rows 4q + i for q = 0 .. 31, then write 32
+// different banks); a 16-byte run stays in one aligned group of four words,
+// permuted by the low two bits of that XOR, which the reader undoes.  Same
+// preconditions as copy_transpose16_kernel.
+template <class S, class D>
+__global__ void __launch_bounds__(256) copy_transpose_b1_kernel(const __grid_constant__ View v, D *dst, int64_t R,
+                                                                      int64_t C, int64_t ld, int64_t b0) {
+    static_assert(sizeof(S) == 1 && sizeof(D) == 1, "one-byte elements");
+    constexpr int T = 128;
+    __shared__ uint32_t tile[T][T / 4];  // [row][column quad], swizzled
+    const int64_t r0 = (int64_t)blockIdx.y * T, c0 = (int64_t)blockIdx.x * T;
+    const int rr = (int)min((int64_t)T, R - r0), cc = (int)min((int64_t)T, C - c0);
+    const int t = threadIdx.x;
+    const int64_t b = b0 + blockIdx.z;
+    const uint8_t *s = (const uint8_t *)v.data + batch_offset(v, b) + c0 * ld + r0;
+    uint32_t w[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {  // block u: row quad t % 32, column quad t / 32 + 8 u
+        const int q = t & 31, cq = (t >> 5) + 8 * u;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int c = 4 * cq + j;
+            w[u][j] = (c < cc && 4 * q < rr) ? *(const uint32_t *)(s + (int64_t)c * ld + 4 * q) : 0u;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int q = t & 31, cq = (t >> 5) + 8 * u;
+        const uint32_t lo01 = __byte_perm(w[u][0], w[u][1], 0x5140), hi01 = __byte_perm(w[u][0], w[u][1], 0x7362);
+        const uint32_t lo23 = __byte_perm(w[u][2], w[u][3], 0x5140), hi23 = __byte_perm(w[u][2], w[u][3], 0x7362);
+        const uint32_t o[4] = {__byte_perm(lo01, lo23, 0x5410), __byte_perm(lo01, lo23, 0x7632),
+                               __byte_perm(hi01, hi23, 0x5410), __byte_perm(hi01, hi23, 0x7632)};
+#pragma unroll
+        for (int i = 0; i < 4; i++) tile[4 * q + i][cq ^ q] = o[i];  // (r >> 2) & 31 = q for r = 4q + i
+    }
+    __syncthreads();
+    D *d = dst + (b * R + r0) * C + c0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {  // 16-byte run k = t % 8 of row t / 8 + 32 u
+        const int r = (t >> 3) + 32 * u, k = t & 7;
+        if (r >= rr || 16 * k >= cc) continue;
+        const int x = (r >> 2) & 31;
+        const uint4 g = *(const uint4 *)&tile[r][(4 * k) ^ (x & ~3)];
+        const uint32_t gv[4] = {g.x, g.y, g.z, g.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const int sel = m ^ (x & 3);
+            ow[m] = sel == 0 ? gv[0] : sel == 1 ? gv[1] : sel == 2 ? gv[2] : gv[3];
+        }
+        if (!std::is_same<S, D>::value) {
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                uint32_t y = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    S xe;
+                    const uint8_t byte = (uint8_t)(ow[m] >> (8 * e));
+                    memcpy(&xe, &byte, 1);
+                    const D de = convert<S, D>(xe);
+                    uint8_t db;
+                    memcpy(&db, &de, 1);
+                    y |= (uint32_t)db << (8 * e);
+                }
+                ow[m] = y;
+            }
+        }
+        *(uint4 *)(d + (int64_t)r * C + 16 * k) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+}
+
+// The same for two-byte elements in and out (f16, i16): a thread loads two
+// columns' 4-byte runs (rows 2q, 2q + 1), swaps their halves into one word
+// per row (__byte_perm) and stores the two words into a word tile [row]
+// [column pair], word w of row r at w ^ ((r >> 1) & 31); 16-byte runs of a
+// row are read back as above.
+template <class S, class D>
+__global__ void __launch_bounds__(256) copy_transpose_b2_kernel(const __grid_constant__ View v, D *dst, int64_t R,
+                                                                      int64_t C, int64_t ld, int64_t b0) {
+    static_assert(sizeof(S) == 2 && sizeof(D) == 2, "two-byte elements");
+    constexpr int T = 128;
+    __shared__ uint32_t tile[T][T / 2];  // [row][column pair], swizzled
+    const int64_t r0 = (int64_t)blockIdx.y * T, c0 = (int64_t)blockIdx.x * T;
+    const int rr = (int)min((int64_t)T, R - r0), cc = (int)min((int64_t)T, C - c0);
+    const int t = threadIdx.x;
+    const int64_t b = b0 + blockIdx.z;
+    const uint16_t *s = (const uint16_t *)v.data + batch_offset(v, b) + c0 * ld + r0;
+#pragma unroll 4
+    for (int u = 0; u < 16; u++) {  // block: row pair q, column pair cp
+        const int idx = t + 256 * u, q = idx & 63, cp = idx >> 6;
+        uint32_t w[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int c = 2 * cp + j;
+            w[j] = (c < cc && 2 * q < rr) ? *(const uint32_t *)(s + (int64_t)c * ld + 2 * q) : 0u;
+        }
+        tile[2 * q][cp ^ (q & 31)] = __byte_perm(w[0], w[1], 0x5410);
+        tile[2 * q + 1][cp ^ (q & 31)] = __byte_perm(w[0], w[1], 0x7632);
+    }
+    __syncthreads();
+    D *d = dst + (b * R + r0) * C + c0;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {  // 16-byte run k = t % 16 of row t / 16 + 16 u
+        const int idx = t + 256 * u, r = idx >> 4, k = idx & 15;
+        if (r >= rr || 8 * k >= cc) continue;
+        const int x = (r >> 1) & 31;
+        const uint4 g = *(const uint4 *)&tile[r][(4 * k) ^ (x & ~3)];
+        const uint32_t gv[4] = {g.x, g.y, g.z, g.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            const int sel = m ^ (x & 3);
+            ow[m] = sel == 0 ? gv[0] : sel == 1 ? gv[1] : sel == 2 ? gv[2] : gv[3];
+        }
+        if (!std::is_same<S, D>::value) {
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                uint32_t y = 0;
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    S xe;
+                    const uint16_t h = (uint16_t)(ow[m] >> (16 * e));
+                    memcpy(&xe, &h, 2);
+                    const D de = convert<S, D>(xe);
+                    uint16_t dh;
+                    memcpy(&dh, &de, 2);
+                    y |= (uint32_t)dh << (16 * e);
+                }
+                ow[m] = y;
+            }
+        }
+        *(uint4 *)(d + (int64_t)r * C + 8 * k) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+}
+
 size_t dtype_size(int dt) {
     switch (dt) {
     case 0: case 3: return 8;               // f64, i64
@@ -266,6 +407,20 @@ int launch_copy(const View &v, void *dst, int64_t n, bool contig, cudaStream_t s
             // one launch per 65535 batches (the grid's z limit)
             for (int64_t b0 = 0; b0 < nb; b0 += 65535) {
                 const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(nb - b0 < 65535 ? nb - b0 : 65535));
+                if constexpr (sizeof(S) == 1 && sizeof(D) == 1) {
+                    if (aligned16) {
+                        copy_transpose_b1_kernel<S, D><<<grid, 256, 0, s>>>(v, (D *)dst, R, C, ld, b0);
+                        ZC_LAUNCHED("tensor copy (tiled transpose, one-byte words)");
+                        continue;
+                    }
+                }
+                if constexpr (sizeof(S) == 2 && sizeof(D) == 2) {
+                    if (aligned16) {
+                        copy_transpose_b2_kernel<S, D><<<grid, 256, 0, s>>>(v, (D *)dst, R, C, ld, b0);
+                        ZC_LAUNCHED("tensor copy (tiled transpose, two-byte words)");
+                        continue;
+                    }
+                }
                 if (aligned16) {
                     copy_transpose16_kernel<S, D><<<grid, 256, 0, s>>>(v, (D *)dst, R, C, ld, b0);
                     ZC_LAUNCHED("tensor copy (tiled transpose, 16-byte)");
