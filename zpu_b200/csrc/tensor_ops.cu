@@ -313,10 +313,10 @@ __global__ void __launch_bounds__(256) copy_transpose_b1_kernel(const __grid_con
 }
 
 // The same for two-byte elements in and out (f16, i16): a thread loads two
-// columns' 4-byte runs (rows 2q, 2q + 1), swaps their halves into one word
-// per row (__byte_perm) and stores the two words into a word tile [row]
-// [column pair], word w of row r at w ^ ((r >> 1) & 31); 16-byte runs of a
-// row are read back as above.
+// columns' 8-byte runs (rows 4q .. 4q + 3), swaps their halves into one
+// word per row (__byte_perm) and stores the four words into a word tile
+// [row][column pair], word w of row r at w ^ ((r >> 2) & 31); 16-byte runs
+// of a row are read back as above.
 template <class S, class D>
 __global__ void __launch_bounds__(256) copy_transpose_b2_kernel(const __grid_constant__ View v, D *dst, int64_t R,
                                                                       int64_t C, int64_t ld, int64_t b0) {
@@ -329,16 +329,19 @@ __global__ void __launch_bounds__(256) copy_transpose_b2_kernel(const __grid_con
     const int64_t b = b0 + blockIdx.z;
     const uint16_t *s = (const uint16_t *)v.data + batch_offset(v, b) + c0 * ld + r0;
 #pragma unroll 4
-    for (int u = 0; u < 16; u++) {  // block: row pair q, column pair cp
-        const int idx = t + 256 * u, q = idx & 63, cp = idx >> 6;
-        uint32_t w[2];
+    for (int u = 0; u < 8; u++) {  // block: row quad q, column pair cp
+        const int idx = t + 256 * u, q = idx & 31, cp = idx >> 5;
+        uint2 w[2];
 #pragma unroll
         for (int j = 0; j < 2; j++) {
             const int c = 2 * cp + j;
-            w[j] = (c < cc && 2 * q < rr) ? *(const uint32_t *)(s + (int64_t)c * ld + 2 * q) : 0u;
+            w[j] = (c < cc && 4 * q < rr) ? *(const uint2 *)(s + (int64_t)c * ld + 4 * q) : make_uint2(0u, 0u);
         }
-        tile[2 * q][cp ^ (q & 31)] = __byte_perm(w[0], w[1], 0x5410);
-        tile[2 * q + 1][cp ^ (q & 31)] = __byte_perm(w[0], w[1], 0x7632);
+        const int x = cp ^ q;
+        tile[4 * q][x] = __byte_perm(w[0].x, w[1].x, 0x5410);
+        tile[4 * q + 1][x] = __byte_perm(w[0].x, w[1].x, 0x7632);
+        tile[4 * q + 2][x] = __byte_perm(w[0].y, w[1].y, 0x5410);
+        tile[4 * q + 3][x] = __byte_perm(w[0].y, w[1].y, 0x7632);
     }
     __syncthreads();
     D *d = dst + (b * R + r0) * C + c0;
@@ -346,7 +349,7 @@ __global__ void __launch_bounds__(256) copy_transpose_b2_kernel(const __grid_con
     for (int u = 0; u < 8; u++) {  // 16-byte run k = t % 16 of row t / 16 + 16 u
         const int idx = t + 256 * u, r = idx >> 4, k = idx & 15;
         if (r >= rr || 8 * k >= cc) continue;
-        const int x = (r >> 1) & 31;
+        const int x = (r >> 2) & 31;
         const uint4 g = *(const uint4 *)&tile[r][(4 * k) ^ (x & ~3)];
         const uint32_t gv[4] = {g.x, g.y, g.z, g.w};
         uint32_t ow[4];
